@@ -1,0 +1,118 @@
+/*
+ * mstar_b200 — C ABI of the B200 (sm_100a) block-quantized linear kernels.
+ *
+ * Drop-in boundary for the reference's native Q8_0/Q4_0 contractions
+ * (rohanchanani/mstar_accelerators). Every entry point below names the
+ * reference interface it replaces. Plain pointers and sizes only; no torch
+ * types. Device pointers are CUDA global memory of the current device.
+ *
+ * Conventions, kept from the reference:
+ *  - *_abi() and *_capability() return int 1 when usable
+ *    (backends/cpu_ggml/encoder.h:29-31).
+ *  - create(...) returns an opaque handle, or NULL with a message in
+ *    (error, error_size) (encoder.h:32-37).
+ *  - run(...)/close(...) return 0 on success, -1 with a message on error,
+ *    and never throw (encoder.cpp:811-834). close rejects a busy handle.
+ *  - The two q8cpu mirrors return errno codes (0, EINVAL, EDOM, ENOTSUP)
+ *    exactly like backends/cpu_q8/readout.c:21-54.
+ * B200 differences: every run takes a cudaStream_t (passed as void *) and is
+ * stream-ordered; extents, alignment and disjointness are validated on the
+ * host before any launch; borrowed inputs must stay valid until the stream
+ * reaches the call's completion. Results that the reference reports through
+ * a return code after computing (a nonfinite readout input) are written to a
+ * caller-visible device status word instead.
+ */
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(_WIN32)
+#define MSTAR_B200_API __declspec(dllexport)
+#else
+#define MSTAR_B200_API __attribute__((visibility("default")))
+#endif
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Activation quantizer rounding variants of ggml quantize_row_q8_0. */
+enum mstar_b200_q8_rounding {
+    MSTAR_B200_Q8_REF = 0, /* ggml-quants.c:276-297: id = 1/d, roundf */
+    MSTAR_B200_Q8_ARM = 1, /* ggml-cpu/arch/arm/quants.c:41-75: id = 1/d, half-even (default) */
+    MSTAR_B200_Q8_X86 = 2, /* ggml-cpu/arch/x86/quants.c:302-350: id = 127/amax, half-even */
+};
+enum mstar_b200_format { MSTAR_B200_Q8_0 = 8, MSTAR_B200_Q4_0 = 4 };
+/* Epilogue flags of mstar_b200_linear_run; applied in this order after the
+ * block-quantized dot, each as the reference's separate fp32 ggml op. */
+enum mstar_b200_epilogue {
+    MSTAR_B200_BIAS = 1,      /* ggml_add(mul_mat, bias)              decoder.cpp:498-500 */
+    MSTAR_B200_GELU = 2,      /* ggml_gelu, fp16-table tanh form      decoder.cpp:580     */
+    MSTAR_B200_RESIDUAL = 4,  /* ggml_add(current, linear)            decoder.cpp:565-581 */
+    MSTAR_B200_GELU_ERF = 8,  /* ggml_gelu_erf (F32 graphs)           decoder.cpp:581     */
+};
+
+/* --- library identity (encoder.h:29-31, backends/torch/q8.py:42-77) -------- */
+MSTAR_B200_API int mstar_b200_abi(void);
+/* 1 iff the current CUDA device is compute capability 10.0 (B200) and this
+ * library's sm_100a kernels load on it; 0 otherwise (never a fallback). */
+MSTAR_B200_API int mstar_b200_capability(void);
+
+/* --- weight packers ------------------------------------------------------------
+ * Logical fp32 [rows][width] (device) -> canonical ggml blocks (device),
+ * bit-exact with the reference packers:
+ *   Q8_0, preround=1: decoder.cpp:307-316 upload_q8 (fp16 pre-round, then
+ *                     quantize_row_q8_0_ref);  preround=0: pi_v3d/q8.py:16-45.
+ *   Q4_0:             cpu_decoder_pack_readout_q4, decoder.cpp:816-842
+ *                     (fp16 pre-round, quantize_row_q4_0_ref); fused=1 rounds
+ *                     x*id+8.5 once (FMA contract), fused=0 twice
+ *                     (tests/test_cpu_ggml_q4_readout.py:72-88).
+ * Rejects nonfinite input ("nonfinite") and fp16 overflow ("overflows F16")
+ * like decoder.cpp:829-833; those checks synchronise the stream. */
+MSTAR_B200_API int mstar_b200_pack(int format, const float *input, uint64_t input_bytes,
+    void *output, uint64_t output_bytes, int64_t rows, int64_t width, int preround, int fused,
+    void *stream, char *error, size_t error_size);
+
+/* --- q8cpu mirrors (backends/cpu_q8/readout.c:21-54) ---------------------------
+ * mstar_b200_q8_quantize: fp32 x[rows][k] (device) -> Q8_0 blocks (device) with
+ * the selected rounding; EDOM if any input is nonfinite (synchronises). */
+MSTAR_B200_API int mstar_b200_q8_quantize(const float *x, void *packed, size_t bytes, int64_t rows,
+    int64_t k, int rounding, void *stream);
+
+/* --- prepared block-quantized linear (ggml mul_mat(Q8_0|Q4_0 W, F32 x) + epilogue)
+ * Replaces the Q8_0 graph nodes of backends/cpu_ggml/encoder.cpp:467-479,
+ * 694-723 and decoder.cpp:498-500, 563-588 and the Q4_0/Q8_0 vocab projection
+ * set by cpu_decoder_set_readout_q4/q8 (decoder_readout.h:11-24).
+ * create: blocks = canonical ggml bytes [rows][width/32] (device, borrowed only
+ * during create; the handle owns its B200 layout copy). bias may be NULL. */
+MSTAR_B200_API void *mstar_b200_linear_create(int format, const void *blocks, uint64_t bytes,
+    int64_t rows, int64_t width, const float *bias, char *error, size_t error_size);
+/* out[m][n] = epilogue(sum_b sumi_b * (d_w * d_x)) for m < queries; x is fp32
+ * [queries][width] (device, row stride x_stride floats), quantized on the fly
+ * with `rounding`; residual [queries][rows] (stride out_stride) if flagged.
+ * The fp32 accumulation follows ggml's generic block order, so GEMV results
+ * are bit-identical to ggml_vec_dot_q8_0_q8_0_generic / q4_0_q8_0_generic. */
+MSTAR_B200_API int mstar_b200_linear_run(void *handle, const float *x, int64_t x_stride,
+    int64_t queries, float *out, int64_t out_stride, const float *residual, int flags,
+    int rounding, void *stream, char *error, size_t error_size);
+/* Exact per-block int32 dots sums[m][n][b] of the same kernel path (the parity
+ * probe for "bit-exact per-block integer dot products"). queries <= 32. */
+MSTAR_B200_API int mstar_b200_linear_block_sums(void *handle, const float *x, int64_t queries,
+    int32_t *sums, uint64_t sums_bytes, int rounding, void *stream, char *error, size_t error_size);
+/* Greedy vocab readout on the same handle: logits[m][rows] (suppressed rows
+ * -inf), then first-index argmax where the first NaN wins
+ * (decoder.cpp:686-696, readout.c:47-53) into token[m] (int64). status[0]
+ * becomes 1 if any x is nonfinite (decoder.cpp:479-487 rejects such a call).
+ * suppressed: device int64 list (may be NULL when count is 0). */
+MSTAR_B200_API int mstar_b200_linear_readout(void *handle, const float *x, int64_t x_stride,
+    int64_t queries, float *logits, int64_t *token, int32_t *status, const int64_t *suppressed,
+    uint64_t suppressed_count, int rounding, void *stream, char *error, size_t error_size);
+MSTAR_B200_API int mstar_b200_linear_close(void *handle, char *error, size_t error_size);
+
+/* q8cpu_readout twin over a prepared Q8_0 handle (readout.c:30-54): quantize
+ * x[k] (one row), all rows' dots, suppression, argmax. errno-style result. */
+MSTAR_B200_API int mstar_b200_q8_readout(void *handle, const float *x, float *out, int64_t *token,
+    int32_t *status, const int64_t *suppressed, size_t suppressed_count, void *stream);
+
+#ifdef __cplusplus
+}
+#endif

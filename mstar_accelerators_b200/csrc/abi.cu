@@ -1,0 +1,348 @@
+// extern "C" boundary of libmstar_b200 (declarations and reference citations
+// in include/mstar_b200.h). Host-side validation happens before any launch;
+// nothing here throws across the C boundary.
+#include <atomic>
+#include <cerrno>
+#include <cmath>
+#include <memory>
+#include <vector>
+
+#include "../../include/mstar_b200.h"
+#include "quant.cuh"
+
+namespace mb {
+
+__global__ void k_probe() {}
+
+struct Linear {
+    int q4 = 0;
+    int64_t rows = 0, width = 0, nb = 0, nb_pad = 0, groups = 0;
+    uint4 *wq = nullptr;
+    __half *ws = nullptr;
+    float *bias = nullptr;
+    // per-handle scratch for one 32-token chunk; calls on one handle must be
+    // ordered on the device (one stream, or explicit events).
+    uint8_t *xf = nullptr;
+    float *xs = nullptr;
+    int *status = nullptr;
+    unsigned long long *keys = nullptr;
+    unsigned int *done = nullptr;
+    std::atomic_flag busy = ATOMIC_FLAG_INIT;
+    uint64_t weight_bytes() const { return uint64_t(groups) * 8 * nb_pad * (q4 ? 18 : 34); }
+    ~Linear() {
+        for (void *p : {(void *)wq, (void *)ws, (void *)bias, (void *)xf, (void *)xs, (void *)status,
+                        (void *)keys, (void *)done})
+            if (p) cudaFree(p);
+    }
+};
+
+struct Busy {
+    std::atomic_flag &flag;
+    explicit Busy(std::atomic_flag &f) : flag(f) {
+        require(!flag.test_and_set(std::memory_order_acquire), "linear handle is busy");
+    }
+    ~Busy() { flag.clear(std::memory_order_release); }
+};
+
+template <class T>
+T *device_alloc(size_t count, const char *what) {
+    void *p = nullptr;
+    cuda_check(cudaMalloc(&p, count * sizeof(T) ? count * sizeof(T) : 16), what);
+    return static_cast<T *>(p);
+}
+
+constexpr int64_t CHUNK = 32;  // tokens per GEMV launch
+
+void quantize_chunk(Linear &h, const float *x, int64_t ldx, int64_t m, int rounding, int *status, cudaStream_t s) {
+    const int64_t mpad = m <= 16 ? 16 : 32;
+    launch_quantize_act(rounding, x, ldx, m, h.width, mpad, h.nb_pad, h.xf, h.xs, nullptr, status, s);
+}
+
+GemvArgs gemv_args(Linear &h, int64_t m) {
+    GemvArgs a{};
+    a.wq = h.wq;
+    a.ws = reinterpret_cast<const __half2 *>(h.ws);
+    a.xf = reinterpret_cast<const uint4 *>(h.xf);
+    a.xs = h.xs;
+    a.groups = h.groups;
+    a.nb_pad = h.nb_pad;
+    a.nb = h.nb;
+    a.n = h.rows;
+    a.m = m;
+    return a;
+}
+
+void check_rounding(int r) { require(r >= 0 && r <= 2, "unknown Q8_0 activation rounding"); }
+
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" {
+
+int mstar_b200_abi(void) { return 1; }
+
+int mstar_b200_capability(void) {
+    int dev = 0, major = 0, minor = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return 0; }
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (major != 10 || minor != 0) return 0;
+    cudaFuncAttributes attr{};
+    if (cudaFuncGetAttributes(&attr, k_probe) != cudaSuccess) { cudaGetLastError(); return 0; }
+    return 1;
+}
+
+int mstar_b200_pack(int format, const float *input, uint64_t input_bytes, void *output, uint64_t output_bytes,
+                    int64_t rows, int64_t width, int preround, int fused, void *stream, char *error,
+                    size_t error_size) {
+    int *flags = nullptr;
+    try {
+        require(format == MSTAR_B200_Q8_0 || format == MSTAR_B200_Q4_0, "unsupported block format");
+        require(rows > 0 && rows <= (int64_t(1) << 31) && width > 0 && width <= 65536 && width % QK == 0,
+                "invalid packing shape");
+        const int q4 = format == MSTAR_B200_Q4_0;
+        const uint64_t count = uint64_t(rows) * uint64_t(width);
+        check_range({input, input_bytes}, count * 4, alignof(float), "packing input");
+        check_range({output, output_bytes}, uint64_t(rows) * (width / QK) * (q4 ? Q4_BYTES : Q8_BYTES), 1,
+                    "packing output");
+        require(disjoint({input, input_bytes}, {output, output_bytes}), "packing input/output overlap");
+        check_device(input, "packing input");
+        check_device(output, "packing output");
+        cudaStream_t s = as_stream(stream);
+        cuda_check(cudaMallocAsync(reinterpret_cast<void **>(&flags), sizeof(int), s), "flag allocation");
+        cuda_check(cudaMemsetAsync(flags, 0, sizeof(int), s), "flag reset");
+        launch_pack(input, static_cast<uint8_t *>(output), rows, width, q4, preround, fused, flags, s);
+        cuda_check(cudaGetLastError(), "pack launch");
+        int host = 0;
+        cuda_check(cudaMemcpyAsync(&host, flags, sizeof(int), cudaMemcpyDeviceToHost, s), "flag read");
+        cuda_check(cudaFreeAsync(flags, s), "flag free");
+        flags = nullptr;
+        cuda_check(cudaStreamSynchronize(s), "pack");
+        require(!(host & 1), "nonfinite weight");
+        require(!(host & 2), "weight overflows F16");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+int mstar_b200_q8_quantize(const float *x, void *packed, size_t bytes, int64_t rows, int64_t k, int rounding,
+                           void *stream) {
+    if (!mstar_b200_capability()) return ENOTSUP;
+    if (!x || !packed || rows <= 0 || k <= 0 || k % QK || rounding < 0 || rounding > 2 ||
+        bytes != size_t(rows) * size_t(k / QK) * Q8_BYTES)
+        return EINVAL;
+    int *status = nullptr;
+    cudaStream_t s = as_stream(stream);
+    if (cudaMallocAsync(reinterpret_cast<void **>(&status), sizeof(int), s) != cudaSuccess) return ENOMEM;
+    cudaMemsetAsync(status, 0, sizeof(int), s);
+    const int64_t nb = k / QK;
+    // quantize rows in groups of 16 "tokens" through the same kernel
+    launch_quantize_act(rounding, x, k, rows, k, ceil_div(rows, 16) * 16, nb, nullptr, nullptr,
+                        static_cast<uint8_t *>(packed), status, s);
+    int host = 0;
+    cudaMemcpyAsync(&host, status, sizeof(int), cudaMemcpyDeviceToHost, s);
+    cudaFreeAsync(status, s);
+    if (cudaStreamSynchronize(s) != cudaSuccess) return EIO;
+    return host ? EDOM : 0;
+}
+
+void *mstar_b200_linear_create(int format, const void *blocks, uint64_t bytes, int64_t rows, int64_t width,
+                               const float *bias, char *error, size_t error_size) {
+    std::unique_ptr<Linear> h;
+    try {
+        require(mstar_b200_capability() == 1, "sm_100a device capability is unavailable");
+        require(format == MSTAR_B200_Q8_0 || format == MSTAR_B200_Q4_0, "unsupported block format");
+        require(rows > 0 && rows <= (int64_t(1) << 31) && width > 0 && width <= 65536 && width % QK == 0,
+                "invalid linear shape");
+        h.reset(new Linear);
+        h->q4 = format == MSTAR_B200_Q4_0;
+        h->rows = rows;
+        h->width = width;
+        h->nb = width / QK;
+        h->nb_pad = h->q4 ? ceil_div(h->nb, 4) * 4 : ceil_div(h->nb, 2) * 2;
+        h->groups = ceil_div(rows, 8);
+        check_range({blocks, bytes}, uint64_t(rows) * h->nb * (h->q4 ? Q4_BYTES : Q8_BYTES), 1, "linear weights");
+        check_device(blocks, "linear weights");
+        const int64_t chunks = h->nb_pad / (h->q4 ? 4 : 2);
+        h->wq = device_alloc<uint4>(size_t(h->groups * chunks * 32), "weight allocation");
+        h->ws = device_alloc<__half>(size_t(h->groups * h->nb_pad * 8), "scale allocation");
+        h->xf = device_alloc<uint8_t>(size_t(h->nb_pad * 2 * 512), "activation scratch");
+        h->xs = device_alloc<float>(size_t(h->nb_pad * 32), "activation scale scratch");
+        h->status = device_alloc<int>(1, "status scratch");
+        h->keys = device_alloc<unsigned long long>(32, "argmax scratch");
+        h->done = device_alloc<unsigned int>(1, "argmax counter");
+        cudaStream_t s = nullptr;
+        cuda_check(cudaMemset(h->keys, 0, 32 * sizeof(unsigned long long)), "argmax reset");
+        cuda_check(cudaMemset(h->done, 0, sizeof(unsigned int)), "counter reset");
+        cuda_check(cudaMemset(h->status, 0, sizeof(int)), "status reset");
+        if (bias) {
+            check_device(bias, "bias");
+            h->bias = device_alloc<float>(size_t(rows), "bias allocation");
+            cuda_check(cudaMemcpy(h->bias, bias, size_t(rows) * 4, cudaMemcpyDeviceToDevice), "bias copy");
+        }
+        launch_repack(h->q4, static_cast<const uint8_t *>(blocks), h->wq, h->ws, rows, h->nb, h->nb_pad,
+                      h->groups, s);
+        cuda_check(cudaGetLastError(), "repack launch");
+        cuda_check(cudaDeviceSynchronize(), "repack");
+        return h.release();
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return nullptr;
+    }
+}
+
+static void validate_run(Linear &h, const float *x, int64_t x_stride, int64_t queries, const float *out,
+                         int64_t out_stride) {
+    require(queries >= 1 && queries <= (int64_t(1) << 31), "invalid query count");
+    require(x_stride >= h.width && out_stride >= h.rows, "invalid row stride");
+    const uint64_t xb = uint64_t((queries - 1) * x_stride + h.width) * 4;
+    const uint64_t ob = uint64_t((queries - 1) * out_stride + h.rows) * 4;
+    check_range({x, xb}, xb, 4, "activations");
+    check_range({out, ob}, ob, 4, "output");
+    require(disjoint({x, xb}, {out, ob}), "output overlaps activations");
+    check_device(x, "activations");
+    check_device(out, "output");
+}
+
+int mstar_b200_linear_run(void *handle, const float *x, int64_t x_stride, int64_t queries, float *out,
+                          int64_t out_stride, const float *residual, int flags, int rounding, void *stream,
+                          char *error, size_t error_size) {
+    try {
+        require(handle, "missing linear handle");
+        auto &h = *static_cast<Linear *>(handle);
+        Busy busy(h.busy);
+        check_rounding(rounding);
+        require((flags & ~15) == 0 && !((flags & 2) && (flags & 8)), "invalid epilogue flags");
+        require(!(flags & 1) || h.bias, "bias epilogue without a prepared bias");
+        validate_run(h, x, x_stride, queries, out, out_stride);
+        if (flags & 4) {
+            const uint64_t rb = uint64_t((queries - 1) * out_stride + h.rows) * 4;
+            check_range({residual, rb}, rb, 4, "residual");
+            require(residual == out || disjoint({residual, rb}, {out, rb}), "residual partially overlaps output");
+            check_device(residual, "residual");
+        } else require(!residual, "residual given without its epilogue flag");
+        cudaStream_t s = as_stream(stream);
+        for (int64_t m0 = 0; m0 < queries; m0 += CHUNK) {
+            const int64_t m = queries - m0 < CHUNK ? queries - m0 : CHUNK;
+            quantize_chunk(h, x + m0 * x_stride, x_stride, m, rounding, h.status, s);
+            GemvArgs a = gemv_args(h, m);
+            a.out = out + m0 * out_stride;
+            a.ldo = out_stride;
+            a.bias = h.bias;
+            a.residual = (flags & 4) ? residual + m0 * out_stride : nullptr;
+            a.flags = flags;
+            launch_gemv(h.q4, a, s);
+        }
+        cuda_check(cudaGetLastError(), "linear launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+int mstar_b200_linear_block_sums(void *handle, const float *x, int64_t queries, int32_t *sums,
+                                 uint64_t sums_bytes, int rounding, void *stream, char *error, size_t error_size) {
+    try {
+        require(handle, "missing linear handle");
+        auto &h = *static_cast<Linear *>(handle);
+        Busy busy(h.busy);
+        check_rounding(rounding);
+        require(queries >= 1 && queries <= CHUNK, "block sums take 1..32 queries");
+        const uint64_t xb = uint64_t(queries * h.width) * 4;
+        check_range({x, xb}, xb, 4, "activations");
+        check_range({sums, sums_bytes}, uint64_t(queries) * h.rows * h.nb * 4, 4, "block sums");
+        check_device(x, "activations");
+        check_device(sums, "block sums");
+        cudaStream_t s = as_stream(stream);
+        quantize_chunk(h, x, h.width, queries, rounding, h.status, s);
+        GemvArgs a = gemv_args(h, queries);
+        a.sums = sums;
+        launch_gemv(h.q4, a, s);
+        cuda_check(cudaGetLastError(), "block sums launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+int mstar_b200_linear_readout(void *handle, const float *x, int64_t x_stride, int64_t queries, float *logits,
+                              int64_t *token, int32_t *status, const int64_t *suppressed,
+                              uint64_t suppressed_count, int rounding, void *stream, char *error,
+                              size_t error_size) {
+    try {
+        require(handle, "missing linear handle");
+        auto &h = *static_cast<Linear *>(handle);
+        Busy busy(h.busy);
+        check_rounding(rounding);
+        require(queries >= 1 && queries <= CHUNK, "readout takes 1..32 queries");
+        validate_run(h, x, x_stride, queries, logits, h.rows);
+        const uint64_t lb = uint64_t(queries * h.rows) * 4;
+        check_range({token, uint64_t(queries) * 8}, uint64_t(queries) * 8, 8, "token");
+        check_range({status, 4}, 4, 4, "status");
+        require(suppressed_count <= uint64_t(h.rows), "suppression count exceeds vocabulary");
+        if (suppressed_count) {
+            check_range({suppressed, suppressed_count * 8}, suppressed_count * 8, 8, "suppression list");
+            check_device(suppressed, "suppression list");
+        } else require(!suppressed, "empty suppression list given a pointer");
+        require(disjoint({logits, lb}, {token, uint64_t(queries) * 8}) && disjoint({logits, lb}, {status, 4}) &&
+                    disjoint({token, uint64_t(queries) * 8}, {status, 4}),
+                "readout outputs overlap");
+        check_device(token, "token");
+        check_device(status, "status");
+        cudaStream_t s = as_stream(stream);
+        cuda_check(cudaMemsetAsync(status, 0, 4, s), "status reset");
+        quantize_chunk(h, x, x_stride, queries, rounding, status, s);
+        GemvArgs a = gemv_args(h, queries);
+        a.out = logits;
+        a.ldo = h.rows;
+        a.keys = h.keys;
+        a.done = h.done;
+        a.token = token;
+        a.suppressed = suppressed;
+        a.suppressed_count = int64_t(suppressed_count);
+        launch_gemv(h.q4, a, s);
+        cuda_check(cudaGetLastError(), "readout launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+int mstar_b200_q8_readout(void *handle, const float *x, float *out, int64_t *token, int32_t *status,
+                          const int64_t *suppressed, size_t suppressed_count, void *stream) {
+    if (!mstar_b200_capability()) return ENOTSUP;
+    if (!handle || !x || !out || !token || !status || (suppressed_count && !suppressed)) return EINVAL;
+    auto &h = *static_cast<Linear *>(handle);
+    if (h.q4 || h.width > 4096) return EINVAL;
+    char e[256];
+    return mstar_b200_linear_readout(handle, x, h.width, 1, out, token, status, suppressed, suppressed_count,
+                                     MSTAR_B200_Q8_ARM, stream, e, sizeof(e))
+               ? EINVAL
+               : 0;
+}
+
+int mstar_b200_linear_close(void *handle, char *error, size_t error_size) {
+    try {
+        if (handle) {
+            auto *h = static_cast<Linear *>(handle);
+            require(!h->busy.test_and_set(std::memory_order_acquire), "cannot close a busy linear handle");
+            cudaDeviceSynchronize();
+            delete h;
+        }
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+}  // extern "C"

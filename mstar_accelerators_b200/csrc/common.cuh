@@ -1,0 +1,152 @@
+// Shared host/device helpers of libmstar_b200 (sm_100a).
+//
+// Device layouts (B200 layout of the canonical ggml blocks; same bytes per
+// block: 34 for Q8_0, 18 for Q4_0):
+//
+//  Weights are the B operand of mma.m16n8k32 (K x N, "col"): lane (g, t) of a
+//  warp holds b0 = W[row g][k 4t..4t+3] and b1 = W[row g][k 16+4t..16+4t+3].
+//  Rows are grouped by 8 ("row group" G = row / 8, padded with zero rows).
+//   Q8_0 quants: wq[G][pair p][lane][16 B]: {block 2p: b0, b1; block 2p+1: b0, b1}
+//   Q4_0 quants: wq[G][quad q][lane][16 B]: {block 4q+j: qs[4t..4t+3]}, j = 0..3;
+//                the low nibbles of those 4 bytes are b0 (elements 4t..4t+3)
+//                and the high nibbles b1 (elements 16+4t..), value = nibble - 8.
+//   scales:      ws[G][block][8 rows] fp16 (row fastest); lane (g, t) reads the
+//                half2 of rows 2t, 2t+1 — the two output columns it owns.
+//  One 16-byte load per lane per warp-step moves 512 contiguous bytes.
+//
+//  Activations are the A operand (M x K, "row"): the quantizer writes them
+//  directly in fragment order, xf[block][mtile][lane][16 B] = {a0, a1, a2, a3}
+//  with a0 = X[g][4t..], a1 = X[g+8][4t..], a2 = X[g][16+4t..],
+//  a3 = X[g+8][16+4t..] for the 16 tokens of the tile, and the fp32 value of
+//  each stored fp16 scale in xs[block][token].
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
+namespace mb {
+
+constexpr int QK = 32;
+constexpr int Q8_BYTES = 34;
+constexpr int Q4_BYTES = 18;
+
+struct Error : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+
+inline void require(bool ok, const char *what) {
+    if (!ok) throw Error(what);
+}
+
+inline void cuda_check(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) throw Error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+inline void message(char *p, size_t n, const char *e) {
+    if (p && n) std::snprintf(p, n, "%s", e);
+}
+
+struct Range {
+    const void *data;
+    uint64_t bytes;
+};
+
+inline bool disjoint(Range a, Range b) {
+    if (!a.bytes || !b.bytes) return true;
+    const uintptr_t x = uintptr_t(a.data), y = uintptr_t(b.data);
+    return x + a.bytes <= y || y + b.bytes <= x;
+}
+
+// Extent/alignment check of a borrowed range (decoder.cpp:29-32 semantics).
+inline void check_range(Range r, uint64_t bytes, size_t alignment, const char *what) {
+    if (!(r.data && r.bytes == bytes && uintptr_t(r.data) % alignment == 0 &&
+          uintptr_t(r.data) <= UINTPTR_MAX - bytes))
+        throw Error(std::string("invalid borrowed storage extent/alignment: ") + what);
+}
+
+// A borrowed pointer must be device-accessible memory of the current device.
+inline void check_device(const void *p, const char *what) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        throw Error(std::string("not a CUDA pointer: ") + what);
+    }
+    int dev = -1;
+    cudaGetDevice(&dev);
+    if (!((a.type == cudaMemoryTypeDevice && a.device == dev) || a.type == cudaMemoryTypeManaged))
+        throw Error(std::string("not device memory of the current device: ") + what);
+}
+
+inline cudaStream_t as_stream(void *s) { return static_cast<cudaStream_t>(s); }
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace mb
+
+// ---------------------------------------------------------------- device side
+#ifdef __CUDACC__
+namespace mb {
+
+__device__ __forceinline__ uint4 ldg_stream(const uint4 *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t word(const uint4 &v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// D = A(16x32 s8, row) * B(32x8 s8, col), int32, C = 0.
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint4 &a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1), "r"(0));
+}
+
+// Q4_0 nibbles of 4 bytes -> (elements 4t..4t+3, elements 16+4t..) as int8x4.
+__device__ __forceinline__ void unpack_q4(uint32_t q, uint32_t &lo, uint32_t &hi) {
+    lo = __vsub4(q & 0x0F0F0F0Fu, 0x08080808u);
+    hi = __vsub4((q >> 4) & 0x0F0F0F0Fu, 0x08080808u);
+}
+
+// ggml stock GELU: tanh form evaluated on the fp16-rounded input, result
+// rounded to fp16 (ggml-cpu/vec.h:963-969, 1000-1013; table ggml-cpu.c:3889).
+__device__ __forceinline__ float gelu_ggml(float x) {
+    if (x <= -10.0f) return 0.0f;
+    if (x >= 10.0f) return x;
+    const float h = __half2float(__float2half_rn(x));
+    const float c = 0.79788456080286535587989211986876f, a = 0.044715f;
+    const float inner = __fmul_rn(__fmul_rn(c, h), __fadd_rn(1.0f, __fmul_rn(__fmul_rn(a, h), h)));
+    const float g = __fmul_rn(__fmul_rn(0.5f, h), __fadd_rn(1.0f, tanhf(inner)));
+    return __half2float(__float2half_rn(g));
+}
+
+// ggml_gelu_erf (ggml-cpu/vec.h:1024-1029).
+__device__ __forceinline__ float gelu_erf(float x) {
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, erff(__fmul_rn(x, 0.70710678118654752440f))));
+}
+
+// Total order used by the fused argmax: NaN above everything, +0 == -0,
+// and ties resolved toward the smaller index (decoder.cpp:686-696).
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index) {
+    uint32_t o;
+    if (v != v) o = 0xFFFFFFFFu;
+    else {
+        if (v == 0.0f) v = 0.0f;
+        const uint32_t b = __float_as_uint(v);
+        o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    }
+    return (static_cast<unsigned long long>(o) << 32) | (0xFFFFFFFFu - index);
+}
+
+}  // namespace mb
+#endif

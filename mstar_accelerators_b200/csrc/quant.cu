@@ -1,0 +1,213 @@
+// Quantizers and layout conversions of libmstar_b200.
+//
+//  k_pack          logical fp32 weights -> canonical ggml Q8_0 / Q4_0 blocks
+//                  (ggml-quants.c:113-147 and :276-297, with the fp16
+//                  pre-round of decoder.cpp:307-316 / :816-842)
+//  k_repack_q8/q4  canonical blocks -> the B200 fragment layout (common.cuh)
+//  k_quantize_act  fp32 activations -> Q8_0 in A-fragment order, with the
+//                  three rounding variants of quantize_row_q8_0
+//                  (ggml-quants.c:276-297, arch/arm/quants.c:41-75,
+//                  arch/x86/quants.c:302-350)
+// Every rounding step is an explicit IEEE intrinsic so that the compiler's
+// contraction cannot change a byte.
+#include "quant.cuh"
+
+namespace mb {
+
+// One thread per 32-element block. flags bit0: nonfinite input, bit1: fp16
+// overflow after the pre-round.
+__global__ void k_pack(const float *__restrict__ in, uint8_t *__restrict__ out, int64_t rows,
+                       int64_t width, int q4, int preround, int fused, int *__restrict__ flags) {
+    const int64_t nb = width / QK;
+    const int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
+    if (i >= rows * nb) return;
+    const float *x = in + i * QK;  // rows are contiguous: block i of the flat array
+    float v[QK];
+    int bad = 0;
+#pragma unroll
+    for (int j = 0; j < QK; ++j) {
+        float a = x[j];
+        if (!isfinite(a)) bad |= 1;
+        if (preround) {
+            a = __half2float(__float2half_rn(a));
+            if (!isfinite(a)) bad |= 2;
+        }
+        v[j] = a;
+    }
+    if (bad) atomicOr(flags, bad);
+    if (q4) {
+        uint8_t *o = out + i * Q4_BYTES;
+        float amax = 0.0f, mx = 0.0f;
+#pragma unroll
+        for (int j = 0; j < QK; ++j)
+            if (amax < fabsf(v[j])) { amax = fabsf(v[j]); mx = v[j]; }
+        const float d = __fdiv_rn(mx, -8.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        const __half h = __float2half_rn(d);
+        const uint16_t hb = __half_as_ushort(h);
+        o[0] = uint8_t(hb & 0xff);
+        o[1] = uint8_t(hb >> 8);
+#pragma unroll
+        for (int j = 0; j < QK / 2; ++j) {
+            float t0, t1;
+            if (fused) {
+                t0 = __fmaf_rn(v[j], id, 8.5f);
+                t1 = __fmaf_rn(v[j + 16], id, 8.5f);
+            } else {
+                t0 = __fadd_rn(__fmul_rn(v[j], id), 8.5f);
+                t1 = __fadd_rn(__fmul_rn(v[j + 16], id), 8.5f);
+            }
+            int q0 = __float2int_rz(t0), q1 = __float2int_rz(t1);
+            q0 = q0 > 15 ? 15 : q0;
+            q1 = q1 > 15 ? 15 : q1;
+            o[2 + j] = uint8_t(q0 | (q1 << 4));
+        }
+    } else {
+        uint8_t *o = out + i * Q8_BYTES;
+        float amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < QK; ++j) amax = fmaxf(amax, fabsf(v[j]));
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        const uint16_t hb = __half_as_ushort(__float2half_rn(d));
+        o[0] = uint8_t(hb & 0xff);
+        o[1] = uint8_t(hb >> 8);
+#pragma unroll
+        for (int j = 0; j < QK; ++j) o[2 + j] = uint8_t(int8_t(int(roundf(__fmul_rn(v[j], id)))));
+    }
+}
+
+__device__ __forceinline__ uint32_t load4(const uint8_t *p) {
+    return uint32_t(p[0]) | (uint32_t(p[1]) << 8) | (uint32_t(p[2]) << 16) | (uint32_t(p[3]) << 24);
+}
+
+// One thread per (group, pair, lane).
+__global__ void k_repack_q8(const uint8_t *__restrict__ blocks, uint4 *__restrict__ wq, int64_t rows,
+                            int64_t nb, int64_t nb_pad, int64_t groups) {
+    const int64_t pairs = nb_pad / 2;
+    const int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
+    if (i >= groups * pairs * 32) return;
+    const int lane = int(i % 32), g = lane >> 2, t = lane & 3;
+    const int64_t p = (i / 32) % pairs, G = i / (32 * pairs);
+    const int64_t row = G * 8 + g;
+    uint32_t w[4] = {0, 0, 0, 0};
+    for (int h = 0; h < 2; ++h) {
+        const int64_t b = 2 * p + h;
+        if (row < rows && b < nb) {
+            const uint8_t *qs = blocks + (row * nb + b) * Q8_BYTES + 2;
+            w[2 * h] = load4(qs + 4 * t);
+            w[2 * h + 1] = load4(qs + 16 + 4 * t);
+        }
+    }
+    wq[i] = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__global__ void k_repack_q4(const uint8_t *__restrict__ blocks, uint4 *__restrict__ wq, int64_t rows,
+                            int64_t nb, int64_t nb_pad, int64_t groups) {
+    const int64_t quads = nb_pad / 4;
+    const int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
+    if (i >= groups * quads * 32) return;
+    const int lane = int(i % 32), g = lane >> 2, t = lane & 3;
+    const int64_t q = (i / 32) % quads, G = i / (32 * quads);
+    const int64_t row = G * 8 + g;
+    uint32_t w[4] = {0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u};  // nibble 8 == value 0
+    for (int j = 0; j < 4; ++j) {
+        const int64_t b = 4 * q + j;
+        if (row < rows && b < nb) w[j] = load4(blocks + (row * nb + b) * Q4_BYTES + 2 + 4 * t);
+    }
+    wq[i] = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// ws[G][b][8] fp16 scales; padding rows/blocks get 0.
+__global__ void k_repack_scales(const uint8_t *__restrict__ blocks, __half *__restrict__ ws, int64_t rows,
+                                int64_t nb, int64_t nb_pad, int64_t groups, int block_bytes) {
+    const int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
+    if (i >= groups * nb_pad * 8) return;
+    const int r = int(i % 8);
+    const int64_t b = (i / 8) % nb_pad, G = i / (8 * nb_pad);
+    const int64_t row = G * 8 + r;
+    uint16_t h = 0;
+    if (row < rows && b < nb) {
+        const uint8_t *p = blocks + (row * nb + b) * block_bytes;
+        h = uint16_t(p[0]) | uint16_t(uint16_t(p[1]) << 8);
+    }
+    ws[i] = __ushort_as_half(h);
+}
+
+// One warp per (token, block): lane j quantizes element j. Tokens >= m and
+// blocks >= nb (padding) produce zero quants and zero scales.
+//   xf     [nb_pad][mtiles][32 lanes][16 B] A fragments (may be null)
+//   xs     [nb_pad][mtiles*16] fp32 scales (may be null)
+//   blocks [m][nb] canonical ggml Q8_0 bytes (may be null)
+template <int MODE>
+__global__ void k_quantize_act(const float *__restrict__ x, int64_t ldx, int64_t m, int64_t k,
+                               int64_t mpad, int64_t nb_pad, uint8_t *__restrict__ xf,
+                               float *__restrict__ xs, uint8_t *__restrict__ blocks,
+                               int *__restrict__ status) {
+    const int lane = threadIdx.x & 31;
+    const int64_t wid = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5;
+    if (wid >= mpad * nb_pad) return;
+    const int64_t token = wid % mpad, b = wid / mpad;
+    const int64_t nb = k / QK;
+    const bool live = token < m && b < nb;
+    float v = live ? x[token * ldx + b * QK + lane] : 0.0f;
+    if (live && !isfinite(v)) atomicOr(status, 1);
+    float amax = fabsf(v);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 127.0f);
+    float id;
+    if (MODE == 2) id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+    else id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float s = __fmul_rn(v, id);
+    const int q = MODE == 0 ? int(roundf(s)) : __float2int_rn(s);
+    const __half hd = __float2half_rn(d);
+    if (xf) {
+        const int64_t mt = token / 16;
+        const int r = int(token % 16), g = r & 7, hi = r >> 3;
+        const int t = (lane & 15) >> 2, half = lane >> 4, j = lane & 3;
+        const int w = hi + 2 * half;
+        const int64_t mtiles = mpad / 16;
+        xf[((b * mtiles + mt) * 32 + (4 * g + t)) * 16 + 4 * w + j] = uint8_t(int8_t(q));
+    }
+    if (lane == 0 && xs) xs[b * mpad + token] = __half2float(hd);
+    if (blocks && live) {
+        uint8_t *o = blocks + (token * nb + b) * Q8_BYTES;
+        o[2 + lane] = uint8_t(int8_t(q));
+        if (lane == 0) {
+            const uint16_t hb = __half_as_ushort(hd);
+            o[0] = uint8_t(hb & 0xff);
+            o[1] = uint8_t(hb >> 8);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ launchers
+void launch_pack(const float *in, uint8_t *out, int64_t rows, int64_t width, int q4, int preround,
+                 int fused, int *flags, cudaStream_t s) {
+    const int64_t n = rows * (width / QK);
+    if (!n) return;
+    k_pack<<<unsigned(ceil_div(n, 128)), 128, 0, s>>>(in, out, rows, width, q4, preround, fused, flags);
+}
+
+void launch_repack(int q4, const uint8_t *blocks, uint4 *wq, __half *ws, int64_t rows, int64_t nb,
+                   int64_t nb_pad, int64_t groups, cudaStream_t s) {
+    const int64_t lanes = groups * (nb_pad / (q4 ? 4 : 2)) * 32;
+    if (q4) k_repack_q4<<<unsigned(ceil_div(lanes, 256)), 256, 0, s>>>(blocks, wq, rows, nb, nb_pad, groups);
+    else k_repack_q8<<<unsigned(ceil_div(lanes, 256)), 256, 0, s>>>(blocks, wq, rows, nb, nb_pad, groups);
+    const int64_t n = groups * nb_pad * 8;
+    k_repack_scales<<<unsigned(ceil_div(n, 256)), 256, 0, s>>>(blocks, ws, rows, nb, nb_pad, groups,
+                                                               q4 ? Q4_BYTES : Q8_BYTES);
+}
+
+void launch_quantize_act(int mode, const float *x, int64_t ldx, int64_t m, int64_t k, int64_t mpad,
+                         int64_t nb_pad, uint8_t *xf, float *xs, uint8_t *blocks, int *status,
+                         cudaStream_t s) {
+    const int64_t threads = mpad * nb_pad * 32;
+    const unsigned grid = unsigned(ceil_div(threads, 256));
+    if (mode == 0) k_quantize_act<0><<<grid, 256, 0, s>>>(x, ldx, m, k, mpad, nb_pad, xf, xs, blocks, status);
+    else if (mode == 2) k_quantize_act<2><<<grid, 256, 0, s>>>(x, ldx, m, k, mpad, nb_pad, xf, xs, blocks, status);
+    else k_quantize_act<1><<<grid, 256, 0, s>>>(x, ldx, m, k, mpad, nb_pad, xf, xs, blocks, status);
+}
+
+}  // namespace mb

@@ -1,0 +1,175 @@
+"""Torch-facing wrappers of the block-quantized kernels.
+
+``pack`` / ``quantize`` produce canonical ggml bytes on the device
+(ggml-quants.c:113-147, :276-297; decoder.cpp:307-316, :816-842).
+``BlockLinear`` is one prepared ``ggml_mul_mat(Q8_0|Q4_0 W, F32 x)`` node with
+its fused epilogue (decoder.cpp:498-500, 563-588) and, on the same handle, the
+greedy vocab readout (decoder.cpp:583-588, 686-696; cpu_q8/readout.c:30-54).
+Every call is enqueued on the current torch CUDA stream; nothing here runs a
+CPU computation in place of a kernel.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import native
+from .native import BIAS, GELU, GELU_ERF, RESIDUAL, check, error_buffer
+
+Q8_BLOCK, Q4_BLOCK = 34, 18
+
+
+def _stream(device=None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _nbytes(t: torch.Tensor) -> int:
+    return t.numel() * t.element_size()
+
+
+def _require_cuda(t: torch.Tensor, what: str, dtype=None) -> None:
+    if t.device.type != "cuda":
+        raise ValueError(f"{what} must be a CUDA tensor")
+    if dtype is not None and t.dtype != dtype:
+        raise ValueError(f"{what} must be {dtype}")
+
+
+def block_bytes(fmt: str) -> int:
+    return {"q8_0": Q8_BLOCK, "q4_0": Q4_BLOCK}[fmt]
+
+
+def pack(weight: torch.Tensor, fmt: str = "q8_0", *, preround: bool = True, fused: bool = True) -> torch.Tensor:
+    """Logical fp32 [rows, width] -> canonical ggml blocks (uint8 [rows, width/32*B]) on the device."""
+    lib = native.require_capability()
+    if weight.ndim != 2 or weight.shape[1] % 32:
+        raise ValueError("packing needs a matrix with block-aligned width")
+    w = weight.detach().to(device="cuda" if weight.device.type != "cuda" else weight.device,
+                           dtype=torch.float32).contiguous()
+    rows, width = w.shape
+    out = torch.empty((rows, width // 32 * block_bytes(fmt)), dtype=torch.uint8, device=w.device)
+    e = error_buffer()
+    check(lib.mstar_b200_pack(native.FORMATS[fmt], w.data_ptr(), _nbytes(w), out.data_ptr(), _nbytes(out),
+                              rows, width, int(preround), int(fused), _stream(w.device), e, len(e)),
+          e, "B200 block packing")
+    return out
+
+
+def quantize(x: torch.Tensor, rounding: str = "arm") -> torch.Tensor:
+    """fp32 [rows, k] -> Q8_0 activation blocks (q8cpu_quantize twin)."""
+    lib = native.require_capability()
+    _require_cuda(x, "activations", torch.float32)
+    x = x.contiguous()
+    rows, k = x.reshape(-1, x.shape[-1]).shape
+    out = torch.empty((rows, k // 32 * Q8_BLOCK), dtype=torch.uint8, device=x.device)
+    status = lib.mstar_b200_q8_quantize(x.data_ptr(), out.data_ptr(), _nbytes(out), rows, k,
+                                        native.ROUNDING[rounding], _stream(x.device))
+    if status:
+        raise native.NativeError(f"B200 Q8_0 quantize failed with errno {status}")
+    return out
+
+
+class BlockLinear:
+    """One prepared block-quantized linear on the current CUDA device."""
+
+    def __init__(self, weight: torch.Tensor | None = None, *, blocks: torch.Tensor | None = None,
+                 fmt: str = "q8_0", bias: torch.Tensor | None = None, rows: int | None = None,
+                 width: int | None = None, preround: bool = True, fused: bool = True):
+        self.lib = native.require_capability()
+        if (weight is None) == (blocks is None):
+            raise ValueError("give exactly one of a logical weight or canonical blocks")
+        if weight is not None:
+            rows, width = weight.shape
+            blocks = pack(weight, fmt, preround=preround, fused=fused)
+        elif rows is None or width is None:
+            raise ValueError("canonical blocks need their logical rows and width")
+        _require_cuda(blocks, "blocks", torch.uint8)
+        blocks = blocks.contiguous()
+        self.fmt, self.rows, self.width = fmt, int(rows), int(width)
+        self.device = blocks.device
+        bias_t = None
+        if bias is not None:
+            bias_t = bias.detach().to(device=self.device, dtype=torch.float32).contiguous()
+            if bias_t.shape != (self.rows,):
+                raise ValueError("bias shape differs from the weight rows")
+        e = error_buffer()
+        torch.cuda.current_stream(self.device).synchronize()
+        handle = self.lib.mstar_b200_linear_create(native.FORMATS[fmt], blocks.data_ptr(), _nbytes(blocks),
+                                                   self.rows, self.width,
+                                                   bias_t.data_ptr() if bias_t is not None else None, e, len(e))
+        if not handle:
+            raise native.NativeError("B200 linear preparation: " + e.value.decode(errors="replace"))
+        self.handle = handle
+        self.has_bias = bias_t is not None
+        self.blocks = blocks  # canonical bytes stay available to callers (and tests)
+
+    # ggml_mul_mat + epilogue -------------------------------------------------
+    def __call__(self, x: torch.Tensor, *, out: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+                 bias: bool = True, gelu: str | None = None, rounding: str = "arm") -> torch.Tensor:
+        _require_cuda(x, "activations", torch.float32)
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, self.width)
+        if x2.stride(-1) != 1:
+            x2 = x2.contiguous()
+        m = x2.shape[0]
+        if out is None:
+            out = torch.empty((*lead, self.rows), dtype=torch.float32, device=x.device)
+        o2 = out.reshape(-1, self.rows)
+        flags = (BIAS if (bias and self.has_bias) else 0)
+        flags |= {None: 0, "tanh": GELU, "erf": GELU_ERF}[gelu]
+        r_ptr = None
+        if residual is not None:
+            r2 = residual.reshape(-1, self.rows)
+            if r2.stride() != o2.stride():
+                raise ValueError("residual layout differs from the output")
+            flags |= RESIDUAL
+            r_ptr = r2.data_ptr()
+        e = error_buffer()
+        check(self.lib.mstar_b200_linear_run(self.handle, x2.data_ptr(), x2.stride(0), m, o2.data_ptr(), o2.stride(0),
+                                             r_ptr, flags, native.ROUNDING[rounding], _stream(x.device), e, len(e)),
+              e, "B200 linear")
+        return out
+
+    def block_sums(self, x: torch.Tensor, rounding: str = "arm") -> torch.Tensor:
+        """Exact int32 per-block dots [M, rows, width/32] of the same kernel path."""
+        _require_cuda(x, "activations", torch.float32)
+        x = x.reshape(-1, self.width).contiguous()
+        sums = torch.empty((x.shape[0], self.rows, self.width // 32), dtype=torch.int32, device=x.device)
+        e = error_buffer()
+        check(self.lib.mstar_b200_linear_block_sums(self.handle, x.data_ptr(), x.shape[0], sums.data_ptr(),
+                                                    _nbytes(sums), native.ROUNDING[rounding], _stream(x.device),
+                                                    e, len(e)), e, "B200 block sums")
+        return sums
+
+    def readout(self, x: torch.Tensor, suppressed: torch.Tensor | None = None, *, rounding: str = "arm",
+                logits: torch.Tensor | None = None, token: torch.Tensor | None = None,
+                status: torch.Tensor | None = None):
+        """Greedy readout of each row of x: (logits [M, rows], token int64 [M], status int32 [1])."""
+        _require_cuda(x, "activations", torch.float32)
+        x2 = x.reshape(-1, self.width)
+        m = x2.shape[0]
+        dev = x.device
+        logits = torch.empty((m, self.rows), dtype=torch.float32, device=dev) if logits is None else logits
+        token = torch.empty((m,), dtype=torch.int64, device=dev) if token is None else token
+        status = torch.empty((1,), dtype=torch.int32, device=dev) if status is None else status
+        count, s_ptr = 0, None
+        if suppressed is not None and suppressed.numel():
+            _require_cuda(suppressed, "suppression list", torch.int64)
+            suppressed = suppressed.contiguous()
+            count, s_ptr = suppressed.numel(), suppressed.data_ptr()
+        e = error_buffer()
+        check(self.lib.mstar_b200_linear_readout(self.handle, x2.data_ptr(), x2.stride(0), m, logits.data_ptr(),
+                                                 token.data_ptr(), status.data_ptr(), s_ptr, count,
+                                                 native.ROUNDING[rounding], _stream(dev), e, len(e)),
+              e, "B200 readout")
+        return logits, token, status
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            e = error_buffer()
+            check(self.lib.mstar_b200_linear_close(self.handle, e, len(e)), e, "B200 linear close")
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,248 @@
+"""Parity of the sm_100a block-quantized kernels with the oracle.
+
+Integer work (packing bytes, quantized activations, per-block int32 dots) is
+compared bit for bit; fp32 outputs are also bit-identical because the GEMV
+folds block dots in ggml's generic order; the GELU epilogue is allowed one
+fp16 ulp (CUDA's tanhf vs the C library's).
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.fixture(scope="module")
+def L():
+    from mstar_accelerators_b200 import linear
+    O.build()
+    return linear
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def weights(rng, n, k, scale=0.02):
+    w = (rng.standard_normal((n, k)) * scale).astype(np.float32)
+    w[0, :32] = 0.0                                   # zero block
+    if n > 2:
+        w[1, :32] = (np.arange(32) - 15.5) / 127.0    # tie-heavy block
+        w[2, 32:64 if k >= 64 else 32] = 1e-12        # fp16-underflow scale
+    return w
+
+
+@pytest.mark.parametrize("fmt,preround,fused", [("q8_0", True, True), ("q8_0", False, True),
+                                                ("q4_0", True, True), ("q4_0", True, False)])
+def test_device_packer_is_bit_exact(L, fmt, preround, fused):
+    rng = np.random.default_rng(1)
+    w = weights(rng, 67, 384)
+    got = host(L.pack(dev(w), fmt, preround=preround, fused=fused))
+    assert np.array_equal(got, O.pack_weights(w, fmt, preround=preround, fused=fused))
+
+
+def test_device_packer_matches_reference_golden(L):
+    z = np.load(GOLDEN / "q8_kat.npz")
+    for i in range(3):
+        got = host(L.pack(dev(z[f"w{i}"]), "q8_0", preround=False))
+        assert bytes(got.reshape(-1)) == bytes(z[f"bytes{i}"])
+    z = np.load(GOLDEN / "q8_pack.npz")
+    assert np.array_equal(host(L.pack(dev(z["w"]), "q8_0", preround=False)), z["packed"])
+    z = np.load(GOLDEN / "q4_pack.npz")
+    assert np.array_equal(host(L.pack(dev(z["x"]), "q4_0", fused=True)), z["ggml"])
+    assert np.array_equal(host(L.pack(dev(z["x"]), "q4_0", fused=False)), z["separate"])
+
+
+def test_device_packer_rejects_nonfinite_and_overflow(L):
+    from mstar_accelerators_b200.native import NativeError
+    w = np.zeros((4, 64), np.float32)
+    w[2, 5] = np.nan
+    with pytest.raises(NativeError, match="nonfinite"):
+        L.pack(dev(w), "q8_0")
+    w[2, 5] = 1e10
+    with pytest.raises(NativeError, match="overflows"):
+        L.pack(dev(w), "q4_0")
+
+
+@pytest.mark.parametrize("mode", ["ref", "arm", "x86"])
+@pytest.mark.parametrize("rows", [1, 7, 33])
+def test_activation_quantizer_is_bit_exact(L, mode, rows):
+    rng = np.random.default_rng(rows)
+    x = (rng.standard_normal((rows, 1536)) * rng.uniform(1e-3, 20, (rows, 1))).astype(np.float32)
+    x[0, :32] = np.arange(32) - 15.5
+    x[-1, 32:64] = 0
+    assert np.array_equal(host(L.quantize(dev(x), mode)), O.quantize_q8_0(x, mode))
+
+
+def test_activation_quantizer_reports_nonfinite(L):
+    from mstar_accelerators_b200.native import NativeError
+    x = np.ones((2, 64), np.float32)
+    x[1, 9] = np.inf
+    with pytest.raises(NativeError, match="errno"):
+        L.quantize(dev(x))
+
+
+SHAPES = [("q8_0", 40, 384), ("q8_0", 37, 96), ("q8_0", 16, 1536), ("q4_0", 40, 384), ("q4_0", 29, 160),
+          ("q4_0", 64, 1536)]
+
+
+@pytest.mark.parametrize("fmt,n,k", SHAPES)
+@pytest.mark.parametrize("m", [1, 5, 16, 17, 32])
+def test_block_sums_are_bit_exact(L, fmt, n, k, m):
+    rng = np.random.default_rng(n * k + m)
+    w = weights(rng, n, k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    lin = L.BlockLinear(dev(w), fmt=fmt)
+    sums = host(lin.block_sums(dev(x), rounding="arm"))
+    blocks = O.pack_weights(w, fmt)
+    xq = O.quantize_q8_0(x, "arm")
+    expect = np.stack([np.stack([O.block_sums(blocks[r], xq[i], fmt) for r in range(n)]) for i in range(m)])
+    assert np.array_equal(sums, expect)
+
+
+@pytest.mark.parametrize("fmt,n,k", SHAPES)
+@pytest.mark.parametrize("m", [1, 4, 16, 17, 32, 33, 70])
+@pytest.mark.parametrize("mode", ["arm", "x86"])
+def test_linear_is_bit_identical_to_generic_ggml(L, fmt, n, k, m, mode):
+    rng = np.random.default_rng(n + k + m)
+    w = weights(rng, n, k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    lin = L.BlockLinear(dev(w), fmt=fmt)
+    got = host(lin(dev(x), rounding=mode))
+    assert np.array_equal(got, O.mul_mat(O.pack_weights(w, fmt), x, fmt, mode=mode))
+
+
+def test_linear_matches_reference_golden(L):
+    z = np.load(GOLDEN / "mul_mat.npz")
+    for tag in ("q8_0_40x384x5", "q4_0_40x384x3", "q8_0_16x1536x2"):
+        fmt = tag[:4]
+        blocks = z[tag + "_blocks"]
+        n, k = blocks.shape[0], z[tag + "_x"].shape[1]
+        lin = L.BlockLinear(blocks=dev(blocks), fmt=fmt, rows=n, width=k)
+        assert np.array_equal(host(lin(dev(z[tag + "_x"]), rounding="x86")), z[tag + "_out"]), tag
+
+
+def test_epilogues(L):
+    rng = np.random.default_rng(9)
+    n, k, m = 96, 384, 6
+    w = weights(rng, n, k)
+    bias = rng.standard_normal(n).astype(np.float32)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    res = rng.standard_normal((m, n)).astype(np.float32)
+    lin = L.BlockLinear(dev(w), bias=dev(bias))
+    base = O.mul_mat(O.pack_weights(w), x)
+    biased = (base + bias).astype(np.float32)
+    assert np.array_equal(host(lin(dev(x))), biased)
+    assert np.array_equal(host(lin(dev(x), bias=False)), base)
+    assert np.array_equal(host(lin(dev(x), residual=dev(res))), (res + biased).astype(np.float32))
+    r = dev(res)
+    lin(dev(x), out=r, residual=r)                      # in-place residual add
+    assert np.array_equal(host(r), (res + biased).astype(np.float32))
+    g = host(lin(dev(x), gelu="tanh"))
+    expect = O.gelu_ggml(biased)
+    ulp = np.abs(expect.astype(np.float16).astype(np.float32)) * 2.0 ** -10 + 1e-7
+    assert np.all(np.abs(g - expect) <= ulp)
+    import math
+    ge = host(lin(dev(x), gelu="erf"))
+    erf = np.vectorize(math.erf)
+    np.testing.assert_allclose(ge, 0.5 * biased * (1 + erf(biased / math.sqrt(2))), rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("m", [1, 3, 32])
+def test_vocab_readout(L, fmt, m):
+    rng = np.random.default_rng(m)
+    n, k = 51865, 384
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    w[777] = w[123]                                     # duplicate rows: a logit tie
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    blocks = O.pack_weights(w, fmt)
+    lin = L.BlockLinear(blocks=dev(blocks), fmt=fmt, rows=n, width=k)
+    sup = np.array([5, 100, 50257, 51864], np.int64)
+    logits, token, status = lin.readout(dev(x), dev(sup))
+    ref = O.mul_mat(blocks, x, fmt)
+    got = host(logits)
+    toks = host(token)
+    for i in range(m):
+        masked, tok = O.argmax(ref[i], sup)
+        assert np.array_equal(got[i], masked)
+        assert toks[i] == tok
+    assert host(status)[0] == 0
+    # a query aligned with the duplicated row makes the tie the maximum: the first index wins
+    x2 = x.copy()
+    x2[0] = w[123] * 400.0
+    _, token2, _ = lin.readout(dev(x2), dev(np.array([], np.int64)).reshape(0))
+    ref2 = O.mul_mat(blocks, x2, fmt)
+    assert ref2[0, 123] == ref2[0, 777] == ref2[0].max()
+    assert host(token2)[0] == 123
+    for i in range(m):
+        assert host(token2)[i] == O.argmax(ref2[i])[1]
+
+
+def test_readout_nan_rule_and_nonfinite_status(L):
+    rng = np.random.default_rng(2)
+    n, k = 300, 64
+    blocks = O.pack_weights((rng.standard_normal((n, k)) * 0.02).astype(np.float32), "q8_0")
+    blocks[200, 0:2] = np.frombuffer(np.float16(np.nan).tobytes(), np.uint8)   # NaN scale -> NaN logit
+    blocks[250, 0:2] = np.frombuffer(np.float16(np.nan).tobytes(), np.uint8)
+    lin = L.BlockLinear(blocks=dev(blocks), fmt="q8_0", rows=n, width=k)
+    x = rng.standard_normal((2, k)).astype(np.float32)
+    _, token, status = lin.readout(dev(x))
+    assert host(token).tolist() == [200, 200] and host(status)[0] == 0
+    x[1, 7] = np.nan
+    _, _, status = lin.readout(dev(x))
+    assert host(status)[0] == 1
+
+
+def test_q8cpu_readout_mirror(L):
+    import errno
+    from mstar_accelerators_b200 import native
+    lib = native.load()
+    rng = np.random.default_rng(4)
+    n, k = 1000, 384
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    lin = L.BlockLinear(dev(w), fmt="q8_0")
+    x = dev(rng.standard_normal(k).astype(np.float32))
+    out = torch.empty(n, device="cuda")
+    tok = torch.empty(1, dtype=torch.int64, device="cuda")
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    assert lib.mstar_b200_q8_readout(lin.handle, x.data_ptr(), out.data_ptr(), tok.data_ptr(), st.data_ptr(),
+                                     None, 0, s) == 0
+    ref = O.mul_mat(O.pack_weights(w), host(x)[None])[0]
+    assert np.array_equal(host(out), ref) and host(tok)[0] == O.argmax(ref)[1]
+    assert lib.mstar_b200_q8_readout(None, x.data_ptr(), out.data_ptr(), tok.data_ptr(), st.data_ptr(),
+                                     None, 0, s) == errno.EINVAL
+
+
+def test_run_validation_errors(L):
+    from mstar_accelerators_b200 import native
+    lin = L.BlockLinear(dev(np.zeros((16, 64), np.float32)))
+    e = native.error_buffer()
+    x = torch.zeros(2, 64, device="cuda")
+    out = torch.zeros(2, 64, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    assert lin.lib.mstar_b200_linear_run(lin.handle, x.data_ptr(), 64, 2, out.data_ptr(), 64, None, native.BIAS, 1,
+                                         s, e, len(e)) == -1
+    assert b"bias" in e.value
+    assert lin.lib.mstar_b200_linear_run(lin.handle, out.data_ptr(), 64, 2, out.data_ptr(), 64, None, 0, 1,
+                                         s, e, len(e)) == -1
+    assert b"overlaps" in e.value
+    assert lin.lib.mstar_b200_linear_run(lin.handle, x.data_ptr(), 64, 2, out.data_ptr(), 64, None, 0, 7,
+                                         s, e, len(e)) == -1
+    assert b"rounding" in e.value
+    host_x = torch.zeros(2, 64)
+    assert lin.lib.mstar_b200_linear_run(lin.handle, host_x.data_ptr(), 64, 2, out.data_ptr(), 64, None, 0, 1,
+                                         s, e, len(e)) == -1
+    lin.close()
+    lin.close()
