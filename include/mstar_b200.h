@@ -87,12 +87,16 @@ MSTAR_B200_API int mstar_b200_q8_quantize(const float *x, void *packed, size_t b
 MSTAR_B200_API void *mstar_b200_linear_create(int format, const void *blocks, uint64_t bytes,
     int64_t rows, int64_t width, const float *bias, char *error, size_t error_size);
 /* out[m][n] = epilogue(sum_b sumi_b * (d_w * d_x)) for m < queries; x is fp32
- * [queries][width] (device, row stride x_stride floats), quantized on the fly
- * with `rounding`; residual [queries][rows] (stride out_stride) if flagged.
- * The fp32 accumulation follows ggml's generic block order, so GEMV results
- * are bit-identical to ggml_vec_dot_q8_0_q8_0_generic / q4_0_q8_0_generic. */
+ * [queries][width] (device, 16-byte aligned rows of stride x_stride floats),
+ * optionally LayerNorm-ed first (ln_weight/ln_bias non-NULL: ggml_norm(eps)
+ * then mul and add, decoder.cpp:501-503), then quantized on the fly with
+ * `rounding`; residual [queries][rows] (stride out_stride) if flagged (it may
+ * alias out exactly). The fp32 accumulation follows ggml's generic block
+ * order, so results are bit-identical to ggml_vec_dot_q8_0_q8_0_generic /
+ * q4_0_q8_0_generic. Queries beyond 32 run in 32-row chunks. */
 MSTAR_B200_API int mstar_b200_linear_run(void *handle, const float *x, int64_t x_stride,
     int64_t queries, float *out, int64_t out_stride, const float *residual, int flags,
+    const float *ln_weight, const float *ln_bias, float ln_eps,
     int rounding, void *stream, char *error, size_t error_size);
 /* Exact per-block int32 dots sums[m][n][b] of the same kernel path (the parity
  * probe for "bit-exact per-block integer dot products"). queries <= 32. */
@@ -105,8 +109,14 @@ MSTAR_B200_API int mstar_b200_linear_block_sums(void *handle, const float *x, in
  * suppressed: device int64 list (may be NULL when count is 0). */
 MSTAR_B200_API int mstar_b200_linear_readout(void *handle, const float *x, int64_t x_stride,
     int64_t queries, float *logits, int64_t *token, int32_t *status, const int64_t *suppressed,
-    uint64_t suppressed_count, int rounding, void *stream, char *error, size_t error_size);
+    uint64_t suppressed_count, const float *ln_weight, const float *ln_bias, float ln_eps,
+    int rounding, void *stream, char *error, size_t error_size);
 MSTAR_B200_API int mstar_b200_linear_close(void *handle, char *error, size_t error_size);
+/* Physical policy, set on an idle handle (the role of
+ * cpu_decoder_set_cross_threads, decoder.h:44-47): warps that split one
+ * 8-row group's K range (1, 2, 4 or 8; 0 restores the automatic choice).
+ * Results are identical for every setting. */
+MSTAR_B200_API int mstar_b200_linear_set_split(void *handle, int warps, char *error, size_t error_size);
 
 /* q8cpu_readout twin over a prepared Q8_0 handle (readout.c:30-54): quantize
  * x[k] (one row), all rows' dots, suppression, argmax. errno-style result. */

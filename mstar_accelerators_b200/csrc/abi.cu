@@ -20,18 +20,19 @@ struct Linear {
     uint4 *wq = nullptr;
     __half *ws = nullptr;
     float *bias = nullptr;
-    // per-handle scratch for one 32-token chunk; calls on one handle must be
-    // ordered on the device (one stream, or explicit events).
-    uint8_t *xf = nullptr;
+    // per-handle device state shared by every call: calls on one handle must
+    // be ordered on the device (one stream, or explicit events).
+    uint32_t *xf = nullptr;  // activation fragments of one 32-query chunk
     float *xs = nullptr;
     int *status = nullptr;
     unsigned long long *keys = nullptr;
     unsigned int *done = nullptr;
+    int wpg_override = 0;  // > 0 forces the split-K fold (tests)
     std::atomic_flag busy = ATOMIC_FLAG_INIT;
     uint64_t weight_bytes() const { return uint64_t(groups) * 8 * nb_pad * (q4 ? 18 : 34); }
     ~Linear() {
-        for (void *p : {(void *)wq, (void *)ws, (void *)bias, (void *)xf, (void *)xs, (void *)status,
-                        (void *)keys, (void *)done})
+        for (void *p : {(void *)wq, (void *)ws, (void *)bias, (void *)xf, (void *)xs, (void *)status, (void *)keys,
+                        (void *)done})
             if (p) cudaFree(p);
     }
 };
@@ -53,12 +54,11 @@ T *device_alloc(size_t count, const char *what) {
 
 constexpr int64_t CHUNK = 32;  // tokens per GEMV launch
 
-void quantize_chunk(Linear &h, const float *x, int64_t ldx, int64_t m, int rounding, int *status, cudaStream_t s) {
+// Quantize one chunk of <= 32 queries, then describe the GEMV over it.
+GemvArgs stage(Linear &h, const float *x, int64_t ldx, int64_t m, int rounding, const float *ln_w,
+               const float *ln_b, float ln_eps, int *status, cudaStream_t s) {
     const int64_t mpad = m <= 16 ? 16 : 32;
-    launch_quantize_act(rounding, x, ldx, m, h.width, mpad, h.nb_pad, h.xf, h.xs, nullptr, status, s);
-}
-
-GemvArgs gemv_args(Linear &h, int64_t m) {
+    launch_quantize_frag(rounding, x, ldx, m, h.width, mpad, h.nb_pad, ln_w, ln_b, ln_eps, h.xf, h.xs, status, s);
     GemvArgs a{};
     a.wq = h.wq;
     a.ws = reinterpret_cast<const __half2 *>(h.ws);
@@ -107,7 +107,7 @@ int mstar_b200_pack(int format, const float *input, uint64_t input_bytes, void *
         const int q4 = format == MSTAR_B200_Q4_0;
         const uint64_t count = uint64_t(rows) * uint64_t(width);
         check_range({input, input_bytes}, count * 4, alignof(float), "packing input");
-        check_range({output, output_bytes}, uint64_t(rows) * (width / QK) * (q4 ? Q4_BYTES : Q8_BYTES), 1,
+        check_range({output, output_bytes}, uint64_t(rows) * (width / QK) * (q4 ? Q4_BYTES : Q8_BYTES), 2,
                     "packing output");
         require(disjoint({input, input_bytes}, {output, output_bytes}), "packing input/output overlap");
         check_device(input, "packing input");
@@ -134,17 +134,15 @@ int mstar_b200_pack(int format, const float *input, uint64_t input_bytes, void *
 int mstar_b200_q8_quantize(const float *x, void *packed, size_t bytes, int64_t rows, int64_t k, int rounding,
                            void *stream) {
     if (!mstar_b200_capability()) return ENOTSUP;
-    if (!x || !packed || rows <= 0 || k <= 0 || k % QK || rounding < 0 || rounding > 2 ||
+    if (!x || !packed || rows <= 0 || k <= 0 || k % QK || rounding < 0 || rounding > 2 || uintptr_t(packed) % 2 ||
         bytes != size_t(rows) * size_t(k / QK) * Q8_BYTES)
         return EINVAL;
     int *status = nullptr;
     cudaStream_t s = as_stream(stream);
     if (cudaMallocAsync(reinterpret_cast<void **>(&status), sizeof(int), s) != cudaSuccess) return ENOMEM;
     cudaMemsetAsync(status, 0, sizeof(int), s);
-    const int64_t nb = k / QK;
     // quantize rows in groups of 16 "tokens" through the same kernel
-    launch_quantize_act(rounding, x, k, rows, k, ceil_div(rows, 16) * 16, nb, nullptr, nullptr,
-                        static_cast<uint8_t *>(packed), status, s);
+    launch_quantize_rows(rounding, x, k, rows, k, static_cast<uint8_t *>(packed), status, s);
     int host = 0;
     cudaMemcpyAsync(&host, status, sizeof(int), cudaMemcpyDeviceToHost, s);
     cudaFreeAsync(status, s);
@@ -168,12 +166,13 @@ void *mstar_b200_linear_create(int format, const void *blocks, uint64_t bytes, i
         h->nb_pad = h->q4 ? ceil_div(h->nb, 4) * 4 : ceil_div(h->nb, 2) * 2;
         h->groups = ceil_div(rows, 8);
         check_range({blocks, bytes}, uint64_t(rows) * h->nb * (h->q4 ? Q4_BYTES : Q8_BYTES), 1, "linear weights");
+        require(gemv_supported(h->nb_pad), "linear width exceeds the decode kernel's shared-memory tile");
+        h->xf = device_alloc<uint32_t>(size_t(h->nb_pad * 2 * 32 * 4), "activation fragments");
+        h->xs = device_alloc<float>(size_t(h->nb_pad * 32), "activation scales");
         check_device(blocks, "linear weights");
         const int64_t chunks = h->nb_pad / (h->q4 ? 4 : 2);
         h->wq = device_alloc<uint4>(size_t(h->groups * chunks * 32), "weight allocation");
         h->ws = device_alloc<__half>(size_t(h->groups * h->nb_pad * 8), "scale allocation");
-        h->xf = device_alloc<uint8_t>(size_t(h->nb_pad * 2 * 512), "activation scratch");
-        h->xs = device_alloc<float>(size_t(h->nb_pad * 32), "activation scale scratch");
         h->status = device_alloc<int>(1, "status scratch");
         h->keys = device_alloc<unsigned long long>(32, "argmax scratch");
         h->done = device_alloc<unsigned int>(1, "argmax counter");
@@ -201,6 +200,7 @@ static void validate_run(Linear &h, const float *x, int64_t x_stride, int64_t qu
                          int64_t out_stride) {
     require(queries >= 1 && queries <= (int64_t(1) << 31), "invalid query count");
     require(x_stride >= h.width && out_stride >= h.rows, "invalid row stride");
+    require(uintptr_t(x) % 16 == 0 && x_stride % 4 == 0, "activation rows must be 16-byte aligned");
     const uint64_t xb = uint64_t((queries - 1) * x_stride + h.width) * 4;
     const uint64_t ob = uint64_t((queries - 1) * out_stride + h.rows) * 4;
     check_range({x, xb}, xb, 4, "activations");
@@ -210,9 +210,20 @@ static void validate_run(Linear &h, const float *x, int64_t x_stride, int64_t qu
     check_device(out, "output");
 }
 
+static void validate_norm(Linear &h, const float *ln_weight, const float *ln_bias, float ln_eps) {
+    if (!ln_weight) {
+        require(!ln_bias, "LayerNorm bias given without its weight");
+        return;
+    }
+    require(ln_bias && std::isfinite(ln_eps) && ln_eps >= 0.0f, "invalid LayerNorm parameters");
+    check_device(ln_weight, "LayerNorm weight");
+    check_device(ln_bias, "LayerNorm bias");
+}
+
 int mstar_b200_linear_run(void *handle, const float *x, int64_t x_stride, int64_t queries, float *out,
-                          int64_t out_stride, const float *residual, int flags, int rounding, void *stream,
-                          char *error, size_t error_size) {
+                          int64_t out_stride, const float *residual, int flags, const float *ln_weight,
+                          const float *ln_bias, float ln_eps, int rounding, void *stream, char *error,
+                          size_t error_size) {
     try {
         require(handle, "missing linear handle");
         auto &h = *static_cast<Linear *>(handle);
@@ -221,6 +232,7 @@ int mstar_b200_linear_run(void *handle, const float *x, int64_t x_stride, int64_
         require((flags & ~15) == 0 && !((flags & 2) && (flags & 8)), "invalid epilogue flags");
         require(!(flags & 1) || h.bias, "bias epilogue without a prepared bias");
         validate_run(h, x, x_stride, queries, out, out_stride);
+        validate_norm(h, ln_weight, ln_bias, ln_eps);
         if (flags & 4) {
             const uint64_t rb = uint64_t((queries - 1) * out_stride + h.rows) * 4;
             check_range({residual, rb}, rb, 4, "residual");
@@ -230,13 +242,13 @@ int mstar_b200_linear_run(void *handle, const float *x, int64_t x_stride, int64_
         cudaStream_t s = as_stream(stream);
         for (int64_t m0 = 0; m0 < queries; m0 += CHUNK) {
             const int64_t m = queries - m0 < CHUNK ? queries - m0 : CHUNK;
-            quantize_chunk(h, x + m0 * x_stride, x_stride, m, rounding, h.status, s);
-            GemvArgs a = gemv_args(h, m);
+            GemvArgs a = stage(h, x + m0 * x_stride, x_stride, m, rounding, ln_weight, ln_bias, ln_eps, h.status, s);
             a.out = out + m0 * out_stride;
             a.ldo = out_stride;
             a.bias = h.bias;
             a.residual = (flags & 4) ? residual + m0 * out_stride : nullptr;
             a.flags = flags;
+            a.wpg_override = h.wpg_override;
             launch_gemv(h.q4, a, s);
         }
         cuda_check(cudaGetLastError(), "linear launch");
@@ -256,13 +268,12 @@ int mstar_b200_linear_block_sums(void *handle, const float *x, int64_t queries, 
         check_rounding(rounding);
         require(queries >= 1 && queries <= CHUNK, "block sums take 1..32 queries");
         const uint64_t xb = uint64_t(queries * h.width) * 4;
-        check_range({x, xb}, xb, 4, "activations");
+        check_range({x, xb}, xb, 16, "activations");
         check_range({sums, sums_bytes}, uint64_t(queries) * h.rows * h.nb * 4, 4, "block sums");
         check_device(x, "activations");
         check_device(sums, "block sums");
         cudaStream_t s = as_stream(stream);
-        quantize_chunk(h, x, h.width, queries, rounding, h.status, s);
-        GemvArgs a = gemv_args(h, queries);
+        GemvArgs a = stage(h, x, h.width, queries, rounding, nullptr, nullptr, 0.0f, h.status, s);
         a.sums = sums;
         launch_gemv(h.q4, a, s);
         cuda_check(cudaGetLastError(), "block sums launch");
@@ -275,8 +286,8 @@ int mstar_b200_linear_block_sums(void *handle, const float *x, int64_t queries, 
 
 int mstar_b200_linear_readout(void *handle, const float *x, int64_t x_stride, int64_t queries, float *logits,
                               int64_t *token, int32_t *status, const int64_t *suppressed,
-                              uint64_t suppressed_count, int rounding, void *stream, char *error,
-                              size_t error_size) {
+                              uint64_t suppressed_count, const float *ln_weight, const float *ln_bias, float ln_eps,
+                              int rounding, void *stream, char *error, size_t error_size) {
     try {
         require(handle, "missing linear handle");
         auto &h = *static_cast<Linear *>(handle);
@@ -284,6 +295,7 @@ int mstar_b200_linear_readout(void *handle, const float *x, int64_t x_stride, in
         check_rounding(rounding);
         require(queries >= 1 && queries <= CHUNK, "readout takes 1..32 queries");
         validate_run(h, x, x_stride, queries, logits, h.rows);
+        validate_norm(h, ln_weight, ln_bias, ln_eps);
         const uint64_t lb = uint64_t(queries * h.rows) * 4;
         check_range({token, uint64_t(queries) * 8}, uint64_t(queries) * 8, 8, "token");
         check_range({status, 4}, 4, 4, "status");
@@ -299,8 +311,7 @@ int mstar_b200_linear_readout(void *handle, const float *x, int64_t x_stride, in
         check_device(status, "status");
         cudaStream_t s = as_stream(stream);
         cuda_check(cudaMemsetAsync(status, 0, 4, s), "status reset");
-        quantize_chunk(h, x, x_stride, queries, rounding, status, s);
-        GemvArgs a = gemv_args(h, queries);
+        GemvArgs a = stage(h, x, x_stride, queries, rounding, ln_weight, ln_bias, ln_eps, status, s);
         a.out = logits;
         a.ldo = h.rows;
         a.keys = h.keys;
@@ -308,6 +319,7 @@ int mstar_b200_linear_readout(void *handle, const float *x, int64_t x_stride, in
         a.token = token;
         a.suppressed = suppressed;
         a.suppressed_count = int64_t(suppressed_count);
+        a.wpg_override = h.wpg_override;
         launch_gemv(h.q4, a, s);
         cuda_check(cudaGetLastError(), "readout launch");
         return 0;
@@ -324,10 +336,25 @@ int mstar_b200_q8_readout(void *handle, const float *x, float *out, int64_t *tok
     auto &h = *static_cast<Linear *>(handle);
     if (h.q4 || h.width > 4096) return EINVAL;
     char e[256];
+    if (uintptr_t(x) % 16) return EINVAL;
     return mstar_b200_linear_readout(handle, x, h.width, 1, out, token, status, suppressed, suppressed_count,
-                                     MSTAR_B200_Q8_ARM, stream, e, sizeof(e))
+                                     nullptr, nullptr, 0.0f, MSTAR_B200_Q8_ARM, stream, e, sizeof(e))
                ? EINVAL
                : 0;
+}
+
+int mstar_b200_linear_set_split(void *handle, int warps, char *error, size_t error_size) {
+    try {
+        require(handle, "missing linear handle");
+        auto &h = *static_cast<Linear *>(handle);
+        Busy busy(h.busy);
+        require(warps == 0 || warps == 1 || warps == 2 || warps == 4 || warps == 8, "split must be 0, 1, 2, 4 or 8");
+        h.wpg_override = warps;
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
 }
 
 int mstar_b200_linear_close(void *handle, char *error, size_t error_size) {

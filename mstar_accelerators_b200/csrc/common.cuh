@@ -93,7 +93,7 @@ namespace mb {
 
 __device__ __forceinline__ uint4 ldg_stream(const uint4 *p) {
     uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "l"(p));
     return v;
@@ -105,11 +105,38 @@ __device__ __forceinline__ uint32_t word(const uint4 &v, int i) {
 
 // D = A(16x32 s8, row) * B(32x8 s8, col), int32, C = 0.
 __device__ __forceinline__ void mma_s8(int (&d)[4], const uint4 &a, uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%10,%10,%10,%10};"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
         : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1), "r"(0));
+}
+
+// Packed fp32 pairs (sm_100 f32x2 pipe): each lane is an IEEE RN operation,
+// bit-identical to the scalar __fmul_rn / __fadd_rn.
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+    float2 r;
+    asm("{.reg .b64 ra, rb, rc; mov.b64 ra, {%2,%3}; mov.b64 rb, {%4,%5}; mul.rn.f32x2 rc, ra, rb; "
+        "mov.b64 {%0,%1}, rc;}"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+    float2 r;
+    asm("{.reg .b64 ra, rb, rc; mov.b64 ra, {%2,%3}; mov.b64 rb, {%4,%5}; add.rn.f32x2 rc, ra, rb; "
+        "mov.b64 {%0,%1}, rc;}"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
+}
+// Exact int -> float for |i| < 2^22 (every Q8_0/Q4_0 block dot is below
+// 32*127*127 < 2^19): the integer is added to the bit pattern of 1.5*2^23,
+// whose unit in the last place is 1, and the bias is subtracted again.
+__device__ __forceinline__ float2 i2f2(int a, int b) {
+    const float2 biased = make_float2(__int_as_float(a + 0x4B400000), __int_as_float(b + 0x4B400000));
+    float2 r;
+    asm("{.reg .b64 ra, rb, rc; mov.b64 ra, {%2,%3}; mov.b64 rb, {%4,%4}; sub.rn.f32x2 rc, ra, rb; "
+        "mov.b64 {%0,%1}, rc;}"
+        : "=f"(r.x), "=f"(r.y) : "f"(biased.x), "f"(biased.y), "f"(12582912.0f));
+    return r;
 }
 
 // Q4_0 nibbles of 4 bytes -> (elements 4t..4t+3, elements 16+4t..) as int8x4.

@@ -36,17 +36,15 @@ __global__ void k_pack(const float *__restrict__ in, uint8_t *__restrict__ out, 
     }
     if (bad) atomicOr(flags, bad);
     if (q4) {
-        uint8_t *o = out + i * Q4_BYTES;
         float amax = 0.0f, mx = 0.0f;
 #pragma unroll
         for (int j = 0; j < QK; ++j)
             if (amax < fabsf(v[j])) { amax = fabsf(v[j]); mx = v[j]; }
         const float d = __fdiv_rn(mx, -8.0f);
         const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        const __half h = __float2half_rn(d);
-        const uint16_t hb = __half_as_ushort(h);
-        o[0] = uint8_t(hb & 0xff);
-        o[1] = uint8_t(hb >> 8);
+        uint16_t *o16 = reinterpret_cast<uint16_t *>(out + i * Q4_BYTES);  // 2-byte aligned
+        o16[0] = __half_as_ushort(__float2half_rn(d));
+        uint32_t pair = 0;
 #pragma unroll
         for (int j = 0; j < QK / 2; ++j) {
             float t0, t1;
@@ -60,20 +58,24 @@ __global__ void k_pack(const float *__restrict__ in, uint8_t *__restrict__ out, 
             int q0 = __float2int_rz(t0), q1 = __float2int_rz(t1);
             q0 = q0 > 15 ? 15 : q0;
             q1 = q1 > 15 ? 15 : q1;
-            o[2 + j] = uint8_t(q0 | (q1 << 4));
+            const uint32_t byte = uint32_t(q0 | (q1 << 4)) & 0xffu;
+            if (j & 1) o16[1 + j / 2] = uint16_t(pair | (byte << 8));
+            else pair = byte;
         }
     } else {
-        uint8_t *o = out + i * Q8_BYTES;
+        uint16_t *o16 = reinterpret_cast<uint16_t *>(out + i * Q8_BYTES);  // 2-byte aligned
         float amax = 0.0f;
 #pragma unroll
         for (int j = 0; j < QK; ++j) amax = fmaxf(amax, fabsf(v[j]));
         const float d = __fdiv_rn(amax, 127.0f);
         const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        const uint16_t hb = __half_as_ushort(__float2half_rn(d));
-        o[0] = uint8_t(hb & 0xff);
-        o[1] = uint8_t(hb >> 8);
+        o16[0] = __half_as_ushort(__float2half_rn(d));
 #pragma unroll
-        for (int j = 0; j < QK; ++j) o[2 + j] = uint8_t(int8_t(int(roundf(__fmul_rn(v[j], id)))));
+        for (int j = 0; j < QK; j += 2) {
+            const uint32_t q0 = uint32_t(int(roundf(__fmul_rn(v[j], id)))) & 0xffu;
+            const uint32_t q1 = uint32_t(int(roundf(__fmul_rn(v[j + 1], id)))) & 0xffu;
+            o16[1 + j / 2] = uint16_t(q0 | (q1 << 8));
+        }
     }
 }
 
@@ -134,24 +136,18 @@ __global__ void k_repack_scales(const uint8_t *__restrict__ blocks, __half *__re
     ws[i] = __ushort_as_half(h);
 }
 
-// One warp per (token, block): lane j quantizes element j. Tokens >= m and
-// blocks >= nb (padding) produce zero quants and zero scales.
-//   xf     [nb_pad][mtiles][32 lanes][16 B] A fragments (may be null)
-//   xs     [nb_pad][mtiles*16] fp32 scales (may be null)
-//   blocks [m][nb] canonical ggml Q8_0 bytes (may be null)
+// One warp per (token, block): lane j quantizes element j into canonical
+// ggml Q8_0 bytes (the q8cpu_quantize mirror). Tokens are rows here.
 template <int MODE>
-__global__ void k_quantize_act(const float *__restrict__ x, int64_t ldx, int64_t m, int64_t k,
-                               int64_t mpad, int64_t nb_pad, uint8_t *__restrict__ xf,
-                               float *__restrict__ xs, uint8_t *__restrict__ blocks,
-                               int *__restrict__ status) {
+__global__ void k_quantize_rows(const float *__restrict__ x, int64_t ldx, int64_t m, int64_t k,
+                                uint8_t *__restrict__ blocks, int *__restrict__ status) {
     const int lane = threadIdx.x & 31;
-    const int64_t wid = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5;
-    if (wid >= mpad * nb_pad) return;
-    const int64_t token = wid % mpad, b = wid / mpad;
     const int64_t nb = k / QK;
-    const bool live = token < m && b < nb;
-    float v = live ? x[token * ldx + b * QK + lane] : 0.0f;
-    if (live && !isfinite(v)) atomicOr(status, 1);
+    const int64_t wid = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5;
+    if (wid >= m * nb) return;
+    const int64_t token = wid / nb, b = wid % nb;
+    const float v = x[token * ldx + b * QK + lane];
+    if (!isfinite(v)) atomicOr(status, 1);
     float amax = fabsf(v);
 #pragma unroll
     for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -161,24 +157,94 @@ __global__ void k_quantize_act(const float *__restrict__ x, int64_t ldx, int64_t
     else id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
     const float s = __fmul_rn(v, id);
     const int q = MODE == 0 ? int(roundf(s)) : __float2int_rn(s);
-    const __half hd = __float2half_rn(d);
-    if (xf) {
-        const int64_t mt = token / 16;
-        const int r = int(token % 16), g = r & 7, hi = r >> 3;
-        const int t = (lane & 15) >> 2, half = lane >> 4, j = lane & 3;
-        const int w = hi + 2 * half;
-        const int64_t mtiles = mpad / 16;
-        xf[((b * mtiles + mt) * 32 + (4 * g + t)) * 16 + 4 * w + j] = uint8_t(int8_t(q));
-    }
-    if (lane == 0 && xs) xs[b * mpad + token] = __half2float(hd);
-    if (blocks && live) {
-        uint8_t *o = blocks + (token * nb + b) * Q8_BYTES;
-        o[2 + lane] = uint8_t(int8_t(q));
-        if (lane == 0) {
-            const uint16_t hb = __half_as_ushort(hd);
-            o[0] = uint8_t(hb & 0xff);
-            o[1] = uint8_t(hb >> 8);
+    // 34-byte blocks are 2-byte aligned: even lanes store a pair of quants
+    const uint32_t mine = uint32_t(q) & 0xffu;
+    const uint32_t next = __shfl_down_sync(0xffffffffu, mine, 1);
+    uint16_t *o16 = reinterpret_cast<uint16_t *>(blocks + (token * nb + b) * Q8_BYTES);
+    if (!(lane & 1)) o16[1 + lane / 2] = uint16_t(mine | (next << 8));
+    if (lane == 0) o16[0] = __half_as_ushort(__float2half_rn(d));
+}
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// One CTA per token (mpad CTAs): optional LayerNorm of the row (ggml_norm,
+// ggml-cpu/ops.cpp:4094-4137, then ggml_mul/ggml_add by the affine), then
+// quantize_row_q8_0 with the selected rounding, written in A-fragment order:
+//   xf [nb_pad][mtiles][32 lanes][4 words], xs [nb_pad][mpad] fp32 scales.
+// Dead tokens (>= m) and padding blocks (>= nb) get zero quants and scales.
+// Launched as a programmatic dependent: it waits for the producer of x, then
+// lets the consuming GEMV start prefetching its weights.
+template <int MODE>
+__global__ void __launch_bounds__(256) k_quantize_frag(const float *__restrict__ x, int64_t ldx, int64_t m,
+                                                       int64_t k, int64_t mpad, int64_t nb_pad,
+                                                       const float *__restrict__ ln_w, const float *__restrict__ ln_b,
+                                                       float ln_eps, uint32_t *__restrict__ xf,
+                                                       float *__restrict__ xs, int *__restrict__ status) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ float red[2][8];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int64_t token = blockIdx.x;
+    const int64_t nb = k / QK;
+    const bool live_token = token < m;
+    const float *xr = x + token * ldx;
+    float mean = 0.0f, rstd = 1.0f;
+    if (ln_w && live_token) {
+        float sum = 0.0f;
+        for (int64_t i = threadIdx.x; i < k; i += blockDim.x) sum += xr[i];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) red[0][warp] = sum;
+        __syncthreads();
+        sum = 0.0f;
+        for (int w = 0; w < nwarps; ++w) sum += red[0][w];
+        mean = sum / float(k);
+        float var = 0.0f;
+        for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+            const float y = xr[i] - mean;
+            var += y * y;
         }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+        if (lane == 0) red[1][warp] = var;
+        __syncthreads();
+        var = 0.0f;
+        for (int w = 0; w < nwarps; ++w) var += red[1][w];
+        rstd = 1.0f / sqrtf(var / float(k) + ln_eps);
+    }
+    const int64_t mtiles = mpad / 16;
+    const int64_t mt = token / 16;
+    const int r = int(token % 16), g = r & 7, hi = r >> 3;
+    const int t = (lane & 15) >> 2, half = lane >> 4;
+    for (int64_t b = warp; b < nb_pad; b += nwarps) {
+        const bool live = live_token && b < nb;
+        float v = 0.0f;
+        if (live) {
+            v = xr[b * QK + lane];
+            if (ln_w) {
+                const int64_t i = b * QK + lane;
+                v = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, mean), rstd), __ldg(ln_w + i)), __ldg(ln_b + i));
+            }
+            if (!isfinite(v)) atomicOr(status, 1);
+        }
+        float amax = fabsf(v);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float d = __fdiv_rn(amax, 127.0f);
+        float id;
+        if (MODE == 2) id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        else id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        const float sv = __fmul_rn(v, id);
+        const int q = MODE == 0 ? int(roundf(sv)) : __float2int_rn(sv);
+        // gather 4 consecutive quants into the word owned by lane (4t + j) / 4
+        uint32_t byte = uint32_t(q) & 0xffu;
+        uint32_t word = byte;
+        word |= __shfl_down_sync(0xffffffffu, byte, 1) << 8;
+        word |= __shfl_down_sync(0xffffffffu, byte, 2) << 16;
+        word |= __shfl_down_sync(0xffffffffu, byte, 3) << 24;
+        if ((lane & 3) == 0) xf[((b * mtiles + mt) * 32 + (4 * g + t)) * 4 + hi + 2 * half] = word;
+        if (lane == 0) xs[b * mpad + token] = __half2float(__float2half_rn(d));
     }
 }
 
@@ -200,14 +266,29 @@ void launch_repack(int q4, const uint8_t *blocks, uint4 *wq, __half *ws, int64_t
                                                                q4 ? Q4_BYTES : Q8_BYTES);
 }
 
-void launch_quantize_act(int mode, const float *x, int64_t ldx, int64_t m, int64_t k, int64_t mpad,
-                         int64_t nb_pad, uint8_t *xf, float *xs, uint8_t *blocks, int *status,
-                         cudaStream_t s) {
-    const int64_t threads = mpad * nb_pad * 32;
+void launch_quantize_rows(int mode, const float *x, int64_t ldx, int64_t m, int64_t k, uint8_t *blocks,
+                          int *status, cudaStream_t s) {
+    const int64_t threads = m * (k / QK) * 32;
     const unsigned grid = unsigned(ceil_div(threads, 256));
-    if (mode == 0) k_quantize_act<0><<<grid, 256, 0, s>>>(x, ldx, m, k, mpad, nb_pad, xf, xs, blocks, status);
-    else if (mode == 2) k_quantize_act<2><<<grid, 256, 0, s>>>(x, ldx, m, k, mpad, nb_pad, xf, xs, blocks, status);
-    else k_quantize_act<1><<<grid, 256, 0, s>>>(x, ldx, m, k, mpad, nb_pad, xf, xs, blocks, status);
+    if (mode == 0) k_quantize_rows<0><<<grid, 256, 0, s>>>(x, ldx, m, k, blocks, status);
+    else if (mode == 2) k_quantize_rows<2><<<grid, 256, 0, s>>>(x, ldx, m, k, blocks, status);
+    else k_quantize_rows<1><<<grid, 256, 0, s>>>(x, ldx, m, k, blocks, status);
+}
+
+void launch_quantize_frag(int mode, const float *x, int64_t ldx, int64_t m, int64_t k, int64_t mpad,
+                          int64_t nb_pad, const float *ln_w, const float *ln_b, float ln_eps, uint32_t *xf,
+                          float *xs, int *status, cudaStream_t s) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(unsigned(mpad));
+    cfg.blockDim = dim3(k >= 1024 ? 256 : 128);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    auto kernel = mode == 0 ? k_quantize_frag<0> : mode == 2 ? k_quantize_frag<2> : k_quantize_frag<1>;
+    cudaLaunchKernelEx(&cfg, kernel, x, ldx, m, k, mpad, nb_pad, ln_w, ln_b, ln_eps, xf, xs, status);
 }
 
 }  // namespace mb

@@ -67,6 +67,21 @@ def quantize(x: torch.Tensor, rounding: str = "arm") -> torch.Tensor:
     return out
 
 
+def _rows(x: torch.Tensor, width: int) -> torch.Tensor:
+    """[..., width] -> a 2-D view with unit inner stride and 16-byte aligned rows."""
+    x2 = x.reshape(-1, width)
+    if x2.stride(-1) != 1 or x2.stride(0) % 4 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    return x2
+
+
+def _norm(norm):
+    if norm is None:
+        return None, None, 0.0
+    weight, bias, eps = norm
+    return weight.data_ptr(), bias.data_ptr(), float(eps)
+
+
 class BlockLinear:
     """One prepared block-quantized linear on the current CUDA device."""
 
@@ -103,12 +118,12 @@ class BlockLinear:
 
     # ggml_mul_mat + epilogue -------------------------------------------------
     def __call__(self, x: torch.Tensor, *, out: torch.Tensor | None = None, residual: torch.Tensor | None = None,
-                 bias: bool = True, gelu: str | None = None, rounding: str = "arm") -> torch.Tensor:
+                 bias: bool = True, gelu: str | None = None, norm: tuple | None = None,
+                 rounding: str = "arm") -> torch.Tensor:
+        """ggml_mul_mat(W, [LayerNorm](x)) + epilogue; norm = (weight, bias, eps) fuses the LayerNorm."""
         _require_cuda(x, "activations", torch.float32)
         lead = x.shape[:-1]
-        x2 = x.reshape(-1, self.width)
-        if x2.stride(-1) != 1:
-            x2 = x2.contiguous()
+        x2 = _rows(x, self.width)
         m = x2.shape[0]
         if out is None:
             out = torch.empty((*lead, self.rows), dtype=torch.float32, device=x.device)
@@ -122,16 +137,23 @@ class BlockLinear:
                 raise ValueError("residual layout differs from the output")
             flags |= RESIDUAL
             r_ptr = r2.data_ptr()
+        lw, lb, eps = _norm(norm)
         e = error_buffer()
         check(self.lib.mstar_b200_linear_run(self.handle, x2.data_ptr(), x2.stride(0), m, o2.data_ptr(), o2.stride(0),
-                                             r_ptr, flags, native.ROUNDING[rounding], _stream(x.device), e, len(e)),
+                                             r_ptr, flags, lw, lb, eps, native.ROUNDING[rounding], _stream(x.device),
+                                             e, len(e)),
               e, "B200 linear")
         return out
+
+    def set_split(self, warps: int) -> None:
+        """Force the K split (1, 2, 4, 8) or restore the automatic choice (0); results do not change."""
+        e = error_buffer()
+        check(self.lib.mstar_b200_linear_set_split(self.handle, warps, e, len(e)), e, "B200 split policy")
 
     def block_sums(self, x: torch.Tensor, rounding: str = "arm") -> torch.Tensor:
         """Exact int32 per-block dots [M, rows, width/32] of the same kernel path."""
         _require_cuda(x, "activations", torch.float32)
-        x = x.reshape(-1, self.width).contiguous()
+        x = _rows(x, self.width).contiguous()
         sums = torch.empty((x.shape[0], self.rows, self.width // 32), dtype=torch.int32, device=x.device)
         e = error_buffer()
         check(self.lib.mstar_b200_linear_block_sums(self.handle, x.data_ptr(), x.shape[0], sums.data_ptr(),
@@ -140,11 +162,11 @@ class BlockLinear:
         return sums
 
     def readout(self, x: torch.Tensor, suppressed: torch.Tensor | None = None, *, rounding: str = "arm",
-                logits: torch.Tensor | None = None, token: torch.Tensor | None = None,
+                norm: tuple | None = None, logits: torch.Tensor | None = None, token: torch.Tensor | None = None,
                 status: torch.Tensor | None = None):
         """Greedy readout of each row of x: (logits [M, rows], token int64 [M], status int32 [1])."""
         _require_cuda(x, "activations", torch.float32)
-        x2 = x.reshape(-1, self.width)
+        x2 = _rows(x, self.width)
         m = x2.shape[0]
         dev = x.device
         logits = torch.empty((m, self.rows), dtype=torch.float32, device=dev) if logits is None else logits
@@ -155,9 +177,10 @@ class BlockLinear:
             _require_cuda(suppressed, "suppression list", torch.int64)
             suppressed = suppressed.contiguous()
             count, s_ptr = suppressed.numel(), suppressed.data_ptr()
+        lw, lb, eps = _norm(norm)
         e = error_buffer()
         check(self.lib.mstar_b200_linear_readout(self.handle, x2.data_ptr(), x2.stride(0), m, logits.data_ptr(),
-                                                 token.data_ptr(), status.data_ptr(), s_ptr, count,
+                                                 token.data_ptr(), status.data_ptr(), s_ptr, count, lw, lb, eps,
                                                  native.ROUNDING[rounding], _stream(dev), e, len(e)),
               e, "B200 readout")
         return logits, token, status

@@ -33,10 +33,13 @@ SIGNATURES = {
     "mstar_b200_pack": (_int, [_int, _vp, _u64, _vp, _u64, _i64, _i64, _int, _int, _vp, *_err]),
     "mstar_b200_q8_quantize": (_int, [_vp, _vp, _sz, _i64, _i64, _int, _vp]),
     "mstar_b200_linear_create": (_vp, [_int, _vp, _u64, _i64, _i64, _vp, *_err]),
-    "mstar_b200_linear_run": (_int, [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _int, _int, _vp, *_err]),
+    "mstar_b200_linear_run": (_int, [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _int, _vp, _vp, C.c_float, _int, _vp,
+                                     *_err]),
     "mstar_b200_linear_block_sums": (_int, [_vp, _vp, _i64, _vp, _u64, _int, _vp, *_err]),
-    "mstar_b200_linear_readout": (_int, [_vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _u64, _int, _vp, *_err]),
+    "mstar_b200_linear_readout": (_int, [_vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _u64, _vp, _vp, C.c_float, _int,
+                                         _vp, *_err]),
     "mstar_b200_linear_close": (_int, [_vp, *_err]),
+    "mstar_b200_linear_set_split": (_int, [_vp, _int, *_err]),
     "mstar_b200_q8_readout": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
 }
 
