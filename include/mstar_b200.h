@@ -123,6 +123,33 @@ MSTAR_B200_API int mstar_b200_linear_set_split(void *handle, int warps, char *er
 MSTAR_B200_API int mstar_b200_q8_readout(void *handle, const float *x, float *out, int64_t *token,
     int32_t *status, const int64_t *suppressed, size_t suppressed_count, void *stream);
 
+/* --- decoder-step glue around the linears (not block-quantized) ----------------
+ * Token + position embedding: x[r] = token_table[ids[r]]*scale +
+ * position_table[positions[r]] (ggml_get_rows + ggml_add, decoder.cpp:513-518;
+ * cpu_decoder_set_token_inputs, decoder_tokens.h:15-24). Out-of-range ids or
+ * positions zero the row and set status bit 2 (value 4). */
+MSTAR_B200_API int mstar_b200_embed(const float *token_table, int64_t vocab, const float *position_table,
+    int64_t positions_count, int64_t width, const int64_t *ids, const int64_t *positions, int64_t rows,
+    float scale, float *x, int32_t *status, void *stream, char *error, size_t error_size);
+/* Multi-head attention over fp16 K/V planes [seq][capacity][heads*64]
+ * (ggml_flash_attn_ext, scale 1/sqrt(64), decoder.cpp:504-511). When k_new/v_new
+ * are given, the `queries` new rows of each sequence are first written at
+ * positions begin[b].. (ggml_set_rows, decoder.cpp:566-567) and attention is
+ * causal up to each query's own position; otherwise every query sees
+ * kv_length[b] keys. shared=1: every sequence reads plane 0 (one encoder state
+ * for the whole batch). Bad positions/lengths set status bit 3 (value 8). */
+MSTAR_B200_API int mstar_b200_attend(const float *q, int64_t q_stride, const float *k_new, const float *v_new,
+    int64_t kv_stride, void *k_plane, void *v_plane, int64_t capacity, int32_t heads, int32_t head_dim,
+    int32_t batch, int32_t queries, const int64_t *begin, const int64_t *kv_length, int32_t causal,
+    int32_t shared, float *out, int64_t out_stride, float scale, int32_t *status, void *stream,
+    char *error, size_t error_size);
+/* Cross K/V planes from the fused projection of the encoder states
+ * (decoder.cpp:247-250, 322-330: one [3072 x 384] Q8_0 matrix for the four
+ * layers' k/v; biases added, then stored fp16 like cross_bias_set_rows). */
+MSTAR_B200_API int mstar_b200_fill_kv(const float *projected, int64_t stride, int64_t k_offset,
+    int64_t v_offset, const float *k_bias, const float *v_bias, void *k_plane, void *v_plane, int64_t rows,
+    int64_t width, void *stream, char *error, size_t error_size);
+
 #ifdef __cplusplus
 }
 #endif

@@ -24,6 +24,7 @@ struct Linear {
     // be ordered on the device (one stream, or explicit events).
     uint32_t *xf = nullptr;  // activation fragments of one 32-query chunk
     float *xs = nullptr;
+    int *xsum = nullptr;
     int *status = nullptr;
     unsigned long long *keys = nullptr;
     unsigned int *done = nullptr;
@@ -31,7 +32,7 @@ struct Linear {
     std::atomic_flag busy = ATOMIC_FLAG_INIT;
     uint64_t weight_bytes() const { return uint64_t(groups) * 8 * nb_pad * (q4 ? 18 : 34); }
     ~Linear() {
-        for (void *p : {(void *)wq, (void *)ws, (void *)bias, (void *)xf, (void *)xs, (void *)status, (void *)keys,
+        for (void *p : {(void *)wq, (void *)ws, (void *)bias, (void *)xf, (void *)xs, (void *)xsum, (void *)status, (void *)keys,
                         (void *)done})
             if (p) cudaFree(p);
     }
@@ -58,12 +59,15 @@ constexpr int64_t CHUNK = 32;  // tokens per GEMV launch
 GemvArgs stage(Linear &h, const float *x, int64_t ldx, int64_t m, int rounding, const float *ln_w,
                const float *ln_b, float ln_eps, int *status, cudaStream_t s) {
     const int64_t mpad = m <= 16 ? 16 : 32;
-    launch_quantize_frag(rounding, x, ldx, m, h.width, mpad, h.nb_pad, ln_w, ln_b, ln_eps, h.xf, h.xs, status, s);
+    launch_quantize_frag(rounding, x, ldx, m, h.width, mpad, h.nb_pad, ln_w, ln_b, ln_eps, h.xf, h.xs, h.xsum, status,
+                         s);
     GemvArgs a{};
+    a.status = status;
     a.wq = h.wq;
     a.ws = reinterpret_cast<const __half2 *>(h.ws);
     a.xf = reinterpret_cast<const uint4 *>(h.xf);
     a.xs = h.xs;
+    a.xsum = h.xsum;
     a.groups = h.groups;
     a.nb_pad = h.nb_pad;
     a.nb = h.nb;
@@ -169,6 +173,7 @@ void *mstar_b200_linear_create(int format, const void *blocks, uint64_t bytes, i
         require(gemv_supported(h->nb_pad), "linear width exceeds the decode kernel's shared-memory tile");
         h->xf = device_alloc<uint32_t>(size_t(h->nb_pad * 2 * 32 * 4), "activation fragments");
         h->xs = device_alloc<float>(size_t(h->nb_pad * 32), "activation scales");
+        h->xsum = device_alloc<int>(size_t(h->nb_pad * 32), "activation block sums");
         check_device(blocks, "linear weights");
         const int64_t chunks = h->nb_pad / (h->q4 ? 4 : 2);
         h->wq = device_alloc<uint4>(size_t(h->groups * chunks * 32), "weight allocation");

@@ -111,6 +111,14 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], const uint4 &a, uint32_t b0,
         : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1), "r"(0));
 }
 
+// D = A(16x32 s8, row) * B(32x8 u8, col), int32, C = 0 (Q4_0 nibbles as u8).
+__device__ __forceinline__ void mma_s8u8(int (&d)[4], const uint4 &a, uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1), "r"(0));
+}
+
 // Packed fp32 pairs (sm_100 f32x2 pipe): each lane is an IEEE RN operation,
 // bit-identical to the scalar __fmul_rn / __fadd_rn.
 __device__ __forceinline__ float2 mul2(float2 a, float2 b) {
@@ -139,10 +147,51 @@ __device__ __forceinline__ float2 i2f2(int a, int b) {
     return r;
 }
 
-// Q4_0 nibbles of 4 bytes -> (elements 4t..4t+3, elements 16+4t..) as int8x4.
+// ---- bulk asynchronous copies (TMA, 1-D) tracked by an mbarrier -------------
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+// One try_wait suspends the thread for up to a system-dependent time limit.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok) : "r"(smem_addr(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Wait for phase `parity` of an mbarrier with an iteration limit; false on timeout.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t limit = 1u << 18) {
+    for (uint32_t i = 0; i < limit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Q4_0 nibbles of 4 bytes -> (elements 4t..4t+3, elements 16+4t..) as unsigned
+// nibbles; the -8 offset is applied after the dot as -8 * (sum of the block's
+// activation quants), which keeps the integer result exact.
 __device__ __forceinline__ void unpack_q4(uint32_t q, uint32_t &lo, uint32_t &hi) {
-    lo = __vsub4(q & 0x0F0F0F0Fu, 0x08080808u);
-    hi = __vsub4((q >> 4) & 0x0F0F0F0Fu, 0x08080808u);
+    lo = q & 0x0F0F0F0Fu;
+    hi = (q >> 4) & 0x0F0F0F0Fu;
 }
 
 // ggml stock GELU: tanh form evaluated on the fp16-rounded input, result

@@ -30,6 +30,7 @@ constexpr int CHUNKS_IN_FLIGHT = 4;
 struct GemvSmem {
     uint4 *xf;
     float *xs;
+    int *xsum;
     float *terms;
     float *stats;
     unsigned long long *best;
@@ -45,8 +46,10 @@ __device__ __forceinline__ void stage_activations(const GemvArgs &a, GemvSmem &s
     const int64_t nf = a.nb_pad * MT * 32;
     for (int64_t i = threadIdx.x; i < nf; i += blockDim.x) s.xf[i] = a.xf[i];
     const int64_t ns = a.nb_pad * MPAD / 4;
-    for (int64_t i = threadIdx.x; i < ns; i += blockDim.x)
+    for (int64_t i = threadIdx.x; i < ns; i += blockDim.x) {
         reinterpret_cast<float4 *>(s.xs)[i] = reinterpret_cast<const float4 *>(a.xs)[i];
+        reinterpret_cast<int4 *>(s.xsum)[i] = reinterpret_cast<const int4 *>(a.xsum)[i];
+    }
     __syncthreads();
 }
 
@@ -65,6 +68,23 @@ __device__ __forceinline__ float finish(const GemvArgs &a, int m, int64_t n, flo
     return v;
 }
 
+// Exact int32 block dots of one m16n8 tile. Q4_0: nibbles n are multiplied
+// unsigned and sum((n - 8) x) = sum(n x) - 8 sum(x) with the block's
+// activation quant sums of rows g and g+8 (xsum_g[0], xsum_g[8]).
+template <bool Q4>
+__device__ __forceinline__ void mma_q(int (&d)[4], const uint4 &a, uint32_t b0, uint32_t b1, const int *xsum_g) {
+    if (Q4) {
+        mma_s8u8(d, a, b0, b1);
+        const int s0 = 8 * xsum_g[0], s1 = 8 * xsum_g[8];
+        d[0] -= s0;
+        d[1] -= s0;
+        d[2] -= s1;
+        d[3] -= s1;
+    } else {
+        mma_s8(d, a, b0, b1);
+    }
+}
+
 // Per-block fp32 terms of one m16n8 tile: rows g (c0, c1) and g+8 (c2, c3)
 // with ggml's generic rounding order (see the file comment).
 template <bool Q4>
@@ -80,45 +100,77 @@ __device__ __forceinline__ void block_terms(const int (&d)[4], float2 dw, float 
     }
 }
 
+// Reduce a per-token argmax key across the 4 lanes sharing row g, then one
+// shared-memory atomic per (warp, token).
+__device__ __forceinline__ void reduce_best(unsigned long long best, unsigned long long *slot, int t) {
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+    }
+    if (t == 0 && best) atomicMax(slot, best);
+}
+
 template <int MT, bool Q4, bool READOUT, bool SUMS, bool SPLIT>
 __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(const GemvArgs a) {
     constexpr int BPC = Q4 ? 4 : 2;  // blocks per 16-byte chunk
     constexpr int MPAD = MT * 16;
+    constexpr int RING = CHUNKS_IN_FLIGHT;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
-    const int wpg = SPLIT ? a.wpg : 1, gpc = SPLIT ? 1 : GEMV_WARPS;
-    const int gi = warp / wpg, ks = warp % wpg;
     const int nb_pad = int(a.nb_pad), nb = int(a.nb), m_live = int(a.m);
     const int chunks = nb_pad / BPC;
-    const int cpw = (chunks + wpg - 1) / wpg;
-    const int c_begin = ks * cpw < chunks ? ks * cpw : chunks;
-    const int c_end = c_begin + cpw < chunks ? c_begin + cpw : chunks;
-    const int64_t G = int64_t(blockIdx.x) * gpc + gi;
-    const bool active = G < a.groups;
+
+    // Work of this warp as a flat sequence of (group, chunk) steps:
+    //   split:   one group per CTA, this warp's contiguous chunk range of it;
+    //   streamed: groups G0, G0 + stride, ... (all chunks of each), so the
+    //            ring of loads runs ahead across group boundaries.
+    int64_t G0, gstride;
+    int c_begin, c_len, ngroups;
+    if (SPLIT) {
+        const int wpg = a.wpg, cpw = (chunks + wpg - 1) / wpg;
+        G0 = blockIdx.x;
+        gstride = 1;
+        c_begin = warp * cpw < chunks ? warp * cpw : chunks;
+        c_len = (c_begin + cpw < chunks ? c_begin + cpw : chunks) - c_begin;
+        ngroups = G0 < a.groups ? 1 : 0;
+    } else {
+        G0 = int64_t(blockIdx.x) * GEMV_WARPS + warp;
+        gstride = int64_t(gridDim.x) * GEMV_WARPS;
+        c_begin = 0;
+        c_len = chunks;
+        ngroups = G0 < a.groups ? int((a.groups - G0 + gstride - 1) / gstride) : 0;
+    }
+    const int total = ngroups * c_len;
 
     GemvSmem s;
     s.xf = reinterpret_cast<uint4 *>(smem_raw);
     s.xs = reinterpret_cast<float *>(s.xf + nb_pad * MT * 32);
-    s.stats = s.xs + nb_pad * MPAD;
+    s.xsum = reinterpret_cast<int *>(s.xs + nb_pad * MPAD);
+    s.stats = reinterpret_cast<float *>(s.xsum + nb_pad * MPAD);
     s.best = reinterpret_cast<unsigned long long *>(s.stats + 2 * MPAD);
     s.terms = reinterpret_cast<float *>(s.best + MPAD);
     if (READOUT && threadIdx.x < MPAD) s.best[threadIdx.x] = 0ull;
 
-    const uint4 *wp = a.wq + (active ? G : 0) * int64_t(chunks) * 32 + lane;
-    const __half2 *sp = a.ws + (active ? G : 0) * int64_t(nb_pad) * 4 + t;
-
-    uint4 w[CHUNKS_IN_FLIGHT];
-    __half2 sc[CHUNKS_IN_FLIGHT][BPC];
-    auto fetch = [&](int c0) {
+    uint4 w[RING];
+    __half2 sc[RING][BPC];
+    int ld_gi = 0, ld_c = 0;  // load cursor: group index (in this warp's sequence) and chunk
+    auto load_next = [&](int u) {
+        if (ld_gi < ngroups) {
+            const int64_t G = G0 + ld_gi * gstride;
+            const int c = c_begin + ld_c;
+            w[u] = ldg_stream(a.wq + (G * chunks + c) * 32 + lane);
+            const __half2 *sp = a.ws + G * int64_t(nb_pad) * 4 + t + c * BPC * 4;
 #pragma unroll
-        for (int u = 0; u < CHUNKS_IN_FLIGHT; ++u)
-            if (active && c0 + u < c_end) {
-                w[u] = ldg_stream(wp + (c0 + u) * 32);
-#pragma unroll
-                for (int j = 0; j < BPC; ++j) sc[u][j] = __ldg(sp + ((c0 + u) * BPC + j) * 4);
+            for (int j = 0; j < BPC; ++j) sc[u][j] = __ldg(sp + j * 4);
+            if (++ld_c == c_len) {
+                ld_c = 0;
+                ++ld_gi;
             }
+        }
     };
-    fetch(c_begin);  // immutable weights: requested before waiting on the producer of x
+#pragma unroll
+    for (int u = 0; u < RING; ++u) load_next(u);  // immutable weights: before waiting on x's producer
     pdl_wait();
     stage_activations<MT>(a, s);
 
@@ -129,14 +181,17 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(const GemvArgs a) {
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = make_float2(0.0f, 0.0f);
     float4 *terms = reinterpret_cast<float4 *>(s.terms);
+    int cu_gi = 0, cu_c = 0;  // compute cursor
 
-    for (int c0 = c_begin; active && c0 < c_end; c0 += CHUNKS_IN_FLIGHT) {
+    for (int s0 = 0; s0 < total; s0 += RING) {
 #pragma unroll
-        for (int u = 0; u < CHUNKS_IN_FLIGHT; ++u) {
-            if (c0 + u >= c_end) break;
+        for (int u = 0; u < RING; ++u) {
+            if (s0 + u >= total) break;
+            const int64_t G = G0 + cu_gi * gstride;
+            const int c = c_begin + cu_c;
 #pragma unroll
             for (int j = 0; j < BPC; ++j) {
-                const int b = (c0 + u) * BPC + j;
+                const int b = c * BPC + j;
                 uint32_t b0, b1;
                 if (Q4) unpack_q4(word(w[u], j), b0, b1);
                 else {
@@ -147,7 +202,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(const GemvArgs a) {
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) {
                     int d[4];
-                    mma_s8(d, s.xf[(b * MT + mt) * 32 + lane], b0, b1);
+                    mma_q<Q4>(d, s.xf[(b * MT + mt) * 32 + lane], b0, b1, s.xsum + b * MPAD + mt * 16 + g);
                     if (SUMS) {
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
@@ -163,6 +218,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(const GemvArgs a) {
                     if (SPLIT) {
                         terms[(b * MT + mt) * 32 + lane] = make_float4(lo_t.x, lo_t.y, hi_t.x, hi_t.y);
                     } else {
+                        // scalar adds: a packed add after a packed multiply may be contracted
                         acc[mt][0].x = __fadd_rn(acc[mt][0].x, lo_t.x);
                         acc[mt][0].y = __fadd_rn(acc[mt][0].y, lo_t.y);
                         if (hi_live[mt]) {
@@ -172,47 +228,48 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(const GemvArgs a) {
                     }
                 }
             }
+            load_next(u);  // refill this ring slot
+            if (++cu_c == c_len) {
+                cu_c = 0;
+                ++cu_gi;
+                if (!SPLIT && !SUMS) {  // group complete: epilogue, reset
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int m = mt * 16 + g + 8 * h;
+                            unsigned long long best = 0ull;
+                            if (m < m_live) {
+#pragma unroll
+                                for (int cc = 0; cc < 2; ++cc) {
+                                    const int64_t n = G * 8 + 2 * t + cc;
+                                    if (n < a.n) {
+                                        const float v = finish<READOUT>(a, m, n, cc ? acc[mt][h].y : acc[mt][h].x);
+                                        if (READOUT) {
+                                            const unsigned long long key = argmax_key(v, uint32_t(n));
+                                            best = key > best ? key : best;
+                                        }
+                                    }
+                                }
+                            }
+                            if (READOUT && mt * 16 + 8 * h < m_live) reduce_best(best, s.best + m, t);
+                            acc[mt][h] = make_float2(0.0f, 0.0f);
+                        }
+                }
+            }
         }
-        fetch(c0 + CHUNKS_IN_FLIGHT);
     }
     if (SUMS) return;
 
-    if (!SPLIT) {
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int m = mt * 16 + g + 8 * h;
-                unsigned long long best = 0ull;
-#pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    const int64_t n = G * 8 + 2 * t + c;
-                    if (active && m < m_live && n < a.n) {
-                        const float2 pair = acc[mt][h];
-                        const float v = finish<READOUT>(a, m, n, c ? pair.y : pair.x);
-                        if (READOUT) {
-                            const unsigned long long key = argmax_key(v, uint32_t(n));
-                            best = key > best ? key : best;
-                        }
-                    }
-                }
-                if (READOUT) {  // lanes 4g..4g+3 share token m: reduce, then one shared atomic
-#pragma unroll
-                    for (int o = 1; o <= 2; o <<= 1) {
-                        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-                        best = other > best ? other : best;
-                    }
-                    if (t == 0 && best) atomicMax(s.best + m, best);
-                }
-            }
-    } else {
+    if (SPLIT) {
         __syncthreads();
         // in-order fold of the per-block terms: one thread per output element
+        const int64_t G = G0;
         for (int o = threadIdx.x; o < MT * 128; o += blockDim.x) {
             const int mt = o / 128, ln = (o / 4) % 32, i = o % 4;
             const int m = mt * 16 + (ln >> 2) + 8 * (i >> 1);
             const int64_t n = G * 8 + 2 * (ln & 3) + (i & 1);
-            if (!active || m >= m_live || n >= a.n) continue;
+            if (G >= a.groups || m >= m_live || n >= a.n) continue;
             const float *tg = s.terms + (mt * 32 + ln) * 4 + i;
             float v = 0.0f;
             for (int b = 0; b < nb; ++b) v = __fadd_rn(v, tg[b * MT * 128]);
@@ -240,6 +297,177 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(const GemvArgs a) {
     }
 }
 
+// Streamed GEMV (unsplit K, many row groups): each warp owns a contiguous run
+// of row groups and walks their chunks in order. Lane 0 keeps STREAM_RING
+// chunks in flight with 1-D TMA bulk copies (weights 512 B + scales 16*BPC B
+// per chunk) into the warp's shared-memory ring, each slot tracked by an
+// mbarrier; the in-flight bytes therefore cost no registers. Every wait is
+// bounded: on timeout the warp sets status bit 1 (value 2), drains its copies
+// (again bounded) and leaves the loop.
+constexpr int STREAM_RING = 8;
+
+template <int MT, bool Q4, bool READOUT>
+__global__ void __launch_bounds__(GEMV_THREADS) k_gemv_stream(const GemvArgs a) {
+    constexpr int BPC = Q4 ? 4 : 2;
+    constexpr int MPAD = MT * 16;
+    constexpr int SC_BYTES = 16 * BPC;
+    constexpr int R = STREAM_RING;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
+    const int nb_pad = int(a.nb_pad), m_live = int(a.m);
+    const int chunks = nb_pad / BPC;
+
+    GemvSmem s;
+    s.xf = reinterpret_cast<uint4 *>(smem_raw);
+    s.xs = reinterpret_cast<float *>(s.xf + nb_pad * MT * 32);
+    s.xsum = reinterpret_cast<int *>(s.xs + nb_pad * MPAD);
+    s.stats = reinterpret_cast<float *>(s.xsum + nb_pad * MPAD);
+    s.best = reinterpret_cast<unsigned long long *>(s.stats + 2 * MPAD);
+    unsigned char *ring = reinterpret_cast<unsigned char *>(s.best + MPAD) + warp * (R * (512 + SC_BYTES + 8));
+    uint4 *wslot = reinterpret_cast<uint4 *>(ring);                     // [R][32] uint4
+    __half2 *sslot = reinterpret_cast<__half2 *>(ring + R * 512);      // [R][BPC*4] half2
+    uint64_t *bar = reinterpret_cast<uint64_t *>(ring + R * (512 + SC_BYTES));
+    if (READOUT && threadIdx.x < MPAD) s.best[threadIdx.x] = 0ull;
+
+    // contiguous group range of this warp
+    const int64_t W = int64_t(gridDim.x) * GEMV_WARPS, wid = int64_t(blockIdx.x) * GEMV_WARPS + warp;
+    const int64_t base = a.groups / W, rem = a.groups % W;
+    const int64_t g_begin = wid * base + (wid < rem ? wid : rem);
+    const int64_t ngroups = base + (wid < rem ? 1 : 0);
+    const int64_t steps = ngroups * chunks;
+
+    if (lane == 0) {
+        for (int u = 0; u < R; ++u) mbar_init(bar + u, 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    int64_t ld_g = g_begin;
+    int ld_c = 0;
+    auto issue = [&](int u) {  // lane 0 only
+        mbar_expect_tx(bar + u, 512 + SC_BYTES);
+        bulk_g2s(wslot + u * 32, a.wq + (ld_g * chunks + ld_c) * 32, 512, bar + u);
+        bulk_g2s(sslot + u * BPC * 4, a.ws + (ld_g * nb_pad + ld_c * BPC) * 4, SC_BYTES, bar + u);
+        if (++ld_c == chunks) {
+            ld_c = 0;
+            ++ld_g;
+        }
+    };
+    if (lane == 0)
+        for (int u = 0; u < R && u < steps; ++u) issue(u);  // immutable weights: before waiting on x
+    pdl_wait();
+    stage_activations<MT>(a, s);
+
+    bool hi_live[MT];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) hi_live[mt] = mt * 16 + 8 < m_live;
+    float2 acc[MT][2];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = make_float2(0.0f, 0.0f);
+    int64_t G = g_begin;
+    int c = 0;
+    int64_t st = 0;
+    bool failed = false;
+    for (; st < steps; ++st) {
+        const int u = int(st % R);
+        const uint32_t parity = uint32_t((st / R) & 1);
+        if (!mbar_wait_bounded(bar + u, parity)) {
+            failed = true;
+            break;
+        }
+        const uint4 wv = wslot[u * 32 + lane];
+        __half2 sc[BPC];
+#pragma unroll
+        for (int j = 0; j < BPC; ++j) sc[j] = sslot[u * BPC * 4 + j * 4 + t];
+        __syncwarp();
+        if (lane == 0 && st + R < steps) {
+            fence_proxy_async();
+            issue(u);
+        }
+#pragma unroll
+        for (int j = 0; j < BPC; ++j) {
+            const int b = c * BPC + j;
+            uint32_t b0, b1;
+            if (Q4) unpack_q4(word(wv, j), b0, b1);
+            else {
+                b0 = word(wv, 2 * j);
+                b1 = word(wv, 2 * j + 1);
+            }
+            const float2 dw = __half22float2(sc[j]);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                int d[4];
+                mma_q<Q4>(d, s.xf[(b * MT + mt) * 32 + lane], b0, b1, s.xsum + b * MPAD + mt * 16 + g);
+                const float dx0 = s.xs[b * MPAD + mt * 16 + g], dx1 = s.xs[b * MPAD + mt * 16 + g + 8];
+                float2 lo_t, hi_t = make_float2(0.0f, 0.0f);
+                block_terms<Q4>(d, dw, dx0, dx1, hi_live[mt], lo_t, hi_t);
+                // scalar adds: a packed add after a packed multiply may be contracted
+                acc[mt][0].x = __fadd_rn(acc[mt][0].x, lo_t.x);
+                acc[mt][0].y = __fadd_rn(acc[mt][0].y, lo_t.y);
+                if (hi_live[mt]) {
+                    acc[mt][1].x = __fadd_rn(acc[mt][1].x, hi_t.x);
+                    acc[mt][1].y = __fadd_rn(acc[mt][1].y, hi_t.y);
+                }
+            }
+        }
+        if (++c == chunks) {  // group complete: epilogue, reset
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int m = mt * 16 + g + 8 * h;
+                    unsigned long long best = 0ull;
+                    if (m < m_live) {
+#pragma unroll
+                        for (int cc = 0; cc < 2; ++cc) {
+                            const int64_t n = G * 8 + 2 * t + cc;
+                            if (n < a.n) {
+                                const float v = finish<READOUT>(a, m, n, cc ? acc[mt][h].y : acc[mt][h].x);
+                                if (READOUT) {
+                                    const unsigned long long key = argmax_key(v, uint32_t(n));
+                                    best = key > best ? key : best;
+                                }
+                            }
+                        }
+                    }
+                    if (READOUT && mt * 16 + 8 * h < m_live) reduce_best(best, s.best + m, t);
+                    acc[mt][h] = make_float2(0.0f, 0.0f);
+                }
+            c = 0;
+            ++G;
+        }
+    }
+    if (failed) {  // report, then drain this warp's copies still in flight (bounded)
+        if (lane == 0 && a.status) atomicOr(a.status, 2);
+        for (int64_t q = st; q < steps && q < st + R; ++q) mbar_wait_bounded(bar + int(q % R), uint32_t((q / R) & 1));
+    }
+
+    if (READOUT) {
+        __shared__ bool last;
+        __syncthreads();
+        if (threadIdx.x < m_live && s.best[threadIdx.x]) atomicMax(a.keys + threadIdx.x, s.best[threadIdx.x]);
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) last = atomicAdd(a.done, 1u) == gridDim.x - 1;
+        __syncthreads();
+        if (last) {
+            __threadfence();
+            if (threadIdx.x < m_live) {
+                const unsigned long long k = atomicExch(a.keys + threadIdx.x, 0ull);
+                a.token[threadIdx.x] = int64_t(0xFFFFFFFFu - uint32_t(k & 0xFFFFFFFFull));
+            }
+            if (threadIdx.x == 0) *a.done = 0u;
+        }
+    }
+}
+
+size_t stream_smem_bytes(int64_t nb_pad, int mt, int q4) {
+    const size_t act = size_t(nb_pad) * mt * 512 + 2 * size_t(nb_pad) * mt * 16 * 4 + 2 * mt * 16 * 4 + mt * 16 * 8;
+    return act + size_t(GEMV_WARPS) * STREAM_RING * (512 + 16 * (q4 ? 4 : 2) + 8);
+}
+
+static int sm_count();
+size_t stream_smem_bytes(int64_t nb_pad, int mt, int q4);
+
 static int sm_count() {
     static int n = 0;
     if (!n) {
@@ -252,7 +480,7 @@ static int sm_count() {
 }
 
 size_t gemv_smem_bytes(int64_t nb_pad, int mt, int wpg) {
-    size_t bytes = size_t(nb_pad) * mt * 512 + size_t(nb_pad) * mt * 16 * 4 + 2 * mt * 16 * 4 + mt * 16 * 8;
+    size_t bytes = size_t(nb_pad) * mt * 512 + 2 * size_t(nb_pad) * mt * 16 * 4 + 2 * mt * 16 * 4 + mt * 16 * 8;
     if (wpg > 1) bytes += size_t(nb_pad) * mt * 512;  // one group per CTA when K is split
     return bytes;
 }
@@ -280,10 +508,41 @@ static void launch_one(GemvArgs a, cudaStream_t s) {
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_LIMIT + 8192));
         configured = SMEM_LIMIT;
     }
+    // split: one CTA per group; streamed: a few CTAs per SM, warps loop over groups
+    int64_t grid = a.wpg == 1 ? ceil_div(a.groups, GEMV_WARPS) : a.groups;
+    if (a.wpg == 1) {
+        const int64_t cap = int64_t(sm_count()) * a.ctas_per_sm;
+        grid = grid < cap ? grid : cap;
+    }
     const int gpc = a.wpg == 1 ? GEMV_WARPS : 1;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(unsigned(ceil_div(a.groups, gpc)));
+    cfg.gridDim = dim3(unsigned(grid));
     cfg.blockDim = dim3(unsigned(32 * a.wpg * gpc));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, a);
+}
+
+template <int MT, bool Q4>
+static void launch_stream(const GemvArgs &a, cudaStream_t s) {
+    const size_t smem = stream_smem_bytes(a.nb_pad, MT, Q4);
+    auto kernel = a.keys ? k_gemv_stream<MT, Q4, true> : k_gemv_stream<MT, Q4, false>;
+    static bool configured[2] = {false, false};
+    if (!configured[a.keys ? 1 : 0]) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_LIMIT + 8192));
+        configured[a.keys ? 1 : 0] = true;
+    }
+    int64_t grid = ceil_div(a.groups, GEMV_WARPS);
+    const int64_t cap = int64_t(sm_count()) * a.ctas_per_sm;
+    grid = grid < cap ? grid : cap;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(unsigned(grid));
+    cfg.blockDim = dim3(GEMV_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -297,6 +556,11 @@ static void launch_one(GemvArgs a, cudaStream_t s) {
 template <int MT, bool Q4>
 static void launch_variant(GemvArgs a, cudaStream_t s) {
     a.wpg = a.sums ? 1 : choose_wpg(a, Q4, MT);
+    if (a.ctas_per_sm <= 0) a.ctas_per_sm = 4;
+    if (!a.sums && a.wpg == 1 && stream_smem_bytes(a.nb_pad, MT, Q4) <= SMEM_LIMIT) {
+        launch_stream<MT, Q4>(a, s);
+        return;
+    }
     if (a.sums) launch_one<MT, Q4, false, true, false>(a, s);
     else if (a.keys) {
         if (a.wpg > 1) launch_one<MT, Q4, true, false, true>(a, s);

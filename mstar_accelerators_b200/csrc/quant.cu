@@ -180,7 +180,8 @@ __global__ void __launch_bounds__(256) k_quantize_frag(const float *__restrict__
                                                        int64_t k, int64_t mpad, int64_t nb_pad,
                                                        const float *__restrict__ ln_w, const float *__restrict__ ln_b,
                                                        float ln_eps, uint32_t *__restrict__ xf,
-                                                       float *__restrict__ xs, int *__restrict__ status) {
+                                                       float *__restrict__ xs, int *__restrict__ xsum,
+                                                       int *__restrict__ status) {
     pdl_wait();
     pdl_trigger();
     __shared__ float red[2][8];
@@ -244,7 +245,13 @@ __global__ void __launch_bounds__(256) k_quantize_frag(const float *__restrict__
         word |= __shfl_down_sync(0xffffffffu, byte, 2) << 16;
         word |= __shfl_down_sync(0xffffffffu, byte, 3) << 24;
         if ((lane & 3) == 0) xf[((b * mtiles + mt) * 32 + (4 * g + t)) * 4 + hi + 2 * half] = word;
-        if (lane == 0) xs[b * mpad + token] = __half2float(__float2half_rn(d));
+        int qsum = q;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+        if (lane == 0) {
+            xs[b * mpad + token] = __half2float(__float2half_rn(d));
+            xsum[b * mpad + token] = qsum;
+        }
     }
 }
 
@@ -277,7 +284,7 @@ void launch_quantize_rows(int mode, const float *x, int64_t ldx, int64_t m, int6
 
 void launch_quantize_frag(int mode, const float *x, int64_t ldx, int64_t m, int64_t k, int64_t mpad,
                           int64_t nb_pad, const float *ln_w, const float *ln_b, float ln_eps, uint32_t *xf,
-                          float *xs, int *status, cudaStream_t s) {
+                          float *xs, int *xsum, int *status, cudaStream_t s) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(unsigned(mpad));
     cfg.blockDim = dim3(k >= 1024 ? 256 : 128);
@@ -288,7 +295,7 @@ void launch_quantize_frag(int mode, const float *x, int64_t ldx, int64_t m, int6
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     auto kernel = mode == 0 ? k_quantize_frag<0> : mode == 2 ? k_quantize_frag<2> : k_quantize_frag<1>;
-    cudaLaunchKernelEx(&cfg, kernel, x, ldx, m, k, mpad, nb_pad, ln_w, ln_b, ln_eps, xf, xs, status);
+    cudaLaunchKernelEx(&cfg, kernel, x, ldx, m, k, mpad, nb_pad, ln_w, ln_b, ln_eps, xf, xs, xsum, status);
 }
 
 }  // namespace mb

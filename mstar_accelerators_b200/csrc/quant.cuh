@@ -13,7 +13,7 @@ void launch_quantize_rows(int mode, const float *x, int64_t ldx, int64_t m, int6
 // fp32 rows [-> LayerNorm] -> Q8_0 A fragments + fp32 scales for the GEMV (PDL launch)
 void launch_quantize_frag(int mode, const float *x, int64_t ldx, int64_t m, int64_t k, int64_t mpad,
                           int64_t nb_pad, const float *ln_w, const float *ln_b, float ln_eps, uint32_t *xf,
-                          float *xs, int *status, cudaStream_t s);
+                          float *xs, int *xsum, int *status, cudaStream_t s);
 
 // Parameters of one fragment-layout GEMV launch (M <= 32 tokens).
 struct GemvArgs {
@@ -23,6 +23,8 @@ struct GemvArgs {
     // activations quantized by launch_quantize_frag (global, L2-resident)
     const uint4 *xf;       // [nb_pad][mtiles][32] A fragments
     const float *xs;       // [nb_pad][mpad] fp32 scales
+    const int *xsum;       // [nb_pad][mpad] sum of each block's activation quants
+    int *status;           // bit 1 (value 2): a bounded pipeline wait timed out
     float *out;            // [m][ldo]
     int64_t ldo;
     const float *bias;     // [n] or null
@@ -37,6 +39,7 @@ struct GemvArgs {
     int64_t suppressed_count;
     int wpg;                   // warps per row group (set by the launcher)
     int wpg_override;          // > 0 forces a split (tests)
+    int ctas_per_sm;           // streamed (unsplit) launches: resident CTAs per SM (0: default)
 };
 
 bool gemv_supported(int64_t nb_pad);
