@@ -30,26 +30,32 @@ __global__ void k_embed(const float *__restrict__ tok, const float *__restrict__
 }
 
 constexpr int ATT_THREADS = 128;
+constexpr int ATT_WARPS = ATT_THREADS / 32;
 constexpr int HEAD_DIM = 64;
 constexpr int MAX_Q = 4;
 
-// One CTA per (sequence b, head h). Queries q_i (i < nq) of sequence b sit at
+// One CTA per (sequence b, head h). Queries q_i (i < NQ) of sequence b sit at
 // positions begin_b + i; the CTA first appends their K/V rows (when given) to
 // the sequence's fp16 planes, then attends query i over keys [0, len_i) with
 // len_i = causal ? begin_b + i + 1 : kv_len_b.
-//   q:    [b][nq][q_stride] fp32, head h at column h*64
+//   q:    [b][NQ][q_stride] fp32, head h at column h*64
 //   k/v new rows (optional): same layout as q with their own column offset
 //   planes: kc/vc [seq][capacity][heads*64] fp16; seq index = shared ? 0 : b
-//   out:  [b][nq][out_stride] fp32, head h at column h*64
+//   out:  [b][NQ][out_stride] fp32, head h at column h*64
+// Scores: one thread per key (64-wide dot from one 128-byte K row). Softmax:
+// block reductions. Weighted sum: warp w owns a contiguous key range, lane l
+// owns dims 2l, 2l+1 (one coalesced half2 per key row), then the four warps'
+// partial sums are added in shared memory.
+template <int NQ>
 __global__ void __launch_bounds__(ATT_THREADS) k_attend(
     const float *__restrict__ q, int64_t q_stride, const float *__restrict__ knew, const float *__restrict__ vnew,
-    int64_t kv_stride, __half *__restrict__ kc, __half *__restrict__ vc, int64_t capacity, int heads, int nq,
+    int64_t kv_stride, __half *__restrict__ kc, __half *__restrict__ vc, int64_t capacity, int heads,
     const int64_t *__restrict__ begin, const int64_t *__restrict__ kv_len, int causal, int shared,
     float *__restrict__ out, int64_t out_stride, float scale, int *__restrict__ status) {
-    extern __shared__ float scores[];  // [nq][capacity]
-    __shared__ float qs[MAX_Q][HEAD_DIM];
-    __shared__ float red[MAX_Q][ATT_THREADS / 32];
-    __shared__ float part[MAX_Q][2][HEAD_DIM];
+    extern __shared__ float scores[];  // [NQ][capacity]
+    __shared__ float qs[NQ][HEAD_DIM];
+    __shared__ float red[NQ][ATT_WARPS];
+    __shared__ float2 part[ATT_WARPS][NQ][32];
     const int b = blockIdx.x / heads, h = blockIdx.x % heads;
     const int width = heads * HEAD_DIM;
     const int64_t seq = shared ? 0 : b;
@@ -58,33 +64,33 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attend(
     __half *vp = vc + seq * capacity * width + h * HEAD_DIM;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
-    // append new rows (positions b0 .. b0+nq-1)
-    if (knew) {
-        if (b0 < 0 || b0 + nq > capacity) {
+    if (knew) {  // append the new rows at positions b0 .. b0+NQ-1
+        if (b0 < 0 || b0 + NQ > capacity) {
             if (tid == 0) atomicOr(status, 8);
             return;
         }
-        for (int i = tid; i < nq * HEAD_DIM; i += ATT_THREADS) {
+        for (int i = tid; i < NQ * HEAD_DIM; i += ATT_THREADS) {
             const int qi = i / HEAD_DIM, dd = i % HEAD_DIM;
-            const int64_t src = (int64_t(b) * nq + qi) * kv_stride + h * HEAD_DIM + dd;
+            const int64_t src = (int64_t(b) * NQ + qi) * kv_stride + h * HEAD_DIM + dd;
             kp[(b0 + qi) * width + dd] = __float2half_rn(knew[src]);
             vp[(b0 + qi) * width + dd] = __float2half_rn(vnew[src]);
         }
     }
-    for (int i = tid; i < nq * HEAD_DIM; i += ATT_THREADS) {
+    for (int i = tid; i < NQ * HEAD_DIM; i += ATT_THREADS) {
         const int qi = i / HEAD_DIM, dd = i % HEAD_DIM;
-        qs[qi][dd] = q[(int64_t(b) * nq + qi) * q_stride + h * HEAD_DIM + dd];
+        qs[qi][dd] = q[(int64_t(b) * NQ + qi) * q_stride + h * HEAD_DIM + dd];
     }
     __syncthreads();
-    const int64_t total = causal ? b0 + nq : kv_len[b];
-    if (total < 0 || total > capacity) {
+    const int64_t total = causal ? b0 + NQ : kv_len[b];
+    if (total < 1 || total > capacity) {
         if (tid == 0) atomicOr(status, 8);
         return;
     }
-    // scores
     for (int64_t j = tid; j < total; j += ATT_THREADS) {
         const uint4 *krow = reinterpret_cast<const uint4 *>(kp + j * width);
-        float acc[MAX_Q] = {0.0f, 0.0f, 0.0f, 0.0f};
+        float acc[NQ];
+#pragma unroll
+        for (int qi = 0; qi < NQ; ++qi) acc[qi] = 0.0f;
 #pragma unroll
         for (int c = 0; c < HEAD_DIM / 8; ++c) {
             const uint4 raw = krow[c];
@@ -92,19 +98,21 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attend(
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const float2 kv = __half22float2(h2[e]);
-                for (int qi = 0; qi < nq; ++qi)
+#pragma unroll
+                for (int qi = 0; qi < NQ; ++qi)
                     acc[qi] = fmaf(qs[qi][8 * c + 2 * e + 1], kv.y, fmaf(qs[qi][8 * c + 2 * e], kv.x, acc[qi]));
             }
         }
-        for (int qi = 0; qi < nq; ++qi) {
+#pragma unroll
+        for (int qi = 0; qi < NQ; ++qi) {
             const int64_t len = causal ? b0 + qi + 1 : total;
             scores[qi * capacity + j] = j < len ? acc[qi] * scale : -INFINITY;
         }
     }
     __syncthreads();
-    // softmax per query
-    float mx[MAX_Q], sum[MAX_Q];
-    for (int qi = 0; qi < nq; ++qi) {
+    float mx[NQ], inv[NQ];
+#pragma unroll
+    for (int qi = 0; qi < NQ; ++qi) {
         float m = -INFINITY;
         for (int64_t j = tid; j < total; j += ATT_THREADS) m = fmaxf(m, scores[qi * capacity + j]);
 #pragma unroll
@@ -112,41 +120,79 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attend(
         if (lane == 0) red[qi][warp] = m;
     }
     __syncthreads();
-    for (int qi = 0; qi < nq; ++qi) {
+#pragma unroll
+    for (int qi = 0; qi < NQ; ++qi) {
         float m = red[qi][0];
-        for (int w = 1; w < ATT_THREADS / 32; ++w) m = fmaxf(m, red[qi][w]);
+#pragma unroll
+        for (int w = 1; w < ATT_WARPS; ++w) m = fmaxf(m, red[qi][w]);
         mx[qi] = m;
     }
     __syncthreads();
-    for (int qi = 0; qi < nq; ++qi) {
-        float s = 0.0f;
+#pragma unroll
+    for (int qi = 0; qi < NQ; ++qi) {
+        float sum = 0.0f;
         for (int64_t j = tid; j < total; j += ATT_THREADS) {
             const float e = __expf(scores[qi * capacity + j] - mx[qi]);
             scores[qi * capacity + j] = e;
-            s += e;
+            sum += e;
         }
 #pragma unroll
-        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) red[qi][warp] = s;
+        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) red[qi][warp] = sum;
     }
     __syncthreads();
-    for (int qi = 0; qi < nq; ++qi) {
-        float s = 0.0f;
-        for (int w = 0; w < ATT_THREADS / 32; ++w) s += red[qi][w];
-        sum[qi] = s;
+#pragma unroll
+    for (int qi = 0; qi < NQ; ++qi) {
+        float sum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < ATT_WARPS; ++w) sum += red[qi][w];
+        inv[qi] = 1.0f / sum;
     }
-    // weighted sum: thread (dd, half) over alternate keys
-    const int dd = tid % HEAD_DIM, hf = tid / HEAD_DIM;
-    float o[MAX_Q] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int64_t j = hf; j < total; j += 2) {
-        const float vv = __half2float(vp[j * width + dd]);
-        for (int qi = 0; qi < nq; ++qi) o[qi] = fmaf(scores[qi * capacity + j], vv, o[qi]);
+    // weighted sum over this warp's key range
+    const int64_t per = (total + ATT_WARPS - 1) / ATT_WARPS;
+    const int64_t j0 = warp * per, j1 = j0 + per < total ? j0 + per : total;
+    float2 o[NQ];
+#pragma unroll
+    for (int qi = 0; qi < NQ; ++qi) o[qi] = make_float2(0.0f, 0.0f);
+    const __half2 *vcol = reinterpret_cast<const __half2 *>(vp) + lane;
+    int64_t j = j0;
+    for (; j + 4 <= j1; j += 4) {
+        float2 v4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v4[u] = __half22float2(vcol[(j + u) * (width / 2)]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int qi = 0; qi < NQ; ++qi) {
+                const float p = scores[qi * capacity + j + u];
+                o[qi].x = fmaf(p, v4[u].x, o[qi].x);
+                o[qi].y = fmaf(p, v4[u].y, o[qi].y);
+            }
     }
-    for (int qi = 0; qi < nq; ++qi) part[qi][hf][dd] = o[qi];
+    for (; j < j1; ++j) {
+        const float2 v = __half22float2(vcol[j * (width / 2)]);
+#pragma unroll
+        for (int qi = 0; qi < NQ; ++qi) {
+            const float p = scores[qi * capacity + j];
+            o[qi].x = fmaf(p, v.x, o[qi].x);
+            o[qi].y = fmaf(p, v.y, o[qi].y);
+        }
+    }
+#pragma unroll
+    for (int qi = 0; qi < NQ; ++qi) part[warp][qi][lane] = o[qi];
     __syncthreads();
-    if (hf == 0)
-        for (int qi = 0; qi < nq; ++qi)
-            out[(int64_t(b) * nq + qi) * out_stride + h * HEAD_DIM + dd] = (part[qi][0][dd] + part[qi][1][dd]) / sum[qi];
+    for (int i = tid; i < NQ * 32; i += ATT_THREADS) {
+        const int qi = i / 32, l = i % 32;
+        float2 acc = part[0][qi][l];
+#pragma unroll
+        for (int w = 1; w < ATT_WARPS; ++w) {
+            acc.x += part[w][qi][l].x;
+            acc.y += part[w][qi][l].y;
+        }
+        float *dst = out + (int64_t(b) * NQ + qi) * out_stride + h * HEAD_DIM + 2 * l;
+        dst[0] = acc.x * inv[qi];
+        dst[1] = acc.y * inv[qi];
+    }
 }
 
 // K/V planes from projected rows: kc/vc[seq][r][:] = fp16(src[r][k_off / v_off + :]) + bias
@@ -204,13 +250,17 @@ int mstar_b200_attend(const float *q, int64_t q_stride, const float *k_new, cons
         require(smem <= 200 * 1024, "attention score tile exceeds shared memory");
         static bool configured = false;
         if (!configured) {
-            cudaFuncSetAttribute(k_attend, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            cudaFuncSetAttribute(k_attend<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            cudaFuncSetAttribute(k_attend<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            cudaFuncSetAttribute(k_attend<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            cudaFuncSetAttribute(k_attend<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
             configured = true;
         }
         cudaStream_t s = as_stream(stream);
-        k_attend<<<unsigned(batch * heads), ATT_THREADS, smem, s>>>(
+        auto kernel = queries == 1 ? k_attend<1> : queries == 2 ? k_attend<2> : queries == 3 ? k_attend<3> : k_attend<4>;
+        kernel<<<unsigned(batch * heads), ATT_THREADS, smem, s>>>(
             q, q_stride, k_new, v_new, kv_stride, static_cast<__half *>(k_plane), static_cast<__half *>(v_plane),
-            capacity, heads, queries, begin, kv_length, causal, shared, out, out_stride, scale, status);
+            capacity, heads, begin, kv_length, causal, shared, out, out_stride, scale, status);
         cuda_check(cudaGetLastError(), "attention launch");
         return 0;
     } catch (const std::exception &e) {
