@@ -1,0 +1,60 @@
+"""Named small workloads for profiling one kernel or one step under ncu.
+
+    python -m mstar_accelerators_b200.cases readout-q4-b32
+    python -m mstar_accelerators_b200.cases decode-step-b32
+
+Each case builds its inputs from fixed seeds, runs a few calls, synchronises
+and prints "ok". The ncu summaries under profiles/ name the case they used.
+"""
+from __future__ import annotations
+
+import sys
+
+import torch
+
+
+def readout_q4_b32():
+    """Whisper-tiny tied Q4_0 readout (51865 x 384), 32 query rows, three calls."""
+    from .linear import BlockLinear
+    g = torch.Generator(device="cuda").manual_seed(1)
+    w = torch.randn(51865, 384, device="cuda", generator=g) * 0.02
+    head = BlockLinear(w, fmt="q4_0")
+    x = torch.randn(32, 384, device="cuda", generator=g)
+    for _ in range(3):
+        head.readout(x)
+
+
+def decode_step_b32():
+    """One Whisper-tiny decoder at batch 32: prefill 4 tokens, capture the greedy
+    decode step as a CUDA graph, replay it twice."""
+    from .whisper import GraphDecoder, WhisperConfig, WhisperDecoderB200, synthetic_weights
+    cfg = WhisperConfig()
+    w = synthetic_weights(cfg, seed=1, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(2)
+    enc = torch.randn((1, cfg.source, cfg.d_model), device="cuda", generator=g)
+    dec = WhisperDecoderB200(w, cfg, batch=32)
+    prompt = torch.randint(0, cfg.vocab, (32, 4), device="cuda", generator=g)
+    _, tok = dec.prefill(prompt, enc)
+    gd = GraphDecoder(dec)
+    gd.tokens.copy_(tok)
+    gd.positions.fill_(4)
+    gd.capture()
+    gd.run(2)
+
+
+CASES = {"readout-q4-b32": readout_q4_b32, "decode-step-b32": decode_step_b32}
+
+
+def main(argv):
+    if len(argv) != 1 or argv[0] not in CASES:
+        print("cases:", ", ".join(CASES))
+        return 2
+    torch.cuda.set_device(0)
+    CASES[argv[0]]()
+    torch.cuda.synchronize()
+    print("ok")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main(sys.argv[1:]))
