@@ -123,6 +123,24 @@ MSTAR_B200_API int mstar_b200_linear_set_split(void *handle, int warps, char *er
 MSTAR_B200_API int mstar_b200_q8_readout(void *handle, const float *x, float *out, int64_t *token,
     int32_t *status, const int64_t *suppressed, size_t suppressed_count, void *stream);
 
+/* --- readout that allocates nothing ------------------------------------------------
+ * No counterpart in the reference. For callers that cannot allocate device
+ * memory (a runtime that owns every device buffer and hands out only planned
+ * ones, or a latency-bound caller that must not pay for cudaMalloc and the
+ * synchronisation it can bring): the q8cpu_readout contract over the caller's
+ * canonical ggml Q8_0 bytes (device, 2-byte aligned) with one fp32 query x[k]
+ * (16-byte aligned): logits[rows] (suppressed rows -inf), token (first index,
+ * first NaN wins), status[0] = 1 if x is nonfinite. Bit-identical to
+ * mstar_b200_q8_readout on a handle created from the same bytes.
+ * Scratch lives in one fixed device array (about 81 KB per device, held until
+ * the process exits) shared by every call: calls that overlap on the GPU race.
+ * Limit k <= 4096: a wider k returns E2BIG; other bad arguments EINVAL.
+ * The first call on a device resolves the array's address (cudaGetSymbolAddress,
+ * that device current); make it before capturing any stream. */
+MSTAR_B200_API int mstar_b200_q8_readout_noalloc(const void *blocks, size_t bytes, int64_t rows, int64_t k,
+    const float *x, float *logits, int64_t *token, int32_t *status, const int64_t *suppressed,
+    size_t suppressed_count, void *stream);
+
 /* --- decoder-step glue around the linears (not block-quantized) ----------------
  * Token + position embedding: x[r] = token_table[ids[r]]*scale +
  * position_table[positions[r]] (ggml_get_rows + ggml_add, decoder.cpp:513-518;

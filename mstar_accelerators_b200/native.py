@@ -45,6 +45,7 @@ SIGNATURES = {
     "mstar_b200_attend": (_int, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64, C.c_int32, C.c_int32, C.c_int32,
                                  C.c_int32, _vp, _vp, C.c_int32, C.c_int32, _vp, _i64, C.c_float, _vp, _vp, *_err]),
     "mstar_b200_fill_kv": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _vp, *_err]),
+    "mstar_b200_q8_readout_noalloc": (_int, [_vp, _sz, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
 }
 
 
