@@ -112,6 +112,14 @@ MSTAR_B200_API int mstar_b200_linear_readout(void *handle, const float *x, int64
     uint64_t suppressed_count, const float *ln_weight, const float *ln_bias, float ln_eps,
     int rounding, void *stream, char *error, size_t error_size);
 MSTAR_B200_API int mstar_b200_linear_close(void *handle, char *error, size_t error_size);
+/* Prepare the tcgen05 GEMM used by linear_run calls of 64..max_queries rows
+ * without a fused LayerNorm (prefill / encoder shapes, the M = 1500 and
+ * M = 24000 mul_mat of encoder.cpp:467-479, 694-723): keeps fp16(q*d) of the
+ * canonical blocks (the same bytes given to create) and an activation buffer
+ * of max_queries rows. Results match ggml's mul_mat to reorder and fp16
+ * product-rounding tolerance (the decode GEMV stays bit-exact). Synchronises. */
+MSTAR_B200_API int mstar_b200_linear_prepare_gemm(void *handle, const void *blocks, uint64_t bytes,
+    int64_t max_queries, char *error, size_t error_size);
 /* Physical policy, set on an idle handle (the role of
  * cpu_decoder_set_cross_threads, decoder.h:44-47): warps that split one
  * 8-row group's K range (1, 2, 4 or 8; 0 restores the automatic choice).

@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "../../include/mstar_b200.h"
+#include "gemm.cuh"
 #include "quant.cuh"
 
 namespace mb {
@@ -29,11 +30,16 @@ struct Linear {
     unsigned long long *keys = nullptr;
     unsigned int *done = nullptr;
     int wpg_override = 0;  // > 0 forces the split-K fold (tests)
+    // tcgen05 GEMM state for calls with more than GEMM_MIN_QUERIES rows
+    __half *w16 = nullptr;        // fp16(q * d) weights [rows][width]
+    __half *x16 = nullptr;        // fp16 dequantized activations [gemm_rows][width]
+    int64_t gemm_rows = 0;
+    CUtensorMap wmap{};
     std::atomic_flag busy = ATOMIC_FLAG_INIT;
     uint64_t weight_bytes() const { return uint64_t(groups) * 8 * nb_pad * (q4 ? 18 : 34); }
     ~Linear() {
         for (void *p : {(void *)wq, (void *)ws, (void *)bias, (void *)xf, (void *)xs, (void *)xsum, (void *)status, (void *)keys,
-                        (void *)done})
+                        (void *)done, (void *)w16, (void *)x16})
             if (p) cudaFree(p);
     }
 };
@@ -53,7 +59,8 @@ T *device_alloc(size_t count, const char *what) {
     return static_cast<T *>(p);
 }
 
-constexpr int64_t CHUNK = 32;  // tokens per GEMV launch
+constexpr int64_t CHUNK = 32;             // tokens per GEMV launch
+constexpr int64_t GEMM_MIN_QUERIES = 64;  // larger calls use the tcgen05 GEMM once it is prepared
 
 // Quantize one chunk of <= 32 queries, then describe the GEMV over it.
 GemvArgs stage(Linear &h, const float *x, int64_t ldx, int64_t m, int rounding, const float *ln_w,
@@ -245,6 +252,16 @@ int mstar_b200_linear_run(void *handle, const float *x, int64_t x_stride, int64_
             check_device(residual, "residual");
         } else require(!residual, "residual given without its epilogue flag");
         cudaStream_t s = as_stream(stream);
+        if (h.w16 && !ln_weight && queries >= GEMM_MIN_QUERIES && queries <= h.gemm_rows) {
+            launch_dequant_act(rounding, x, x_stride, queries, h.width, h.x16, h.status, s);
+            CUtensorMap xmap;
+            make_fp16_map(&xmap, h.x16, queries, h.width, GEMM_TILE_M);
+            GemmArgs g{queries, h.rows, h.width, out, out_stride, h.bias, (flags & 4) ? residual : nullptr, flags,
+                       h.status};
+            launch_gemm(xmap, h.wmap, g, s);
+            cuda_check(cudaGetLastError(), "GEMM launch");
+            return 0;
+        }
         for (int64_t m0 = 0; m0 < queries; m0 += CHUNK) {
             const int64_t m = queries - m0 < CHUNK ? queries - m0 : CHUNK;
             GemvArgs a = stage(h, x + m0 * x_stride, x_stride, m, rounding, ln_weight, ln_bias, ln_eps, h.status, s);
@@ -346,6 +363,36 @@ int mstar_b200_q8_readout(void *handle, const float *x, float *out, int64_t *tok
                                      nullptr, nullptr, 0.0f, MSTAR_B200_Q8_ARM, stream, e, sizeof(e))
                ? EINVAL
                : 0;
+}
+
+int mstar_b200_linear_prepare_gemm(void *handle, const void *blocks, uint64_t bytes, int64_t max_queries,
+                                   char *error, size_t error_size) {
+    try {
+        require(handle, "missing linear handle");
+        auto &h = *static_cast<Linear *>(handle);
+        Busy busy(h.busy);
+        require(max_queries >= GEMM_MIN_QUERIES && max_queries <= (int64_t(1) << 31), "invalid GEMM query capacity");
+        check_range({blocks, bytes}, uint64_t(h.rows) * h.nb * (h.q4 ? Q4_BYTES : Q8_BYTES), 1, "linear weights");
+        check_device(blocks, "linear weights");
+        cuda_check(cudaDeviceSynchronize(), "GEMM preparation");
+        if (!h.w16) {
+            h.w16 = device_alloc<__half>(size_t(h.rows * h.width), "fp16 GEMM weights");
+            launch_dequant_weights(static_cast<const uint8_t *>(blocks), h.w16, h.rows, h.nb, h.q4, nullptr);
+            cuda_check(cudaGetLastError(), "weight dequantization");
+            make_fp16_map(&h.wmap, h.w16, h.rows, h.width, GEMM_TILE_N);
+        }
+        if (max_queries > h.gemm_rows) {
+            if (h.x16) cudaFree(h.x16);
+            h.x16 = nullptr;
+            h.x16 = device_alloc<__half>(size_t(max_queries * h.width), "fp16 GEMM activations");
+            h.gemm_rows = max_queries;
+        }
+        cuda_check(cudaDeviceSynchronize(), "GEMM preparation");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
 }
 
 int mstar_b200_linear_set_split(void *handle, int warps, char *error, size_t error_size) {

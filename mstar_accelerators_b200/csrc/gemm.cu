@@ -1,0 +1,279 @@
+// Prefill / encoder shapes (M >> 32 rows): tcgen05 GEMM over the block-
+// quantized operands dequantized to fp16 (the "dequant staging" form of the
+// Q8_0 contraction): A = fp16(x_q * d_x) with x_q, d_x the Q8_0 activation
+// quantization of ggml quantize_row_q8_0 (selected rounding), B = fp16(w_q * d_w)
+// from the canonical weight blocks. The block-quantized values are preserved up
+// to one fp16 rounding of each product of a quant and its scale; the
+// contraction accumulates in fp32 in TMEM, so results match ggml's mul_mat to
+// reorder + fp16-rounding tolerance (the decode GEMV keeps the exact integer
+// path).
+//
+// Kernel: one 128 x 256 output tile per CTA, 6 warps:
+//   warp 0  TMA producer: 2-D tiled bulk tensor copies (128B swizzle) of the
+//           A (128 x 64) and B (256 x 64) K-slices into a 4-stage ring;
+//   warp 1  allocates 256 TMEM columns; one thread issues tcgen05.mma
+//           kind::f16 (M=128, N=256, K=16, fp32 accumulate) and commits each
+//           stage back to the producer, and the last one to the epilogue;
+//   warps 2-5 epilogue: tcgen05.ld 32x32b.x32 from their TMEM lane quarter,
+//           bias / GELU / residual, fp32 stores.
+// Every mbarrier wait is bounded; a timeout sets status bit value 2 and the
+// CTA skips to the end (TMEM is still released).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "../../include/mstar_b200.h"
+#include "gemm.cuh"
+
+namespace mb {
+
+constexpr int GEMM_BM = 128, GEMM_BN = 256, GEMM_BK = 64, GEMM_STAGES = 4;
+constexpr int GEMM_A_BYTES = GEMM_BM * GEMM_BK * 2;
+constexpr int GEMM_B_BYTES = GEMM_BN * GEMM_BK * 2;
+constexpr int GEMM_STAGE_BYTES = GEMM_A_BYTES + GEMM_B_BYTES;
+constexpr int GEMM_THREADS = 192;
+constexpr uint32_t GEMM_TMEM_COLS = 256;
+// instruction descriptor: D f32 (bits 4-5 = 1), A/B f16 (0), K-major A and B,
+// N >> 3 at bits 17-22, M >> 4 at bits 24-28
+constexpr uint32_t GEMM_IDESC = (1u << 4) | (uint32_t(GEMM_BN >> 3) << 17) | (uint32_t(GEMM_BM >> 4) << 24);
+constexpr size_t GEMM_SMEM = size_t(GEMM_STAGES) * GEMM_STAGE_BYTES + 1024 + 256;
+
+// UMMA shared-memory descriptor of a K-major, 128B-swizzled tile whose rows
+// are 128 bytes (64 fp16) and whose 8-row groups are 1024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = uint64_t((saddr >> 4) & 0x3FFF);
+    d |= uint64_t(1) << 16;             // leading byte offset (16 B; unused for swizzled K-major)
+    d |= uint64_t(1024 >> 4) << 32;     // stride byte offset: 8 rows x 128 B
+    d |= uint64_t(1) << 46;             // descriptor version for tcgen05
+    d |= uint64_t(2) << 61;             // SWIZZLE_128B
+    return d;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }"
+        ::"r"(tmem), "l"(da), "l"(db), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+        "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm_f16(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const GemmArgs a) {
+    extern __shared__ __align__(1024) unsigned char gemm_smem[];
+    unsigned char *base = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(gemm_smem) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(base + GEMM_STAGES * GEMM_STAGE_BYTES);
+    uint64_t *empty = full + GEMM_STAGES;
+    uint64_t *done = empty + GEMM_STAGES;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    __shared__ int failed;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t m0 = int64_t(blockIdx.y) * GEMM_BM, n0 = int64_t(blockIdx.x) * GEMM_BN;
+    const int kt = int((a.K + GEMM_BK - 1) / GEMM_BK);
+
+    if (threadIdx.x == 0) {
+        failed = 0;
+        for (int s = 0; s < GEMM_STAGES; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 1);
+        }
+        mbar_init(done, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(GEMM_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int i = 0; i < kt; ++i) {
+                const int s = i % GEMM_STAGES;
+                if (!mbar_wait_bounded(empty + s, uint32_t(((i / GEMM_STAGES) & 1) ^ 1))) {
+                    atomicOr(&failed, 1);
+                    break;
+                }
+                unsigned char *sa = base + s * GEMM_STAGE_BYTES;
+                mbar_expect_tx(full + s, GEMM_STAGE_BYTES);
+                tma_load_2d(sa, &ta, i * GEMM_BK, int(m0), full + s);
+                tma_load_2d(sa + GEMM_A_BYTES, &tb, i * GEMM_BK, int(n0), full + s);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (int i = 0; i < kt; ++i) {
+                const int s = i % GEMM_STAGES;
+                if (!mbar_wait_bounded(full + s, uint32_t((i / GEMM_STAGES) & 1))) {
+                    atomicOr(&failed, 1);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sa = smem_addr(base + s * GEMM_STAGE_BYTES);
+                const uint64_t da = sw128_desc(sa), db = sw128_desc(sa + GEMM_A_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < GEMM_BK / 16; ++kk)   // K=16 per MMA: +32 B in the swizzled row
+                    umma_f16(tmem, da + uint64_t(2 * kk), db + uint64_t(2 * kk), GEMM_IDESC, (i | kk) != 0);
+                umma_commit(empty + s);
+            }
+            umma_commit(done);
+        }
+    } else {
+        const int q = warp & 3;  // TMEM lane quarter this warp may read
+        if (!mbar_wait_bounded(done, 0)) {
+            atomicOr(&failed, 1);
+        } else {
+            tc_fence_after();
+            const int64_t row = m0 + 32 * q + lane;
+            for (int c = 0; c < GEMM_BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(c * 32), r);
+                if (row < a.M) {
+                    float *orow = a.out + row * a.ldo;
+                    const float *rrow = a.residual ? a.residual + row * a.ldo : nullptr;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int64_t n = n0 + c * 32 + j;
+                        if (n < a.N) {
+                            float v = __uint_as_float(r[j]);
+                            if (a.flags & 1) v = __fadd_rn(v, a.bias[n]);
+                            if (a.flags & 2) v = gelu_ggml(v);
+                            else if (a.flags & 8) v = gelu_erf(v);
+                            if (a.flags & 4) v = __fadd_rn(rrow[n], v);
+                            orow[n] = v;
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x == 0 && failed && a.status) atomicOr(a.status, 2);
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(GEMM_TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// fp16 dequantized operands ---------------------------------------------------
+// weights: canonical Q8_0 / Q4_0 blocks [rows][nb] -> fp16(q * d) [rows][K]
+__global__ void k_dequant_weights(const uint8_t *__restrict__ blocks, __half *__restrict__ out, int64_t rows,
+                                  int64_t nb, int q4) {
+    const int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;  // one thread per element
+    if (i >= rows * nb * QK) return;
+    const int64_t r = i / (nb * QK), k = i % (nb * QK), b = k / QK, j = k % QK;
+    const uint8_t *blk = blocks + (r * nb + b) * (q4 ? Q4_BYTES : Q8_BYTES);
+    const float d = __half2float(__ushort_as_half(uint16_t(blk[0]) | uint16_t(uint16_t(blk[1]) << 8)));
+    int q;
+    if (q4) q = (j < 16 ? (blk[2 + j] & 0x0F) : (blk[2 + j - 16] >> 4)) - 8;
+    else q = int8_t(blk[2 + j]);
+    out[i] = __float2half_rn(__fmul_rn(float(q), d));
+}
+
+// activations: fp32 rows -> Q8_0 quantization (selected rounding) -> fp16(q * d)
+template <int MODE>
+__global__ void k_dequant_act(const float *__restrict__ x, int64_t ldx, int64_t m, int64_t k,
+                              __half *__restrict__ out, int *__restrict__ status) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nb = k / QK;
+    const int64_t wid = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5;
+    if (wid >= m * nb) return;
+    const int64_t token = wid / nb, b = wid % nb;
+    const float v = x[token * ldx + b * QK + lane];
+    if (!isfinite(v) && status) atomicOr(status, 1);
+    float amax = fabsf(v);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 127.0f);
+    float id;
+    if (MODE == 2) id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+    else id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float sv = __fmul_rn(v, id);
+    const int q = MODE == 0 ? int(roundf(sv)) : __float2int_rn(sv);
+    const float dh = __half2float(__float2half_rn(d));
+    out[token * k + b * QK + lane] = __float2half_rn(__fmul_rn(float(q), dh));
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        cuda_check(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q),
+                   "cuTensorMapEncodeTiled lookup");
+        require(p && q == cudaDriverEntryPointSuccess, "cuTensorMapEncodeTiled is unavailable");
+        fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2-D fp16 tensor map over a row-major [rows][k] matrix, box = 64 x box_rows, 128B swizzle
+void make_fp16_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t k, int box_rows) {
+    require(uintptr_t(ptr) % 16 == 0 && (k * 2) % 16 == 0, "GEMM operand must be 16-byte aligned with 16-byte rows");
+    const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(rows)};
+    const cuuint64_t strides[1] = {cuuint64_t(k * 2)};
+    const cuuint32_t box[2] = {cuuint32_t(GEMM_BK), cuuint32_t(box_rows)};
+    const cuuint32_t estride[2] = {1, 1};
+    const CUresult r = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(ptr), dims, strides,
+                                   box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    require(r == CUDA_SUCCESS, "tensor map encoding failed");
+}
+
+void launch_dequant_weights(const uint8_t *blocks, __half *out, int64_t rows, int64_t nb, int q4, cudaStream_t s) {
+    const int64_t n = rows * nb * QK;
+    k_dequant_weights<<<unsigned(ceil_div(n, 256)), 256, 0, s>>>(blocks, out, rows, nb, q4);
+}
+
+void launch_dequant_act(int mode, const float *x, int64_t ldx, int64_t m, int64_t k, __half *out, int *status,
+                        cudaStream_t s) {
+    const int64_t threads = m * (k / QK) * 32;
+    const unsigned grid = unsigned(ceil_div(threads, 256));
+    if (mode == 0) k_dequant_act<0><<<grid, 256, 0, s>>>(x, ldx, m, k, out, status);
+    else if (mode == 2) k_dequant_act<2><<<grid, 256, 0, s>>>(x, ldx, m, k, out, status);
+    else k_dequant_act<1><<<grid, 256, 0, s>>>(x, ldx, m, k, out, status);
+}
+
+void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &a, cudaStream_t s) {
+    static bool configured = false;
+    if (!configured) {
+        cuda_check(cudaFuncSetAttribute(k_gemm_f16, cudaFuncAttributeMaxDynamicSharedMemorySize, int(GEMM_SMEM)),
+                   "GEMM shared-memory attribute");
+        configured = true;
+    }
+    const dim3 grid(unsigned(ceil_div(a.N, GEMM_BN)), unsigned(ceil_div(a.M, GEMM_BM)));
+    k_gemm_f16<<<grid, GEMM_THREADS, GEMM_SMEM, s>>>(ta, tb, a);
+}
+
+}  // namespace mb

@@ -115,6 +115,7 @@ class BlockLinear:
         self.handle = handle
         self.has_bias = bias_t is not None
         self.blocks = blocks  # canonical bytes stay available to callers (and tests)
+        self.gemm_rows = 0
 
     # ggml_mul_mat + epilogue -------------------------------------------------
     def __call__(self, x: torch.Tensor, *, out: torch.Tensor | None = None, residual: torch.Tensor | None = None,
@@ -144,6 +145,13 @@ class BlockLinear:
                                              e, len(e)),
               e, "B200 linear")
         return out
+
+    def prepare_gemm(self, max_queries: int) -> None:
+        """Enable the tcgen05 GEMM for calls of 64..max_queries rows (allocates and synchronises)."""
+        e = error_buffer()
+        check(self.lib.mstar_b200_linear_prepare_gemm(self.handle, self.blocks.data_ptr(), _nbytes(self.blocks),
+                                                      int(max_queries), e, len(e)), e, "B200 GEMM preparation")
+        self.gemm_rows = int(max_queries)
 
     def set_split(self, warps: int) -> None:
         """Force the K split (1, 2, 4, 8) or restore the automatic choice (0); results do not change."""

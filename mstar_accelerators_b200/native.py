@@ -40,6 +40,7 @@ SIGNATURES = {
                                          _vp, *_err]),
     "mstar_b200_linear_close": (_int, [_vp, *_err]),
     "mstar_b200_linear_set_split": (_int, [_vp, _int, *_err]),
+    "mstar_b200_linear_prepare_gemm": (_int, [_vp, _vp, _u64, _i64, *_err]),
     "mstar_b200_q8_readout": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "mstar_b200_embed": (_int, [_vp, _i64, _vp, _i64, _i64, _vp, _vp, _i64, C.c_float, _vp, _vp, _vp, *_err]),
     "mstar_b200_attend": (_int, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64, C.c_int32, C.c_int32, C.c_int32,
