@@ -42,7 +42,20 @@ def decode_step_b32():
     gd.run(2)
 
 
-CASES = {"readout-q4-b32": readout_q4_b32, "decode-step-b32": decode_step_b32}
+def gemm_q8_8192x5120x1280():
+    """Q8_0 prefill GEMM of a Whisper-large fc1 shape (N=5120, K=1280) over 8192 rows, three calls."""
+    from .linear import BlockLinear
+    g = torch.Generator(device="cuda").manual_seed(1)
+    lin = BlockLinear(torch.randn(5120, 1280, device="cuda", generator=g) * 0.02)
+    lin.prepare_gemm(8192)
+    x = torch.randn(8192, 1280, device="cuda", generator=g)
+    out = torch.empty(8192, 5120, device="cuda")
+    for _ in range(3):
+        lin(x, out=out)
+
+
+CASES = {"readout-q4-b32": readout_q4_b32, "decode-step-b32": decode_step_b32,
+         "gemm-q8-8192x5120x1280": gemm_q8_8192x5120x1280}
 
 
 def main(argv):

@@ -30,6 +30,7 @@ struct Linear {
     unsigned long long *keys = nullptr;
     unsigned int *done = nullptr;
     int wpg_override = 0;  // > 0 forces the split-K fold (tests)
+    bool gemv_ok = true;   // the decode GEMV's shared-memory tile fits this width (K <= 4096)
     // tcgen05 GEMM state for calls with more than GEMM_MIN_QUERIES rows
     __half *w16 = nullptr;        // fp16(q * d) weights [rows][width]
     __half *x16 = nullptr;        // fp16 dequantized activations [gemm_rows][width]
@@ -177,7 +178,7 @@ void *mstar_b200_linear_create(int format, const void *blocks, uint64_t bytes, i
         h->nb_pad = h->q4 ? ceil_div(h->nb, 4) * 4 : ceil_div(h->nb, 2) * 2;
         h->groups = ceil_div(rows, 8);
         check_range({blocks, bytes}, uint64_t(rows) * h->nb * (h->q4 ? Q4_BYTES : Q8_BYTES), 1, "linear weights");
-        require(gemv_supported(h->nb_pad), "linear width exceeds the decode kernel's shared-memory tile");
+        h->gemv_ok = gemv_supported(h->nb_pad);
         h->xf = device_alloc<uint32_t>(size_t(h->nb_pad * 2 * 32 * 4), "activation fragments");
         h->xs = device_alloc<float>(size_t(h->nb_pad * 32), "activation scales");
         h->xsum = device_alloc<int>(size_t(h->nb_pad * 32), "activation block sums");
@@ -262,6 +263,7 @@ int mstar_b200_linear_run(void *handle, const float *x, int64_t x_stride, int64_
             cuda_check(cudaGetLastError(), "GEMM launch");
             return 0;
         }
+        require(h.gemv_ok, "width beyond 4096 needs the prepared GEMM and at least 64 queries without LayerNorm");
         for (int64_t m0 = 0; m0 < queries; m0 += CHUNK) {
             const int64_t m = queries - m0 < CHUNK ? queries - m0 : CHUNK;
             GemvArgs a = stage(h, x + m0 * x_stride, x_stride, m, rounding, ln_weight, ln_bias, ln_eps, h.status, s);
@@ -289,6 +291,7 @@ int mstar_b200_linear_block_sums(void *handle, const float *x, int64_t queries, 
         Busy busy(h.busy);
         check_rounding(rounding);
         require(queries >= 1 && queries <= CHUNK, "block sums take 1..32 queries");
+        require(h.gemv_ok, "block sums need a width of at most 4096");
         const uint64_t xb = uint64_t(queries * h.width) * 4;
         check_range({x, xb}, xb, 16, "activations");
         check_range({sums, sums_bytes}, uint64_t(queries) * h.rows * h.nb * 4, 4, "block sums");
@@ -316,6 +319,7 @@ int mstar_b200_linear_readout(void *handle, const float *x, int64_t x_stride, in
         Busy busy(h.busy);
         check_rounding(rounding);
         require(queries >= 1 && queries <= CHUNK, "readout takes 1..32 queries");
+        require(h.gemv_ok, "readout needs a width of at most 4096");
         validate_run(h, x, x_stride, queries, logits, h.rows);
         validate_norm(h, ln_weight, ln_bias, ln_eps);
         const uint64_t lb = uint64_t(queries * h.rows) * 4;

@@ -8,14 +8,16 @@
 // reorder + fp16-rounding tolerance (the decode GEMV keeps the exact integer
 // path).
 //
-// Kernel: one 128 x 256 output tile per CTA, 6 warps:
+// Kernel: persistent (one CTA per SM walking 128 x 256 output tiles), 6 warps:
 //   warp 0  TMA producer: 2-D tiled bulk tensor copies (128B swizzle) of the
 //           A (128 x 64) and B (256 x 64) K-slices into a 4-stage ring;
-//   warp 1  allocates 256 TMEM columns; one thread issues tcgen05.mma
-//           kind::f16 (M=128, N=256, K=16, fp32 accumulate) and commits each
-//           stage back to the producer, and the last one to the epilogue;
+//   warp 1  allocates 512 TMEM columns (two fp32 accumulators of 256 columns);
+//           one thread issues tcgen05.mma kind::f16 (M=128, N=256, K=16) into
+//           the free accumulator, commits each stage back to the producer and
+//           each finished tile to the epilogue;
 //   warps 2-5 epilogue: tcgen05.ld 32x32b.x32 from their TMEM lane quarter,
-//           bias / GELU / residual, fp32 stores.
+//           bias / GELU / residual, fp32 stores, then release the accumulator,
+//           so tile i's epilogue overlaps tile i+1's MMAs.
 // Every mbarrier wait is bounded; a timeout sets status bit value 2 and the
 // CTA skips to the end (TMEM is still released).
 #include <cuda.h>
@@ -31,7 +33,8 @@ constexpr int GEMM_A_BYTES = GEMM_BM * GEMM_BK * 2;
 constexpr int GEMM_B_BYTES = GEMM_BN * GEMM_BK * 2;
 constexpr int GEMM_STAGE_BYTES = GEMM_A_BYTES + GEMM_B_BYTES;
 constexpr int GEMM_THREADS = 192;
-constexpr uint32_t GEMM_TMEM_COLS = 256;
+constexpr int GEMM_GROUP_M = 8;
+constexpr uint32_t GEMM_TMEM_COLS = 512;  // two 256-column fp32 accumulators
 // instruction descriptor: D f32 (bits 4-5 = 1), A/B f16 (0), K-major A and B,
 // N >> 3 at bits 17-22, M >> 4 at bits 24-28
 constexpr uint32_t GEMM_IDESC = (1u << 4) | (uint32_t(GEMM_BN >> 3) << 17) | (uint32_t(GEMM_BM >> 4) << 24);
@@ -88,12 +91,25 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     unsigned char *base = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(gemm_smem) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(base + GEMM_STAGES * GEMM_STAGE_BYTES);
     uint64_t *empty = full + GEMM_STAGES;
-    uint64_t *done = empty + GEMM_STAGES;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    uint64_t *acc_full = empty + GEMM_STAGES;   // [2] MMA -> epilogue
+    uint64_t *acc_empty = acc_full + 2;         // [2] epilogue -> MMA (4 warp arrivals)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
     __shared__ int failed;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t m0 = int64_t(blockIdx.y) * GEMM_BM, n0 = int64_t(blockIdx.x) * GEMM_BN;
     const int kt = int((a.K + GEMM_BK - 1) / GEMM_BK);
+    const int64_t tiles_n = (a.N + GEMM_BN - 1) / GEMM_BN, tiles_m = (a.M + GEMM_BM - 1) / GEMM_BM;
+    const int64_t tiles = tiles_n * tiles_m;
+    // grouped order: groups of GEMM_GROUP_M row tiles, n fastest inside a group,
+    // so the tiles in flight at once touch a few A row panels and all of B,
+    // both of which stay in L2 while the fp32 output streams past
+    auto tile_coords = [&](int64_t tile, int64_t &m0, int64_t &n0) {
+        const int64_t per_group = int64_t(GEMM_GROUP_M) * tiles_n;
+        const int64_t first_m = (tile / per_group) * GEMM_GROUP_M;
+        const int64_t gsz = tiles_m - first_m < GEMM_GROUP_M ? tiles_m - first_m : GEMM_GROUP_M;
+        const int64_t r = tile % per_group;
+        m0 = (first_m + r % gsz) * GEMM_BM;
+        n0 = (r / gsz) * GEMM_BN;
+    };
 
     if (threadIdx.x == 0) {
         failed = 0;
@@ -101,7 +117,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             mbar_init(full + s, 1);
             mbar_init(empty + s, 1);
         }
-        mbar_init(done, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(acc_full + b, 1);
+            mbar_init(acc_empty + b, 4);
+        }
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -117,63 +136,109 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            for (int i = 0; i < kt; ++i) {
-                const int s = i % GEMM_STAGES;
-                if (!mbar_wait_bounded(empty + s, uint32_t(((i / GEMM_STAGES) & 1) ^ 1))) {
-                    atomicOr(&failed, 1);
-                    break;
+            int64_t it = 0;
+            for (int64_t tile = blockIdx.x; tile < tiles && !failed; tile += gridDim.x) {
+                int64_t m0, n0;
+                tile_coords(tile, m0, n0);
+                for (int i = 0; i < kt; ++i, ++it) {
+                    const int s = int(it % GEMM_STAGES);
+                    if (!mbar_wait_bounded(empty + s, uint32_t(((it / GEMM_STAGES) & 1) ^ 1))) {
+                        atomicOr(&failed, 1);
+                        break;
+                    }
+                    unsigned char *sa = base + s * GEMM_STAGE_BYTES;
+                    mbar_expect_tx(full + s, GEMM_STAGE_BYTES);
+                    tma_load_2d(sa, &ta, i * GEMM_BK, int(m0), full + s);
+                    tma_load_2d(sa + GEMM_A_BYTES, &tb, i * GEMM_BK, int(n0), full + s);
                 }
-                unsigned char *sa = base + s * GEMM_STAGE_BYTES;
-                mbar_expect_tx(full + s, GEMM_STAGE_BYTES);
-                tma_load_2d(sa, &ta, i * GEMM_BK, int(m0), full + s);
-                tma_load_2d(sa + GEMM_A_BYTES, &tb, i * GEMM_BK, int(n0), full + s);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            for (int i = 0; i < kt; ++i) {
-                const int s = i % GEMM_STAGES;
-                if (!mbar_wait_bounded(full + s, uint32_t((i / GEMM_STAGES) & 1))) {
+            int64_t it = 0, local = 0;
+            for (int64_t tile = blockIdx.x; tile < tiles && !failed; tile += gridDim.x, ++local) {
+                const int buf = int(local & 1);
+                // wait until the epilogue has drained this accumulator buffer (use local/2 - 1)
+                if (!mbar_wait_bounded(acc_empty + buf, uint32_t(((local >> 1) & 1) ^ 1))) {
                     atomicOr(&failed, 1);
                     break;
                 }
                 tc_fence_after();
-                const uint32_t sa = smem_addr(base + s * GEMM_STAGE_BYTES);
-                const uint64_t da = sw128_desc(sa), db = sw128_desc(sa + GEMM_A_BYTES);
+                const uint32_t acc = tmem + uint32_t(buf * GEMM_BN);
+                for (int i = 0; i < kt; ++i, ++it) {
+                    const int s = int(it % GEMM_STAGES);
+                    if (!mbar_wait_bounded(full + s, uint32_t((it / GEMM_STAGES) & 1))) {
+                        atomicOr(&failed, 1);
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_addr(base + s * GEMM_STAGE_BYTES);
+                    const uint64_t da = sw128_desc(sa), db = sw128_desc(sa + GEMM_A_BYTES);
 #pragma unroll
-                for (int kk = 0; kk < GEMM_BK / 16; ++kk)   // K=16 per MMA: +32 B in the swizzled row
-                    umma_f16(tmem, da + uint64_t(2 * kk), db + uint64_t(2 * kk), GEMM_IDESC, (i | kk) != 0);
-                umma_commit(empty + s);
+                    for (int kk = 0; kk < GEMM_BK / 16; ++kk)   // K=16 per MMA: +32 B in the swizzled row
+                        umma_f16(acc, da + uint64_t(2 * kk), db + uint64_t(2 * kk), GEMM_IDESC, (i | kk) != 0);
+                    umma_commit(empty + s);
+                }
+                umma_commit(acc_full + buf);
             }
-            umma_commit(done);
         }
     } else {
         const int q = warp & 3;  // TMEM lane quarter this warp may read
-        if (!mbar_wait_bounded(done, 0)) {
-            atomicOr(&failed, 1);
-        } else {
+        int64_t local = 0;
+        for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+            const int buf = int(local & 1);
+            if (!mbar_wait_bounded(acc_full + buf, uint32_t((local >> 1) & 1))) {
+                atomicOr(&failed, 1);
+                break;
+            }
             tc_fence_after();
+            int64_t m0, n0;
+            tile_coords(tile, m0, n0);
             const int64_t row = m0 + 32 * q + lane;
             for (int c = 0; c < GEMM_BN / 32; ++c) {
                 uint32_t r[32];
-                tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(c * 32), r);
+                tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(buf * GEMM_BN + c * 32), r);
                 if (row < a.M) {
                     float *orow = a.out + row * a.ldo;
                     const float *rrow = a.residual ? a.residual + row * a.ldo : nullptr;
+                    const int64_t nc = n0 + c * 32;
+                    if (nc + 32 <= a.N && !(a.flags & 10) && (reinterpret_cast<uintptr_t>(orow + nc) & 15) == 0 &&
+                        (!rrow || (reinterpret_cast<uintptr_t>(rrow + nc) & 15) == 0)) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int64_t n = n0 + c * 32 + j;
-                        if (n < a.N) {
-                            float v = __uint_as_float(r[j]);
-                            if (a.flags & 1) v = __fadd_rn(v, a.bias[n]);
-                            if (a.flags & 2) v = gelu_ggml(v);
-                            else if (a.flags & 8) v = gelu_erf(v);
-                            if (a.flags & 4) v = __fadd_rn(rrow[n], v);
-                            orow[n] = v;
+                        for (int j = 0; j < 32; j += 4) {
+                            float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                   __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+                            if (a.flags & 1) {
+                                const float4 bb = *reinterpret_cast<const float4 *>(a.bias + nc + j);
+                                v.x = __fadd_rn(v.x, bb.x); v.y = __fadd_rn(v.y, bb.y);
+                                v.z = __fadd_rn(v.z, bb.z); v.w = __fadd_rn(v.w, bb.w);
+                            }
+                            if (a.flags & 4) {
+                                const float4 rr = *reinterpret_cast<const float4 *>(rrow + nc + j);
+                                v.x = __fadd_rn(rr.x, v.x); v.y = __fadd_rn(rr.y, v.y);
+                                v.z = __fadd_rn(rr.z, v.z); v.w = __fadd_rn(rr.w, v.w);
+                            }
+                            *reinterpret_cast<float4 *>(orow + nc + j) = v;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int64_t n = nc + j;
+                            if (n < a.N) {
+                                float v = __uint_as_float(r[j]);
+                                if (a.flags & 1) v = __fadd_rn(v, a.bias[n]);
+                                if (a.flags & 2) v = gelu_ggml(v);
+                                else if (a.flags & 8) v = gelu_erf(v);
+                                if (a.flags & 4) v = __fadd_rn(rrow[n], v);
+                                orow[n] = v;
+                            }
                         }
                     }
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + buf);
         }
     }
     tc_fence_before();
@@ -272,7 +337,15 @@ void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &a
                    "GEMM shared-memory attribute");
         configured = true;
     }
-    const dim3 grid(unsigned(ceil_div(a.N, GEMM_BN)), unsigned(ceil_div(a.M, GEMM_BM)));
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    const int64_t tiles = ceil_div(a.N, GEMM_BN) * ceil_div(a.M, GEMM_BM);
+    const unsigned grid = unsigned(tiles < sms ? tiles : sms);  // persistent: one CTA per SM
     k_gemm_f16<<<grid, GEMM_THREADS, GEMM_SMEM, s>>>(ta, tb, a);
 }
 
