@@ -41,7 +41,7 @@ enum mstar_b200_q8_rounding {
     MSTAR_B200_Q8_ARM = 1, /* ggml-cpu/arch/arm/quants.c:41-75: id = 1/d, half-even (default) */
     MSTAR_B200_Q8_X86 = 2, /* ggml-cpu/arch/x86/quants.c:302-350: id = 127/amax, half-even */
 };
-enum mstar_b200_format { MSTAR_B200_Q8_0 = 8, MSTAR_B200_Q4_0 = 4 };
+enum mstar_b200_format { MSTAR_B200_Q8_0 = 8, MSTAR_B200_Q4_0 = 4, MSTAR_B200_BF16 = 16 };
 /* Epilogue flags of mstar_b200_linear_run; applied in this order after the
  * block-quantized dot, each as the reference's separate fp32 ggml op. */
 enum mstar_b200_epilogue {
@@ -130,6 +130,33 @@ MSTAR_B200_API int mstar_b200_linear_set_split(void *handle, int warps, char *er
  * x[k] (one row), all rows' dots, suppression, argmax. errno-style result. */
 MSTAR_B200_API int mstar_b200_q8_readout(void *handle, const float *x, float *out, int64_t *token,
     int32_t *status, const int64_t *suppressed, size_t suppressed_count, void *stream);
+
+/* --- Qwen3-Omni thinker MoE expert FFN ----------------------------------------------
+ * Router (ConsistentBF16Router.forward, qwen3_omni/amd/router_consistency.py:54-62):
+ * x bf16 [tokens][hidden], router_weight bf16 [experts][hidden] -> logits rounded
+ * to bf16, softmax in fp32, top_k (ties: lower expert index), optional
+ * renormalisation (norm_topk_prob) -> topk_weights fp32 / topk_ids int32
+ * [tokens][top_k]. 1..256 experts. */
+MSTAR_B200_API int mstar_b200_moe_route(const void *x, int64_t tokens, int64_t hidden,
+    const void *router_weight, int32_t experts, int32_t top_k, int32_t renormalize,
+    float *topk_weights, int32_t *topk_ids, void *stream, char *error, size_t error_size);
+/* Expert weights of one MoE layer (the experts_backend of SmallTokenThinkerMoE,
+ * thinker_moe.py:104-188; layout preparation.py:13-36): w1 [E][2I][H] (gate rows
+ * then up rows), w2 [E][H][I], as bf16 (format BF16) or canonical Q8_0 blocks
+ * along the last dimension (format Q8_0, no counterpart in the reference).
+ * Borrowed during create only. max_tokens bounds a run's token count. */
+MSTAR_B200_API void *mstar_b200_moe_create(int32_t format, const void *w1, uint64_t w1_bytes,
+    const void *w2, uint64_t w2_bytes, int32_t experts, int32_t intermediate, int32_t hidden,
+    int32_t top_k, int32_t max_tokens, char *error, size_t error_size);
+/* out bf16 [tokens][hidden] = sum over slots of bf16(down(bf16 SwiGLU(gate, up)) * w):
+ * the bf16 rounding points of gate_up_vector / down_vector_reduce
+ * (thinker_moe.py:17-83) and the slot-ordered fp32 sum (:75-81). Q8_0 format:
+ * x and mid are Q8_0-quantized (rounding) before each contraction. Status bit
+ * value 4: an expert id outside [0, E); value 2: a bounded wait timed out. */
+MSTAR_B200_API int mstar_b200_moe_run(void *handle, const void *x, int64_t tokens,
+    const float *topk_weights, const int32_t *topk_ids, void *out, int32_t *status, int32_t rounding,
+    void *stream, char *error, size_t error_size);
+MSTAR_B200_API int mstar_b200_moe_close(void *handle, char *error, size_t error_size);
 
 /* --- readout that allocates nothing ------------------------------------------------
  * No counterpart in the reference. For callers that cannot allocate device

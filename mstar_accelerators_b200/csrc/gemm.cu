@@ -25,6 +25,7 @@
 
 #include "../../include/mstar_b200.h"
 #include "gemm.cuh"
+#include "tcgen05.cuh"
 
 namespace mb {
 
@@ -39,51 +40,6 @@ constexpr uint32_t GEMM_TMEM_COLS = 512;  // two 256-column fp32 accumulators
 // N >> 3 at bits 17-22, M >> 4 at bits 24-28
 constexpr uint32_t GEMM_IDESC = (1u << 4) | (uint32_t(GEMM_BN >> 3) << 17) | (uint32_t(GEMM_BM >> 4) << 24);
 constexpr size_t GEMM_SMEM = size_t(GEMM_STAGES) * GEMM_STAGE_BYTES + 1024 + 256;
-
-// UMMA shared-memory descriptor of a K-major, 128B-swizzled tile whose rows
-// are 128 bytes (64 fp16) and whose 8-row groups are 1024 bytes apart.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    uint64_t d = uint64_t((saddr >> 4) & 0x3FFF);
-    d |= uint64_t(1) << 16;             // leading byte offset (16 B; unused for swizzled K-major)
-    d |= uint64_t(1024 >> 4) << 32;     // stride byte offset: 8 rows x 128 B
-    d |= uint64_t(1) << 46;             // descriptor version for tcgen05
-    d |= uint64_t(2) << 61;             // SWIZZLE_128B
-    return d;
-}
-
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }"
-        ::"r"(tmem), "l"(da), "l"(db), "r"(idesc), "r"(acc)
-        : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
-        "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
 
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_f16(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const GemmArgs a) {

@@ -1,0 +1,711 @@
+// Qwen3-Omni thinker MoE expert FFN on B200.
+//
+// Reference semantics (rohanchanani/mstar_accelerators):
+//  router  ConsistentBF16Router.forward (implementations/qwen3_omni/amd/
+//          router_consistency.py:54-62): logits = bf16(x . Wr^T) (fp32
+//          accumulation), p = softmax_fp32(logits), top-k, w /= sum(w).
+//  experts SmallTokenThinkerMoE (thinker_moe.py:17-105): per (token, slot)
+//          g = bf16(x . w_gate), u = bf16(x . w_up), act = bf16(g * sigmoid(g)),
+//          mid = bf16(act * u); y_s = bf16((mid . w_down) * w_s);
+//          out = bf16(sum over slots s = 0..k-1 of fp32(y_s)), in slot order.
+//  layout  w1 [E][2I][H] (gate rows [0, I), up rows [I, 2I)), w2 [E][H][I]
+//          (preparation.py:13-36; thinker_moe.py:57-66).
+// Q8_0 variant (no counterpart in the reference, composed from its pieces):
+// expert weights are Q8_0 blocks; x and mid are Q8_0-quantized per 32-block
+// (quantize_row_q8_0, selected rounding) before each contraction; the bf16
+// rounding points above are kept.
+//
+// B200 pipeline for T tokens (all on one stream, no host synchronisation):
+//  k_router      CTA per 16 tokens: logits, softmax, top-k, renorm
+//  k_moe_count / k_moe_plan / k_moe_scatter
+//                counting sort of the T*k (token, slot) pairs by expert and a
+//                device-side work list of 128-row tiles per expert
+//  k_moe_gather  permuted activation rows (bf16 copy, or Q8_0 quantize ->
+//                fp16 dequant for the Q8_0 variant)
+//  k_moe_gemm<SWIGLU>  grouped tcgen05 GEMM x_perm . w1^T with gate/up rows
+//                interleaved per 256-row tile, so one epilogue thread holds a
+//                row's gate and up values and writes mid (bf16, or Q8_0
+//                quantized -> fp16 for the Q8_0 variant)
+//  k_moe_gemm<DOWN>    grouped GEMM mid . w2^T, epilogue y = bf16(acc * w_slot)
+//  k_moe_combine out[t] = bf16(sum_s fp32(y[pair(t, s)])) in slot order
+// Operands of one MMA always share their type (both bf16 or both fp16).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include <atomic>
+#include <memory>
+
+#include "../../include/mstar_b200.h"
+#include "gemm.cuh"
+#include "tcgen05.cuh"
+
+namespace mb {
+
+constexpr int MOE_BM = 128, MOE_BN = 256, MOE_BK = 64, MOE_STAGES = 4, MOE_THREADS = 192;
+constexpr int MOE_A_BYTES = MOE_BM * MOE_BK * 2, MOE_B_BYTES = MOE_BN * MOE_BK * 2;
+constexpr int MOE_STAGE_BYTES = MOE_A_BYTES + MOE_B_BYTES;
+constexpr size_t MOE_SMEM = size_t(MOE_STAGES) * MOE_STAGE_BYTES + 1024 + 256;
+constexpr int MOE_MAX_TOPK = 8;
+constexpr int ROUTER_TOKENS = 16;
+constexpr int ROUTER_CHUNK = 256;
+
+__device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// ------------------------------------------------------------------ router
+// CTA of E threads (one per expert) over ROUTER_TOKENS tokens.
+__global__ void k_router(const __nv_bfloat16 *__restrict__ x, const __nv_bfloat16 *__restrict__ wr, int T, int H,
+                         int E, int topk, int renorm, float *__restrict__ topk_w, int32_t *__restrict__ topk_ids) {
+    __shared__ float xs[ROUTER_TOKENS][ROUTER_CHUNK];
+    __shared__ float logits[ROUTER_TOKENS][256];
+    const int e = threadIdx.x;
+    const int t0 = blockIdx.x * ROUTER_TOKENS;
+    const int nt = T - t0 < ROUTER_TOKENS ? T - t0 : ROUTER_TOKENS;
+    float acc[ROUTER_TOKENS];
+#pragma unroll
+    for (int i = 0; i < ROUTER_TOKENS; ++i) acc[i] = 0.0f;
+    for (int k0 = 0; k0 < H; k0 += ROUTER_CHUNK) {
+        const int kc = H - k0 < ROUTER_CHUNK ? H - k0 : ROUTER_CHUNK;
+        __syncthreads();
+        for (int i = threadIdx.x; i < ROUTER_TOKENS * kc; i += blockDim.x) {
+            const int tt = i / kc, kk = i % kc;
+            xs[tt][kk] = tt < nt ? __bfloat162float(x[int64_t(t0 + tt) * H + k0 + kk]) : 0.0f;
+        }
+        __syncthreads();
+        if (e < E) {
+            const __nv_bfloat16 *w = wr + int64_t(e) * H + k0;
+            for (int kk = 0; kk < kc; ++kk) {
+                const float wv = __bfloat162float(w[kk]);
+#pragma unroll
+                for (int i = 0; i < ROUTER_TOKENS; ++i) acc[i] = fmaf(xs[i][kk], wv, acc[i]);
+            }
+        }
+    }
+    if (e < E) {
+#pragma unroll
+        for (int i = 0; i < ROUTER_TOKENS; ++i) logits[i][e] = bf16r(acc[i]);  // F.linear output dtype
+    }
+    __syncthreads();
+    // one warp per token: softmax (fp32) and top-k by repeated argmax (lower index wins ties)
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    for (int tt = warp; tt < nt; tt += nwarps) {
+        float mx = -INFINITY;
+        for (int j = lane; j < E; j += 32) mx = fmaxf(mx, logits[tt][j]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float sum = 0.0f;
+        for (int j = lane; j < E; j += 32) sum += expf(logits[tt][j] - mx);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        __syncwarp();
+        for (int j = lane; j < E; j += 32) logits[tt][j] = expf(logits[tt][j] - mx) / sum;
+        __syncwarp();
+        float chosen[MOE_MAX_TOPK];
+        int ids[MOE_MAX_TOPK];
+        float total = 0.0f;
+        for (int r = 0; r < topk; ++r) {
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
+            for (int j = lane; j < E; j += 32) {
+                const float v = logits[tt][j];
+                if (v > bv || (v == bv && j < bi)) { bv = v; bi = j; }
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+            }
+            chosen[r] = bv;
+            ids[r] = bi;
+            total += bv;
+            __syncwarp();
+            if (lane == 0) logits[tt][bi] = -INFINITY;
+            __syncwarp();
+        }
+        if (lane < topk) {
+            float w = chosen[0];
+            int id = ids[0];
+            for (int r = 1; r < topk; ++r)
+                if (lane == r) { w = chosen[r]; id = ids[r]; }
+            topk_w[int64_t(t0 + tt) * topk + lane] = renorm ? w / total : w;
+            topk_ids[int64_t(t0 + tt) * topk + lane] = id;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ permutation
+struct MoePlan {
+    int *counts;      // [E]
+    int *offsets;     // [E]
+    int *cursor;      // [E]
+    int *tiles;       // [max_tiles][3]: expert, row_start, row_end (permuted rows)
+    int *num_tiles;   // [1]
+    int *perm;        // [P] permuted position -> pair (token * k + slot)
+    int *inv;         // [P] pair -> permuted position
+};
+
+__global__ void k_moe_count(const int32_t *__restrict__ ids, int P, int E, int *__restrict__ counts,
+                            int *__restrict__ status) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= P) return;
+    const int e = ids[i];
+    if (e < 0 || e >= E) {
+        atomicOr(status, 4);
+        return;
+    }
+    atomicAdd(counts + e, 1);
+}
+
+// single CTA: exclusive scan of counts, per-expert cursors, 128-row tile list
+__global__ void k_moe_plan(MoePlan p, int E, int max_tiles) {
+    __shared__ int cnt[1024], mt[1024];
+    const int tid = threadIdx.x;
+    for (int e = tid; e < E; e += blockDim.x) {
+        cnt[e] = p.counts[e];
+        mt[e] = (cnt[e] + MOE_BM - 1) / MOE_BM;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int off = 0, tiles = 0;
+        for (int e = 0; e < E; ++e) {
+            p.offsets[e] = off;
+            p.cursor[e] = 0;
+            for (int j = 0; j < mt[e] && tiles < max_tiles; ++j, ++tiles) {
+                p.tiles[3 * tiles] = e;
+                p.tiles[3 * tiles + 1] = off + j * MOE_BM;
+                const int end = off + (j + 1) * MOE_BM;
+                p.tiles[3 * tiles + 2] = end < off + cnt[e] ? end : off + cnt[e];
+            }
+            off += cnt[e];
+        }
+        *p.num_tiles = tiles;
+    }
+}
+
+__global__ void k_moe_scatter(const int32_t *__restrict__ ids, int P, int E, MoePlan p) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= P) return;
+    const int e = ids[i];
+    if (e < 0 || e >= E) return;
+    const int pos = p.offsets[e] + atomicAdd(p.cursor + e, 1);
+    p.perm[pos] = i;
+    p.inv[i] = pos;
+}
+
+// permuted activation rows: row pos <- x[perm[pos] / k]
+// q8: quantize each 32-block (selected rounding) of fp32(x) and store fp16(q * d)
+__global__ void k_moe_gather(const __nv_bfloat16 *__restrict__ x, const int *__restrict__ perm, int P, int H, int topk,
+                             int q8, int rounding, void *__restrict__ xp) {
+    const int pos = blockIdx.x;
+    if (pos >= P) return;
+    const int64_t t = perm[pos] / topk;
+    const __nv_bfloat16 *src = x + t * H;
+    if (!q8) {
+        __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(xp) + int64_t(pos) * H;
+        for (int i = threadIdx.x; i < H; i += blockDim.x) dst[i] = src[i];
+        return;
+    }
+    __half *dst = static_cast<__half *>(xp) + int64_t(pos) * H;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    for (int b = warp; b < H / QK; b += nwarps) {
+        const float v = __bfloat162float(src[b * QK + lane]);
+        float amax = fabsf(v);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float d = __fdiv_rn(amax, 127.0f);
+        float id;
+        if (rounding == 2) id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        else id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        const float sv = __fmul_rn(v, id);
+        const int q = rounding == 0 ? int(roundf(sv)) : __float2int_rn(sv);
+        dst[b * QK + lane] = __float2half_rn(__fmul_rn(float(q), __half2float(__float2half_rn(d))));
+    }
+}
+
+// out[t][n] = bf16(sum_s fp32(y[inv[t*k + s]][n])) in slot order
+__global__ void k_moe_combine(const __nv_bfloat16 *__restrict__ y, const int *__restrict__ inv, int T, int H, int topk,
+                              __nv_bfloat16 *__restrict__ out) {
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    int rows[MOE_MAX_TOPK];
+    for (int s = 0; s < topk; ++s) rows[s] = inv[t * topk + s];
+    for (int n = threadIdx.x; n < H; n += blockDim.x) {
+        float acc = 0.0f;
+        for (int s = 0; s < topk; ++s) acc = __fadd_rn(acc, __bfloat162float(y[int64_t(rows[s]) * H + n]));
+        out[int64_t(t) * H + n] = __float2bfloat16_rn(acc);
+    }
+}
+
+// ------------------------------------------------------------------ grouped GEMM
+struct MoeGemmArgs {
+    const int *tiles;      // [num_tiles][3]
+    const int *num_tiles;
+    int n_tiles;           // 256-wide output tiles per expert (w rows / 256)
+    int w_rows;            // rows of one expert's weight matrix (2I or H)
+    int K;
+    // SWIGLU epilogue: mid [P][I] bf16 (or fp16 Q8_0-dequantized when q8)
+    void *mid;
+    int I;
+    int q8, rounding;
+    // DOWN epilogue: y [P][H] bf16 = bf16(acc * topk_w[perm[row]])
+    __nv_bfloat16 *y;
+    const float *topk_w;
+    const int *perm;
+    int *status;
+};
+
+constexpr int MOE_SWIGLU = 0, MOE_DOWN = 1;
+
+__device__ __forceinline__ float silu_bf16(float g) {
+    // act = bf16(g * sigmoid(g)) on the bf16-rounded g (thinker_moe.py:44-47)
+    return bf16r(g * (1.0f / (1.0f + expf(-g))));
+}
+
+template <int MODE, bool BF16>
+__global__ void __launch_bounds__(MOE_THREADS, 1)
+    k_moe_gemm(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const MoeGemmArgs a) {
+    // instruction descriptor: D f32, A/B bf16 (1) or f16 (0), K-major, N=256, M=128
+    constexpr uint32_t IDESC = (1u << 4) | ((BF16 ? 1u : 0u) << 7) | ((BF16 ? 1u : 0u) << 10) |
+                               (uint32_t(MOE_BN >> 3) << 17) | (uint32_t(MOE_BM >> 4) << 24);
+    extern __shared__ __align__(1024) unsigned char moe_smem[];
+    unsigned char *base = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(moe_smem) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(base + MOE_STAGES * MOE_STAGE_BYTES);
+    uint64_t *empty = full + MOE_STAGES;
+    uint64_t *acc_full = empty + MOE_STAGES;
+    uint64_t *acc_empty = acc_full + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    __shared__ int failed;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kt = (a.K + MOE_BK - 1) / MOE_BK;
+    const int64_t tiles = int64_t(*a.num_tiles) * a.n_tiles;  // written by k_moe_plan earlier on the stream
+
+    if (threadIdx.x == 0) {
+        failed = 0;
+        for (int s = 0; s < MOE_STAGES; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(acc_full + b, 1);
+            mbar_init(acc_empty + b, 4);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(512u)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    // tile = m-tile (list entry) * n_tiles + n-tile: n fastest, so CTAs working at the
+    // same time share the A rows of an expert and stream that expert's weight tiles
+    auto coords = [&](int64_t tile, int &e, int &r0, int &r1, int &nt) {
+        const int mt = int(tile / a.n_tiles);
+        nt = int(tile % a.n_tiles);
+        e = a.tiles[3 * mt];
+        r0 = a.tiles[3 * mt + 1];
+        r1 = a.tiles[3 * mt + 2];
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int64_t it = 0;
+            for (int64_t tile = blockIdx.x; tile < tiles && !failed; tile += gridDim.x) {
+                int e, r0, r1, nt;
+                coords(tile, e, r0, r1, nt);
+                for (int i = 0; i < kt; ++i, ++it) {
+                    const int s = int(it % MOE_STAGES);
+                    if (!mbar_wait_bounded(empty + s, uint32_t(((it / MOE_STAGES) & 1) ^ 1))) {
+                        atomicOr(&failed, 1);
+                        break;
+                    }
+                    unsigned char *sa = base + s * MOE_STAGE_BYTES;
+                    mbar_expect_tx(full + s, MOE_STAGE_BYTES);
+                    tma_load_2d(sa, &ta, i * MOE_BK, r0, full + s);
+                    tma_load_2d(sa + MOE_A_BYTES, &tb, i * MOE_BK, e * a.w_rows + nt * MOE_BN, full + s);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int64_t it = 0, local = 0;
+            for (int64_t tile = blockIdx.x; tile < tiles && !failed; tile += gridDim.x, ++local) {
+                const int buf = int(local & 1);
+                if (!mbar_wait_bounded(acc_empty + buf, uint32_t(((local >> 1) & 1) ^ 1))) {
+                    atomicOr(&failed, 1);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t acc = tmem + uint32_t(buf * MOE_BN);
+                for (int i = 0; i < kt; ++i, ++it) {
+                    const int s = int(it % MOE_STAGES);
+                    if (!mbar_wait_bounded(full + s, uint32_t((it / MOE_STAGES) & 1))) {
+                        atomicOr(&failed, 1);
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_addr(base + s * MOE_STAGE_BYTES);
+                    const uint64_t da = sw128_desc(sa), db = sw128_desc(sa + MOE_A_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < MOE_BK / 16; ++kk)
+                        umma_f16(acc, da + uint64_t(2 * kk), db + uint64_t(2 * kk), IDESC, (i | kk) != 0);
+                    umma_commit(empty + s);
+                }
+                umma_commit(acc_full + buf);
+            }
+        }
+    } else {
+        const int q = warp & 3;
+        int64_t local = 0;
+        for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+            const int buf = int(local & 1);
+            if (!mbar_wait_bounded(acc_full + buf, uint32_t((local >> 1) & 1))) {
+                atomicOr(&failed, 1);
+                break;
+            }
+            tc_fence_after();
+            int e, r0, r1, nt;
+            coords(tile, e, r0, r1, nt);
+            const int row = r0 + 32 * q + lane;
+            const uint32_t tb0 = tmem + (uint32_t(32 * q) << 16) + uint32_t(buf * MOE_BN);
+            if (MODE == MOE_SWIGLU) {
+                // columns [0,128) gate, [128,256) up of output columns nt*128 + [0,128)
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t g[32], u[32];
+                    tmem_ld32(tb0 + uint32_t(c * 32), g);
+                    tmem_ld32(tb0 + uint32_t(128 + c * 32), u);
+                    if (row < r1) {
+                        float mid[32];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const float gv = bf16r(__uint_as_float(g[j]));
+                            const float uv = bf16r(__uint_as_float(u[j]));
+                            mid[j] = bf16r(silu_bf16(gv) * uv);
+                        }
+                        const int64_t col = int64_t(nt) * 128 + c * 32;
+                        if (!a.q8) {
+                            __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(a.mid) + int64_t(row) * a.I + col;
+#pragma unroll
+                            for (int j = 0; j < 32; j += 2)
+                                *reinterpret_cast<__nv_bfloat162 *>(dst + j) = __floats2bfloat162_rn(mid[j], mid[j + 1]);
+                        } else {
+                            // this thread's 32 values are one Q8_0 block of the row
+                            float amax = 0.0f;
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(mid[j]));
+                            const float d = __fdiv_rn(amax, 127.0f);
+                            float id;
+                            if (a.rounding == 2) id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+                            else id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+                            const float dh = __half2float(__float2half_rn(d));
+                            __half *dst = static_cast<__half *>(a.mid) + int64_t(row) * a.I + col;
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) {
+                                const float sv = __fmul_rn(mid[j], id);
+                                const int qv = a.rounding == 0 ? int(roundf(sv)) : __float2int_rn(sv);
+                                dst[j] = __float2half_rn(__fmul_rn(float(qv), dh));
+                            }
+                        }
+                    }
+                }
+            } else {
+                const float w = row < r1 ? a.topk_w[a.perm[row]] : 0.0f;
+                for (int c = 0; c < MOE_BN / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld32(tb0 + uint32_t(c * 32), r);
+                    if (row < r1) {
+                        __nv_bfloat16 *dst = a.y + int64_t(row) * (int64_t(a.n_tiles) * MOE_BN) +
+                                             int64_t(nt) * MOE_BN + c * 32;
+#pragma unroll
+                        for (int j = 0; j < 32; j += 2)
+                            *reinterpret_cast<__nv_bfloat162 *>(dst + j) =
+                                __floats2bfloat162_rn(__uint_as_float(r[j]) * w, __uint_as_float(r[j + 1]) * w);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + buf);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x == 0 && failed && a.status) atomicOr(a.status, 2);
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u) : "memory");
+    }
+}
+
+// ------------------------------------------------------------------ weight preparation
+// w1 rows interleaved per 256-row tile: tile j = gate rows [128j, 128j+128)
+// then up rows [I + 128j, ...); values fp16(q*d) (Q8_0) or the bf16 input.
+__global__ void k_moe_prep_w1(const void *__restrict__ src, int q8, int E, int I, int H, void *__restrict__ dst) {
+    const int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;  // element of dst [E][2I][H]
+    if (i >= int64_t(E) * 2 * I * H) return;
+    const int64_t k = i % H, r = (i / H) % (2 * I), e = i / (int64_t(H) * 2 * I);
+    const int64_t tile = r / 256, within = r % 256;
+    const int64_t srow = within < 128 ? tile * 128 + within : I + tile * 128 + (within - 128);
+    const int64_t s_elem = (e * 2 * I + srow) * H + k;
+    if (!q8) {
+        static_cast<__nv_bfloat16 *>(dst)[i] = static_cast<const __nv_bfloat16 *>(src)[s_elem];
+        return;
+    }
+    const uint8_t *blk = static_cast<const uint8_t *>(src) + ((e * 2 * I + srow) * (H / QK) + k / QK) * Q8_BYTES;
+    const float d = __half2float(__ushort_as_half(uint16_t(blk[0]) | uint16_t(uint16_t(blk[1]) << 8)));
+    static_cast<__half *>(dst)[i] = __float2half_rn(__fmul_rn(float(int8_t(blk[2 + k % QK])), d));
+}
+
+__global__ void k_moe_prep_w2(const void *__restrict__ src, int q8, int64_t count, int K, void *__restrict__ dst) {
+    const int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;  // element of [E*H][I]
+    if (i >= count) return;
+    if (!q8) {
+        static_cast<__nv_bfloat16 *>(dst)[i] = static_cast<const __nv_bfloat16 *>(src)[i];
+        return;
+    }
+    const int64_t row = i / K, k = i % K;
+    const uint8_t *blk = static_cast<const uint8_t *>(src) + (row * (K / QK) + k / QK) * Q8_BYTES;
+    const float d = __half2float(__ushort_as_half(uint16_t(blk[0]) | uint16_t(uint16_t(blk[1]) << 8)));
+    static_cast<__half *>(dst)[i] = __float2half_rn(__fmul_rn(float(int8_t(blk[2 + k % QK])), d));
+}
+
+// 2-D 16-bit tensor map (bf16 or fp16) over [rows][k], box 64 x box_rows, 128B swizzle
+static PFN_cuTensorMapEncodeTiled_v12000 moe_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        cuda_check(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q), "tensor map lookup");
+        require(p && q == cudaDriverEntryPointSuccess, "cuTensorMapEncodeTiled is unavailable");
+        fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+static void make_map16(CUtensorMap *map, const void *ptr, int64_t rows, int64_t k, int box_rows, bool bf16) {
+    require(uintptr_t(ptr) % 16 == 0 && (k * 2) % 16 == 0, "MoE operand must be 16-byte aligned");
+    const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(rows)};
+    const cuuint64_t strides[1] = {cuuint64_t(k * 2)};
+    const cuuint32_t box[2] = {cuuint32_t(MOE_BK), cuuint32_t(box_rows)};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = moe_encode()(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                                    const_cast<void *>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    require(r == CUDA_SUCCESS, "MoE tensor map encoding failed");
+}
+
+struct Moe {
+    int q8 = 0, E = 0, I = 0, H = 0, topk = 0, max_tokens = 0, max_tiles = 0;
+    void *w1 = nullptr, *w2 = nullptr;   // prepared 16-bit weights
+    void *xp = nullptr, *mid = nullptr;  // permuted activations / intermediate
+    __nv_bfloat16 *y = nullptr;          // per-pair down outputs
+    int *ibuf = nullptr;                 // counts, offsets, cursor, tiles, num_tiles, perm, inv
+    int *status = nullptr;
+    MoePlan plan{};
+    CUtensorMap map_w1{}, map_w2{}, map_x{}, map_mid{};
+    std::atomic_flag busy = ATOMIC_FLAG_INIT;
+    ~Moe() {
+        for (void *p : {w1, w2, xp, mid, (void *)y, (void *)ibuf, (void *)status})
+            if (p) cudaFree(p);
+    }
+};
+
+static int moe_sms() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+template <int MODE, bool BF16>
+static void launch_moe_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const MoeGemmArgs &a, int max_tiles,
+                            cudaStream_t s) {
+    auto kernel = k_moe_gemm<MODE, BF16>;
+    static bool configured = false;
+    if (!configured) {
+        cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(MOE_SMEM)),
+                   "MoE GEMM shared memory");
+        configured = true;
+    }
+    const int64_t upper = int64_t(max_tiles) * a.n_tiles;
+    const unsigned grid = unsigned(upper < moe_sms() ? upper : moe_sms());
+    kernel<<<grid, MOE_THREADS, MOE_SMEM, s>>>(ta, tb, a);
+}
+
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" {
+
+int mstar_b200_moe_route(const void *x, int64_t tokens, int64_t hidden, const void *router_weight, int32_t experts,
+                         int32_t top_k, int32_t renormalize, float *topk_weights, int32_t *topk_ids, void *stream,
+                         char *error, size_t error_size) {
+    try {
+        require(x && router_weight && topk_weights && topk_ids, "missing router operand");
+        require(tokens >= 1 && hidden >= 1 && experts >= 1 && experts <= 256, "router geometry: 1..256 experts");
+        require(top_k >= 1 && top_k <= MOE_MAX_TOPK && top_k <= experts, "top_k outside 1..8");
+        check_device(x, "router input");
+        check_device(router_weight, "router weight");
+        check_device(topk_weights, "top-k weights");
+        check_device(topk_ids, "top-k ids");
+        const unsigned grid = unsigned(ceil_div(tokens, ROUTER_TOKENS));
+        k_router<<<grid, unsigned((experts + 31) / 32 * 32), 0, as_stream(stream)>>>(
+            static_cast<const __nv_bfloat16 *>(x), static_cast<const __nv_bfloat16 *>(router_weight), int(tokens),
+            int(hidden), experts, top_k, renormalize, topk_weights, topk_ids);
+        cuda_check(cudaGetLastError(), "router launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+void *mstar_b200_moe_create(int32_t format, const void *w1, uint64_t w1_bytes, const void *w2, uint64_t w2_bytes,
+                            int32_t experts, int32_t intermediate, int32_t hidden, int32_t top_k, int32_t max_tokens,
+                            char *error, size_t error_size) {
+    std::unique_ptr<Moe> m;
+    try {
+        require(mstar_b200_capability() == 1, "sm_100a device capability is unavailable");
+        require(format == MSTAR_B200_Q8_0 || format == MSTAR_B200_BF16, "MoE weights are Q8_0 or BF16");
+        require(experts >= 1 && experts <= 1024 && intermediate % 128 == 0 && intermediate > 0 && hidden % 256 == 0 &&
+                    hidden > 0 && top_k >= 1 && top_k <= MOE_MAX_TOPK && max_tokens >= 1,
+                "MoE geometry: I multiple of 128, H multiple of 256, 1 <= top_k <= 8");
+        m.reset(new Moe);
+        m->q8 = format == MSTAR_B200_Q8_0;
+        m->E = experts;
+        m->I = intermediate;
+        m->H = hidden;
+        m->topk = top_k;
+        m->max_tokens = max_tokens;
+        const int64_t E = experts, I = intermediate, H = hidden, P = int64_t(max_tokens) * top_k;
+        const uint64_t w1_expect = m->q8 ? uint64_t(E * 2 * I * (H / QK) * Q8_BYTES) : uint64_t(E * 2 * I * H * 2);
+        const uint64_t w2_expect = m->q8 ? uint64_t(E * H * (I / QK) * Q8_BYTES) : uint64_t(E * H * I * 2);
+        check_range({w1, w1_bytes}, w1_expect, 2, "expert w1");
+        check_range({w2, w2_bytes}, w2_expect, 2, "expert w2");
+        check_device(w1, "expert w1");
+        check_device(w2, "expert w2");
+        m->max_tiles = int(P / MOE_BM + E + 1);
+        cuda_check(cudaMalloc(&m->w1, size_t(E * 2 * I * H * 2)), "w1 allocation");
+        cuda_check(cudaMalloc(&m->w2, size_t(E * H * I * 2)), "w2 allocation");
+        cuda_check(cudaMalloc(&m->xp, size_t((P + MOE_BM) * H * 2)), "permuted activations");
+        cuda_check(cudaMalloc(&m->mid, size_t((P + MOE_BM) * I * 2)), "intermediate");
+        cuda_check(cudaMalloc(reinterpret_cast<void **>(&m->y), size_t(P * H * 2)), "expert outputs");
+        const int64_t ints = 3 * E + 3 * int64_t(m->max_tiles) + 1 + 2 * P;
+        cuda_check(cudaMalloc(reinterpret_cast<void **>(&m->ibuf), size_t(ints * 4)), "plan buffers");
+        cuda_check(cudaMalloc(reinterpret_cast<void **>(&m->status), 4), "status");
+        cuda_check(cudaMemset(m->status, 0, 4), "status reset");
+        cuda_check(cudaMemset(m->xp, 0, size_t((P + MOE_BM) * H * 2)), "activation reset");
+        cuda_check(cudaMemset(m->mid, 0, size_t((P + MOE_BM) * I * 2)), "intermediate reset");
+        int *p = m->ibuf;
+        m->plan.counts = p;
+        m->plan.offsets = p + E;
+        m->plan.cursor = p + 2 * E;
+        m->plan.tiles = p + 3 * E;
+        m->plan.num_tiles = p + 3 * E + 3 * m->max_tiles;
+        m->plan.perm = m->plan.num_tiles + 1;
+        m->plan.inv = m->plan.perm + P;
+        const int64_t n1 = E * 2 * I * H, n2 = E * H * I;
+        k_moe_prep_w1<<<unsigned(ceil_div(n1, 256)), 256>>>(w1, m->q8, int(E), int(I), int(H), m->w1);
+        k_moe_prep_w2<<<unsigned(ceil_div(n2, 256)), 256>>>(w2, m->q8, n2, int(I), m->w2);
+        cuda_check(cudaGetLastError(), "weight preparation");
+        cuda_check(cudaDeviceSynchronize(), "weight preparation");
+        const bool bf16 = !m->q8;
+        make_map16(&m->map_w1, m->w1, E * 2 * I, H, MOE_BN, bf16);
+        make_map16(&m->map_w2, m->w2, E * H, I, MOE_BN, bf16);
+        make_map16(&m->map_x, m->xp, P + MOE_BM, H, MOE_BM, bf16);
+        make_map16(&m->map_mid, m->mid, P + MOE_BM, I, MOE_BM, bf16);
+        return m.release();
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return nullptr;
+    }
+}
+
+int mstar_b200_moe_run(void *handle, const void *x, int64_t tokens, const float *topk_weights,
+                       const int32_t *topk_ids, void *out, int32_t *status, int32_t rounding, void *stream,
+                       char *error, size_t error_size) {
+    try {
+        require(handle, "missing MoE handle");
+        auto &m = *static_cast<Moe *>(handle);
+        require(!m.busy.test_and_set(std::memory_order_acquire), "MoE handle is busy");
+        struct Release {
+            std::atomic_flag &f;
+            ~Release() { f.clear(std::memory_order_release); }
+        } release{m.busy};
+        require(tokens >= 1 && tokens <= m.max_tokens, "token count outside the prepared capacity");
+        require(rounding >= 0 && rounding <= 2, "unknown Q8_0 activation rounding");
+        require(x && topk_weights && topk_ids && out && status, "missing MoE operand");
+        const uint64_t xb = uint64_t(tokens) * m.H * 2;
+        require(disjoint({x, xb}, {out, xb}), "MoE output overlaps its input");
+        for (const void *p : {x, (const void *)topk_weights, (const void *)topk_ids, (const void *)out,
+                              (const void *)status})
+            check_device(p, "MoE operand");
+        cudaStream_t s = as_stream(stream);
+        const int P = int(tokens) * m.topk;
+        cuda_check(cudaMemsetAsync(status, 0, 4, s), "status reset");
+        cuda_check(cudaMemsetAsync(m.plan.counts, 0, size_t(m.E) * 4, s), "count reset");
+        k_moe_count<<<unsigned(ceil_div(P, 256)), 256, 0, s>>>(topk_ids, P, m.E, m.plan.counts, status);
+        k_moe_plan<<<1, 256, 0, s>>>(m.plan, m.E, m.max_tiles);
+        k_moe_scatter<<<unsigned(ceil_div(P, 256)), 256, 0, s>>>(topk_ids, P, m.E, m.plan);
+        k_moe_gather<<<unsigned(P), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), m.plan.perm, P, m.H, m.topk,
+                                                 m.q8, rounding, m.xp);
+        MoeGemmArgs g{};
+        g.tiles = m.plan.tiles;
+        g.num_tiles = m.plan.num_tiles;
+        g.status = status;
+        g.q8 = m.q8;
+        g.rounding = rounding;
+        g.perm = m.plan.perm;
+        g.topk_w = topk_weights;
+        // gate/up: N = 2I rows per expert, output I columns of mid
+        g.n_tiles = 2 * m.I / MOE_BN;
+        g.w_rows = 2 * m.I;
+        g.K = m.H;
+        g.mid = m.mid;
+        g.I = m.I;
+        if (m.q8) launch_moe_gemm<MOE_SWIGLU, false>(m.map_x, m.map_w1, g, m.max_tiles, s);
+        else launch_moe_gemm<MOE_SWIGLU, true>(m.map_x, m.map_w1, g, m.max_tiles, s);
+        // down: N = H rows per expert, K = I
+        g.n_tiles = m.H / MOE_BN;
+        g.w_rows = m.H;
+        g.K = m.I;
+        g.y = m.y;
+        if (m.q8) launch_moe_gemm<MOE_DOWN, false>(m.map_mid, m.map_w2, g, m.max_tiles, s);
+        else launch_moe_gemm<MOE_DOWN, true>(m.map_mid, m.map_w2, g, m.max_tiles, s);
+        k_moe_combine<<<unsigned(tokens), 256, 0, s>>>(m.y, m.plan.inv, int(tokens), m.H, m.topk,
+                                                        static_cast<__nv_bfloat16 *>(out));
+        cuda_check(cudaGetLastError(), "MoE launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+int mstar_b200_moe_close(void *handle, char *error, size_t error_size) {
+    try {
+        if (handle) {
+            auto *m = static_cast<Moe *>(handle);
+            require(!m->busy.test_and_set(std::memory_order_acquire), "cannot close a busy MoE handle");
+            cudaDeviceSynchronize();
+            delete m;
+        }
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+}  // extern "C"

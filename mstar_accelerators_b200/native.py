@@ -19,8 +19,8 @@ HEADER = PACKAGE.parent / "include" / "mstar_b200.h"
 
 Q8_REF, Q8_ARM, Q8_X86 = 0, 1, 2
 ROUNDING = {"ref": Q8_REF, "arm": Q8_ARM, "x86": Q8_X86}
-Q8_0, Q4_0 = 8, 4
-FORMATS = {"q8_0": Q8_0, "q4_0": Q4_0}
+Q8_0, Q4_0, BF16 = 8, 4, 16
+FORMATS = {"q8_0": Q8_0, "q4_0": Q4_0, "bf16": BF16}
 BIAS, GELU, RESIDUAL, GELU_ERF = 1, 2, 4, 8
 
 _vp, _i64, _u64, _sz, _int = C.c_void_p, C.c_int64, C.c_uint64, C.c_size_t, C.c_int
@@ -46,6 +46,11 @@ SIGNATURES = {
     "mstar_b200_attend": (_int, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64, C.c_int32, C.c_int32, C.c_int32,
                                  C.c_int32, _vp, _vp, C.c_int32, C.c_int32, _vp, _i64, C.c_float, _vp, _vp, *_err]),
     "mstar_b200_fill_kv": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _vp, *_err]),
+    "mstar_b200_moe_route": (_int, [_vp, _i64, _i64, _vp, C.c_int32, C.c_int32, C.c_int32, _vp, _vp, _vp, *_err]),
+    "mstar_b200_moe_create": (_vp, [C.c_int32, _vp, _u64, _vp, _u64, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                    C.c_int32, *_err]),
+    "mstar_b200_moe_run": (_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, C.c_int32, _vp, *_err]),
+    "mstar_b200_moe_close": (_int, [_vp, *_err]),
     "mstar_b200_q8_readout_noalloc": (_int, [_vp, _sz, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
 }
 
