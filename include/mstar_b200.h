@@ -134,11 +134,11 @@ MSTAR_B200_API int mstar_b200_q8_readout(void *handle, const float *x, float *ou
 /* --- Qwen3-Omni thinker MoE expert FFN ----------------------------------------------
  * Router (ConsistentBF16Router.forward, qwen3_omni/amd/router_consistency.py:54-62):
  * x bf16 [tokens][hidden], router_weight bf16 [experts][hidden] -> logits rounded
- * to bf16, softmax in fp32, top_k (ties: lower expert index), optional
- * renormalisation (norm_topk_prob) -> topk_weights fp32 / topk_ids int32
- * [tokens][top_k]. 1..256 experts. */
+ * to bf16 (written to logits fp32 [tokens][experts]), softmax in fp32, top_k
+ * (ties: lower expert index), optional renormalisation (norm_topk_prob) ->
+ * topk_weights fp32 / topk_ids int32 [tokens][top_k]. 1..256 experts. */
 MSTAR_B200_API int mstar_b200_moe_route(const void *x, int64_t tokens, int64_t hidden,
-    const void *router_weight, int32_t experts, int32_t top_k, int32_t renormalize,
+    const void *router_weight, int32_t experts, int32_t top_k, int32_t renormalize, float *logits,
     float *topk_weights, int32_t *topk_ids, void *stream, char *error, size_t error_size);
 /* Expert weights of one MoE layer (the experts_backend of SmallTokenThinkerMoE,
  * thinker_moe.py:104-188; layout preparation.py:13-36): w1 [E][2I][H] (gate rows

@@ -53,84 +53,117 @@ constexpr int ROUTER_CHUNK = 256;
 __device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
 // ------------------------------------------------------------------ router
-// CTA of E threads (one per expert) over ROUTER_TOKENS tokens.
-__global__ void k_router(const __nv_bfloat16 *__restrict__ x, const __nv_bfloat16 *__restrict__ wr, int T, int H,
-                         int E, int topk, int renorm, float *__restrict__ topk_w, int32_t *__restrict__ topk_ids) {
-    __shared__ float xs[ROUTER_TOKENS][ROUTER_CHUNK];
-    __shared__ float logits[ROUTER_TOKENS][256];
-    const int e = threadIdx.x;
+// Logits: CTA (32 warps) per (16 tokens, 32 experts). The 16 token rows sit in
+// shared memory as bf16; warp w owns expert e and its lanes stream the expert's
+// row with 16-byte loads, accumulating 16 fp32 dots that are then reduced
+// across the warp. Output logits[t][e] = bf16(dot) (F.linear's output dtype).
+__global__ void __launch_bounds__(1024) k_router_logits(const __nv_bfloat16 *__restrict__ x,
+                                                        const __nv_bfloat16 *__restrict__ wr, int T, int H, int E,
+                                                        float *__restrict__ logits) {
+    extern __shared__ __align__(16) __nv_bfloat16 xs[];  // [ROUTER_TOKENS][H]
     const int t0 = blockIdx.x * ROUTER_TOKENS;
     const int nt = T - t0 < ROUTER_TOKENS ? T - t0 : ROUTER_TOKENS;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int vec = H / 8;  // uint4 per row
+    for (int i = threadIdx.x; i < ROUTER_TOKENS * vec; i += blockDim.x) {
+        const int tt = i / vec, c = i % vec;
+        reinterpret_cast<uint4 *>(xs)[i] =
+            tt < nt ? reinterpret_cast<const uint4 *>(x + int64_t(t0 + tt) * H)[c] : make_uint4(0, 0, 0, 0);
+    }
+    __syncthreads();
+    const int e = blockIdx.y * 32 + warp;
+    if (e >= E) return;
     float acc[ROUTER_TOKENS];
 #pragma unroll
     for (int i = 0; i < ROUTER_TOKENS; ++i) acc[i] = 0.0f;
-    for (int k0 = 0; k0 < H; k0 += ROUTER_CHUNK) {
-        const int kc = H - k0 < ROUTER_CHUNK ? H - k0 : ROUTER_CHUNK;
-        __syncthreads();
-        for (int i = threadIdx.x; i < ROUTER_TOKENS * kc; i += blockDim.x) {
-            const int tt = i / kc, kk = i % kc;
-            xs[tt][kk] = tt < nt ? __bfloat162float(x[int64_t(t0 + tt) * H + k0 + kk]) : 0.0f;
-        }
-        __syncthreads();
-        if (e < E) {
-            const __nv_bfloat16 *w = wr + int64_t(e) * H + k0;
-            for (int kk = 0; kk < kc; ++kk) {
-                const float wv = __bfloat162float(w[kk]);
+    const uint4 *wrow = reinterpret_cast<const uint4 *>(wr + int64_t(e) * H);
+    for (int c = lane; c < vec; c += 32) {
+        const uint4 wv = __ldg(wrow + c);
+        const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&wv);
+        float wf[8];
 #pragma unroll
-                for (int i = 0; i < ROUTER_TOKENS; ++i) acc[i] = fmaf(xs[i][kk], wv, acc[i]);
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(w2[j]);
+            wf[2 * j] = f.x;
+            wf[2 * j + 1] = f.y;
+        }
+#pragma unroll
+        for (int tt = 0; tt < ROUTER_TOKENS; ++tt) {
+            const uint4 xv = reinterpret_cast<const uint4 *>(xs + tt * H)[c];
+            const __nv_bfloat162 *x2 = reinterpret_cast<const __nv_bfloat162 *>(&xv);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 f = __bfloat1622float2(x2[j]);
+                acc[tt] = fmaf(f.y, wf[2 * j + 1], fmaf(f.x, wf[2 * j], acc[tt]));
             }
         }
     }
-    if (e < E) {
 #pragma unroll
-        for (int i = 0; i < ROUTER_TOKENS; ++i) logits[i][e] = bf16r(acc[i]);  // F.linear output dtype
+    for (int tt = 0; tt < ROUTER_TOKENS; ++tt) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) acc[tt] += __shfl_xor_sync(0xffffffffu, acc[tt], o);
     }
-    __syncthreads();
-    // one warp per token: softmax (fp32) and top-k by repeated argmax (lower index wins ties)
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    for (int tt = warp; tt < nt; tt += nwarps) {
-        float mx = -INFINITY;
-        for (int j = lane; j < E; j += 32) mx = fmaxf(mx, logits[tt][j]);
+    if (lane < nt) {
+        float v = acc[0];
 #pragma unroll
-        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float sum = 0.0f;
-        for (int j = lane; j < E; j += 32) sum += expf(logits[tt][j] - mx);
+        for (int tt = 1; tt < ROUTER_TOKENS; ++tt)
+            if (lane == tt) v = acc[tt];
+        logits[int64_t(t0 + lane) * E + e] = bf16r(v);
+    }
+}
+
+// One warp per token: softmax in fp32, top-k by repeated argmax (lower index
+// wins ties), optional renormalisation.
+__global__ void k_router_topk(const float *__restrict__ logits, int T, int E, int topk, int renorm,
+                              float *__restrict__ topk_w, int32_t *__restrict__ topk_ids) {
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= T) return;
+    constexpr int MAXV = 8;  // E <= 256
+    float v[MAXV];
+    const float *row = logits + int64_t(t) * E;
+    float mx = -INFINITY;
 #pragma unroll
-        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        __syncwarp();
-        for (int j = lane; j < E; j += 32) logits[tt][j] = expf(logits[tt][j] - mx) / sum;
-        __syncwarp();
-        float chosen[MOE_MAX_TOPK];
-        int ids[MOE_MAX_TOPK];
-        float total = 0.0f;
-        for (int r = 0; r < topk; ++r) {
-            float bv = -INFINITY;
-            int bi = 0x7fffffff;
-            for (int j = lane; j < E; j += 32) {
-                const float v = logits[tt][j];
-                if (v > bv || (v == bv && j < bi)) { bv = v; bi = j; }
-            }
+    for (int i = 0; i < MAXV; ++i) {
+        const int j = lane + 32 * i;
+        v[i] = j < E ? row[j] : -INFINITY;
+        mx = fmaxf(mx, v[i]);
+    }
 #pragma unroll
-            for (int o = 16; o; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-            }
-            chosen[r] = bv;
-            ids[r] = bi;
-            total += bv;
-            __syncwarp();
-            if (lane == 0) logits[tt][bi] = -INFINITY;
-            __syncwarp();
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i)
+        if (lane + 32 * i < E) sum += expf(v[i] - mx);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) v[i] = lane + 32 * i < E ? expf(v[i] - mx) / sum : -INFINITY;
+    float chosen = 0.0f, total = 0.0f;
+    int chosen_id = 0;
+    for (int r = 0; r < topk; ++r) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+            const int j = lane + 32 * i;
+            if (j < E && (v[i] > bv || (v[i] == bv && j < bi))) { bv = v[i]; bi = j; }
         }
-        if (lane < topk) {
-            float w = chosen[0];
-            int id = ids[0];
-            for (int r = 1; r < topk; ++r)
-                if (lane == r) { w = chosen[r]; id = ids[r]; }
-            topk_w[int64_t(t0 + tt) * topk + lane] = renorm ? w / total : w;
-            topk_ids[int64_t(t0 + tt) * topk + lane] = id;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
         }
+        if (lane == r) { chosen = bv; chosen_id = bi; }
+        total += bv;
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i)
+            if (lane + 32 * i == bi) v[i] = -INFINITY;
+    }
+    if (lane < topk) {
+        topk_w[int64_t(t) * topk + lane] = renorm ? chosen / total : chosen;
+        topk_ids[int64_t(t) * topk + lane] = chosen_id;
     }
 }
 
@@ -549,20 +582,34 @@ using namespace mb;
 extern "C" {
 
 int mstar_b200_moe_route(const void *x, int64_t tokens, int64_t hidden, const void *router_weight, int32_t experts,
-                         int32_t top_k, int32_t renormalize, float *topk_weights, int32_t *topk_ids, void *stream,
-                         char *error, size_t error_size) {
+                         int32_t top_k, int32_t renormalize, float *logits, float *topk_weights, int32_t *topk_ids,
+                         void *stream, char *error, size_t error_size) {
     try {
-        require(x && router_weight && topk_weights && topk_ids, "missing router operand");
+        require(x && router_weight && logits && topk_weights && topk_ids, "missing router operand");
         require(tokens >= 1 && hidden >= 1 && experts >= 1 && experts <= 256, "router geometry: 1..256 experts");
         require(top_k >= 1 && top_k <= MOE_MAX_TOPK && top_k <= experts, "top_k outside 1..8");
         check_device(x, "router input");
         check_device(router_weight, "router weight");
         check_device(topk_weights, "top-k weights");
         check_device(topk_ids, "top-k ids");
-        const unsigned grid = unsigned(ceil_div(tokens, ROUTER_TOKENS));
-        k_router<<<grid, unsigned((experts + 31) / 32 * 32), 0, as_stream(stream)>>>(
-            static_cast<const __nv_bfloat16 *>(x), static_cast<const __nv_bfloat16 *>(router_weight), int(tokens),
-            int(hidden), experts, top_k, renormalize, topk_weights, topk_ids);
+        require(hidden % 8 == 0 && uintptr_t(x) % 16 == 0 && uintptr_t(router_weight) % 16 == 0,
+                "router rows must be 16-byte aligned");
+        const size_t smem = size_t(ROUTER_TOKENS) * hidden * 2;
+        require(smem <= 200 * 1024, "router token tile exceeds shared memory");
+        static bool configured = false;
+        if (!configured) {
+            cuda_check(cudaFuncSetAttribute(k_router_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
+                       "router shared memory");
+            configured = true;
+        }
+        check_device(logits, "router logits");
+        cudaStream_t s = as_stream(stream);
+        const dim3 grid(unsigned(ceil_div(tokens, ROUTER_TOKENS)), unsigned(ceil_div(experts, 32)));
+        k_router_logits<<<grid, 1024, smem, s>>>(static_cast<const __nv_bfloat16 *>(x),
+                                                 static_cast<const __nv_bfloat16 *>(router_weight), int(tokens),
+                                                 int(hidden), experts, logits);
+        k_router_topk<<<unsigned(ceil_div(tokens, 8)), 256, 0, s>>>(logits, int(tokens), experts, top_k, renormalize,
+                                                                   topk_weights, topk_ids);
         cuda_check(cudaGetLastError(), "router launch");
         return 0;
     } catch (const std::exception &e) {

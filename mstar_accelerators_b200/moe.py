@@ -16,7 +16,8 @@ from .linear import _stream
 from .native import check, error_buffer
 
 
-def route(x: torch.Tensor, router_weight: torch.Tensor, top_k: int = 8, renormalize: bool = True):
+def route(x: torch.Tensor, router_weight: torch.Tensor, top_k: int = 8, renormalize: bool = True,
+          logits: torch.Tensor | None = None):
     """bf16 x [T, H], router weight [E, H] -> (topk weights fp32 [T, k], topk ids int32 [T, k])."""
     lib = native.require_capability()
     if x.dtype != torch.bfloat16 or router_weight.dtype != torch.bfloat16:
@@ -27,9 +28,12 @@ def route(x: torch.Tensor, router_weight: torch.Tensor, top_k: int = 8, renormal
     E = w.shape[0]
     weights = torch.empty((T, top_k), dtype=torch.float32, device=x.device)
     ids = torch.empty((T, top_k), dtype=torch.int32, device=x.device)
+    if logits is None:
+        logits = torch.empty((T, E), dtype=torch.float32, device=x.device)
     e = error_buffer()
-    check(lib.mstar_b200_moe_route(x.data_ptr(), T, H, w.data_ptr(), E, top_k, int(renormalize), weights.data_ptr(),
-                                   ids.data_ptr(), _stream(x.device), e, len(e)), e, "B200 MoE router")
+    check(lib.mstar_b200_moe_route(x.data_ptr(), T, H, w.data_ptr(), E, top_k, int(renormalize), logits.data_ptr(),
+                                   weights.data_ptr(), ids.data_ptr(), _stream(x.device), e, len(e)),
+          e, "B200 MoE router")
     return weights, ids
 
 

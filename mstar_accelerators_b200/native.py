@@ -46,7 +46,8 @@ SIGNATURES = {
     "mstar_b200_attend": (_int, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64, C.c_int32, C.c_int32, C.c_int32,
                                  C.c_int32, _vp, _vp, C.c_int32, C.c_int32, _vp, _i64, C.c_float, _vp, _vp, *_err]),
     "mstar_b200_fill_kv": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _vp, *_err]),
-    "mstar_b200_moe_route": (_int, [_vp, _i64, _i64, _vp, C.c_int32, C.c_int32, C.c_int32, _vp, _vp, _vp, *_err]),
+    "mstar_b200_moe_route": (_int, [_vp, _i64, _i64, _vp, C.c_int32, C.c_int32, C.c_int32, _vp, _vp, _vp, _vp,
+                                    *_err]),
     "mstar_b200_moe_create": (_vp, [C.c_int32, _vp, _u64, _vp, _u64, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                     C.c_int32, *_err]),
     "mstar_b200_moe_run": (_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, C.c_int32, _vp, *_err]),
