@@ -50,6 +50,13 @@ enum mstar_b200_epilogue {
     MSTAR_B200_RESIDUAL = 4,  /* ggml_add(current, linear)            decoder.cpp:565-581 */
     MSTAR_B200_GELU_ERF = 8,  /* ggml_gelu_erf (F32 graphs)           decoder.cpp:581     */
 };
+/* Element type of activation rows handed to mstar_b200_stage_rows. */
+enum mstar_b200_activation { MSTAR_B200_ACT_F32 = 0, MSTAR_B200_ACT_F16 = 1 };
+/* Output form of mstar_b200_linear_gemm. STAGED: every 32-column block is
+ * Q8_0-quantized (rounding) and stored as fp16(q * d), i.e. already the staged
+ * activation operand of the next GEMM (the handle's row count, i.e. the output
+ * width, must then be a multiple of 32). */
+enum mstar_b200_output { MSTAR_B200_OUT_F32 = 0, MSTAR_B200_OUT_F16 = 1, MSTAR_B200_OUT_STAGED = 2 };
 
 /* --- library identity (encoder.h:29-31, backends/torch/q8.py:42-77) -------- */
 MSTAR_B200_API int mstar_b200_abi(void);
@@ -120,6 +127,24 @@ MSTAR_B200_API int mstar_b200_linear_close(void *handle, char *error, size_t err
  * product-rounding tolerance (the decode GEMV stays bit-exact). Synchronises. */
 MSTAR_B200_API int mstar_b200_linear_prepare_gemm(void *handle, const void *blocks, uint64_t bytes,
     int64_t max_queries, char *error, size_t error_size);
+/* The prepared GEMM on an operand that is already staged: staged = fp16(q * d)
+ * [rows][width] of the Q8_0-quantized activations (from mstar_b200_stage_rows,
+ * mstar_b200_stage_conv or a previous call's STAGED output; 16-byte aligned),
+ * so a chain of encoder linears (encoder.cpp:694-733) never materialises its
+ * fp32 activations. Output element (r, n) goes to out row
+ *   o(r) = segment_rows ? (r / segment_rows) * out_segment_rows + r % segment_rows : r
+ * (a per-utterance padded plane such as the F16 K/V rows padded to 256 of
+ * qkv_scatter, encoder.cpp:202-234, when out_segment_rows > segment_rows), in
+ * out_format, after the flagged epilogue (bias, GELU, then + residual row
+ * residual_period ? r % residual_period : r, stride residual_stride: the
+ * positional table of encoder.cpp:682 repeats per utterance). Pass status
+ * (device int32): bit value 1 nonfinite STAGED input, 2 a bounded wait timed out.
+ * rows may exceed the capacity given to prepare_gemm (no handle buffer is used). */
+MSTAR_B200_API int mstar_b200_linear_gemm(void *handle, const void *staged, uint64_t staged_bytes, int64_t rows,
+    void *out, uint64_t out_bytes, int64_t out_stride, int32_t out_format, const float *residual,
+    uint64_t residual_bytes, int64_t residual_stride, int64_t residual_period, int64_t segment_rows,
+    int64_t out_segment_rows, int32_t flags, int32_t rounding, int32_t *status, void *stream, char *error,
+    size_t error_size);
 /* Physical policy, set on an idle handle (the role of
  * cpu_decoder_set_cross_threads, decoder.h:44-47): warps that split one
  * 8-row group's K range (1, 2, 4 or 8; 0 restores the automatic choice).
@@ -157,6 +182,32 @@ MSTAR_B200_API int mstar_b200_moe_run(void *handle, const void *x, int64_t token
     const float *topk_weights, const int32_t *topk_ids, void *out, int32_t *status, int32_t rounding,
     void *stream, char *error, size_t error_size);
 MSTAR_B200_API int mstar_b200_moe_close(void *handle, char *error, size_t error_size);
+
+/* --- encoder graph staging (backends/cpu_ggml/encoder.cpp:400-754) ------------------
+ * stage_rows: rows of x (fp32 or fp16, stride x_stride elements), optionally
+ * LayerNorm-ed first (ln_weight/ln_bias: encoder_norm_affine, encoder.cpp:117-142;
+ * width <= 1536), Q8_0-quantized per 32 elements (ggml quantize_row_q8_0,
+ * `rounding`) and written as fp16(q * d) [rows][width], the staged activation
+ * operand of mstar_b200_linear_gemm. staged_bytes = rows * width * 2.
+ * status bit value 1: a nonfinite input (quantized as is, like ggml). */
+MSTAR_B200_API int mstar_b200_stage_rows(const void *x, int32_t x_format, int64_t x_stride, int64_t rows,
+    int64_t width, const float *ln_weight, const float *ln_bias, float ln_eps, void *staged,
+    uint64_t staged_bytes, int32_t rounding, int32_t *status, void *stream, char *error, size_t error_size);
+/* stage_conv: the columns of convolution_q8 (encoder.cpp:45-52; ggml_im2col with
+ * kernel 3, padding 1, dilation 1) of `batch` utterances, source fp32 either
+ * channel-major [batch][channels][time_in] (the mel input) or time-major
+ * [batch][time_in][channels] (the first convolution's output rows); output row
+ * b * time_out + t, column c * 3 + tap, zero columns up to k_padded (3 * channels
+ * rounded up to 32, encoder.cpp:551), time_out = (time_in - 1) / stride + 1;
+ * staged as in stage_rows. */
+MSTAR_B200_API int mstar_b200_stage_conv(const float *source, int32_t time_major, int64_t batch,
+    int64_t channels, int64_t time_in, int32_t stride, int64_t k_padded, void *staged, uint64_t staged_bytes,
+    int32_t rounding, int32_t *status, void *stream, char *error, size_t error_size);
+/* layer_norm: fp32 rows -> ggml_norm(eps), mul, add (the final encoder_norm_affine,
+ * encoder.cpp:733) -> fp32 out; width <= 1536. */
+MSTAR_B200_API int mstar_b200_layer_norm(const float *x, int64_t x_stride, int64_t rows, int64_t width,
+    const float *weight, const float *bias, float eps, float *out, int64_t out_stride, void *stream,
+    char *error, size_t error_size);
 
 /* --- readout that allocates nothing ------------------------------------------------
  * No counterpart in the reference. For callers that cannot allocate device

@@ -257,8 +257,19 @@ int mstar_b200_linear_run(void *handle, const float *x, int64_t x_stride, int64_
             launch_dequant_act(rounding, x, x_stride, queries, h.width, h.x16, h.status, s);
             CUtensorMap xmap;
             make_fp16_map(&xmap, h.x16, queries, h.width, GEMM_TILE_M);
-            GemmArgs g{queries, h.rows, h.width, out, out_stride, h.bias, (flags & 4) ? residual : nullptr, flags,
-                       h.status};
+            GemmArgs g{};
+            g.M = queries;
+            g.N = h.rows;
+            g.K = h.width;
+            g.out = out;
+            g.ldo = out_stride;
+            g.bias = h.bias;
+            g.residual = (flags & 4) ? residual : nullptr;
+            g.ldr = out_stride;
+            g.flags = flags;
+            g.out_mode = GEMM_OUT_F32;
+            g.rounding = rounding;
+            g.status = h.status;
             launch_gemm(xmap, h.wmap, g, s);
             cuda_check(cudaGetLastError(), "GEMM launch");
             return 0;
@@ -392,6 +403,82 @@ int mstar_b200_linear_prepare_gemm(void *handle, const void *blocks, uint64_t by
             h.gemm_rows = max_queries;
         }
         cuda_check(cudaDeviceSynchronize(), "GEMM preparation");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+int mstar_b200_linear_gemm(void *handle, const void *staged, uint64_t staged_bytes, int64_t rows, void *out,
+                           uint64_t out_bytes, int64_t out_stride, int32_t out_format, const float *residual,
+                           uint64_t residual_bytes, int64_t residual_stride, int64_t residual_period,
+                           int64_t segment_rows, int64_t out_segment_rows, int32_t flags, int32_t rounding,
+                           int32_t *status, void *stream, char *error, size_t error_size) {
+    try {
+        require(handle, "missing linear handle");
+        auto &h = *static_cast<Linear *>(handle);
+        Busy busy(h.busy);
+        require(h.w16, "linear_gemm needs prepare_gemm first");
+        check_rounding(rounding);
+        require((flags & ~15) == 0 && !((flags & 2) && (flags & 8)), "invalid epilogue flags");
+        require(!(flags & 1) || h.bias, "bias epilogue without a prepared bias");
+        require(out_format == MSTAR_B200_OUT_F32 || out_format == MSTAR_B200_OUT_F16 ||
+                    out_format == MSTAR_B200_OUT_STAGED,
+                "unknown output format");
+        require(out_format != MSTAR_B200_OUT_STAGED || h.rows % QK == 0, "staged output needs a multiple of 32 rows");
+        require(rows >= 1 && rows <= (int64_t(1) << 31), "invalid row count");
+        require(out_stride >= h.rows, "invalid output stride");
+        require(segment_rows >= 0 && (segment_rows == 0) == (out_segment_rows == 0) &&
+                    (segment_rows == 0 || out_segment_rows >= segment_rows),
+                "invalid output segments");
+        require(status, "missing status word");
+        const uint64_t sb = uint64_t(rows) * h.width * 2;
+        check_range({staged, staged_bytes}, sb, 16, "staged operand");
+        // output rows span up to the last segment's padded extent
+        const int64_t last = segment_rows ? ((rows - 1) / segment_rows) * out_segment_rows + (rows - 1) % segment_rows
+                                          : rows - 1;
+        const int64_t out_rows = segment_rows ? ceil_div(rows, segment_rows) * out_segment_rows : rows;
+        require(last < out_rows, "output segment arithmetic");
+        const uint64_t esz = out_format == MSTAR_B200_OUT_F32 ? 4 : 2;
+        const uint64_t ob = uint64_t((out_rows - 1) * out_stride + h.rows) * esz;
+        check_range({out, out_bytes}, ob, esz == 4 ? 4 : 2, "output");
+        require(disjoint({staged, sb}, {out, ob}), "output overlaps the staged operand");
+        if (flags & 4) {
+            require(residual_stride >= h.rows && residual_period >= 0, "invalid residual layout");
+            const int64_t res_rows = residual_period ? (residual_period < rows ? residual_period : rows) : rows;
+            const uint64_t rb = uint64_t((res_rows - 1) * residual_stride + h.rows) * 4;
+            check_range({residual, residual_bytes}, rb, 4, "residual");
+            const bool same = static_cast<const void *>(residual) == out && out_format == MSTAR_B200_OUT_F32 &&
+                              residual_stride == out_stride && !residual_period && !segment_rows;
+            require(same || disjoint({residual, rb}, {out, ob}), "residual partially overlaps output");
+            check_device(residual, "residual");
+        } else require(!residual && !residual_period, "residual given without its epilogue flag");
+        check_device(staged, "staged operand");
+        check_device(out, "output");
+        check_device(status, "status word");
+        cudaStream_t s = as_stream(stream);
+        CUtensorMap xmap;
+        make_fp16_map(&xmap, staged, rows, h.width, GEMM_TILE_M);
+        GemmArgs g{};
+        g.M = rows;
+        g.N = h.rows;
+        g.K = h.width;
+        g.out = out;
+        g.ldo = out_stride;
+        g.bias = h.bias;
+        g.residual = (flags & 4) ? residual : nullptr;
+        g.ldr = residual_stride;
+        g.res_period = residual_period;
+        g.seg_rows = segment_rows;
+        g.out_seg_rows = out_segment_rows;
+        g.flags = flags;
+        g.out_mode = out_format == MSTAR_B200_OUT_F32 ? GEMM_OUT_F32
+                     : out_format == MSTAR_B200_OUT_F16 ? GEMM_OUT_F16 : GEMM_OUT_Q8;
+        g.rounding = rounding;
+        g.status = status;
+        launch_gemm(xmap, h.wmap, g, s);
+        cuda_check(cudaGetLastError(), "GEMM launch");
         return 0;
     } catch (const std::exception &e) {
         message(error, error_size, e.what());

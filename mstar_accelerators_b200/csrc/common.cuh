@@ -198,6 +198,13 @@ __device__ __forceinline__ void unpack_q4(uint32_t q, uint32_t &lo, uint32_t &hi
 }
 
 // ggml stock GELU: tanh form evaluated on the fp16-rounded input, result
+// bits of a packed half2 (for 16-byte vector stores)
+__device__ __forceinline__ uint32_t half2_bits(__half2 h) {
+    uint32_t u;
+    memcpy(&u, &h, sizeof(u));
+    return u;
+}
+
 // rounded to fp16 (ggml-cpu/vec.h:963-969, 1000-1013; table ggml-cpu.c:3889).
 __device__ __forceinline__ float gelu_ggml(float x) {
     if (x <= -10.0f) return 0.0f;

@@ -15,9 +15,12 @@
 //           one thread issues tcgen05.mma kind::f16 (M=128, N=256, K=16) into
 //           the free accumulator, commits each stage back to the producer and
 //           each finished tile to the epilogue;
-//   warps 2-5 epilogue: tcgen05.ld 32x32b.x32 from their TMEM lane quarter,
-//           bias / GELU / residual, fp32 stores, then release the accumulator,
-//           so tile i's epilogue overlaps tile i+1's MMAs.
+//   warps 2-5 epilogue: tcgen05.ld 32x32b.x32 from their TMEM lane quarter
+//           (one thread = one row x 32 columns = one Q8_0 block), bias / GELU /
+//           residual, then fp32 or fp16 stores, or the block's Q8_0
+//           quantization stored as fp16(q * d) (the next GEMM's staged A
+//           operand); then release the accumulator, so tile i's epilogue
+//           overlaps tile i+1's MMAs.
 // Every mbarrier wait is bounded; a timeout sets status bit value 2 and the
 // CTA skips to the end (TMEM is still released).
 #include <cuda.h>
@@ -151,32 +154,96 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             int64_t m0, n0;
             tile_coords(tile, m0, n0);
             const int64_t row = m0 + 32 * q + lane;
+            const int64_t orow_i = a.seg_rows ? (row / a.seg_rows) * a.out_seg_rows + row % a.seg_rows : row;
+            const int64_t rrow_i = a.res_period ? row % a.res_period : row;
             for (int c = 0; c < GEMM_BN / 32; ++c) {
                 uint32_t r[32];
                 tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(buf * GEMM_BN + c * 32), r);
                 if (row < a.M) {
-                    float *orow = a.out + row * a.ldo;
-                    const float *rrow = a.residual ? a.residual + row * a.ldo : nullptr;
+                    const float *rrow = a.residual ? a.residual + rrow_i * a.ldr : nullptr;
                     const int64_t nc = n0 + c * 32;
-                    if (nc + 32 <= a.N && !(a.flags & 10) && (reinterpret_cast<uintptr_t>(orow + nc) & 15) == 0 &&
-                        (!rrow || (reinterpret_cast<uintptr_t>(rrow + nc) & 15) == 0)) {
+                    if (nc + 32 <= a.N) {
+                        // whole 32-column block: bias, activation, residual, then the output mode
+                        float v[32];
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                                   __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-                            if (a.flags & 1) {
+                        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                        if (a.flags & 1) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4) {
                                 const float4 bb = *reinterpret_cast<const float4 *>(a.bias + nc + j);
-                                v.x = __fadd_rn(v.x, bb.x); v.y = __fadd_rn(v.y, bb.y);
-                                v.z = __fadd_rn(v.z, bb.z); v.w = __fadd_rn(v.w, bb.w);
+                                v[j] = __fadd_rn(v[j], bb.x); v[j + 1] = __fadd_rn(v[j + 1], bb.y);
+                                v[j + 2] = __fadd_rn(v[j + 2], bb.z); v[j + 3] = __fadd_rn(v[j + 3], bb.w);
                             }
-                            if (a.flags & 4) {
-                                const float4 rr = *reinterpret_cast<const float4 *>(rrow + nc + j);
-                                v.x = __fadd_rn(rr.x, v.x); v.y = __fadd_rn(rr.y, v.y);
-                                v.z = __fadd_rn(rr.z, v.z); v.w = __fadd_rn(rr.w, v.w);
+                        }
+                        if (a.flags & 2) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[j] = gelu_ggml(v[j]);
+                        } else if (a.flags & 8) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+                        }
+                        if (a.flags & 4) {
+                            if ((reinterpret_cast<uintptr_t>(rrow + nc) & 15) == 0) {
+#pragma unroll
+                                for (int j = 0; j < 32; j += 4) {
+                                    const float4 rr = *reinterpret_cast<const float4 *>(rrow + nc + j);
+                                    v[j] = __fadd_rn(rr.x, v[j]); v[j + 1] = __fadd_rn(rr.y, v[j + 1]);
+                                    v[j + 2] = __fadd_rn(rr.z, v[j + 2]); v[j + 3] = __fadd_rn(rr.w, v[j + 3]);
+                                }
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(rrow[nc + j], v[j]);
                             }
-                            *reinterpret_cast<float4 *>(orow + nc + j) = v;
+                        }
+                        if (a.out_mode == GEMM_OUT_F32) {
+                            float *o = static_cast<float *>(a.out) + orow_i * a.ldo + nc;
+                            if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+                                for (int j = 0; j < 32; j += 4)
+                                    *reinterpret_cast<float4 *>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < 32; ++j) o[j] = v[j];
+                            }
+                        } else {
+                            if (a.out_mode == GEMM_OUT_Q8) {
+                                float amax = 0.0f;
+                                bool finite = true;
+#pragma unroll
+                                for (int j = 0; j < 32; ++j) {
+                                    amax = fmaxf(amax, fabsf(v[j]));
+                                    finite = finite && isfinite(v[j]);
+                                }
+                                if (!finite && a.status) atomicOr(a.status, 1);
+                                const float d = __fdiv_rn(amax, 127.0f);
+                                const float id = a.rounding == 2 ? (amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f)
+                                                                 : (d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f);
+                                const float dh = __half2float(__float2half_rn(d));
+#pragma unroll
+                                for (int j = 0; j < 32; ++j) {
+                                    const float sv = __fmul_rn(v[j], id);
+                                    const int qv = a.rounding == 0 ? int(roundf(sv)) : __float2int_rn(sv);
+                                    v[j] = __fmul_rn(float(qv), dh);
+                                }
+                            }
+                            __half *o = static_cast<__half *>(a.out) + orow_i * a.ldo + nc;
+                            if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+                                for (int j = 0; j < 32; j += 8) {
+                                    uint4 pk;
+                                    pk.x = half2_bits(__floats2half2_rn(v[j], v[j + 1]));
+                                    pk.y = half2_bits(__floats2half2_rn(v[j + 2], v[j + 3]));
+                                    pk.z = half2_bits(__floats2half2_rn(v[j + 4], v[j + 5]));
+                                    pk.w = half2_bits(__floats2half2_rn(v[j + 6], v[j + 7]));
+                                    *reinterpret_cast<uint4 *>(o + j) = pk;
+                                }
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < 32; ++j) o[j] = __float2half_rn(v[j]);
+                            }
                         }
                     } else {
+                        // ragged last block (fp32 / fp16 output only; Q8_0 staging needs N % 32 == 0)
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
                             const int64_t n = nc + j;
@@ -186,7 +253,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                                 if (a.flags & 2) v = gelu_ggml(v);
                                 else if (a.flags & 8) v = gelu_erf(v);
                                 if (a.flags & 4) v = __fadd_rn(rrow[n], v);
-                                orow[n] = v;
+                                if (a.out_mode == GEMM_OUT_F32) static_cast<float *>(a.out)[orow_i * a.ldo + n] = v;
+                                else static_cast<__half *>(a.out)[orow_i * a.ldo + n] = __float2half_rn(v);
                             }
                         }
                     }

@@ -7,18 +7,39 @@ namespace mb {
 
 struct GemmArgs {
     int64_t M, N, K;
-    float *out;             // [M][ldo]
+    void *out;              // [rows][ldo]: fp32, or fp16 for the fp16 / Q8_0-staging output modes
     int64_t ldo;
     const float *bias;      // [N] or null
-    const float *residual;  // [M][ldo] or null (may alias out)
+    const float *residual;  // [rows][ldr] fp32 or null (may alias an fp32 out)
+    int64_t ldr;
+    int64_t res_period;     // > 0: residual row = row % res_period (a table shared by every segment)
+    int64_t seg_rows;       // > 0: output row = (row / seg_rows) * out_seg_rows + row % seg_rows
+    int64_t out_seg_rows;
     int flags;              // MSTAR_B200_BIAS / GELU / RESIDUAL / GELU_ERF
-    int *status;            // bit value 2: a bounded pipeline wait timed out
+    int out_mode;           // GEMM_OUT_F32 / GEMM_OUT_F16 / GEMM_OUT_Q8
+    int rounding;           // Q8_0 rounding of GEMM_OUT_Q8
+    int *status;            // bit value 2: a bounded pipeline wait timed out; 1: nonfinite Q8_0 input
 };
+
+// Output modes: fp32 rows; fp16 rows; or each 32-column block Q8_0-quantized
+// (ggml quantize_row_q8_0, selected rounding) and stored as fp16(q * d), the
+// staged A operand of the next GEMM.
+constexpr int GEMM_OUT_F32 = 0, GEMM_OUT_F16 = 1, GEMM_OUT_Q8 = 2;
 
 void make_fp16_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t k, int box_rows);
 void launch_dequant_weights(const uint8_t *blocks, __half *out, int64_t rows, int64_t nb, int q4, cudaStream_t s);
 void launch_dequant_act(int mode, const float *x, int64_t ldx, int64_t m, int64_t k, __half *out, int *status,
                         cudaStream_t s);
+// rows of fp32 or fp16 [-> LayerNorm] -> Q8_0 (selected rounding) -> fp16(q * d) [rows][k]
+void launch_stage_rows(int mode, const void *x, int x_f16, int64_t ldx, int64_t rows, int64_t k, const float *ln_w,
+                       const float *ln_b, float ln_eps, __half *out, int64_t ldo, int *status, cudaStream_t s);
+// 1-D convolution columns (kernel 3, padding 1, dilation 1) -> Q8_0 -> fp16(q * d),
+// K = 3 * channels zero-padded to k_padded; row = b * time_out + t, column = c * 3 + tap
+void launch_stage_conv(int mode, const float *src, int time_major, int64_t batch, int64_t channels,
+                       int64_t time_in, int64_t time_out, int stride, int64_t k_padded, __half *out, int *status,
+                       cudaStream_t s);
+void launch_layer_norm(const float *x, int64_t ldx, int64_t rows, int64_t k, const float *w, const float *b, float eps,
+                       float *out, int64_t ldo, cudaStream_t s);
 void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &a, cudaStream_t s);
 
 constexpr int GEMM_TILE_M = 128, GEMM_TILE_N = 256;

@@ -1,0 +1,283 @@
+// Operand staging for the tcgen05 GEMM of the encoder graph
+// (backends/cpu_ggml/encoder.cpp:400-754), one warp per 32-element Q8_0 block:
+//   k_stage_rows  fp32 or fp16 rows [-> LayerNorm] -> Q8_0 -> fp16(q * d): the
+//                 activation side of ggml_mul_mat(Q8_0 W, x) after
+//                 encoder_norm_affine (encoder.cpp:117-142) or on the fp32
+//                 attention output;
+//   k_stage_conv  the im2col columns of convolution_q8 (encoder.cpp:45-52: kernel
+//                 3, padding 1, column = channel * 3 + tap, K zero-padded to a
+//                 multiple of 32, encoder.cpp:551) quantized the same way;
+//   k_layer_norm  the final encoder_norm_affine to fp32 (encoder.cpp:733).
+// Q8_0 quantization follows ggml quantize_row_q8_0 with the selected rounding
+// (ref / ARM / x86); a nonfinite input sets status bit value 1.
+#include <cmath>
+
+#include "../../include/mstar_b200.h"
+#include "gemm.cuh"
+
+namespace mb {
+
+constexpr int STAGE_WARPS = 8;
+constexpr int STAGE_MAX_PER_LANE = 48;  // LayerNorm rows keep <= 48 * 32 = 1536 values in registers
+
+template <int MODE>
+__device__ __forceinline__ float q8_staged(float v, int *status) {
+    if (!isfinite(v) && status) atomicOr(status, 1);
+    float amax = fabsf(v);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 127.0f);
+    float id;
+    if (MODE == 2) id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+    else id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float sv = __fmul_rn(v, id);
+    const int q = MODE == 0 ? int(roundf(sv)) : __float2int_rn(sv);
+    return __fmul_rn(float(q), __half2float(__float2half_rn(d)));
+}
+
+template <bool F16>
+__device__ __forceinline__ float load_elem(const void *x, int64_t i) {
+    if (F16) return __half2float(static_cast<const __half *>(x)[i]);
+    return static_cast<const float *>(x)[i];
+}
+
+// ggml_compute_forward_norm_f32 (ggml-cpu/ops.cpp:4094-4137): mean, centred
+// variance, y = (x - mean) * (1 / sqrt(var + eps)); then ggml mul and add.
+// The sums are warp-reduced (the reference sums sequentially), so the
+// normalised value can differ in the last ulp.
+template <bool F16>
+__device__ __forceinline__ void row_stats(const void *x, int64_t base, int64_t k, float eps, float (&vals)[STAGE_MAX_PER_LANE],
+                                          float &mean, float &rstd) {
+    const int lane = threadIdx.x & 31;
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < STAGE_MAX_PER_LANE; ++i) {
+        const int64_t e = int64_t(i) * 32 + lane;
+        vals[i] = e < k ? load_elem<F16>(x, base + e) : 0.0f;
+        sum += vals[i];
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    mean = sum / float(k);
+    float var = 0.0f;
+#pragma unroll
+    for (int i = 0; i < STAGE_MAX_PER_LANE; ++i) {
+        const int64_t e = int64_t(i) * 32 + lane;
+        if (e < k) {
+            const float y = __fsub_rn(vals[i], mean);
+            var = __fadd_rn(var, __fmul_rn(y, y));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+    rstd = 1.0f / sqrtf(var / float(k) + eps);
+}
+
+template <int MODE, bool F16, bool LN>
+__global__ void __launch_bounds__(STAGE_WARPS * 32)
+    k_stage_rows(const void *__restrict__ x, int64_t ldx, int64_t rows, int64_t k, const float *__restrict__ ln_w,
+                 const float *__restrict__ ln_b, float eps, __half *__restrict__ out, int64_t ldo,
+                 int *__restrict__ status) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = int64_t(blockIdx.x) * STAGE_WARPS + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const int64_t nb = k / QK;
+    if (LN) {
+        float vals[STAGE_MAX_PER_LANE];
+        float mean, rstd;
+        row_stats<F16>(x, row * ldx, k, eps, vals, mean, rstd);
+#pragma unroll
+        for (int i = 0; i < STAGE_MAX_PER_LANE; ++i) {
+            if (i < nb) {
+                const int64_t e = int64_t(i) * 32 + lane;
+                const float v = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(vals[i], mean), rstd), __ldg(ln_w + e)),
+                                          __ldg(ln_b + e));
+                out[row * ldo + e] = __float2half_rn(q8_staged<MODE>(v, status));
+            }
+        }
+    } else {
+        for (int64_t b = 0; b < nb; ++b) {
+            const int64_t e = b * 32 + lane;
+            out[row * ldo + e] = __float2half_rn(q8_staged<MODE>(load_elem<F16>(x, row * ldx + e), status));
+        }
+    }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(STAGE_WARPS * 32)
+    k_stage_conv(const float *__restrict__ src, int time_major, int64_t batch, int64_t channels, int64_t time_in,
+                 int64_t time_out, int stride, int64_t k_padded, __half *__restrict__ out, int *__restrict__ status) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nb = k_padded / QK;
+    const int64_t wid = int64_t(blockIdx.x) * STAGE_WARPS + (threadIdx.x >> 5);
+    if (wid >= batch * time_out * nb) return;
+    const int64_t row = wid / nb, blk = wid % nb;
+    const int64_t b = row / time_out, t = row % time_out;
+    const int64_t col = blk * 32 + lane;
+    float v = 0.0f;
+    if (col < 3 * channels) {
+        const int64_t c = col / 3, ti = t * stride + col % 3 - 1;
+        if (ti >= 0 && ti < time_in)
+            v = time_major ? src[(b * time_in + ti) * channels + c] : src[(b * channels + c) * time_in + ti];
+    }
+    out[row * k_padded + col] = __float2half_rn(q8_staged<MODE>(v, status));
+}
+
+__global__ void __launch_bounds__(STAGE_WARPS * 32)
+    k_layer_norm(const float *__restrict__ x, int64_t ldx, int64_t rows, int64_t k, const float *__restrict__ w,
+                 const float *__restrict__ bias, float eps, float *__restrict__ out, int64_t ldo) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = int64_t(blockIdx.x) * STAGE_WARPS + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    float vals[STAGE_MAX_PER_LANE];
+    float mean, rstd;
+    row_stats<false>(x, row * ldx, k, eps, vals, mean, rstd);
+#pragma unroll
+    for (int i = 0; i < STAGE_MAX_PER_LANE; ++i) {
+        const int64_t e = int64_t(i) * 32 + lane;
+        if (e < k)
+            out[row * ldo + e] =
+                __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(vals[i], mean), rstd), __ldg(w + e)), __ldg(bias + e));
+    }
+}
+
+template <int MODE>
+static void stage_rows_mode(const void *x, int x_f16, int64_t ldx, int64_t rows, int64_t k, const float *ln_w,
+                            const float *ln_b, float eps, __half *out, int64_t ldo, int *status, cudaStream_t s) {
+    const unsigned grid = unsigned(ceil_div(rows, STAGE_WARPS));
+    const int threads = STAGE_WARPS * 32;
+    if (x_f16) {
+        if (ln_w) k_stage_rows<MODE, true, true><<<grid, threads, 0, s>>>(x, ldx, rows, k, ln_w, ln_b, eps, out, ldo, status);
+        else k_stage_rows<MODE, true, false><<<grid, threads, 0, s>>>(x, ldx, rows, k, ln_w, ln_b, eps, out, ldo, status);
+    } else {
+        if (ln_w) k_stage_rows<MODE, false, true><<<grid, threads, 0, s>>>(x, ldx, rows, k, ln_w, ln_b, eps, out, ldo, status);
+        else k_stage_rows<MODE, false, false><<<grid, threads, 0, s>>>(x, ldx, rows, k, ln_w, ln_b, eps, out, ldo, status);
+    }
+}
+
+void launch_stage_rows(int mode, const void *x, int x_f16, int64_t ldx, int64_t rows, int64_t k, const float *ln_w,
+                       const float *ln_b, float ln_eps, __half *out, int64_t ldo, int *status, cudaStream_t s) {
+    if (mode == 0) stage_rows_mode<0>(x, x_f16, ldx, rows, k, ln_w, ln_b, ln_eps, out, ldo, status, s);
+    else if (mode == 2) stage_rows_mode<2>(x, x_f16, ldx, rows, k, ln_w, ln_b, ln_eps, out, ldo, status, s);
+    else stage_rows_mode<1>(x, x_f16, ldx, rows, k, ln_w, ln_b, ln_eps, out, ldo, status, s);
+}
+
+void launch_stage_conv(int mode, const float *src, int time_major, int64_t batch, int64_t channels, int64_t time_in,
+                       int64_t time_out, int stride, int64_t k_padded, __half *out, int *status, cudaStream_t s) {
+    const unsigned grid = unsigned(ceil_div(batch * time_out * (k_padded / QK), STAGE_WARPS));
+    const int threads = STAGE_WARPS * 32;
+    if (mode == 0)
+        k_stage_conv<0><<<grid, threads, 0, s>>>(src, time_major, batch, channels, time_in, time_out, stride, k_padded, out, status);
+    else if (mode == 2)
+        k_stage_conv<2><<<grid, threads, 0, s>>>(src, time_major, batch, channels, time_in, time_out, stride, k_padded, out, status);
+    else
+        k_stage_conv<1><<<grid, threads, 0, s>>>(src, time_major, batch, channels, time_in, time_out, stride, k_padded, out, status);
+}
+
+void launch_layer_norm(const float *x, int64_t ldx, int64_t rows, int64_t k, const float *w, const float *b, float eps,
+                       float *out, int64_t ldo, cudaStream_t s) {
+    k_layer_norm<<<unsigned(ceil_div(rows, STAGE_WARPS)), STAGE_WARPS * 32, 0, s>>>(x, ldx, rows, k, w, b, eps, out, ldo);
+}
+
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" {
+
+int mstar_b200_stage_rows(const void *x, int32_t x_format, int64_t x_stride, int64_t rows, int64_t width,
+                          const float *ln_weight, const float *ln_bias, float ln_eps, void *staged,
+                          uint64_t staged_bytes, int32_t rounding, int32_t *status, void *stream, char *error,
+                          size_t error_size) {
+    try {
+        require(x_format == MSTAR_B200_ACT_F32 || x_format == MSTAR_B200_ACT_F16, "staged rows are fp32 or fp16");
+        require(rounding >= 0 && rounding <= 2, "unknown Q8_0 activation rounding");
+        require(rows >= 1 && rows <= (int64_t(1) << 31) && width >= QK && width % QK == 0 && width <= 65536,
+                "invalid staging shape");
+        require(x_stride >= width, "invalid row stride");
+        if (ln_weight) {
+            require(ln_bias && std::isfinite(ln_eps) && ln_eps >= 0.0f, "invalid LayerNorm parameters");
+            require(width <= int64_t(STAGE_MAX_PER_LANE) * 32, "LayerNorm rows are at most 1536 wide");
+            check_device(ln_weight, "LayerNorm weight");
+            check_device(ln_bias, "LayerNorm bias");
+        } else require(!ln_bias, "LayerNorm bias given without its weight");
+        const uint64_t esz = x_format == MSTAR_B200_ACT_F16 ? 2 : 4;
+        const uint64_t xb = uint64_t((rows - 1) * x_stride + width) * esz;
+        const uint64_t ob = uint64_t(rows * width) * 2;
+        check_range({x, xb}, xb, esz, "activations");
+        check_range({staged, staged_bytes}, ob, 16, "staged operand");
+        require(disjoint({x, xb}, {staged, ob}), "staged operand overlaps activations");
+        require(status, "missing status word");
+        check_device(x, "activations");
+        check_device(staged, "staged operand");
+        check_device(status, "status word");
+        launch_stage_rows(rounding, x, x_format == MSTAR_B200_ACT_F16, x_stride, rows, width, ln_weight, ln_bias, ln_eps,
+                          static_cast<__half *>(staged), width, status, as_stream(stream));
+        cuda_check(cudaGetLastError(), "staging launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+int mstar_b200_stage_conv(const float *source, int32_t time_major, int64_t batch, int64_t channels, int64_t time_in,
+                          int32_t stride, int64_t k_padded, void *staged, uint64_t staged_bytes, int32_t rounding,
+                          int32_t *status, void *stream, char *error, size_t error_size) {
+    try {
+        require(rounding >= 0 && rounding <= 2, "unknown Q8_0 activation rounding");
+        require(time_major == 0 || time_major == 1, "layout flag is 0 (channel-major) or 1 (time-major)");
+        require(stride == 1 || stride == 2, "convolution stride is 1 or 2");
+        require(batch >= 1 && batch <= 4096 && channels >= 1 && channels <= 65536 && time_in >= 1 &&
+                    time_in <= (int64_t(1) << 24),
+                "invalid convolution shape");
+        require(k_padded % QK == 0 && k_padded >= 3 * channels && k_padded < 3 * channels + 64,
+                "padded K must be 3 * channels rounded up to a multiple of 32 (at most 63 zeros)");
+        const int64_t time_out = (time_in + 2 - 3) / stride + 1;
+        require(batch * time_out <= (int64_t(1) << 31), "too many convolution rows");
+        const uint64_t sb = uint64_t(batch * channels * time_in) * 4;
+        const uint64_t ob = uint64_t(batch * time_out * k_padded) * 2;
+        check_range({source, sb}, sb, 4, "convolution input");
+        check_range({staged, staged_bytes}, ob, 16, "staged operand");
+        require(disjoint({source, sb}, {staged, ob}), "staged operand overlaps the input");
+        require(status, "missing status word");
+        check_device(source, "convolution input");
+        check_device(staged, "staged operand");
+        check_device(status, "status word");
+        launch_stage_conv(rounding, source, time_major, batch, channels, time_in, time_out, stride, k_padded,
+                          static_cast<__half *>(staged), status, as_stream(stream));
+        cuda_check(cudaGetLastError(), "convolution staging launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+int mstar_b200_layer_norm(const float *x, int64_t x_stride, int64_t rows, int64_t width, const float *weight,
+                          const float *bias, float eps, float *out, int64_t out_stride, void *stream, char *error,
+                          size_t error_size) {
+    try {
+        require(rows >= 1 && rows <= (int64_t(1) << 31) && width >= 1 && width <= int64_t(STAGE_MAX_PER_LANE) * 32,
+                "LayerNorm rows are 1..1536 wide");
+        require(x_stride >= width && out_stride >= width, "invalid row stride");
+        require(weight && bias && std::isfinite(eps) && eps >= 0.0f, "invalid LayerNorm parameters");
+        const uint64_t xb = uint64_t((rows - 1) * x_stride + width) * 4;
+        const uint64_t ob = uint64_t((rows - 1) * out_stride + width) * 4;
+        check_range({x, xb}, xb, 4, "LayerNorm input");
+        check_range({out, ob}, ob, 4, "LayerNorm output");
+        require(disjoint({x, xb}, {out, ob}), "LayerNorm output overlaps its input");
+        check_device(x, "LayerNorm input");
+        check_device(out, "LayerNorm output");
+        check_device(weight, "LayerNorm weight");
+        check_device(bias, "LayerNorm bias");
+        launch_layer_norm(x, x_stride, rows, width, weight, bias, eps, out, out_stride, as_stream(stream));
+        cuda_check(cudaGetLastError(), "LayerNorm launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+}  // extern "C"

@@ -67,6 +67,74 @@ def quantize(x: torch.Tensor, rounding: str = "arm") -> torch.Tensor:
     return out
 
 
+def stage_rows(x: torch.Tensor, *, norm: tuple | None = None, rounding: str = "arm",
+               out: torch.Tensor | None = None, status: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 / fp16 rows [..., K] [-> LayerNorm] -> staged GEMM operand fp16(q * d) [rows, K]."""
+    lib = native.require_capability()
+    _require_cuda(x, "activations")
+    if x.dtype not in (torch.float32, torch.float16):
+        raise ValueError("staged rows are fp32 or fp16")
+    k = x.shape[-1]
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    rows = x2.shape[0]
+    if out is None:
+        out = torch.empty((rows, k), dtype=torch.float16, device=x.device)
+    if status is None:
+        status = torch.zeros(1, dtype=torch.int32, device=x.device)
+    lw, lb, eps = _norm(norm)
+    e = error_buffer()
+    check(lib.mstar_b200_stage_rows(x2.data_ptr(), native.ACT_F16 if x.dtype == torch.float16 else native.ACT_F32,
+                                    x2.stride(0), rows, k, lw, lb, eps, out.data_ptr(), rows * k * 2,
+                                    native.ROUNDING[rounding], status.data_ptr(), _stream(x.device), e, len(e)),
+          e, "B200 row staging")
+    return out
+
+
+def stage_conv(source: torch.Tensor, *, time_major: bool, stride: int, k_padded: int, rounding: str = "arm",
+               out: torch.Tensor | None = None, status: torch.Tensor | None = None) -> torch.Tensor:
+    """Convolution columns (kernel 3, padding 1) of fp32 [B, C, T] (or [B, T, C] when time_major),
+    Q8_0-staged as fp16 [B * T_out, k_padded]."""
+    lib = native.require_capability()
+    _require_cuda(source, "convolution input", torch.float32)
+    src = source.contiguous()
+    if time_major:
+        batch, time_in, channels = src.shape
+    else:
+        batch, channels, time_in = src.shape
+    time_out = (time_in - 1) // stride + 1
+    if out is None:
+        out = torch.empty((batch * time_out, k_padded), dtype=torch.float16, device=src.device)
+    if status is None:
+        status = torch.zeros(1, dtype=torch.int32, device=src.device)
+    e = error_buffer()
+    check(lib.mstar_b200_stage_conv(src.data_ptr(), int(time_major), batch, channels, time_in, stride, k_padded,
+                                    out.data_ptr(), batch * time_out * k_padded * 2, native.ROUNDING[rounding],
+                                    status.data_ptr(), _stream(src.device), e, len(e)),
+          e, "B200 convolution staging")
+    return out
+
+
+def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-5,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """ggml_norm(eps) * weight + bias over the last dimension of fp32 rows."""
+    lib = native.require_capability()
+    _require_cuda(x, "LayerNorm input", torch.float32)
+    k = x.shape[-1]
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    o2 = out.reshape(-1, k)
+    e = error_buffer()
+    check(lib.mstar_b200_layer_norm(x2.data_ptr(), x2.stride(0), x2.shape[0], k, weight.data_ptr(), bias.data_ptr(),
+                                    float(eps), o2.data_ptr(), o2.stride(0), _stream(x.device), e, len(e)),
+          e, "B200 LayerNorm")
+    return out
+
+
 def _rows(x: torch.Tensor, width: int) -> torch.Tensor:
     """[..., width] -> a 2-D view with unit inner stride and 16-byte aligned rows."""
     x2 = x.reshape(-1, width)
@@ -152,6 +220,53 @@ class BlockLinear:
         check(self.lib.mstar_b200_linear_prepare_gemm(self.handle, self.blocks.data_ptr(), _nbytes(self.blocks),
                                                       int(max_queries), e, len(e)), e, "B200 GEMM preparation")
         self.gemm_rows = int(max_queries)
+
+    def gemm(self, staged: torch.Tensor, *, out: torch.Tensor | None = None, out_format: str = "f32",
+             residual: torch.Tensor | None = None, residual_period: int = 0, segments: tuple[int, int] = (0, 0),
+             bias: bool = True, gelu: str | None = None, rounding: str = "arm",
+             status: torch.Tensor | None = None) -> torch.Tensor:
+        """The prepared tcgen05 GEMM on a staged fp16 operand [rows, width].
+
+        out_format: "f32", "f16" or "staged" (Q8_0-staged fp16, the next GEMM's operand).
+        segments = (rows per segment, output rows per segment) places each segment's
+        rows at the start of a padded output plane; residual_period repeats a residual
+        table every that many rows."""
+        if not self.gemm_rows:
+            raise ValueError("prepare_gemm must run before gemm")
+        _require_cuda(staged, "staged operand", torch.float16)
+        if staged.ndim != 2 or staged.shape[1] != self.width or not staged.is_contiguous():
+            raise ValueError("staged operand must be a contiguous [rows, width] fp16 matrix")
+        rows = staged.shape[0]
+        fmt = {"f32": native.OUT_F32, "f16": native.OUT_F16, "staged": native.OUT_STAGED}[out_format]
+        seg, out_seg = segments
+        out_rows = -(-rows // seg) * out_seg if seg else rows
+        dtype = torch.float32 if out_format == "f32" else torch.float16
+        if out is None:
+            out = torch.empty((out_rows, self.rows), dtype=dtype, device=staged.device)
+        o2 = out.reshape(-1, out.shape[-1])
+        if o2.dtype != dtype or o2.stride(-1) != 1:
+            raise ValueError("output dtype or layout differs from the output format")
+        flags = (BIAS if (bias and self.has_bias) else 0)
+        flags |= {None: 0, "tanh": GELU, "erf": GELU_ERF}[gelu]
+        r_ptr, r_bytes, r_stride = None, 0, 0
+        if residual is not None:
+            r2 = residual.reshape(-1, residual.shape[-1])
+            _require_cuda(r2, "residual", torch.float32)
+            flags |= RESIDUAL
+            r_rows = min(residual_period, rows) if residual_period else rows
+            r_ptr, r_stride = r2.data_ptr(), r2.stride(0)
+            r_bytes = ((r_rows - 1) * r_stride + self.rows) * 4
+        if status is None:
+            status = torch.zeros(1, dtype=torch.int32, device=staged.device)
+        o_bytes = ((out_rows - 1) * o2.stride(0) + self.rows) * o2.element_size()
+        e = error_buffer()
+        check(self.lib.mstar_b200_linear_gemm(self.handle, staged.data_ptr(), rows * self.width * 2, rows,
+                                              o2.data_ptr(), o_bytes, o2.stride(0), fmt, r_ptr, r_bytes, r_stride,
+                                              int(residual_period), int(seg), int(out_seg), flags,
+                                              native.ROUNDING[rounding], status.data_ptr(), _stream(staged.device),
+                                              e, len(e)),
+              e, "B200 GEMM")
+        return out
 
     def set_split(self, warps: int) -> None:
         """Force the K split (1, 2, 4, 8) or restore the automatic choice (0); results do not change."""

@@ -22,6 +22,8 @@ ROUNDING = {"ref": Q8_REF, "arm": Q8_ARM, "x86": Q8_X86}
 Q8_0, Q4_0, BF16 = 8, 4, 16
 FORMATS = {"q8_0": Q8_0, "q4_0": Q4_0, "bf16": BF16}
 BIAS, GELU, RESIDUAL, GELU_ERF = 1, 2, 4, 8
+ACT_F32, ACT_F16 = 0, 1
+OUT_F32, OUT_F16, OUT_STAGED = 0, 1, 2
 
 _vp, _i64, _u64, _sz, _int = C.c_void_p, C.c_int64, C.c_uint64, C.c_size_t, C.c_int
 _err = [C.c_char_p, _sz]
@@ -41,6 +43,13 @@ SIGNATURES = {
     "mstar_b200_linear_close": (_int, [_vp, *_err]),
     "mstar_b200_linear_set_split": (_int, [_vp, _int, *_err]),
     "mstar_b200_linear_prepare_gemm": (_int, [_vp, _vp, _u64, _i64, *_err]),
+    "mstar_b200_linear_gemm": (_int, [_vp, _vp, _u64, _i64, _vp, _u64, _i64, C.c_int32, _vp, _u64, _i64, _i64, _i64,
+                                      _i64, C.c_int32, C.c_int32, _vp, _vp, *_err]),
+    "mstar_b200_stage_rows": (_int, [_vp, C.c_int32, _i64, _i64, _i64, _vp, _vp, C.c_float, _vp, _u64, C.c_int32, _vp,
+                                     _vp, *_err]),
+    "mstar_b200_stage_conv": (_int, [_vp, C.c_int32, _i64, _i64, _i64, C.c_int32, _i64, _vp, _u64, C.c_int32, _vp, _vp,
+                                     *_err]),
+    "mstar_b200_layer_norm": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, C.c_float, _vp, _i64, _vp, *_err]),
     "mstar_b200_q8_readout": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "mstar_b200_embed": (_int, [_vp, _i64, _vp, _i64, _i64, _vp, _vp, _i64, C.c_float, _vp, _vp, _vp, *_err]),
     "mstar_b200_attend": (_int, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64, C.c_int32, C.c_int32, C.c_int32,

@@ -61,6 +61,8 @@ def lib():
         L.orc_argmax.argtypes = [_f32p, C.c_int64, _i64p, C.c_int64]
         L.orc_argmax.restype = C.c_int64
         L.orc_gelu_ggml.argtypes = [C.c_float]
+        L.orc_gelu_ggml_rows.argtypes = [_f32p, _f32p, C.c_int64]
+        L.orc_gelu_ggml_rows.restype = None
         L.orc_gelu_ggml.restype = C.c_float
         _lib = L
     return _lib
@@ -167,9 +169,10 @@ def dequantize(blocks: np.ndarray, fmt="q8_0") -> np.ndarray:
 
 
 def gelu_ggml(x) -> np.ndarray:
-    f = lib().orc_gelu_ggml
     x = _f32(x)
-    return np.array([f(float(v)) for v in x.reshape(-1)], np.float32).reshape(x.shape)
+    y = np.empty_like(x)
+    lib().orc_gelu_ggml_rows(x.reshape(-1), y.reshape(-1), x.size)
+    return y
 
 
 def ref_quantize(x, which: str) -> np.ndarray:

@@ -267,3 +267,8 @@ float orc_gelu_ggml(float x) {
     const float g = 0.5f * h * (1.0f + tanhf(c * h * (1.0f + a * h * h)));
     return orc_fp16_to_fp32(orc_fp32_to_fp16(g));
 }
+
+/* orc_gelu_ggml over n values (ggml_vec_gelu_f32 on a row). */
+void orc_gelu_ggml_rows(const float *x, float *y, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) y[i] = orc_gelu_ggml(x[i]);
+}
