@@ -2,6 +2,7 @@
 
     python -m mstar_accelerators_b200.cases readout-q4-b32
     python -m mstar_accelerators_b200.cases decode-step-b32
+    python -m mstar_accelerators_b200.cases encoder-large-b16
 
 Each case builds its inputs from fixed seeds, runs a few calls, synchronises
 and prints "ok". The ncu summaries under profiles/ name the case they used.
@@ -54,8 +55,30 @@ def gemm_q8_8192x5120x1280():
         lin(x, out=out)
 
 
+def _encoder(cfg, batch, calls):
+    from .encoder import WhisperEncoderB200, synthetic_mel, synthetic_weights
+    w = {k: v.cuda() for k, v in synthetic_weights(cfg, seed=1).items()}
+    mel = synthetic_mel(cfg, batch, seed=2).cuda()
+    enc = WhisperEncoderB200(w, cfg, max_batch=batch)
+    for _ in range(calls):
+        enc(mel)
+
+
+def encoder_tiny_b1():
+    """Whisper-tiny encoder (4 layers, width 384) on one utterance, two calls."""
+    from .encoder import TINY
+    _encoder(TINY, 1, 2)
+
+
+def encoder_large_b16():
+    """Whisper-large-v3-shaped encoder (32 layers, width 1280) on 16 utterances, two calls."""
+    from .encoder import LARGE_V3
+    _encoder(LARGE_V3, 16, 2)
+
+
 CASES = {"readout-q4-b32": readout_q4_b32, "decode-step-b32": decode_step_b32,
-         "gemm-q8-8192x5120x1280": gemm_q8_8192x5120x1280}
+         "gemm-q8-8192x5120x1280": gemm_q8_8192x5120x1280, "encoder-tiny-b1": encoder_tiny_b1,
+         "encoder-large-b16": encoder_large_b16}
 
 
 def main(argv):

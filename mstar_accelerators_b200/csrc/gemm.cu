@@ -8,14 +8,15 @@
 // reorder + fp16-rounding tolerance (the decode GEMV keeps the exact integer
 // path).
 //
-// Kernel: persistent (one CTA per SM walking 128 x 256 output tiles), 6 warps:
+// Kernel: persistent (one CTA per SM walking 128 x 256 output tiles), 10 warps:
 //   warp 0  TMA producer: 2-D tiled bulk tensor copies (128B swizzle) of the
 //           A (128 x 64) and B (256 x 64) K-slices into a 4-stage ring;
 //   warp 1  allocates 512 TMEM columns (two fp32 accumulators of 256 columns);
 //           one thread issues tcgen05.mma kind::f16 (M=128, N=256, K=16) into
 //           the free accumulator, commits each stage back to the producer and
 //           each finished tile to the epilogue;
-//   warps 2-5 epilogue: tcgen05.ld 32x32b.x32 from their TMEM lane quarter
+//   warps 2-9 epilogue: two warps per TMEM lane quarter (warp % 4), each
+//           taking half of the 256 columns: tcgen05.ld 32x32b.x32
 //           (one thread = one row x 32 columns = one Q8_0 block), bias / GELU /
 //           residual, then fp32 or fp16 stores, or the block's Q8_0
 //           quantization stored as fp16(q * d) (the next GEMM's staged A
@@ -36,7 +37,8 @@ constexpr int GEMM_BM = 128, GEMM_BN = 256, GEMM_BK = 64, GEMM_STAGES = 4;
 constexpr int GEMM_A_BYTES = GEMM_BM * GEMM_BK * 2;
 constexpr int GEMM_B_BYTES = GEMM_BN * GEMM_BK * 2;
 constexpr int GEMM_STAGE_BYTES = GEMM_A_BYTES + GEMM_B_BYTES;
-constexpr int GEMM_THREADS = 192;
+constexpr int GEMM_EPI_WARPS = 8;  // two warps per TMEM lane quarter, each owning half the columns
+constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 constexpr int GEMM_GROUP_M = 8;
 constexpr uint32_t GEMM_TMEM_COLS = 512;  // two 256-column fp32 accumulators
 // instruction descriptor: D f32 (bits 4-5 = 1), A/B f16 (0), K-major A and B,
@@ -51,7 +53,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     uint64_t *full = reinterpret_cast<uint64_t *>(base + GEMM_STAGES * GEMM_STAGE_BYTES);
     uint64_t *empty = full + GEMM_STAGES;
     uint64_t *acc_full = empty + GEMM_STAGES;   // [2] MMA -> epilogue
-    uint64_t *acc_empty = acc_full + 2;         // [2] epilogue -> MMA (4 warp arrivals)
+    uint64_t *acc_empty = acc_full + 2;         // [2] epilogue -> MMA (one arrival per epilogue warp)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
     __shared__ int failed;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -78,7 +80,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(acc_full + b, 1);
-            mbar_init(acc_empty + b, 4);
+            mbar_init(acc_empty + b, GEMM_EPI_WARPS);
         }
         fence_mbar_init();
     }
@@ -143,6 +145,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
     } else {
         const int q = warp & 3;  // TMEM lane quarter this warp may read
+        const int c0 = ((warp - 2) / 4) * (GEMM_BN / 32 / (GEMM_EPI_WARPS / 4));  // first 32-column chunk it owns
         int64_t local = 0;
         for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
             const int buf = int(local & 1);
@@ -156,7 +159,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const int64_t row = m0 + 32 * q + lane;
             const int64_t orow_i = a.seg_rows ? (row / a.seg_rows) * a.out_seg_rows + row % a.seg_rows : row;
             const int64_t rrow_i = a.res_period ? row % a.res_period : row;
-            for (int c = 0; c < GEMM_BN / 32; ++c) {
+            for (int c = c0; c < c0 + GEMM_BN / 32 / (GEMM_EPI_WARPS / 4); ++c) {
                 uint32_t r[32];
                 tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(buf * GEMM_BN + c * 32), r);
                 if (row < a.M) {

@@ -1,13 +1,14 @@
 // Operand staging for the tcgen05 GEMM of the encoder graph
-// (backends/cpu_ggml/encoder.cpp:400-754), one warp per 32-element Q8_0 block:
-//   k_stage_rows  fp32 or fp16 rows [-> LayerNorm] -> Q8_0 -> fp16(q * d): the
+// (backends/cpu_ggml/encoder.cpp:400-754):
+//   k_stage_rows  (a warp per row, 16-byte vector loads, a Q8_0 block per 8 lanes)
+//                 fp32 or fp16 rows [-> LayerNorm] -> Q8_0 -> fp16(q * d): the
 //                 activation side of ggml_mul_mat(Q8_0 W, x) after
 //                 encoder_norm_affine (encoder.cpp:117-142) or on the fp32
 //                 attention output;
-//   k_stage_conv  the im2col columns of convolution_q8 (encoder.cpp:45-52: kernel
+//   k_stage_conv  (a warp per Q8_0 block) the im2col columns of convolution_q8 (encoder.cpp:45-52: kernel
 //                 3, padding 1, column = channel * 3 + tap, K zero-padded to a
 //                 multiple of 32, encoder.cpp:551) quantized the same way;
-//   k_layer_norm  the final encoder_norm_affine to fp32 (encoder.cpp:733).
+//   k_layer_norm  the final encoder_norm_affine to fp32 (encoder.cpp:725).
 // Q8_0 quantization follows ggml quantize_row_q8_0 with the selected rounding
 // (ref / ARM / x86); a nonfinite input sets status bit value 1.
 #include <cmath>
@@ -35,42 +36,89 @@ __device__ __forceinline__ float q8_staged(float v, int *status) {
     return __fmul_rn(float(q), __half2float(__float2half_rn(d)));
 }
 
+// Vectorised row staging: lane l of a warp owns the 4 consecutive elements of
+// chunk c = i * 32 + l, so one Q8_0 block is 8 consecutive lanes and every
+// load / store instruction of the warp covers 128 contiguous elements.
 template <bool F16>
-__device__ __forceinline__ float load_elem(const void *x, int64_t i) {
-    if (F16) return __half2float(static_cast<const __half *>(x)[i]);
-    return static_cast<const float *>(x)[i];
+__device__ __forceinline__ float4 load4(const void *x, int64_t e) {
+    if (F16) {
+        const uint2 u = *reinterpret_cast<const uint2 *>(static_cast<const __half *>(x) + e);
+        __half2 lo, hi;
+        memcpy(&lo, &u.x, 4);
+        memcpy(&hi, &u.y, 4);
+        const float2 a = __half22float2(lo), b = __half22float2(hi);
+        return make_float4(a.x, a.y, b.x, b.y);
+    }
+    return *reinterpret_cast<const float4 *>(static_cast<const float *>(x) + e);
 }
+
+__device__ __forceinline__ void store4(__half *out, int64_t e, float4 v) {
+    uint2 u;
+    u.x = half2_bits(__floats2half2_rn(v.x, v.y));
+    u.y = half2_bits(__floats2half2_rn(v.z, v.w));
+    *reinterpret_cast<uint2 *>(out + e) = u;
+}
+
+// Q8_0 quantization (ggml quantize_row_q8_0, rounding MODE) of the block held by
+// 8 consecutive lanes, 4 values each; returns fp16-exact q * fp16(d) as fp32.
+template <int MODE>
+__device__ __forceinline__ float4 q8_block8(float4 v, int *status) {
+    if (!(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w)) && status) atomicOr(status, 1);
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 127.0f);
+    float id;
+    if (MODE == 2) id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+    else id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float dh = __half2float(__float2half_rn(d));
+    auto q = [&](float x) {
+        const float sv = __fmul_rn(x, id);
+        return __fmul_rn(float(MODE == 0 ? int(roundf(sv)) : __float2int_rn(sv)), dh);
+    };
+    return make_float4(q(v.x), q(v.y), q(v.z), q(v.w));
+}
+
+constexpr int STAGE_MAX_CHUNKS = STAGE_MAX_PER_LANE / 4;  // float4 chunks a lane keeps for a LayerNorm row
+constexpr int STAGE_BATCH = 4;                            // chunk rows in flight per lane without LayerNorm
 
 // ggml_compute_forward_norm_f32 (ggml-cpu/ops.cpp:4094-4137): mean, centred
 // variance, y = (x - mean) * (1 / sqrt(var + eps)); then ggml mul and add.
 // The sums are warp-reduced (the reference sums sequentially), so the
 // normalised value can differ in the last ulp.
 template <bool F16>
-__device__ __forceinline__ void row_stats(const void *x, int64_t base, int64_t k, float eps, float (&vals)[STAGE_MAX_PER_LANE],
-                                          float &mean, float &rstd) {
+__device__ __forceinline__ void row_stats4(const void *x, int64_t base, int64_t chunks, float eps,
+                                           float4 (&vals)[STAGE_MAX_CHUNKS], float &mean, float &rstd) {
     const int lane = threadIdx.x & 31;
     float sum = 0.0f;
 #pragma unroll
-    for (int i = 0; i < STAGE_MAX_PER_LANE; ++i) {
-        const int64_t e = int64_t(i) * 32 + lane;
-        vals[i] = e < k ? load_elem<F16>(x, base + e) : 0.0f;
-        sum += vals[i];
+    for (int i = 0; i < STAGE_MAX_CHUNKS; ++i) {
+        const int64_t c = int64_t(i) * 32 + lane;
+        vals[i] = c < chunks ? load4<F16>(x, base + 4 * c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        sum = __fadd_rn(sum, __fadd_rn(__fadd_rn(vals[i].x, vals[i].y), __fadd_rn(vals[i].z, vals[i].w)));
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    mean = sum / float(k);
+    const float k = float(chunks * 4);
+    mean = sum / k;
     float var = 0.0f;
 #pragma unroll
-    for (int i = 0; i < STAGE_MAX_PER_LANE; ++i) {
-        const int64_t e = int64_t(i) * 32 + lane;
-        if (e < k) {
-            const float y = __fsub_rn(vals[i], mean);
-            var = __fadd_rn(var, __fmul_rn(y, y));
+    for (int i = 0; i < STAGE_MAX_CHUNKS; ++i) {
+        const int64_t c = int64_t(i) * 32 + lane;
+        if (c < chunks) {
+            const float a = __fsub_rn(vals[i].x, mean), b = __fsub_rn(vals[i].y, mean);
+            const float e = __fsub_rn(vals[i].z, mean), f = __fsub_rn(vals[i].w, mean);
+            var = __fadd_rn(var, __fadd_rn(__fadd_rn(__fmul_rn(a, a), __fmul_rn(b, b)),
+                                           __fadd_rn(__fmul_rn(e, e), __fmul_rn(f, f))));
         }
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
-    rstd = 1.0f / sqrtf(var / float(k) + eps);
+    rstd = 1.0f / sqrtf(var / k + eps);
+}
+
+__device__ __forceinline__ float norm_affine(float v, float mean, float rstd, float w, float b) {
+    return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, mean), rstd), w), b);
 }
 
 template <int MODE, bool F16, bool LN>
@@ -81,24 +129,45 @@ __global__ void __launch_bounds__(STAGE_WARPS * 32)
     const int lane = threadIdx.x & 31;
     const int64_t row = int64_t(blockIdx.x) * STAGE_WARPS + (threadIdx.x >> 5);
     if (row >= rows) return;
-    const int64_t nb = k / QK;
+    const int64_t chunks = k / 4;
     if (LN) {
-        float vals[STAGE_MAX_PER_LANE];
+        float4 vals[STAGE_MAX_CHUNKS];
         float mean, rstd;
-        row_stats<F16>(x, row * ldx, k, eps, vals, mean, rstd);
+        row_stats4<F16>(x, row * ldx, chunks, eps, vals, mean, rstd);
 #pragma unroll
-        for (int i = 0; i < STAGE_MAX_PER_LANE; ++i) {
-            if (i < nb) {
-                const int64_t e = int64_t(i) * 32 + lane;
-                const float v = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(vals[i], mean), rstd), __ldg(ln_w + e)),
-                                          __ldg(ln_b + e));
-                out[row * ldo + e] = __float2half_rn(q8_staged<MODE>(v, status));
+        for (int i = 0; i < STAGE_MAX_CHUNKS; ++i) {
+            if (int64_t(i) * 32 < chunks) {  // warp-uniform: every lane takes part in the block shuffles
+                const int64_t c = int64_t(i) * 32 + lane;
+                float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (c < chunks) {
+                    const float4 w = *reinterpret_cast<const float4 *>(ln_w + 4 * c);
+                    const float4 b = *reinterpret_cast<const float4 *>(ln_b + 4 * c);
+                    v = make_float4(norm_affine(vals[i].x, mean, rstd, w.x, b.x),
+                                    norm_affine(vals[i].y, mean, rstd, w.y, b.y),
+                                    norm_affine(vals[i].z, mean, rstd, w.z, b.z),
+                                    norm_affine(vals[i].w, mean, rstd, w.w, b.w));
+                }
+                v = q8_block8<MODE>(v, status);
+                if (c < chunks) store4(out, row * ldo + 4 * c, v);
             }
         }
     } else {
-        for (int64_t b = 0; b < nb; ++b) {
-            const int64_t e = b * 32 + lane;
-            out[row * ldo + e] = __float2half_rn(q8_staged<MODE>(load_elem<F16>(x, row * ldx + e), status));
+        const int64_t crow = (chunks + 31) / 32;
+        for (int64_t i0 = 0; i0 < crow; i0 += STAGE_BATCH) {
+            float4 v[STAGE_BATCH];
+#pragma unroll
+            for (int u = 0; u < STAGE_BATCH; ++u) {
+                const int64_t c = (i0 + u) * 32 + lane;
+                v[u] = c < chunks ? load4<F16>(x, row * ldx + 4 * c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int u = 0; u < STAGE_BATCH; ++u) {
+                if (i0 + u < crow) {
+                    const int64_t c = (i0 + u) * 32 + lane;
+                    const float4 q = q8_block8<MODE>(v[u], status);
+                    if (c < chunks) store4(out, row * ldo + 4 * c, q);
+                }
+            }
         }
     }
 }
@@ -129,15 +198,20 @@ __global__ void __launch_bounds__(STAGE_WARPS * 32)
     const int lane = threadIdx.x & 31;
     const int64_t row = int64_t(blockIdx.x) * STAGE_WARPS + (threadIdx.x >> 5);
     if (row >= rows) return;
-    float vals[STAGE_MAX_PER_LANE];
+    const int64_t chunks = k / 4;
+    float4 vals[STAGE_MAX_CHUNKS];
     float mean, rstd;
-    row_stats<false>(x, row * ldx, k, eps, vals, mean, rstd);
+    row_stats4<false>(x, row * ldx, chunks, eps, vals, mean, rstd);
 #pragma unroll
-    for (int i = 0; i < STAGE_MAX_PER_LANE; ++i) {
-        const int64_t e = int64_t(i) * 32 + lane;
-        if (e < k)
-            out[row * ldo + e] =
-                __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(vals[i], mean), rstd), __ldg(w + e)), __ldg(bias + e));
+    for (int i = 0; i < STAGE_MAX_CHUNKS; ++i) {
+        const int64_t c = int64_t(i) * 32 + lane;
+        if (c < chunks) {
+            const float4 g = *reinterpret_cast<const float4 *>(w + 4 * c);
+            const float4 b = *reinterpret_cast<const float4 *>(bias + 4 * c);
+            *reinterpret_cast<float4 *>(out + row * ldo + 4 * c) =
+                make_float4(norm_affine(vals[i].x, mean, rstd, g.x, b.x), norm_affine(vals[i].y, mean, rstd, g.y, b.y),
+                            norm_affine(vals[i].z, mean, rstd, g.z, b.z), norm_affine(vals[i].w, mean, rstd, g.w, b.w));
+        }
     }
 }
 
@@ -194,10 +268,12 @@ int mstar_b200_stage_rows(const void *x, int32_t x_format, int64_t x_stride, int
         require(rounding >= 0 && rounding <= 2, "unknown Q8_0 activation rounding");
         require(rows >= 1 && rows <= (int64_t(1) << 31) && width >= QK && width % QK == 0 && width <= 65536,
                 "invalid staging shape");
-        require(x_stride >= width, "invalid row stride");
+        require(x_stride >= width && x_stride % 4 == 0, "row stride must be a multiple of 4 elements");
+        require(uintptr_t(x) % (x_format == MSTAR_B200_ACT_F16 ? 8 : 16) == 0, "activation rows must be aligned");
         if (ln_weight) {
             require(ln_bias && std::isfinite(ln_eps) && ln_eps >= 0.0f, "invalid LayerNorm parameters");
             require(width <= int64_t(STAGE_MAX_PER_LANE) * 32, "LayerNorm rows are at most 1536 wide");
+            require(uintptr_t(ln_weight) % 16 == 0 && uintptr_t(ln_bias) % 16 == 0, "LayerNorm vectors must be 16-byte aligned");
             check_device(ln_weight, "LayerNorm weight");
             check_device(ln_bias, "LayerNorm bias");
         } else require(!ln_bias, "LayerNorm bias given without its weight");
@@ -258,10 +334,15 @@ int mstar_b200_layer_norm(const float *x, int64_t x_stride, int64_t rows, int64_
                           const float *bias, float eps, float *out, int64_t out_stride, void *stream, char *error,
                           size_t error_size) {
     try {
-        require(rows >= 1 && rows <= (int64_t(1) << 31) && width >= 1 && width <= int64_t(STAGE_MAX_PER_LANE) * 32,
-                "LayerNorm rows are 1..1536 wide");
-        require(x_stride >= width && out_stride >= width, "invalid row stride");
+        require(rows >= 1 && rows <= (int64_t(1) << 31) && width >= 4 && width % 4 == 0 &&
+                    width <= int64_t(STAGE_MAX_PER_LANE) * 32,
+                "LayerNorm rows are 4..1536 wide, a multiple of 4");
+        require(x_stride >= width && out_stride >= width && x_stride % 4 == 0 && out_stride % 4 == 0,
+                "row strides must be multiples of 4 elements");
         require(weight && bias && std::isfinite(eps) && eps >= 0.0f, "invalid LayerNorm parameters");
+        require(uintptr_t(x) % 16 == 0 && uintptr_t(out) % 16 == 0 && uintptr_t(weight) % 16 == 0 &&
+                    uintptr_t(bias) % 16 == 0,
+                "LayerNorm operands must be 16-byte aligned");
         const uint64_t xb = uint64_t((rows - 1) * x_stride + width) * 4;
         const uint64_t ob = uint64_t((rows - 1) * out_stride + width) * 4;
         check_range({x, xb}, xb, 4, "LayerNorm input");

@@ -3,14 +3,14 @@ encoder (backends/cpu_ggml/encoder.cpp:400-754) as a chain of tcgen05 GEMMs over
 staged Q8_0 operands.
 
 Per utterance (mel [mels, 2 * positions] fp32, channel-major like the
-reference's ``audio_features`` input, encoder.cpp:657):
+reference's ``audio_features`` input, encoder.cpp:642-643):
   conv1  im2col (kernel 3, pad 1) -> Q8_0 GEMM, K zero-padded to 32
          (convolution_q8, encoder.cpp:45-52, 551), + bias, ggml GELU (tanh table);
   conv2  the same over conv1's time-major output with stride 2, + bias, GELU,
-         + embed_positions (encoder.cpp:682) fused as a residual with period
+         + embed_positions (encoder.cpp:689) fused as a residual with period
          ``positions``;
   layer  LayerNorm fused into the Q8_0 staging of the fused QKV GEMM
-         (encoder.cpp:467-479, 686-689); its epilogue adds the q/k/v biases and
+         (encoder.cpp:467-479, 692-696); its epilogue adds the q/k/v biases and
          writes fp16 rows into per-utterance planes padded to 256 positions whose
          tail stays zero (qkv_scatter, encoder.cpp:202-234); attention over the
          padded keys, scale 1/sqrt(head_dim) (fused_attention, encoder.cpp:371-388);
@@ -19,7 +19,7 @@ reference's ``audio_features`` input, encoder.cpp:657):
          applies GELU and Q8_0-quantizes each 32-column block straight into fc2's
          staged operand (encoder_bias_gelu, encoder.cpp:91-112); fc2 + bias +
          residual in place;
-  final  LayerNorm to fp32 ``encoder_states`` (encoder.cpp:733).
+  final  LayerNorm to fp32 ``encoder_states`` (encoder.cpp:725).
 
 The GEMMs, staging, LayerNorm and epilogues are this library's kernels. The
 attention itself (outside the block-quantized path) is
@@ -123,7 +123,7 @@ class WhisperEncoderB200:
 
         def conv(name, channels, kp):
             w = W[name + ".weight"].reshape(d, 3 * channels)
-            if kp > 3 * channels:  # only the added K columns are zero (encoder.cpp:608-621)
+            if kp > 3 * channels:  # only the added K columns are zero (encoder.cpp:620-634)
                 w = torch.cat([w, torch.zeros((d, kp - 3 * channels), device=dev)], dim=1)
             lin = BlockLinear(w.contiguous(), bias=W[name + ".bias"])
             lin.prepare_gemm(64)
@@ -136,7 +136,8 @@ class WhisperEncoderB200:
         for i in range(cfg.layers):
             p = f"encoder.layers.{i}."
             qkv_w = torch.cat([W[p + f"self_attn.{n}_proj.weight"] for n in "qkv"], dim=0)
-            qkv_b = torch.cat([W[p + f"self_attn.{n}_proj.bias"] for n in "qkv"], dim=0)
+            # a checkpoint without a key bias (public Whisper) adds +0 (encoder.cpp:655-663)
+            qkv_b = torch.cat([W.get(p + f"self_attn.{n}_proj.bias", torch.zeros(d, device=dev)) for n in "qkv"], dim=0)
             layer = {
                 "ln1": (W[p + "self_attn_layer_norm.weight"], W[p + "self_attn_layer_norm.bias"], cfg.eps),
                 "ln2": (W[p + "final_layer_norm.weight"], W[p + "final_layer_norm.bias"], cfg.eps),
