@@ -19,7 +19,7 @@ INCLUDE = PACKAGE.parent / "include"
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
-    "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+    "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "-Xcompiler", "-ffp-contract=off",
     "--expt-relaxed-constexpr",
     "-Xptxas", "-warn-spills",
 ]

@@ -30,6 +30,7 @@ struct Linear {
     unsigned long long *keys = nullptr;
     unsigned int *done = nullptr;
     int wpg_override = 0;  // > 0 forces the split-K fold (tests)
+    const uint16_t *gelu = nullptr;  // ggml GELU table of the handle's device
     bool gemv_ok = true;   // the decode GEMV's shared-memory tile fits this width (K <= 4096)
     // tcgen05 GEMM state for calls with more than GEMM_MIN_QUERIES rows
     __half *w16 = nullptr;        // fp16(q * d) weights [rows][width]
@@ -179,6 +180,7 @@ void *mstar_b200_linear_create(int format, const void *blocks, uint64_t bytes, i
         h->groups = ceil_div(rows, 8);
         check_range({blocks, bytes}, uint64_t(rows) * h->nb * (h->q4 ? Q4_BYTES : Q8_BYTES), 1, "linear weights");
         h->gemv_ok = gemv_supported(h->nb_pad);
+        h->gelu = gelu_table();
         h->xf = device_alloc<uint32_t>(size_t(h->nb_pad * 2 * 32 * 4), "activation fragments");
         h->xs = device_alloc<float>(size_t(h->nb_pad * 32), "activation scales");
         h->xsum = device_alloc<int>(size_t(h->nb_pad * 32), "activation block sums");
@@ -267,6 +269,7 @@ int mstar_b200_linear_run(void *handle, const float *x, int64_t x_stride, int64_
             g.residual = (flags & 4) ? residual : nullptr;
             g.ldr = out_stride;
             g.flags = flags;
+            g.gelu = h.gelu;
             g.out_mode = GEMM_OUT_F32;
             g.rounding = rounding;
             g.status = h.status;
@@ -283,6 +286,7 @@ int mstar_b200_linear_run(void *handle, const float *x, int64_t x_stride, int64_
             a.bias = h.bias;
             a.residual = (flags & 4) ? residual + m0 * out_stride : nullptr;
             a.flags = flags;
+            a.gelu = h.gelu;
             a.wpg_override = h.wpg_override;
             launch_gemv(h.q4, a, s);
         }
@@ -473,6 +477,7 @@ int mstar_b200_linear_gemm(void *handle, const void *staged, uint64_t staged_byt
         g.seg_rows = segment_rows;
         g.out_seg_rows = out_segment_rows;
         g.flags = flags;
+        g.gelu = h.gelu;
         g.out_mode = out_format == MSTAR_B200_OUT_F32 ? GEMM_OUT_F32
                      : out_format == MSTAR_B200_OUT_F16 ? GEMM_OUT_F16 : GEMM_OUT_Q8;
         g.rounding = rounding;

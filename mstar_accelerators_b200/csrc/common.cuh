@@ -197,7 +197,6 @@ __device__ __forceinline__ void unpack_q4(uint32_t q, uint32_t &lo, uint32_t &hi
     hi = (q >> 4) & 0x0F0F0F0Fu;
 }
 
-// ggml stock GELU: tanh form evaluated on the fp16-rounded input, result
 // bits of a packed half2 (for 16-byte vector stores)
 __device__ __forceinline__ uint32_t half2_bits(__half2 h) {
     uint32_t u;
@@ -205,16 +204,27 @@ __device__ __forceinline__ uint32_t half2_bits(__half2 h) {
     return u;
 }
 
-// rounded to fp16 (ggml-cpu/vec.h:963-969, 1000-1013; table ggml-cpu.c:3889).
-__device__ __forceinline__ float gelu_ggml(float x) {
-    if (x <= -10.0f) return 0.0f;
-    if (x >= 10.0f) return x;
-    const float h = __half2float(__float2half_rn(x));
-    const float c = 0.79788456080286535587989211986876f, a = 0.044715f;
-    const float inner = __fmul_rn(__fmul_rn(c, h), __fadd_rn(1.0f, __fmul_rn(__fmul_rn(a, h), h)));
-    const float g = __fmul_rn(__fmul_rn(0.5f, h), __fadd_rn(1.0f, tanhf(inner)));
-    return __half2float(__float2half_rn(g));
+// ggml stock GELU (ggml-cpu/vec.h:963-969, 1000-1013): x <= -10 gives 0,
+// x >= 10 gives x, anything else the entry of ggml's fp16 table indexed by the
+// fp16 bits of x. The table (gelu.cu) is built on the host exactly as the CPU
+// backend builds its own at start-up (ggml-cpu.c:3889, with the host's tanhf),
+// restricted to the entries -10 < x < 10 can reach (|h| <= 10): entry
+// (bits & 0x7FFF) for +h, 0x4901 + (bits & 0x7FFF) for -h.
+constexpr uint32_t GELU_HALF_ENTRIES = 0x4901u;                  // fp16 magnitudes 0 .. 10.0
+constexpr int GELU_TABLE_ENTRIES = int(2 * GELU_HALF_ENTRIES);   // 37378 x 2 bytes
+constexpr size_t GELU_TABLE_BYTES = (size_t(GELU_TABLE_ENTRIES) * 2 + 15) / 16 * 16;
+
+__device__ __forceinline__ float gelu_ggml(float x, const uint16_t *table) {
+    const uint32_t bits = __half_as_ushort(__float2half_rn(x));
+    const uint32_t mag = min(bits & 0x7FFFu, GELU_HALF_ENTRIES - 1u);  // NaN and |x| >= 10 are decided below
+    const float t = __half2float(__ushort_as_half(table[mag + ((bits & 0x8000u) ? GELU_HALF_ENTRIES : 0u)]));
+    const float r = x <= -10.0f ? 0.0f : t;
+    return x >= 10.0f || x != x ? x : r;
 }
+
+// ggml's GELU table on the current device (built and uploaded on first use,
+// synchronises: call it outside stream capture).
+const uint16_t *gelu_table();
 
 // ggml_gelu_erf (ggml-cpu/vec.h:1024-1029).
 __device__ __forceinline__ float gelu_erf(float x) {

@@ -10,7 +10,9 @@
 //
 // Kernel: persistent (one CTA per SM walking 128 x 256 output tiles), 10 warps:
 //   warp 0  TMA producer: 2-D tiled bulk tensor copies (128B swizzle) of the
-//           A (128 x 64) and B (256 x 64) K-slices into a 4-stage ring;
+//           A (128 x 64) and B (256 x 64) K-slices into a 4-stage ring (3 stages
+//           when the epilogue applies GELU: the fourth stage's room holds
+//           ggml's fp16 GELU table);
 //   warp 1  allocates 512 TMEM columns (two fp32 accumulators of 256 columns);
 //           one thread issues tcgen05.mma kind::f16 (M=128, N=256, K=16) into
 //           the free accumulator, commits each stage back to the producer and
@@ -33,7 +35,7 @@
 
 namespace mb {
 
-constexpr int GEMM_BM = 128, GEMM_BN = 256, GEMM_BK = 64, GEMM_STAGES = 4;
+constexpr int GEMM_BM = 128, GEMM_BN = 256, GEMM_BK = 64;
 constexpr int GEMM_A_BYTES = GEMM_BM * GEMM_BK * 2;
 constexpr int GEMM_B_BYTES = GEMM_BN * GEMM_BK * 2;
 constexpr int GEMM_STAGE_BYTES = GEMM_A_BYTES + GEMM_B_BYTES;
@@ -44,8 +46,14 @@ constexpr uint32_t GEMM_TMEM_COLS = 512;  // two 256-column fp32 accumulators
 // instruction descriptor: D f32 (bits 4-5 = 1), A/B f16 (0), K-major A and B,
 // N >> 3 at bits 17-22, M >> 4 at bits 24-28
 constexpr uint32_t GEMM_IDESC = (1u << 4) | (uint32_t(GEMM_BN >> 3) << 17) | (uint32_t(GEMM_BM >> 4) << 24);
-constexpr size_t GEMM_SMEM = size_t(GEMM_STAGES) * GEMM_STAGE_BYTES + 1024 + 256;
+// Shared memory: the operand ring, then barriers, then (GELU variant) ggml's
+// GELU table; the GELU variant gives one ring stage to the table.
+template <int STAGES, bool GELU_TABLE>
+constexpr size_t gemm_smem_bytes() {
+    return size_t(STAGES) * GEMM_STAGE_BYTES + 1024 + 256 + (GELU_TABLE ? GELU_TABLE_BYTES : 0);
+}
 
+template <int GEMM_STAGES, bool GELU_TABLE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_f16(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const GemmArgs a) {
     extern __shared__ __align__(1024) unsigned char gemm_smem[];
@@ -55,8 +63,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     uint64_t *acc_full = empty + GEMM_STAGES;   // [2] MMA -> epilogue
     uint64_t *acc_empty = acc_full + 2;         // [2] epilogue -> MMA (one arrival per epilogue warp)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    uint16_t *gelu_smem = reinterpret_cast<uint16_t *>(base + GEMM_STAGES * GEMM_STAGE_BYTES + 256);
     __shared__ int failed;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (GELU_TABLE)
+        for (int i = threadIdx.x; i < int(GELU_TABLE_BYTES / 16); i += blockDim.x)
+            reinterpret_cast<uint4 *>(gelu_smem)[i] = __ldg(reinterpret_cast<const uint4 *>(a.gelu) + i);
     const int kt = int((a.K + GEMM_BK - 1) / GEMM_BK);
     const int64_t tiles_n = (a.N + GEMM_BN - 1) / GEMM_BN, tiles_m = (a.M + GEMM_BM - 1) / GEMM_BM;
     const int64_t tiles = tiles_n * tiles_m;
@@ -178,9 +190,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                                 v[j + 2] = __fadd_rn(v[j + 2], bb.z); v[j + 3] = __fadd_rn(v[j + 3], bb.w);
                             }
                         }
-                        if (a.flags & 2) {
+                        if (GELU_TABLE && (a.flags & 2)) {
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) v[j] = gelu_ggml(v[j]);
+                            for (int j = 0; j < 32; ++j) v[j] = gelu_ggml(v[j], gelu_smem);
                         } else if (a.flags & 8) {
 #pragma unroll
                             for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
@@ -253,7 +265,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                             if (n < a.N) {
                                 float v = __uint_as_float(r[j]);
                                 if (a.flags & 1) v = __fadd_rn(v, a.bias[n]);
-                                if (a.flags & 2) v = gelu_ggml(v);
+                                if (GELU_TABLE && (a.flags & 2)) v = gelu_ggml(v, gelu_smem);
                                 else if (a.flags & 8) v = gelu_erf(v);
                                 if (a.flags & 4) v = __fadd_rn(rrow[n], v);
                                 if (a.out_mode == GEMM_OUT_F32) static_cast<float *>(a.out)[orow_i * a.ldo + n] = v;
@@ -360,7 +372,11 @@ void launch_dequant_act(int mode, const float *x, int64_t ldx, int64_t m, int64_
 void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &a, cudaStream_t s) {
     static bool configured = false;
     if (!configured) {
-        cuda_check(cudaFuncSetAttribute(k_gemm_f16, cudaFuncAttributeMaxDynamicSharedMemorySize, int(GEMM_SMEM)),
+        cuda_check(cudaFuncSetAttribute(k_gemm_f16<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(gemm_smem_bytes<4, false>())),
+                   "GEMM shared-memory attribute");
+        cuda_check(cudaFuncSetAttribute(k_gemm_f16<3, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(gemm_smem_bytes<3, true>())),
                    "GEMM shared-memory attribute");
         configured = true;
     }
@@ -373,7 +389,8 @@ void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &a
     }
     const int64_t tiles = ceil_div(a.N, GEMM_BN) * ceil_div(a.M, GEMM_BM);
     const unsigned grid = unsigned(tiles < sms ? tiles : sms);  // persistent: one CTA per SM
-    k_gemm_f16<<<grid, GEMM_THREADS, GEMM_SMEM, s>>>(ta, tb, a);
+    if (a.flags & 2) k_gemm_f16<3, true><<<grid, GEMM_THREADS, gemm_smem_bytes<3, true>(), s>>>(ta, tb, a);
+    else k_gemm_f16<4, false><<<grid, GEMM_THREADS, gemm_smem_bytes<4, false>(), s>>>(ta, tb, a);
 }
 
 }  // namespace mb

@@ -16,6 +16,7 @@ struct GemmArgs {
     int64_t seg_rows;       // > 0: output row = (row / seg_rows) * out_seg_rows + row % seg_rows
     int64_t out_seg_rows;
     int flags;              // MSTAR_B200_BIAS / GELU / RESIDUAL / GELU_ERF
+    const uint16_t *gelu;   // ggml GELU table (gelu_table()), copied to shared memory with the GELU flag
     int out_mode;           // GEMM_OUT_F32 / GEMM_OUT_F16 / GEMM_OUT_Q8
     int rounding;           // Q8_0 rounding of GEMM_OUT_Q8
     int *status;            // bit value 2: a bounded pipeline wait timed out; 1: nonfinite Q8_0 input

@@ -57,7 +57,7 @@ __device__ __forceinline__ void stage_activations(const GemvArgs &a, GemvSmem &s
 template <bool READOUT>
 __device__ __forceinline__ float finish(const GemvArgs &a, int m, int64_t n, float v) {
     if (a.flags & 1) v = __fadd_rn(v, __ldg(a.bias + n));
-    if (a.flags & 2) v = gelu_ggml(v);
+    if (a.flags & 2) v = gelu_ggml(v, a.gelu);
     else if (a.flags & 8) v = gelu_erf(v);
     if (a.flags & 4) v = __fadd_rn(a.residual[m * a.ldo + n], v);
     if (READOUT) {
@@ -133,7 +133,8 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(const GemvArgs a) {
         gstride = 1;
         c_begin = warp * cpw < chunks ? warp * cpw : chunks;
         c_len = (c_begin + cpw < chunks ? c_begin + cpw : chunks) - c_begin;
-        ngroups = G0 < a.groups ? 1 : 0;
+        // a warp left without chunks (chunks not a multiple of cpw) loads nothing
+        ngroups = G0 < a.groups && c_len > 0 ? 1 : 0;
     } else {
         G0 = int64_t(blockIdx.x) * GEMV_WARPS + warp;
         gstride = int64_t(gridDim.x) * GEMV_WARPS;

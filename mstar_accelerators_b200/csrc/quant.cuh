@@ -30,6 +30,7 @@ struct GemvArgs {
     const float *bias;     // [n] or null
     const float *residual; // [m][ldo] or null
     int flags;
+    const uint16_t *gelu;  // ggml GELU table (gelu_table()), needed with the GELU flag
     int32_t *sums;         // debug: [m][n][nb] exact block sums, or null
     // fused readout (argmax) state; keys == null disables it
     unsigned long long *keys;  // [32] running per-token maxima, all zero between calls
