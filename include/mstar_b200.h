@@ -130,14 +130,14 @@ MSTAR_B200_API int mstar_b200_linear_prepare_gemm(void *handle, const void *bloc
 /* The prepared GEMM on an operand that is already staged: staged = fp16(q * d)
  * [rows][width] of the Q8_0-quantized activations (from mstar_b200_stage_rows,
  * mstar_b200_stage_conv or a previous call's STAGED output; 16-byte aligned),
- * so a chain of encoder linears (encoder.cpp:694-733) never materialises its
+ * so a chain of encoder linears (encoder.cpp:692-725) never materialises its
  * fp32 activations. Output element (r, n) goes to out row
  *   o(r) = segment_rows ? (r / segment_rows) * out_segment_rows + r % segment_rows : r
  * (a per-utterance padded plane such as the F16 K/V rows padded to 256 of
  * qkv_scatter, encoder.cpp:202-234, when out_segment_rows > segment_rows), in
  * out_format, after the flagged epilogue (bias, GELU, then + residual row
  * residual_period ? r % residual_period : r, stride residual_stride: the
- * positional table of encoder.cpp:682 repeats per utterance). Pass status
+ * positional table of encoder.cpp:689 repeats per utterance). Pass status
  * (device int32): bit value 1 nonfinite STAGED input, 2 a bounded wait timed out.
  * rows may exceed the capacity given to prepare_gemm (no handle buffer is used). */
 MSTAR_B200_API int mstar_b200_linear_gemm(void *handle, const void *staged, uint64_t staged_bytes, int64_t rows,
@@ -177,7 +177,9 @@ MSTAR_B200_API void *mstar_b200_moe_create(int32_t format, const void *w1, uint6
  * the bf16 rounding points of gate_up_vector / down_vector_reduce
  * (thinker_moe.py:17-83) and the slot-ordered fp32 sum (:75-81). Q8_0 format:
  * x and mid are Q8_0-quantized (rounding) before each contraction. Status bit
- * value 4: an expert id outside [0, E); value 2: a bounded wait timed out. */
+ * value 4: an expert id outside [0, E) (that slot contributes nothing, the
+ * skip_invalid behaviour of the reference backends); value 2: a bounded wait
+ * timed out. */
 MSTAR_B200_API int mstar_b200_moe_run(void *handle, const void *x, int64_t tokens,
     const float *topk_weights, const int32_t *topk_ids, void *out, int32_t *status, int32_t rounding,
     void *stream, char *error, size_t error_size);
@@ -204,7 +206,7 @@ MSTAR_B200_API int mstar_b200_stage_conv(const float *source, int32_t time_major
     int64_t channels, int64_t time_in, int32_t stride, int64_t k_padded, void *staged, uint64_t staged_bytes,
     int32_t rounding, int32_t *status, void *stream, char *error, size_t error_size);
 /* layer_norm: fp32 rows -> ggml_norm(eps), mul, add (the final encoder_norm_affine,
- * encoder.cpp:733) -> fp32 out; width <= 1536. */
+ * encoder.cpp:725) -> fp32 out; width <= 1536. */
 MSTAR_B200_API int mstar_b200_layer_norm(const float *x, int64_t x_stride, int64_t rows, int64_t width,
     const float *weight, const float *bias, float eps, float *out, int64_t out_stride, void *stream,
     char *error, size_t error_size);

@@ -174,8 +174,9 @@ struct MoePlan {
     int *cursor;      // [E]
     int *tiles;       // [max_tiles][3]: expert, row_start, row_end (permuted rows)
     int *num_tiles;   // [1]
-    int *perm;        // [P] permuted position -> pair (token * k + slot)
-    int *inv;         // [P] pair -> permuted position
+    int *perm;        // [P] permuted position -> pair (token * k + slot); valid below *valid
+    int *inv;         // [P] pair -> permuted position, -1 for a pair with an expert id outside [0, E)
+    int *valid;       // [1] pairs with a valid expert id (the permuted rows in use)
 };
 
 __global__ void k_moe_count(const int32_t *__restrict__ ids, int P, int E, int *__restrict__ counts,
@@ -213,6 +214,7 @@ __global__ void k_moe_plan(MoePlan p, int E, int max_tiles) {
             off += cnt[e];
         }
         *p.num_tiles = tiles;
+        *p.valid = off;
     }
 }
 
@@ -220,7 +222,10 @@ __global__ void k_moe_scatter(const int32_t *__restrict__ ids, int P, int E, Moe
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= P) return;
     const int e = ids[i];
-    if (e < 0 || e >= E) return;
+    if (e < 0 || e >= E) {  // contributes nothing (status bit value 4 is already set)
+        p.inv[i] = -1;
+        return;
+    }
     const int pos = p.offsets[e] + atomicAdd(p.cursor + e, 1);
     p.perm[pos] = i;
     p.inv[i] = pos;
@@ -228,10 +233,11 @@ __global__ void k_moe_scatter(const int32_t *__restrict__ ids, int P, int E, Moe
 
 // permuted activation rows: row pos <- x[perm[pos] / k]
 // q8: quantize each 32-block (selected rounding) of fp32(x) and store fp16(q * d)
-__global__ void k_moe_gather(const __nv_bfloat16 *__restrict__ x, const int *__restrict__ perm, int P, int H, int topk,
-                             int q8, int rounding, void *__restrict__ xp) {
+__global__ void k_moe_gather(const __nv_bfloat16 *__restrict__ x, const int *__restrict__ perm,
+                             const int *__restrict__ valid, int P, int H, int topk, int q8, int rounding,
+                             void *__restrict__ xp) {
     const int pos = blockIdx.x;
-    if (pos >= P) return;
+    if (pos >= P || pos >= *valid) return;
     const int64_t t = perm[pos] / topk;
     const __nv_bfloat16 *src = x + t * H;
     if (!q8) {
@@ -265,7 +271,8 @@ __global__ void k_moe_combine(const __nv_bfloat16 *__restrict__ y, const int *__
     for (int s = 0; s < topk; ++s) rows[s] = inv[t * topk + s];
     for (int n = threadIdx.x; n < H; n += blockDim.x) {
         float acc = 0.0f;
-        for (int s = 0; s < topk; ++s) acc = __fadd_rn(acc, __bfloat162float(y[int64_t(rows[s]) * H + n]));
+        for (int s = 0; s < topk; ++s)
+            if (rows[s] >= 0) acc = __fadd_rn(acc, __bfloat162float(y[int64_t(rows[s]) * H + n]));
         out[int64_t(t) * H + n] = __float2bfloat16_rn(acc);
     }
 }
@@ -648,7 +655,7 @@ void *mstar_b200_moe_create(int32_t format, const void *w1, uint64_t w1_bytes, c
         cuda_check(cudaMalloc(&m->xp, size_t((P + MOE_BM) * H * 2)), "permuted activations");
         cuda_check(cudaMalloc(&m->mid, size_t((P + MOE_BM) * I * 2)), "intermediate");
         cuda_check(cudaMalloc(reinterpret_cast<void **>(&m->y), size_t(P * H * 2)), "expert outputs");
-        const int64_t ints = 3 * E + 3 * int64_t(m->max_tiles) + 1 + 2 * P;
+        const int64_t ints = 3 * E + 3 * int64_t(m->max_tiles) + 1 + 2 * P + 1;
         cuda_check(cudaMalloc(reinterpret_cast<void **>(&m->ibuf), size_t(ints * 4)), "plan buffers");
         cuda_check(cudaMalloc(reinterpret_cast<void **>(&m->status), 4), "status");
         cuda_check(cudaMemset(m->status, 0, 4), "status reset");
@@ -662,6 +669,8 @@ void *mstar_b200_moe_create(int32_t format, const void *w1, uint64_t w1_bytes, c
         m->plan.num_tiles = p + 3 * E + 3 * m->max_tiles;
         m->plan.perm = m->plan.num_tiles + 1;
         m->plan.inv = m->plan.perm + P;
+        m->plan.valid = m->plan.inv + P;
+        cuda_check(cudaMemset(m->ibuf, 0, size_t(ints * 4)), "plan reset");
         const int64_t n1 = E * 2 * I * H, n2 = E * H * I;
         k_moe_prep_w1<<<unsigned(ceil_div(n1, 256)), 256>>>(w1, m->q8, int(E), int(I), int(H), m->w1);
         k_moe_prep_w2<<<unsigned(ceil_div(n2, 256)), 256>>>(w2, m->q8, n2, int(I), m->w2);
@@ -705,7 +714,7 @@ int mstar_b200_moe_run(void *handle, const void *x, int64_t tokens, const float 
         k_moe_count<<<unsigned(ceil_div(P, 256)), 256, 0, s>>>(topk_ids, P, m.E, m.plan.counts, status);
         k_moe_plan<<<1, 256, 0, s>>>(m.plan, m.E, m.max_tiles);
         k_moe_scatter<<<unsigned(ceil_div(P, 256)), 256, 0, s>>>(topk_ids, P, m.E, m.plan);
-        k_moe_gather<<<unsigned(P), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), m.plan.perm, P, m.H, m.topk,
+        k_moe_gather<<<unsigned(P), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), m.plan.perm, m.plan.valid, P, m.H, m.topk,
                                                  m.q8, rounding, m.xp);
         MoeGemmArgs g{};
         g.tiles = m.plan.tiles;

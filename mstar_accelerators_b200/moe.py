@@ -96,3 +96,58 @@ class ThinkerMoEB200:
             self.close()
         except Exception:
             pass
+
+
+class ThinkerExpertsBackend:
+    """``experts_backend`` of one thinker MoE layer: the role SmallTokenThinkerMoE
+    plays on gfx942 (thinker_moe.py:104-188, installed by select_expert_kernels,
+    qwen3_omni/amd/moe.py:6-22), for every token count. Called like the
+    reference backends, ``backend(hidden_states, w1, w2, topk_weights, topk_ids,
+    *, skip_invalid=False)``, with the layer's own gate_up_proj [E, 2I, H] and
+    down_proj [E, H, I]; the B200 layout is prepared once from those tensors.
+    Calls with more than ``max_tokens`` rows run in row chunks (tokens are
+    independent). Ids outside [0, E) add nothing, with or without skip_invalid.
+    """
+
+    def __init__(self, w1: torch.Tensor, w2: torch.Tensor, *, top_k: int = 8, max_tokens: int = 2048):
+        self._weights = (w1.data_ptr(), w2.data_ptr())
+        self.max_tokens = max_tokens
+        self.moe = ThinkerMoEB200(w1.detach(), w2.detach(), fmt="bf16", top_k=top_k, max_tokens=max_tokens)
+
+    def __call__(self, hidden_states, w1, w2, topk_weights, topk_ids, *, skip_invalid=False):
+        if (w1.data_ptr(), w2.data_ptr()) != self._weights:
+            raise ValueError("this experts backend was prepared for other expert weights")
+        x = hidden_states.reshape(-1, hidden_states.shape[-1])
+        if x.shape[0] <= self.max_tokens:
+            return self.moe(x, topk_weights, topk_ids).view(hidden_states.shape)
+        out = torch.empty_like(x)
+        for t0 in range(0, x.shape[0], self.max_tokens):
+            t1 = min(t0 + self.max_tokens, x.shape[0])
+            self.moe(x[t0:t1], topk_weights[t0:t1], topk_ids[t0:t1], out=out[t0:t1])
+        return out.view(hidden_states.shape)
+
+    def close(self):
+        self.moe.close()
+
+
+def install_thinker_experts(module, *, experts: int = 128, intermediate: int = 768, hidden: int = 2048,
+                            top_k: int = 8, max_tokens: int = 2048) -> int:
+    """Give every thinker MoE layer under ``module`` (a child with an
+    ``experts_backend`` and ``experts.gate_up_proj`` [E, 2I, H] / ``experts.down_proj``
+    [E, H, I] of the thinker geometry, MoEProblem(128, 768, 2048, 8)) a
+    ThinkerExpertsBackend; returns how many were installed."""
+    count = 0
+    for child in module.modules():
+        if not hasattr(child, "experts_backend"):
+            continue
+        bank = getattr(child, "experts", None)
+        w1, w2 = getattr(bank, "gate_up_proj", None), getattr(bank, "down_proj", None)
+        if w1 is None or w2 is None:
+            continue
+        if tuple(w1.shape) != (experts, 2 * intermediate, hidden) or tuple(w2.shape) != (experts, hidden, intermediate):
+            continue
+        if w1.dtype != torch.bfloat16 or w2.dtype != torch.bfloat16 or w1.device.type != "cuda":
+            continue
+        child.experts_backend = ThinkerExpertsBackend(w1, w2, top_k=top_k, max_tokens=max_tokens)
+        count += 1
+    return count

@@ -74,12 +74,58 @@ def test_experts_match_oracle(fmt, geom, T):
     backend.close()
 
 
-def test_experts_reject_out_of_range_ids():
+def test_experts_skip_out_of_range_ids():
+    """An id outside [0, E) sets status bit value 4 and its slot adds nothing."""
     from mstar_accelerators_b200 import moe
     E, I, H, k, w1, w2, wr = make("small", 5)
     backend = moe.ThinkerMoEB200(w1.cuda(), w2.cuda(), fmt="bf16", top_k=k, max_tokens=8)
-    x = torch.randn((2, H)).to(torch.bfloat16).cuda()
-    ids = torch.tensor([[0, 1, 2, 3], [4, 5, 6, E]], dtype=torch.int32).cuda()
-    backend(x, torch.full((2, k), 0.25).cuda(), ids)
+    x = torch.randn((2, H), generator=torch.Generator().manual_seed(6)).to(torch.bfloat16)
+    ids = np.array([[0, 1, 2, 3], [4, 5, 6, E]], np.int32)
+    w = np.full((2, k), 0.25, np.float32)
+    out = backend(x.cuda(), torch.from_numpy(w).cuda(), torch.from_numpy(ids).cuda()).float().cpu().numpy()
     assert int(backend.status.cpu()[0]) & 4
+    w_skip = w.copy()
+    w_skip[1, 3] = 0.0  # the invalid slot contributes +0 (bf16(0 * y) = 0)
+    ids_skip = ids.copy()
+    ids_skip[1, 3] = 0
+    ref = M.experts_bf16(bf(x), bf(w1), bf(w2), w_skip, ids_skip)
+    scale = np.abs(ref).max()
+    assert np.abs(out - ref).max() <= 2e-2 * scale
     backend.close()
+
+
+def test_thinker_experts_backend_installs_and_chunks():
+    """install_thinker_experts swaps the experts_backend of thinker-shaped MoE
+    layers; the backend keeps the reference call signature and splits calls
+    larger than max_tokens into row chunks with identical results."""
+    from mstar_accelerators_b200 import moe
+    E, I, H, k, w1, w2, wr = make("thinker", 7)
+
+    class Bank(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.gate_up_proj = torch.nn.Parameter(w1.cuda(), requires_grad=False)
+            self.down_proj = torch.nn.Parameter(w2.cuda(), requires_grad=False)
+
+    class Layer(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.experts = Bank()
+            self.experts_backend = None
+
+    root = torch.nn.Sequential(Layer(), torch.nn.Linear(4, 4))
+    assert moe.install_thinker_experts(root, max_tokens=64) == 1
+    layer = root[0]
+    T = 150
+    x = torch.randn((T, H), generator=torch.Generator().manual_seed(8)).to(torch.bfloat16)
+    rw, rids, _ = M.route(bf(x), bf(wr), k)
+    args = (x.cuda(), layer.experts.gate_up_proj, layer.experts.down_proj, torch.from_numpy(rw).cuda(),
+            torch.from_numpy(rids).cuda())
+    chunked = layer.experts_backend(*args).float().cpu().numpy()
+    whole = moe.ThinkerMoEB200(w1.cuda(), w2.cuda(), top_k=k, max_tokens=T)
+    ref = whole(args[0], args[3], args[4]).float().cpu().numpy()
+    np.testing.assert_array_equal(chunked, ref)
+    with pytest.raises(ValueError):
+        layer.experts_backend(args[0], args[2], args[1], args[3], args[4])
+    whole.close()
+    layer.experts_backend.close()
