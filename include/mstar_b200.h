@@ -145,6 +145,18 @@ MSTAR_B200_API int mstar_b200_linear_gemm(void *handle, const void *staged, uint
     uint64_t residual_bytes, int64_t residual_stride, int64_t residual_period, int64_t segment_rows,
     int64_t out_segment_rows, int32_t flags, int32_t rounding, int32_t *status, void *stream, char *error,
     size_t error_size);
+/* Row-parallel partial product for tensor parallelism (the K-sharded fc2 / out
+ * projection of accelerations/whisper/cpu_tp2/decoder_all_reduce.py:64-90): the
+ * prepared GEMM on this rank's staged operand (its K shard), fp32, no bias;
+ * activation row r is stored by the epilogue straight into
+ * peer_out[r / owner_rows] (a device array of `world` device pointers, peers'
+ * receive buffers mapped into this process, e.g. symmetric memory) at row
+ * rank * owner_rows + r % owner_rows, stride out_stride floats: each rank's
+ * slot in the owner's [world][owner_rows][N] receive buffer. Peer pointers are
+ * not checked on the host. */
+MSTAR_B200_API int mstar_b200_linear_gemm_partial(void *handle, const void *staged, uint64_t staged_bytes,
+    int64_t rows, float *const *peer_out, int32_t world, int32_t rank, int64_t owner_rows, int64_t out_stride,
+    int32_t *status, void *stream, char *error, size_t error_size);
 /* Physical policy, set on an idle handle (the role of
  * cpu_decoder_set_cross_threads, decoder.h:44-47): warps that split one
  * 8-row group's K range (1, 2, 4 or 8; 0 restores the automatic choice).
@@ -184,6 +196,14 @@ MSTAR_B200_API int mstar_b200_moe_run(void *handle, const void *x, int64_t token
     const float *topk_weights, const int32_t *topk_ids, void *out, int32_t *status, int32_t rounding,
     void *stream, char *error, size_t error_size);
 MSTAR_B200_API int mstar_b200_moe_close(void *handle, char *error, size_t error_size);
+/* Slot-ordered combine of expert outputs gathered by the caller (expert
+ * parallelism: rows returned by their owners, moe_sum_reduce of
+ * thinker_moe.py:75-81): out[t] = bf16(sum_s fp32(y[rows[t*top_k + s]])) in slot
+ * order; y bf16 [y_rows][hidden], rows int32 (a row outside [0, y_rows) adds
+ * nothing), out bf16 [tokens][hidden]. */
+MSTAR_B200_API int mstar_b200_moe_combine(const void *y, int64_t y_rows, const int32_t *rows, int64_t tokens,
+    int32_t top_k, int64_t hidden, void *out, void *stream, char *error, size_t error_size);
+
 
 /* --- encoder graph staging (backends/cpu_ggml/encoder.cpp:400-754) ------------------
  * stage_rows: rows of x (fp32 or fp16, stride x_stride elements), optionally
@@ -210,6 +230,28 @@ MSTAR_B200_API int mstar_b200_stage_conv(const float *source, int32_t time_major
 MSTAR_B200_API int mstar_b200_layer_norm(const float *x, int64_t x_stride, int64_t rows, int64_t width,
     const float *weight, const float *bias, float eps, float *out, int64_t out_stride, void *stream,
     char *error, size_t error_size);
+
+/* --- tensor parallelism over peer memory (accelerations/whisper/cpu_tp2/decoder_all_reduce.py:64-90) ---
+ * tp_barrier: the rank's device counter is incremented to g; every rank then
+ * stores g into flag_ptrs[p][rank] for all p (system-scope release after a
+ * system fence) and waits until my_flags[p] >= g for every p (acquire,
+ * bounded: on timeout status bit value 16). flag_ptrs: device array of `world`
+ * pointers to each rank's int32[world] flags; flags and counters are zero
+ * before the first barrier and every rank calls the barrier equally often
+ * (the counter lives on the device, so a captured graph replays correctly).
+ * tp_reduce: for this owner's `owned` rows: x = x + (sum over the `world`
+ * partial slots of recv [world][owner_rows][width] in rank order + bias)
+ * (encoder_bias_residual order, encoder.cpp:146-166), in place; with
+ * ln_weight, the new rows are also LayerNorm-ed, Q8_0-quantized (rounding) and
+ * stored as fp16(q * d) into every rank's staged operand staged_ptrs[p]
+ * ([M][width] fp16, rows row0 ..): the all-gather of the next
+ * column-parallel GEMM's input. width <= 1536. */
+MSTAR_B200_API int mstar_b200_tp_barrier(int32_t *const *flag_ptrs, int32_t *my_flags, int32_t rank, int32_t world,
+    int32_t *counter, int32_t *status, void *stream, char *error, size_t error_size);
+MSTAR_B200_API int mstar_b200_tp_reduce(const float *recv, int32_t world, int64_t owner_rows, int64_t owned,
+    int64_t width, const float *bias, float *x, const float *ln_weight, const float *ln_bias, float ln_eps,
+    void *const *staged_ptrs, int64_t row0, int32_t rounding, int32_t *status, void *stream, char *error,
+    size_t error_size);
 
 /* --- readout that allocates nothing ------------------------------------------------
  * No counterpart in the reference. For callers that cannot allocate device
@@ -239,16 +281,24 @@ MSTAR_B200_API int mstar_b200_embed(const float *token_table, int64_t vocab, con
     float scale, float *x, int32_t *status, void *stream, char *error, size_t error_size);
 /* Multi-head attention over fp16 K/V planes [seq][capacity][heads*64]
  * (ggml_flash_attn_ext, scale 1/sqrt(64), decoder.cpp:504-511). When k_new/v_new
- * are given, the `queries` new rows of each sequence are first written at
- * positions begin[b].. (ggml_set_rows, decoder.cpp:566-567) and attention is
- * causal up to each query's own position; otherwise every query sees
- * kv_length[b] keys. shared=1: every sequence reads plane 0 (one encoder state
- * for the whole batch). Bad positions/lengths set status bit 3 (value 8). */
+ * are given (causal, per-sequence planes), the `queries` new rows of each
+ * sequence are first written at positions begin[b].. (ggml_set_rows,
+ * decoder.cpp:566-567) and attention is causal up to each query's own
+ * position; otherwise every query sees kv_length[b] keys. shared=1: every
+ * sequence reads plane 0 (one encoder state for the whole batch), and all
+ * batch*queries rows (at most 128) are attended together against each K/V tile,
+ * with the keys split across CTAs (flash-decoding) whose partial results are
+ * kept in `workspace` and merged by a second kernel. workspace: device,
+ * 256-byte aligned, exactly mstar_b200_attend_workspace() bytes for the same
+ * geometry; calls sharing a workspace must be stream-ordered.
+ * Bad positions/lengths set status bit 3 (value 8) and zero those rows. */
+MSTAR_B200_API uint64_t mstar_b200_attend_workspace(int32_t heads, int32_t batch, int32_t queries,
+    int64_t capacity, int32_t shared);
 MSTAR_B200_API int mstar_b200_attend(const float *q, int64_t q_stride, const float *k_new, const float *v_new,
     int64_t kv_stride, void *k_plane, void *v_plane, int64_t capacity, int32_t heads, int32_t head_dim,
     int32_t batch, int32_t queries, const int64_t *begin, const int64_t *kv_length, int32_t causal,
-    int32_t shared, float *out, int64_t out_stride, float scale, int32_t *status, void *stream,
-    char *error, size_t error_size);
+    int32_t shared, float *out, int64_t out_stride, float scale, int32_t *status, void *workspace,
+    uint64_t workspace_bytes, void *stream, char *error, size_t error_size);
 /* Cross K/V planes from the fused projection of the encoder states
  * (decoder.cpp:247-250, 322-330: one [3072 x 384] Q8_0 matrix for the four
  * layers' k/v; biases added, then stored fp16 like cross_bias_set_rows). */

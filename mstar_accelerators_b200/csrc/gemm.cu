@@ -169,8 +169,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             int64_t m0, n0;
             tile_coords(tile, m0, n0);
             const int64_t row = m0 + 32 * q + lane;
-            const int64_t orow_i = a.seg_rows ? (row / a.seg_rows) * a.out_seg_rows + row % a.seg_rows : row;
+            int64_t orow_i = a.seg_rows ? (row / a.seg_rows) * a.out_seg_rows + row % a.seg_rows : row;
             const int64_t rrow_i = a.res_period ? row % a.res_period : row;
+            void *obase = a.out;
+            if (a.peers && row < a.M) {  // partial rows into the owning rank's receive slot (NVLink stores)
+                obase = a.peers[row / a.owner_rows];
+                orow_i = int64_t(a.rank) * a.owner_rows + row % a.owner_rows;
+            }
             for (int c = c0; c < c0 + GEMM_BN / 32 / (GEMM_EPI_WARPS / 4); ++c) {
                 uint32_t r[32];
                 tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(buf * GEMM_BN + c * 32), r);
@@ -211,7 +216,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                             }
                         }
                         if (a.out_mode == GEMM_OUT_F32) {
-                            float *o = static_cast<float *>(a.out) + orow_i * a.ldo + nc;
+                            float *o = static_cast<float *>(obase) + orow_i * a.ldo + nc;
                             if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
 #pragma unroll
                                 for (int j = 0; j < 32; j += 4)
@@ -241,7 +246,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                                     v[j] = __fmul_rn(float(qv), dh);
                                 }
                             }
-                            __half *o = static_cast<__half *>(a.out) + orow_i * a.ldo + nc;
+                            __half *o = static_cast<__half *>(obase) + orow_i * a.ldo + nc;
                             if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
 #pragma unroll
                                 for (int j = 0; j < 32; j += 8) {
@@ -268,8 +273,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                                 if (GELU_TABLE && (a.flags & 2)) v = gelu_ggml(v, gelu_smem);
                                 else if (a.flags & 8) v = gelu_erf(v);
                                 if (a.flags & 4) v = __fadd_rn(rrow[n], v);
-                                if (a.out_mode == GEMM_OUT_F32) static_cast<float *>(a.out)[orow_i * a.ldo + n] = v;
-                                else static_cast<__half *>(a.out)[orow_i * a.ldo + n] = __float2half_rn(v);
+                                if (a.out_mode == GEMM_OUT_F32) static_cast<float *>(obase)[orow_i * a.ldo + n] = v;
+                                else static_cast<__half *>(obase)[orow_i * a.ldo + n] = __float2half_rn(v);
                             }
                         }
                     }

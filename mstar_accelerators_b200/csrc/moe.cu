@@ -277,6 +277,23 @@ __global__ void k_moe_combine(const __nv_bfloat16 *__restrict__ y, const int *__
     }
 }
 
+// Same slot-ordered sum over caller-given rows (expert parallelism: the rows
+// come back from their owners in send order); a row outside [0, y_rows) adds
+// nothing.
+__global__ void k_moe_combine_rows(const __nv_bfloat16 *__restrict__ y, int64_t y_rows, const int *__restrict__ rows,
+                                   int T, int H, int topk, __nv_bfloat16 *__restrict__ out) {
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    int r[MOE_MAX_TOPK];
+    for (int s = 0; s < topk; ++s) r[s] = rows[int64_t(t) * topk + s];
+    for (int n = threadIdx.x; n < H; n += blockDim.x) {
+        float acc = 0.0f;
+        for (int s = 0; s < topk; ++s)
+            if (r[s] >= 0 && r[s] < y_rows) acc = __fadd_rn(acc, __bfloat162float(y[int64_t(r[s]) * H + n]));
+        out[int64_t(t) * H + n] = __float2bfloat16_rn(acc);
+    }
+}
+
 // ------------------------------------------------------------------ grouped GEMM
 struct MoeGemmArgs {
     const int *tiles;      // [num_tiles][3]
@@ -742,6 +759,28 @@ int mstar_b200_moe_run(void *handle, const void *x, int64_t tokens, const float 
         k_moe_combine<<<unsigned(tokens), 256, 0, s>>>(m.y, m.plan.inv, int(tokens), m.H, m.topk,
                                                         static_cast<__nv_bfloat16 *>(out));
         cuda_check(cudaGetLastError(), "MoE launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+int mstar_b200_moe_combine(const void *y, int64_t y_rows, const int32_t *rows, int64_t tokens, int32_t top_k,
+                           int64_t hidden, void *out, void *stream, char *error, size_t error_size) {
+    try {
+        require(y && rows && out, "missing combine operand");
+        require(tokens >= 1 && tokens <= (int64_t(1) << 24) && top_k >= 1 && top_k <= MOE_MAX_TOPK && hidden >= 1 &&
+                    hidden <= 65536 && y_rows >= 0 && y_rows <= (int64_t(1) << 31),
+                "invalid combine geometry");
+        check_device(y, "expert outputs");
+        check_device(rows, "slot rows");
+        check_device(out, "combined output");
+        cudaStream_t s = as_stream(stream);
+        k_moe_combine_rows<<<unsigned(tokens), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(y), y_rows, rows,
+                                                            int(tokens), int(hidden), top_k,
+                                                            static_cast<__nv_bfloat16 *>(out));
+        cuda_check(cudaGetLastError(), "combine launch");
         return 0;
     } catch (const std::exception &e) {
         message(error, error_size, e.what());

@@ -1,0 +1,127 @@
+"""Expert parallelism for the thinker MoE layer over torch.distributed (NCCL).
+
+Each of the W ranks holds experts [r*E/W, (r+1)*E/W) (16 of 128 at W = 8) and
+the full routing of its own tokens. One forward:
+
+  1. dispatch: the (token, slot) pairs are ordered by owning rank (stable, so
+     slot order inside a rank is kept); send counts are exchanged with one
+     all_to_all of W int64 and read on the host (the split sizes of the next
+     collectives); token rows (bf16), local expert ids and routing weights
+     travel with all_to_all_single;
+  2. every rank runs its local experts on the received pairs as a top-1 MoE
+     whose routing weight is the pair's weight, so each returned row is
+     y_s = bf16((mid . w_down) * w_s) exactly as in down_vector_reduce
+     (thinker_moe.py:51-83);
+  3. combine: the rows go back with the reversed splits and every token sums
+     its slots in slot order in fp32, then rounds to bf16 (moe_sum_reduce,
+     thinker_moe.py:75-81; mstar_b200_moe_combine).
+
+Results are therefore bit-identical to the single-GPU layer on the same
+inputs. Every rank takes the same collective steps in the same order, also
+with zero pairs for a peer. The local expert computation is a callable so the
+host logic is testable on CPU with gloo.
+"""
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+LocalExperts = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
+Combine = Callable[[torch.Tensor, torch.Tensor, int], torch.Tensor]
+
+
+def owned_experts(experts: int, world: int, rank: int) -> range:
+    if experts % world:
+        raise ValueError("experts must divide evenly over the ranks")
+    per = experts // world
+    return range(rank * per, (rank + 1) * per)
+
+
+class ExpertParallelMoE:
+    """One thinker MoE layer sharded by experts over ``group``."""
+
+    def __init__(self, local_experts: LocalExperts, combine: Combine, *, experts: int, top_k: int, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.experts, self.top_k = experts, top_k
+        self.owned = owned_experts(experts, self.world, self.rank)
+        self.local = local_experts
+        self.combine = combine
+
+    @classmethod
+    def b200(cls, w1: torch.Tensor, w2: torch.Tensor, *, experts: int, top_k: int = 8, group=None,
+             capacity: int = 8192) -> "ExpertParallelMoE":
+        """The B200 layer: w1 [E, 2I, H] / w2 [E, H, I] bf16 (the full layer, on this
+        rank's device); this rank keeps its experts. ``capacity`` bounds the pairs
+        one local launch takes (larger receptions run in chunks)."""
+        from . import native
+        from .moe import ThinkerMoEB200
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        own = owned_experts(experts, world, rank)
+        local = ThinkerMoEB200(w1[own.start:own.stop].contiguous(), w2[own.start:own.stop].contiguous(), fmt="bf16",
+                               top_k=1, max_tokens=capacity)
+        return cls(b200_local_experts(local, capacity), b200_combine(native.require_capability()), experts=experts,
+                   top_k=top_k, group=group)
+
+    def _exchange(self, send: torch.Tensor, send_counts: list[int], recv_counts: list[int]) -> torch.Tensor:
+        recv = send.new_empty((sum(recv_counts),) + tuple(send.shape[1:]))
+        dist.all_to_all_single(recv, send, output_split_sizes=recv_counts, input_split_sizes=send_counts,
+                               group=self.group)
+        return recv
+
+    def __call__(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
+        """x [T, H] bf16, topk_weights [T, k] fp32, topk_ids [T, k] -> [T, H] bf16."""
+        T, H = x.shape
+        k = self.top_k
+        per = self.experts // self.world
+        ids = topk_ids.reshape(-1).long()
+        if ids.numel() and (int(ids.min()) < 0 or int(ids.max()) >= self.experts):
+            raise ValueError("expert id outside [0, experts)")
+        dest = ids // per
+        order = torch.sort(dest, stable=True).indices          # send position -> pair index
+        counts = torch.bincount(dest, minlength=self.world)
+        recv_counts_t = torch.empty_like(counts)
+        dist.all_to_all_single(recv_counts_t, counts, group=self.group)
+        send_counts = counts.cpu().tolist()
+        recv_counts = recv_counts_t.cpu().tolist()
+        rows = x[order // k]
+        local_ids = (ids[order] - dest[order] * per).to(torch.int32)
+        weights = topk_weights.reshape(-1)[order].to(torch.float32)
+        r_rows = self._exchange(rows.contiguous(), send_counts, recv_counts)
+        r_ids = self._exchange(local_ids.contiguous(), send_counts, recv_counts)
+        r_w = self._exchange(weights.contiguous(), send_counts, recv_counts)
+        y_local = self.local(r_rows, r_w, r_ids)               # [received, H] bf16, one row per pair
+        y_back = self._exchange(y_local.contiguous(), recv_counts, send_counts)
+        inverse = torch.empty_like(order)
+        inverse[order] = torch.arange(order.numel(), device=order.device)
+        return self.combine(y_back, inverse.to(torch.int32), k)
+
+
+def b200_local_experts(moe, capacity: int) -> LocalExperts:
+    """Adapter: a top-1 ThinkerMoEB200 holding this rank's experts, run over the
+    received pairs (local expert id, routing weight) in chunks of ``capacity``."""
+    def run(rows, weights, ids):
+        out = rows.new_empty((rows.shape[0], rows.shape[1]))
+        for p0 in range(0, rows.shape[0], capacity):
+            p1 = min(p0 + capacity, rows.shape[0])
+            moe(rows[p0:p1], weights[p0:p1].view(-1, 1), ids[p0:p1].view(-1, 1), out=out[p0:p1])
+        return out
+    return run
+
+
+def b200_combine(lib) -> Combine:
+    from .linear import _stream
+    from .native import check, error_buffer
+
+    def run(y, rows, top_k):
+        T = rows.numel() // top_k
+        out = torch.empty((T, y.shape[1]), dtype=torch.bfloat16, device=rows.device)
+        e = error_buffer()
+        check(lib.mstar_b200_moe_combine(y.data_ptr() if y.numel() else rows.data_ptr(), y.shape[0],
+                                         rows.contiguous().data_ptr(), T, top_k, y.shape[1], out.data_ptr(),
+                                         _stream(rows.device), e, len(e)), e, "B200 MoE combine")
+        return out
+    return run

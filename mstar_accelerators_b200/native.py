@@ -45,6 +45,11 @@ SIGNATURES = {
     "mstar_b200_linear_prepare_gemm": (_int, [_vp, _vp, _u64, _i64, *_err]),
     "mstar_b200_linear_gemm": (_int, [_vp, _vp, _u64, _i64, _vp, _u64, _i64, C.c_int32, _vp, _u64, _i64, _i64, _i64,
                                       _i64, C.c_int32, C.c_int32, _vp, _vp, *_err]),
+    "mstar_b200_linear_gemm_partial": (_int, [_vp, _vp, _u64, _i64, _vp, C.c_int32, C.c_int32, _i64, _i64, _vp, _vp,
+                                              *_err]),
+    "mstar_b200_tp_barrier": (_int, [_vp, _vp, C.c_int32, C.c_int32, _vp, _vp, _vp, *_err]),
+    "mstar_b200_tp_reduce": (_int, [_vp, C.c_int32, _i64, _i64, _i64, _vp, _vp, _vp, _vp, C.c_float, _vp, _i64,
+                                    C.c_int32, _vp, _vp, *_err]),
     "mstar_b200_stage_rows": (_int, [_vp, C.c_int32, _i64, _i64, _i64, _vp, _vp, C.c_float, _vp, _u64, C.c_int32, _vp,
                                      _vp, *_err]),
     "mstar_b200_stage_conv": (_int, [_vp, C.c_int32, _i64, _i64, _i64, C.c_int32, _i64, _vp, _u64, C.c_int32, _vp, _vp,
@@ -52,8 +57,10 @@ SIGNATURES = {
     "mstar_b200_layer_norm": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, C.c_float, _vp, _i64, _vp, *_err]),
     "mstar_b200_q8_readout": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "mstar_b200_embed": (_int, [_vp, _i64, _vp, _i64, _i64, _vp, _vp, _i64, C.c_float, _vp, _vp, _vp, *_err]),
+    "mstar_b200_attend_workspace": (_u64, [C.c_int32, C.c_int32, C.c_int32, _i64, C.c_int32]),
     "mstar_b200_attend": (_int, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64, C.c_int32, C.c_int32, C.c_int32,
-                                 C.c_int32, _vp, _vp, C.c_int32, C.c_int32, _vp, _i64, C.c_float, _vp, _vp, *_err]),
+                                 C.c_int32, _vp, _vp, C.c_int32, C.c_int32, _vp, _i64, C.c_float, _vp, _vp, _u64,
+                                 _vp, *_err]),
     "mstar_b200_fill_kv": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _vp, *_err]),
     "mstar_b200_moe_route": (_int, [_vp, _i64, _i64, _vp, C.c_int32, C.c_int32, C.c_int32, _vp, _vp, _vp, _vp,
                                     *_err]),
@@ -61,6 +68,7 @@ SIGNATURES = {
                                     C.c_int32, *_err]),
     "mstar_b200_moe_run": (_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, C.c_int32, _vp, *_err]),
     "mstar_b200_moe_close": (_int, [_vp, *_err]),
+    "mstar_b200_moe_combine": (_int, [_vp, _i64, _vp, _i64, C.c_int32, _i64, _vp, _vp, *_err]),
     "mstar_b200_q8_readout_noalloc": (_int, [_vp, _sz, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
 }
 

@@ -143,6 +143,14 @@ class WhisperDecoderB200:
         self.cross_len = torch.full((B,), cfg.source, dtype=torch.int64, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self._bufs = {}
+        # split-attention workspaces per (queries, capacity, shared), zero-filled once
+        self._ws = {}
+        for nq in range(1, 5):
+            for cap, sh in ((cfg.target, False), (cfg.source, self.shared_cross)):
+                n = int(self.lib.mstar_b200_attend_workspace(cfg.heads, B, nq, cap, int(sh)))
+                if n == 0:
+                    raise ValueError("attention geometry outside the kernel's limits")
+                self._ws[(nq, cap, sh)] = torch.zeros(n, dtype=torch.uint8, device=dev)
 
     # ------------------------------------------------------------------ buffers
     def _buf(self, name, shape, dtype=torch.float32):
@@ -161,6 +169,7 @@ class WhisperDecoderB200:
               e, "B200 embedding")
 
     def _attend(self, q, q_stride, k_new, v_new, kv_stride, kp, vp, capacity, nq, begin, kv_len, causal, shared, out):
+        ws = self._ws[(nq, capacity, bool(shared))]
         e = error_buffer()
         check(self.lib.mstar_b200_attend(q.data_ptr(), q_stride, k_new.data_ptr() if k_new is not None else None,
                                          v_new.data_ptr() if v_new is not None else None, kv_stride,
@@ -168,7 +177,7 @@ class WhisperDecoderB200:
                                          begin.data_ptr() if begin is not None else None,
                                          kv_len.data_ptr() if kv_len is not None else None, int(causal), int(shared),
                                          out.data_ptr(), out.stride(0), 1.0 / math.sqrt(64), self.status.data_ptr(),
-                                         _stream(self.device), e, len(e)),
+                                         ws.data_ptr(), ws.numel(), _stream(self.device), e, len(e)),
               e, "B200 attention")
 
     def _body(self, x: torch.Tensor, nq: int, begin: torch.Tensor):
