@@ -312,7 +312,9 @@ def run_b200(args):
                    "sample": f"{n} decode steps of the 33 block-quantized linears (batch 32) through the "
                              "vendored ggml x86 kernels on the host cores; attention/LayerNorm excluded"}
         clk = clocks.summary()
-        launches_per_step = 1 + cfg.layers * 14 + 2
+        # embedding; per layer 6 linears (quantize + GEMV), self attention, cross attention (tiles + merge);
+        # readout (quantize + streamed GEMV with argmax)
+        launches_per_step = 1 + cfg.layers * (6 * 2 + 1 + 2) + 2
         line = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,

@@ -145,18 +145,6 @@ MSTAR_B200_API int mstar_b200_linear_gemm(void *handle, const void *staged, uint
     uint64_t residual_bytes, int64_t residual_stride, int64_t residual_period, int64_t segment_rows,
     int64_t out_segment_rows, int32_t flags, int32_t rounding, int32_t *status, void *stream, char *error,
     size_t error_size);
-/* Row-parallel partial product for tensor parallelism (the K-sharded fc2 / out
- * projection of accelerations/whisper/cpu_tp2/decoder_all_reduce.py:64-90): the
- * prepared GEMM on this rank's staged operand (its K shard), fp32, no bias;
- * activation row r is stored by the epilogue straight into
- * peer_out[r / owner_rows] (a device array of `world` device pointers, peers'
- * receive buffers mapped into this process, e.g. symmetric memory) at row
- * rank * owner_rows + r % owner_rows, stride out_stride floats: each rank's
- * slot in the owner's [world][owner_rows][N] receive buffer. Peer pointers are
- * not checked on the host. */
-MSTAR_B200_API int mstar_b200_linear_gemm_partial(void *handle, const void *staged, uint64_t staged_bytes,
-    int64_t rows, float *const *peer_out, int32_t world, int32_t rank, int64_t owner_rows, int64_t out_stride,
-    int32_t *status, void *stream, char *error, size_t error_size);
 /* Physical policy, set on an idle handle (the role of
  * cpu_decoder_set_cross_threads, decoder.h:44-47): warps that split one
  * 8-row group's K range (1, 2, 4 or 8; 0 restores the automatic choice).
@@ -239,16 +227,20 @@ MSTAR_B200_API int mstar_b200_layer_norm(const float *x, int64_t x_stride, int64
  * pointers to each rank's int32[world] flags; flags and counters are zero
  * before the first barrier and every rank calls the barrier equally often
  * (the counter lives on the device, so a captured graph replays correctly).
- * tp_reduce: for this owner's `owned` rows: x = x + (sum over the `world`
- * partial slots of recv [world][owner_rows][width] in rank order + bias)
- * (encoder_bias_residual order, encoder.cpp:146-166), in place; with
+ * tp_reduce: for this owner's `owned` rows (global rows row0 ..): x = x +
+ * (sum over ranks p = 0 .. world-1 of part_ptrs[p][row0 + r] + bias), the
+ * partial products read in rank order from every rank's [M][width] fp32
+ * partial buffer (peer loads, coalesced), then the bias, then the residual
+ * (encoder_bias_residual order, encoder.cpp:146-166), x updated in place; with
  * ln_weight, the new rows are also LayerNorm-ed, Q8_0-quantized (rounding) and
  * stored as fp16(q * d) into every rank's staged operand staged_ptrs[p]
  * ([M][width] fp16, rows row0 ..): the all-gather of the next
- * column-parallel GEMM's input. width <= 1536. */
+ * column-parallel GEMM's input. width <= 1536. Pointer arrays are device
+ * arrays of `world` device pointers (peer mappings, e.g. symmetric memory),
+ * not checked on the host. */
 MSTAR_B200_API int mstar_b200_tp_barrier(int32_t *const *flag_ptrs, int32_t *my_flags, int32_t rank, int32_t world,
     int32_t *counter, int32_t *status, void *stream, char *error, size_t error_size);
-MSTAR_B200_API int mstar_b200_tp_reduce(const float *recv, int32_t world, int64_t owner_rows, int64_t owned,
+MSTAR_B200_API int mstar_b200_tp_reduce(const float *const *part_ptrs, int32_t world, int64_t owned,
     int64_t width, const float *bias, float *x, const float *ln_weight, const float *ln_bias, float ln_eps,
     void *const *staged_ptrs, int64_t row0, int32_t rounding, int32_t *status, void *stream, char *error,
     size_t error_size);

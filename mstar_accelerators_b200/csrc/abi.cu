@@ -491,44 +491,6 @@ int mstar_b200_linear_gemm(void *handle, const void *staged, uint64_t staged_byt
     }
 }
 
-int mstar_b200_linear_gemm_partial(void *handle, const void *staged, uint64_t staged_bytes, int64_t rows,
-                                   float *const *peer_out, int32_t world, int32_t rank, int64_t owner_rows,
-                                   int64_t out_stride, int32_t *status, void *stream, char *error, size_t error_size) {
-    try {
-        require(handle, "missing linear handle");
-        auto &h = *static_cast<Linear *>(handle);
-        Busy busy(h.busy);
-        require(h.w16, "linear_gemm_partial needs prepare_gemm first");
-        require(world >= 1 && world <= 8 && rank >= 0 && rank < world, "invalid rank / world");
-        require(rows >= 1 && owner_rows >= 1 && owner_rows * world >= rows, "owners must cover every row");
-        require(out_stride >= h.rows && out_stride % 4 == 0, "invalid output stride");
-        require(peer_out && status, "missing partial-output operand");
-        check_range({staged, staged_bytes}, uint64_t(rows) * h.width * 2, 16, "staged operand");
-        check_device(staged, "staged operand");
-        check_device(status, "status word");
-        CUtensorMap xmap;
-        make_fp16_map(&xmap, staged, rows, h.width, GEMM_TILE_M);
-        GemmArgs g{};
-        g.M = rows;
-        g.N = h.rows;
-        g.K = h.width;
-        g.out = nullptr;
-        g.ldo = out_stride;
-        g.flags = 0;
-        g.out_mode = GEMM_OUT_F32;
-        g.status = status;
-        g.peers = peer_out;
-        g.owner_rows = owner_rows;
-        g.rank = rank;
-        launch_gemm(xmap, h.wmap, g, as_stream(stream));
-        cuda_check(cudaGetLastError(), "GEMM launch");
-        return 0;
-    } catch (const std::exception &e) {
-        message(error, error_size, e.what());
-        return -1;
-    }
-}
-
 int mstar_b200_linear_set_split(void *handle, int warps, char *error, size_t error_size) {
     try {
         require(handle, "missing linear handle");

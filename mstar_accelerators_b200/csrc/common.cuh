@@ -197,6 +197,30 @@ __device__ __forceinline__ void unpack_q4(uint32_t q, uint32_t &lo, uint32_t &hi
     hi = (q >> 4) & 0x0F0F0F0Fu;
 }
 
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialization attribute may start while its predecessor still runs;
+// pdl_wait() blocks until the predecessor grid has completed and its memory is
+// visible, pdl_trigger() lets this kernel's own dependent start launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch with programmatic stream serialization (the kernel must pdl_wait()
+// before reading what earlier kernels wrote).
+template <class... K, class... A>
+inline void launch_pdl(void (*kernel)(K...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, static_cast<K>(args)...);
+}
+
 // bits of a packed half2 (for 16-byte vector stores)
 __device__ __forceinline__ uint32_t half2_bits(__half2 h) {
     uint32_t u;

@@ -14,6 +14,8 @@ namespace mb {
 __global__ void k_embed(const float *__restrict__ tok, const float *__restrict__ pos, const int64_t *__restrict__ ids,
                         const int64_t *__restrict__ positions, float scale, float *__restrict__ x, int64_t n,
                         int64_t d, int64_t vocab, int64_t npos, int *__restrict__ status) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t r = blockIdx.x;
     if (r >= n) return;
     const int64_t id = ids[r], p = positions[r];
@@ -102,6 +104,8 @@ __global__ void __launch_bounds__(ATT_MAX_THREADS) k_attend_tiles(const AttArgs 
     auto row_seq = [&](int r) { return a.shared ? r / a.nq : grp; };
     auto row_q = [&](int r) { return a.shared ? int64_t(r) : int64_t(grp) * a.nq + r; };  // global query row
 
+    pdl_wait();  // q, begin / kv_len and the planes come from the kernels before this one
+    pdl_trigger();
     if (tid == 0) maxlim = 0;
     __syncthreads();
     for (int r = tid; r < mtiles * 16; r += blockDim.x) {
@@ -301,6 +305,8 @@ __global__ void __launch_bounds__(ATT_MAX_THREADS) k_attend_tiles(const AttArgs 
 
 // Merge of the key splits: one CTA per (group, head, row), one thread per dim.
 __global__ void __launch_bounds__(HEAD_DIM) k_attend_merge(const AttArgs a) {
+    pdl_wait();
+    pdl_trigger();
     const int R = a.rows;
     const int r = blockIdx.x % R, gh = blockIdx.x / R;
     const int h = gh % a.heads, grp = gh / a.heads;
@@ -372,8 +378,8 @@ int mstar_b200_embed(const float *token_table, int64_t vocab, const float *posit
         require(token_table && position_table && ids && positions && x && status, "missing embedding operand");
         require(rows > 0 && width > 0 && vocab > 0 && positions_count > 0, "invalid embedding shape");
         cudaStream_t s = as_stream(stream);
-        k_embed<<<unsigned(rows), 128, 0, s>>>(token_table, position_table, ids, positions, scale, x, rows, width,
-                                               vocab, positions_count, status);
+        launch_pdl(k_embed, dim3(unsigned(rows)), dim3(128), 0, s, token_table, position_table, ids, positions, scale,
+                   x, rows, width, vocab, positions_count, status);
         cuda_check(cudaGetLastError(), "embedding launch");
         return 0;
     } catch (const std::exception &e) {
@@ -446,9 +452,9 @@ int mstar_b200_attend(const float *q, int64_t q_stride, const float *k_new, cons
         cudaStream_t s = as_stream(stream);
         const unsigned grid = unsigned(p.groups * heads * p.splits);
         const int threads = 32 * (p.rows > 64 ? (p.rows + 15) / 16 : 4);
-        if (causal) k_attend_tiles<true><<<grid, threads, smem, s>>>(a);
-        else k_attend_tiles<false><<<grid, threads, smem, s>>>(a);
-        if (p.splits > 1) k_attend_merge<<<unsigned(p.groups * heads * p.rows), HEAD_DIM, 0, s>>>(a);
+        if (causal) launch_pdl(k_attend_tiles<true>, dim3(grid), dim3(threads), smem, s, a);
+        else launch_pdl(k_attend_tiles<false>, dim3(grid), dim3(threads), smem, s, a);
+        if (p.splits > 1) launch_pdl(k_attend_merge, dim3(unsigned(p.groups * heads * p.rows)), dim3(HEAD_DIM), 0, s, a);
         cuda_check(cudaGetLastError(), "attention launch");
         return 0;
     } catch (const std::exception &e) {

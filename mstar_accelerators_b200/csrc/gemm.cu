@@ -169,13 +169,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             int64_t m0, n0;
             tile_coords(tile, m0, n0);
             const int64_t row = m0 + 32 * q + lane;
-            int64_t orow_i = a.seg_rows ? (row / a.seg_rows) * a.out_seg_rows + row % a.seg_rows : row;
+            const int64_t orow_i = a.seg_rows ? (row / a.seg_rows) * a.out_seg_rows + row % a.seg_rows : row;
             const int64_t rrow_i = a.res_period ? row % a.res_period : row;
-            void *obase = a.out;
-            if (a.peers && row < a.M) {  // partial rows into the owning rank's receive slot (NVLink stores)
-                obase = a.peers[row / a.owner_rows];
-                orow_i = int64_t(a.rank) * a.owner_rows + row % a.owner_rows;
-            }
+            void *const obase = a.out;
             for (int c = c0; c < c0 + GEMM_BN / 32 / (GEMM_EPI_WARPS / 4); ++c) {
                 uint32_t r[32];
                 tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(buf * GEMM_BN + c * 32), r);

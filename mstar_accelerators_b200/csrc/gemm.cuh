@@ -20,11 +20,6 @@ struct GemmArgs {
     int out_mode;           // GEMM_OUT_F32 / GEMM_OUT_F16 / GEMM_OUT_Q8
     int rounding;           // Q8_0 rounding of GEMM_OUT_Q8
     int *status;            // bit value 2: a bounded pipeline wait timed out; 1: nonfinite Q8_0 input
-    // tensor-parallel partials (fp32 out only): row r goes to peers[r / owner_rows], row
-    // rank * owner_rows + r % owner_rows (this rank's slot in the owner's receive buffer)
-    float *const *peers;
-    int64_t owner_rows;
-    int rank;
 };
 
 // Output modes: fp32 rows; fp16 rows; or each 32-column block Q8_0-quantized

@@ -36,7 +36,6 @@ struct GemvSmem {
     unsigned long long *best;
 };
 
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Copy this call's activation fragments and scales (written by the quantize
 // kernel that precedes this launch) into shared memory.
@@ -173,6 +172,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(const GemvArgs a) {
 #pragma unroll
     for (int u = 0; u < RING; ++u) load_next(u);  // immutable weights: before waiting on x's producer
     pdl_wait();
+    pdl_trigger();  // the next kernel may launch now; it waits for this grid before reading
     stage_activations<MT>(a, s);
 
     bool hi_live[MT];
@@ -356,6 +356,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv_stream(const GemvArgs a) 
     if (lane == 0)
         for (int u = 0; u < R && u < steps; ++u) issue(u);  // immutable weights: before waiting on x
     pdl_wait();
+    pdl_trigger();  // the next kernel may launch now; it waits for this grid before reading
     stage_activations<MT>(a, s);
 
     bool hi_live[MT];

@@ -165,8 +165,6 @@ __global__ void k_quantize_rows(const float *__restrict__ x, int64_t ldx, int64_
     if (lane == 0) o16[0] = __half_as_ushort(__float2half_rn(d));
 }
 
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // One CTA per token (mpad CTAs): optional LayerNorm of the row (ggml_norm,
 // ggml-cpu/ops.cpp:4094-4137, then ggml_mul/ggml_add by the affine), then

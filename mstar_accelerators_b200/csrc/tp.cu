@@ -4,15 +4,19 @@
 // accelerations/whisper/cpu_tp2/decoder_all_reduce.py:64-90), done with plain
 // peer loads and stores over NVLink into symmetric device buffers (no NCCL, no
 // multicast):
-//   * the row-parallel GEMM's epilogue stores its fp32 partial rows straight
-//     into the receive slot of the rank that owns those rows (GemmArgs.peers);
+//   * every rank's row-parallel GEMM writes its fp32 partial product [M][N]
+//     into its own peer-visible buffer (local HBM, the GEMM's normal epilogue);
 //   * k_tp_barrier: every rank raises a generation counter in every peer's
 //     flag array and waits (bounded) for all peers' counters;
-//   * k_tp_reduce: each owner sums the W partial slots in rank order, adds the
-//     bias, then the residual (x = x + (sum + b), encoder_bias_residual order),
-//     keeps its rows, and optionally LayerNorm-stages the new rows (Q8_0 ->
-//     fp16(q * d)) straight into every rank's staged operand, which is the
+//   * k_tp_reduce: each owner of a row range pulls the W partial rows with
+//     coalesced peer loads, sums them in rank order, adds the bias, then the
+//     residual (x = x + (sum + b), encoder_bias_residual order), keeps its rows,
+//     and optionally LayerNorm-stages the new rows (Q8_0 -> fp16(q * d)) with
+//     coalesced peer stores into every rank's staged operand, which is the
 //     all-gather the next column-parallel GEMM needs.
+// Remote reads and writes are whole 512-byte warp segments; a row-per-thread
+// push of the partials from the GEMM epilogue instead splits every row into
+// 16-byte remote stores.
 #include <cmath>
 
 #include "../../include/mstar_b200.h"
@@ -55,13 +59,13 @@ __global__ void k_tp_barrier(int *const *flags, int *mine, int rank, int world, 
     }
 }
 
-// One warp per owned row. recv: [world][owner_rows][n] fp32 partial slots;
-// x: [owner_rows][n] fp32 residual rows of this owner (updated in place).
+// One warp per owned row. parts[p]: rank p's [M][n] fp32 partial product;
+// x: [owned][n] fp32 residual rows of this owner (updated in place).
 template <int MODE>
 __global__ void __launch_bounds__(TP_WARPS * 32)
-    k_tp_reduce(const float *__restrict__ recv, int world, int64_t owner_rows, int64_t owned, int64_t n,
-                const float *__restrict__ bias, float *__restrict__ x, const float *__restrict__ ln_w,
-                const float *__restrict__ ln_b, float eps, __half *const *staged, int64_t row0, int *status) {
+    k_tp_reduce(const float *const *parts, int world, int64_t owned, int64_t n, const float *__restrict__ bias,
+                float *__restrict__ x, const float *__restrict__ ln_w, const float *__restrict__ ln_b, float eps,
+                __half *const *staged, int64_t row0, int *status) {
     const int lane = threadIdx.x & 31;
     const int64_t r = int64_t(blockIdx.x) * TP_WARPS + (threadIdx.x >> 5);
     if (r >= owned) return;
@@ -73,9 +77,9 @@ __global__ void __launch_bounds__(TP_WARPS * 32)
         const int64_t c = int64_t(i) * 32 + lane;
         v[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         if (c < chunks) {
-            float4 acc = *reinterpret_cast<const float4 *>(recv + r * n + 4 * c);
+            float4 acc = *reinterpret_cast<const float4 *>(parts[0] + (row0 + r) * n + 4 * c);
             for (int s = 1; s < world; ++s) {
-                const float4 p = *reinterpret_cast<const float4 *>(recv + (int64_t(s) * owner_rows + r) * n + 4 * c);
+                const float4 p = *reinterpret_cast<const float4 *>(parts[s] + (row0 + r) * n + 4 * c);
                 acc.x = __fadd_rn(acc.x, p.x);
                 acc.y = __fadd_rn(acc.y, p.y);
                 acc.z = __fadd_rn(acc.z, p.z);
@@ -165,37 +169,35 @@ int mstar_b200_tp_barrier(int32_t *const *flag_ptrs, int32_t *my_flags, int32_t 
     }
 }
 
-int mstar_b200_tp_reduce(const float *recv, int32_t world, int64_t owner_rows, int64_t owned, int64_t width,
+int mstar_b200_tp_reduce(const float *const *part_ptrs, int32_t world, int64_t owned, int64_t width,
                          const float *bias, float *x, const float *ln_weight, const float *ln_bias, float ln_eps,
                          void *const *staged_ptrs, int64_t row0, int32_t rounding, int32_t *status, void *stream,
                          char *error, size_t error_size) {
     try {
         require(world >= 1 && world <= TP_MAX_WORLD, "invalid world size");
-        require(owner_rows >= 1 && owned >= 0 && owned <= owner_rows, "invalid owned rows");
+        require(owned >= 0 && row0 >= 0, "invalid owned rows");
         require(width >= 4 && width % 32 == 0 && width <= 4 * 32 * TP_MAX_CHUNKS, "width must be 32..1536, /32");
-        require(recv && bias && x && status, "missing reduction operand");
-        require(uintptr_t(recv) % 16 == 0 && uintptr_t(x) % 16 == 0 && uintptr_t(bias) % 16 == 0,
-                "reduction operands must be 16-byte aligned");
+        require(part_ptrs && bias && x && status, "missing reduction operand");
+        require(uintptr_t(x) % 16 == 0 && uintptr_t(bias) % 16 == 0, "reduction operands must be 16-byte aligned");
         require(rounding >= 0 && rounding <= 2, "unknown Q8_0 activation rounding");
         if (ln_weight) {
             require(ln_bias && staged_ptrs && std::isfinite(ln_eps) && ln_eps >= 0.0f, "invalid LayerNorm staging");
             require(uintptr_t(ln_weight) % 16 == 0 && uintptr_t(ln_bias) % 16 == 0, "LayerNorm vectors unaligned");
         }
-        check_device(recv, "receive slots");
         check_device(x, "owned rows");
         if (owned == 0) return 0;
         const unsigned grid = unsigned(ceil_div(owned, TP_WARPS));
         auto *dst = reinterpret_cast<__half *const *>(staged_ptrs);
         cudaStream_t s = as_stream(stream);
         if (rounding == 0)
-            k_tp_reduce<0><<<grid, TP_WARPS * 32, 0, s>>>(recv, world, owner_rows, owned, width, bias, x, ln_weight,
-                                                         ln_bias, ln_eps, dst, row0, status);
+            k_tp_reduce<0><<<grid, TP_WARPS * 32, 0, s>>>(part_ptrs, world, owned, width, bias, x, ln_weight, ln_bias,
+                                                         ln_eps, dst, row0, status);
         else if (rounding == 2)
-            k_tp_reduce<2><<<grid, TP_WARPS * 32, 0, s>>>(recv, world, owner_rows, owned, width, bias, x, ln_weight,
-                                                         ln_bias, ln_eps, dst, row0, status);
+            k_tp_reduce<2><<<grid, TP_WARPS * 32, 0, s>>>(part_ptrs, world, owned, width, bias, x, ln_weight, ln_bias,
+                                                         ln_eps, dst, row0, status);
         else
-            k_tp_reduce<1><<<grid, TP_WARPS * 32, 0, s>>>(recv, world, owner_rows, owned, width, bias, x, ln_weight,
-                                                         ln_bias, ln_eps, dst, row0, status);
+            k_tp_reduce<1><<<grid, TP_WARPS * 32, 0, s>>>(part_ptrs, world, owned, width, bias, x, ln_weight, ln_bias,
+                                                         ln_eps, dst, row0, status);
         cuda_check(cudaGetLastError(), "reduction launch");
         return 0;
     } catch (const std::exception &e) {

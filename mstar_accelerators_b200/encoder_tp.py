@@ -8,13 +8,14 @@ encoder block):
   * the convolution stems run replicated (1-2 % of the work);
   * QKV is column-parallel by heads (an uneven split when the heads do not
     divide, e.g. 20 heads over 8 ranks), attention runs on the local heads;
-  * out_proj is row-parallel (its K = the local heads' columns): the GEMM
-    epilogue stores fp32 partial rows into the receive slot of the rank that
-    owns those rows (rows are split evenly into W owner ranges);
-  * after a peer barrier each owner sums the W partials in rank order, adds the
-    bias once, then the residual (x = x + (sum + b)), LayerNorms and Q8_0-stages
-    the new rows straight into every rank's staged operand (the all-gather of
-    the next column-parallel GEMM), and a second barrier publishes them;
+  * out_proj is row-parallel (its K = the local heads' columns): every rank
+    writes its fp32 partial product into its own peer-visible buffer; rows are
+    split evenly into W owner ranges;
+  * after a peer barrier each owner pulls its rows' W partials over NVLink
+    (coalesced peer loads), sums them in rank order, adds the bias once, then
+    the residual (x = x + (sum + b)), LayerNorms and Q8_0-stages the new rows
+    straight into every rank's staged operand with peer stores (the all-gather
+    of the next column-parallel GEMM), and a second barrier publishes them;
   * fc1 is column-parallel (bias + GELU + Q8_0-staged output local), fc2
     row-parallel with the same fused reduction, whose staging applies the next
     layer's first LayerNorm;
@@ -137,20 +138,20 @@ class WhisperEncoderTP:
         self.hidden16 = torch.empty((M, self.f_local), dtype=torch.float16, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
-        # symmetric (peer-mapped) buffers: partial slots, the all-gathered staged LayerNorm rows, flags
+        # symmetric (peer-mapped) buffers: partial products, the all-gathered staged LayerNorm rows, flags
         pg = group if group is not None else dist.group.WORLD
         if hasattr(symm, "is_symm_mem_enabled_for_group") and not symm.is_symm_mem_enabled_for_group(pg.group_name):
             symm.enable_symm_mem_for_group(pg.group_name)
-        self.recv = symm.empty(self.world * self.owner_rows_max * d, dtype=torch.float32, device=dev)
+        self.part = symm.empty(M * d, dtype=torch.float32, device=dev)
         self.ln_staged = symm.empty(M * d, dtype=torch.float16, device=dev)
         self.flags = symm.empty(self.world, dtype=torch.int32, device=dev)
         self.flags.zero_()
         torch.cuda.synchronize()
         pg = group if group is not None else dist.group.WORLD
-        self._h = [symm.rendezvous(t, pg) for t in (self.recv, self.ln_staged, self.flags)]
+        self._h = [symm.rendezvous(t, pg) for t in (self.part, self.ln_staged, self.flags)]
         def ptrs(h):
             return torch.tensor(h.buffer_ptrs, dtype=torch.int64, device=dev)
-        self.recv_ptrs, self.staged_ptrs, self.flag_ptrs = (ptrs(h) for h in self._h)
+        self.part_ptrs, self.staged_ptrs, self.flag_ptrs = (ptrs(h) for h in self._h)
         dist.barrier(group=group)
 
     # ------------------------------------------------------------------ pieces
@@ -160,18 +161,15 @@ class WhisperEncoderTP:
                                              self.counter.data_ptr(), self.status.data_ptr(), _stream(self.device),
                                              e, len(e)), e, "B200 TP barrier")
 
-    def _partial(self, lin: BlockLinear, staged: torch.Tensor, owner_rows: int):
-        e = error_buffer()
-        rows = staged.shape[0]
-        check(self.lib.mstar_b200_linear_gemm_partial(lin.handle, staged.data_ptr(), rows * lin.width * 2, rows,
-                                                      self.recv_ptrs.data_ptr(), self.world, self.rank, owner_rows,
-                                                      lin.rows, self.status.data_ptr(), _stream(self.device), e,
-                                                      len(e)), e, "B200 TP partial GEMM")
+    def _partial(self, lin: BlockLinear, staged: torch.Tensor):
+        """Row-parallel partial product [M][width] fp32 into this rank's peer-visible buffer."""
+        lin.gemm(staged, out=self.part[:staged.shape[0] * lin.rows].view(-1, lin.rows), bias=False,
+                 rounding=self.rounding, status=self.status)
 
     def _reduce(self, owner_rows: int, owned: int, bias: torch.Tensor, norm):
         lw, lb, eps = (norm[0].data_ptr(), norm[1].data_ptr(), float(norm[2])) if norm else (None, None, 0.0)
         e = error_buffer()
-        check(self.lib.mstar_b200_tp_reduce(self.recv.data_ptr(), self.world, owner_rows, owned, self.cfg.width,
+        check(self.lib.mstar_b200_tp_reduce(self.part_ptrs.data_ptr(), self.world, owned, self.cfg.width,
                                             bias.data_ptr(), self.x_own.data_ptr(), lw, lb, eps,
                                             self.staged_ptrs.data_ptr() if norm else None, self.rank * owner_rows,
                                             native.ROUNDING[self.rounding], self.status.data_ptr(),
@@ -179,10 +177,11 @@ class WhisperEncoderTP:
 
     # ------------------------------------------------------------------ forward
     # Buffer hazards between ranks are covered by the barrier after each partial
-    # GEMM (every rank has finished the GEMMs that read ln_staged and the
-    # reduction that read recv before any owner writes them again) and the
-    # barrier after each reduction (the staged rows are complete before the
-    # next column-parallel GEMM reads them).
+    # GEMM (every partial is complete, and every rank has finished the GEMMs
+    # that read ln_staged, before any owner reads partials or writes staged
+    # rows) and the barrier after each reduction (the staged rows are complete
+    # before the next column-parallel GEMM reads them, and every owner has read
+    # the partials before any rank overwrites its partial buffer).
     def forward(self, mel: torch.Tensor) -> torch.Tensor:
         """mel fp32 [batch, mels, 2 * positions] (the same on every rank) ->
         encoder_states fp32 [batch, positions, width] on every rank."""
@@ -217,13 +216,13 @@ class WhisperEncoderTP:
             v = qkv[:, :, 2 * dl:].unflatten(-1, (H, hd)).transpose(1, 2)
             att = F.scaled_dot_product_attention(q, k, v, scale=hd ** -0.5).transpose(1, 2).reshape(M, dl)
             sa = stage_rows(att, rounding=r, out=self.att_staged[:M], status=st)
-            self._partial(L["out"], sa, own_rows)
+            self._partial(L["out"], sa)
             self._barrier()
             self._reduce(own_rows, owned, L["out_b"], L["ln2"])
             self._barrier()
             h = L["fc1"].gemm(ln_staged, out=self.hidden16[:M], out_format="staged", gelu="tanh", rounding=r,
                               status=st)
-            self._partial(L["fc2"], h, own_rows)
+            self._partial(L["fc2"], h)
             self._barrier()
             nxt = self.layers[i + 1]["ln1"] if i + 1 < len(self.layers) else None
             self._reduce(own_rows, owned, L["fc2_b"], nxt)

@@ -53,7 +53,7 @@ class ExpertParallelMoE:
 
     @classmethod
     def b200(cls, w1: torch.Tensor, w2: torch.Tensor, *, experts: int, top_k: int = 8, group=None,
-             capacity: int = 8192) -> "ExpertParallelMoE":
+             capacity: int = 65536) -> "ExpertParallelMoE":
         """The B200 layer: w1 [E, 2I, H] / w2 [E, H, I] bf16 (the full layer, on this
         rank's device); this rank keeps its experts. ``capacity`` bounds the pairs
         one local launch takes (larger receptions run in chunks)."""
@@ -85,8 +85,8 @@ class ExpertParallelMoE:
         counts = torch.bincount(dest, minlength=self.world)
         recv_counts_t = torch.empty_like(counts)
         dist.all_to_all_single(recv_counts_t, counts, group=self.group)
-        send_counts = counts.cpu().tolist()
-        recv_counts = recv_counts_t.cpu().tolist()
+        both = torch.stack([counts, recv_counts_t]).cpu()  # the one host synchronisation: split sizes
+        send_counts, recv_counts = both[0].tolist(), both[1].tolist()
         rows = x[order // k]
         local_ids = (ids[order] - dest[order] * per).to(torch.int32)
         weights = topk_weights.reshape(-1)[order].to(torch.float32)
