@@ -245,6 +245,45 @@ MSTAR_B200_API int mstar_b200_tp_reduce(const float *const *part_ptrs, int32_t w
     void *const *staged_ptrs, int64_t row0, int32_t rounding, int32_t *status, void *stream, char *error,
     size_t error_size);
 
+/* --- the whole decoder step as one persistent kernel ------------------------------
+ * One greedy decode step of the Whisper decoder graph (decoder.cpp:489-600,
+ * 683-696) for `batch` sequences (one new token each) as a single cooperative
+ * launch: embedding, every layer (LayerNorm + Q8_0 activations, fused QKV,
+ * causal self attention appending K/V at positions[b], out projection +
+ * residual, LayerNorm, cross query, cross attention over the cross planes,
+ * out projection + residual, LayerNorm, fc1 + GELU, fc2 + residual), final
+ * LayerNorm, the readout with suppression and the argmax into next_token.
+ * The arithmetic is that of mstar_b200_linear_run / _readout and
+ * mstar_b200_attend on the same handles and planes, so logits and tokens are
+ * identical to the multi-launch step. Handles: linears[i] = {QKV [3w x w],
+ * out [w x w], cross query [w x w], cross out [w x w], fc1 [ffn x w], fc2 [w x ffn]}
+ * (Q8_0), head = the readout ([vocab x w], Q4_0 or Q8_0); norms[i] = {ln1 w, b,
+ * ln2 w, b, ln3 w, b}. Every pointer is borrowed and must outlive the step
+ * handle (close the step before its linear handles); the buffers are fixed at
+ * create, so a captured graph replays the step. Bounded barrier waits set
+ * status bit value 32. */
+typedef struct mstar_b200_decode_step_config {
+    int32_t batch, layers, width, heads, ffn, target, source, shared_cross, rounding;
+    float eps;
+    const float *token_table, *position_table;
+    int64_t vocab, positions_count;
+    void *linears[8][6];
+    const float *norms[8][6];
+    void *self_k[8], *self_v[8], *cross_k[8], *cross_v[8];
+    void *head;
+    const float *final_norm_weight, *final_norm_bias;
+    const int64_t *suppressed;
+    uint64_t suppressed_count;
+    const int64_t *tokens, *positions, *cross_length;
+    float *logits;        /* [batch][vocab] or NULL */
+    int64_t *next_token;  /* [batch] */
+    int32_t *status;
+} mstar_b200_decode_step_config;
+MSTAR_B200_API void *mstar_b200_decode_step_create(const mstar_b200_decode_step_config *config, char *error,
+    size_t error_size);
+MSTAR_B200_API int mstar_b200_decode_step_run(void *step, void *stream, char *error, size_t error_size);
+MSTAR_B200_API int mstar_b200_decode_step_close(void *step, char *error, size_t error_size);
+
 /* --- readout that allocates nothing ------------------------------------------------
  * No counterpart in the reference. For callers that cannot allocate device
  * memory (a runtime that owns every device buffer and hands out only planned

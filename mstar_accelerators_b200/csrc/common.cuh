@@ -83,7 +83,7 @@ inline void check_device(const void *p, const char *what) {
 
 inline cudaStream_t as_stream(void *s) { return static_cast<cudaStream_t>(s); }
 
-inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+__host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 }  // namespace mb
 

@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(256) k_quantize_frag(const float *__restrict__
         float var = 0.0f;
         for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
             const float y = xr[i] - mean;
-            var += y * y;
+            var = fmaf(y, y, var);
         }
 #pragma unroll
         for (int o = 16; o; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);

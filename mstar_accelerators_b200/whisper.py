@@ -20,6 +20,7 @@ step can be captured in one CUDA graph.
 """
 from __future__ import annotations
 
+import ctypes as C
 import math
 from dataclasses import dataclass
 
@@ -263,11 +264,82 @@ class WhisperDecoderB200:
         self.head.close()
 
 
+class _StepConfig(C.Structure):
+    """mstar_b200_decode_step_config (include/mstar_b200.h)."""
+    _fields_ = [(n, C.c_int32) for n in ("batch", "layers", "width", "heads", "ffn", "target", "source",
+                                         "shared_cross", "rounding")] + [
+        ("eps", C.c_float), ("token_table", C.c_void_p), ("position_table", C.c_void_p), ("vocab", C.c_int64),
+        ("positions_count", C.c_int64), ("linears", (C.c_void_p * 6) * 8), ("norms", (C.c_void_p * 6) * 8),
+        ("self_k", C.c_void_p * 8), ("self_v", C.c_void_p * 8), ("cross_k", C.c_void_p * 8),
+        ("cross_v", C.c_void_p * 8), ("head", C.c_void_p), ("final_norm_weight", C.c_void_p),
+        ("final_norm_bias", C.c_void_p), ("suppressed", C.c_void_p), ("suppressed_count", C.c_uint64),
+        ("tokens", C.c_void_p), ("positions", C.c_void_p), ("cross_length", C.c_void_p), ("logits", C.c_void_p),
+        ("next_token", C.c_void_p), ("status", C.c_void_p)]
+
+
+class PersistentStep:
+    """The greedy decode step of a WhisperDecoderB200 as one persistent kernel
+    (mstar_b200_decode_step_*): reads tokens / positions, writes logits and
+    next tokens; identical results to WhisperDecoderB200.decode_into."""
+
+    def __init__(self, dec: "WhisperDecoderB200", tokens: torch.Tensor, positions: torch.Tensor,
+                 logits: torch.Tensor | None, next_token: torch.Tensor):
+        cfg = dec.cfg
+        if cfg.layers > 8:
+            raise ValueError("the step kernel takes at most 8 layers")
+        c = _StepConfig()
+        c.batch, c.layers, c.width, c.heads, c.ffn = dec.batch, cfg.layers, cfg.d_model, cfg.heads, cfg.ffn
+        c.target, c.source, c.shared_cross = cfg.target, cfg.source, int(dec.shared_cross)
+        c.rounding, c.eps = native.ROUNDING[dec.rounding], cfg.eps
+        c.token_table, c.position_table = dec.tok.data_ptr(), dec.pos.data_ptr()
+        c.vocab, c.positions_count = cfg.vocab, cfg.target
+        for i, Lr in enumerate(dec.layers):
+            for k, name in enumerate(("qkv", "out", "cq", "cout", "fc1", "fc2")):
+                c.linears[i][k] = Lr[name].handle
+            for k, (ln, j) in enumerate((("ln1", 0), ("ln1", 1), ("ln2", 0), ("ln2", 1), ("ln3", 0), ("ln3", 1))):
+                c.norms[i][k] = Lr[ln][j].data_ptr()
+            c.self_k[i], c.self_v[i] = dec.self_k[i].data_ptr(), dec.self_v[i].data_ptr()
+            c.cross_k[i], c.cross_v[i] = dec.cross_k[i].data_ptr(), dec.cross_v[i].data_ptr()
+        c.head = dec.head.handle
+        c.final_norm_weight, c.final_norm_bias = dec.lnf[0].data_ptr(), dec.lnf[1].data_ptr()
+        sup = dec.suppressed.get("decode")
+        self._sup = sup  # keep alive
+        if sup is not None and sup.numel():
+            c.suppressed, c.suppressed_count = sup.data_ptr(), sup.numel()
+        c.tokens, c.positions, c.cross_length = tokens.data_ptr(), positions.data_ptr(), dec.cross_len.data_ptr()
+        c.logits = logits.data_ptr() if logits is not None else None
+        c.next_token, c.status = next_token.data_ptr(), dec.status.data_ptr()
+        self.lib, self.dec = dec.lib, dec
+        e = error_buffer()
+        torch.cuda.synchronize(dec.device)
+        h = self.lib.mstar_b200_decode_step_create(C.byref(c), e, len(e))
+        if not h:
+            raise native.NativeError("B200 decode step: " + e.value.decode(errors="replace"))
+        self.handle = h
+
+    def run(self):
+        e = error_buffer()
+        check(self.lib.mstar_b200_decode_step_run(self.handle, _stream(self.dec.device), e, len(e)), e,
+              "B200 decode step")
+
+    def close(self):
+        if getattr(self, "handle", None):
+            e = error_buffer()
+            check(self.lib.mstar_b200_decode_step_close(self.handle, e, len(e)), e, "B200 decode step close")
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class GraphDecoder:
     """The whole greedy decode step captured once as a CUDA graph; replay feeds
     back its own next tokens (positions advance by one per step)."""
 
-    def __init__(self, dec: WhisperDecoderB200):
+    def __init__(self, dec: WhisperDecoderB200, persistent: bool = False):
         self.dec = dec
         B, dev = dec.batch, dec.device
         self.tokens = torch.zeros(B, dtype=torch.int64, device=dev)
@@ -275,9 +347,14 @@ class GraphDecoder:
         self.logits = torch.empty((B, dec.cfg.vocab), device=dev)
         self.next = torch.zeros(B, dtype=torch.int64, device=dev)
         self.graph = None
+        # persistent: the step is one cooperative kernel instead of ~60 launches
+        self.step = PersistentStep(dec, self.tokens, self.positions, self.logits, self.next) if persistent else None
 
     def _step(self):
-        self.dec.decode_into(self.tokens, self.positions, self.logits, self.next)
+        if self.step is not None:
+            self.step.run()
+        else:
+            self.dec.decode_into(self.tokens, self.positions, self.logits, self.next)
         self.tokens.copy_(self.next)
         self.positions.add_(1)
 

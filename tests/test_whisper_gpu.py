@@ -108,3 +108,44 @@ def test_batch_rows_are_independent(setup):
     assert torch.equal(l3[1], l1[0]) and int(t3[1]) == int(t1[0])
     many.close()
     one.close()
+
+
+@pytest.mark.parametrize("B,fmt,shared", [(32, "q4_0", True), (5, "q8_0", True), (3, "q4_0", False)])
+def test_persistent_step_equals_multi_launch_step(setup, B, fmt, shared):
+    """The one-kernel decode step (mstar_b200_decode_step_*) produces the same
+    logits, bit for bit, and the same tokens as the multi-launch step on the same
+    state, over several steps with the tokens fed back; a captured graph of the
+    persistent step replays it."""
+    from mstar_accelerators_b200.whisper import GraphDecoder, WhisperDecoderB200
+    cfg, weights, enc = setup
+    rng = np.random.default_rng(B)
+    prompt = torch.from_numpy(rng.integers(0, cfg.vocab, (B, 4))).cuda()
+    encs = enc.cuda() if shared else enc.cuda().repeat(B, 1, 1)
+    ref_dec = WhisperDecoderB200(weights, cfg, batch=B, readout_format=fmt, shared_cross=shared)
+    _, tok = ref_dec.prefill(prompt, encs)
+    one = WhisperDecoderB200(weights, cfg, batch=B, readout_format=fmt, shared_cross=shared)
+    _, tok1 = one.prefill(prompt, encs)
+    assert torch.equal(tok, tok1)
+    ref = GraphDecoder(ref_dec)
+    per = GraphDecoder(one, persistent=True)
+    for gd in (ref, per):
+        gd.tokens.copy_(tok)
+        gd.positions.fill_(4)
+    for step in range(3):
+        ref._step()
+        per._step()
+        torch.cuda.synchronize()
+        assert torch.equal(ref.logits, per.logits), step
+        assert torch.equal(ref.tokens, per.tokens), step
+    assert int(one.status.item()) == 0
+    per.capture()
+    ref.capture()
+    for step in range(3):
+        ref.run(1)
+        per.run(1)
+        torch.cuda.synchronize()
+        assert torch.equal(ref.logits, per.logits), ("graph", step)
+        assert torch.equal(ref.tokens, per.tokens), ("graph", step)
+    per.step.close()
+    ref_dec.close()
+    one.close()
