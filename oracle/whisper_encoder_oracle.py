@@ -5,10 +5,10 @@ CPU composition of the reference's stock-Q8 Whisper encoder graph
   conv i   convolution_q8 (encoder.cpp:45-52): ggml_im2col (kernel 3, pad 1,
            column = channel * 3 + tap) zero-padded to a multiple of 32 columns
            (encoder.cpp:551), mul_mat with the Q8_0 kernel matrix packed from the
-           fp16-rounded weights with zero added columns (encoder.cpp:608-621),
-           + bias, ggml GELU (encoder.cpp:675, activation() at :327-329);
-           conv1's output is transposed to channel rows for conv2 (encoder.cpp:678)
-  x        = conv2 output + embed_positions (encoder.cpp:682)
+           fp16-rounded weights with zero added columns (encoder.cpp:620-634),
+           + bias, ggml GELU (encoder.cpp:672, activation() at :327-329);
+           conv1's output is transposed to channel rows for conv2 (encoder.cpp:675)
+  x        = conv2 output + embed_positions (encoder.cpp:689)
   layer    n = norm_affine(x) (encoder_norm_affine, :117-142); all = mul_mat(qkv, n);
            q = all_q + b_q, k = fp16(all_k + b_k), v = fp16(all_v + b_v), K/V
            zero-padded to a multiple of 256 rows (qkv_scatter, :202-234);
@@ -16,7 +16,7 @@ CPU composition of the reference's stock-Q8 Whisper encoder graph
            x = x + (mul_mat(out, a) + b) (encoder_bias_residual, :146-166);
            n = norm_affine(x); h = gelu(mul_mat(fc1, n) + b1) (:91-112);
            x = x + (mul_mat(fc2, h) + b2)
-  output   norm_affine(x) (:733)
+  output   norm_affine(x) (:725)
 mul_mat is oracle.mul_mat (generic ggml order, activations quantized with the
 selected rounding). LayerNorm follows ggml_compute_forward_norm_f32
 (ggml-cpu/ops.cpp:4094-4137) with float64 sums. Attention is evaluated in
