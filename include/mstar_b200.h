@@ -119,6 +119,14 @@ MSTAR_B200_API int mstar_b200_linear_readout(void *handle, const float *x, int64
     uint64_t suppressed_count, const float *ln_weight, const float *ln_bias, float ln_eps,
     int rounding, void *stream, char *error, size_t error_size);
 MSTAR_B200_API int mstar_b200_linear_close(void *handle, char *error, size_t error_size);
+/* Prepare the vocab-readout tile layout of a handle (16 weight rows per tile,
+ * the whole tile's fragments and scales contiguous): later linear_readout
+ * calls on the handle use the tile kernel, bit-identical to the GEMV path.
+ * Takes the canonical blocks given to create. Synchronises. Replaces nothing
+ * in the reference: its readout is the same ggml_mul_mat + argmax
+ * (decoder.cpp:686-696). */
+MSTAR_B200_API int mstar_b200_linear_prepare_readout(void *handle, const void *blocks, uint64_t bytes,
+    char *error, size_t error_size);
 /* Prepare the tcgen05 GEMM used by linear_run calls of 64..max_queries rows
  * without a fused LayerNorm (prefill / encoder shapes, the M = 1500 and
  * M = 24000 mul_mat of encoder.cpp:467-479, 694-723): keeps fp16(q*d) of the

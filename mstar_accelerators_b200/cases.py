@@ -15,11 +15,12 @@ import torch
 
 
 def readout_q4_b32():
-    """Whisper-tiny tied Q4_0 readout (51865 x 384), 32 query rows, three calls."""
+    """Whisper-tiny tied Q4_0 readout (51865 x 384, tile layout), 32 query rows, three calls."""
     from .linear import BlockLinear
     g = torch.Generator(device="cuda").manual_seed(1)
     w = torch.randn(51865, 384, device="cuda", generator=g) * 0.02
     head = BlockLinear(w, fmt="q4_0")
+    head.prepare_readout()
     x = torch.randn(32, 384, device="cuda", generator=g)
     for _ in range(3):
         head.readout(x)

@@ -49,6 +49,13 @@ GemvArgs stage(Linear &h, const float *x, int64_t ldx, int64_t m, int rounding, 
 
 void check_rounding(int r) { require(r >= 0 && r <= 2, "unknown Q8_0 activation rounding"); }
 
+// readout.cu
+bool readout_tiles_fit(int64_t rows, int64_t nb, int q4);
+void launch_readout_repack(int q4, const uint8_t *blocks, uint8_t *wt, int64_t rows, int64_t nb, cudaStream_t s);
+void launch_readout(const Linear &h, const float *x, int64_t ldx, int64_t m, const float *ln_w,
+                    const float *ln_b, float eps, int mode, float *logits, int64_t *token, int *status,
+                    const int64_t *suppressed, int64_t nsup, cudaStream_t s);
+
 }  // namespace mb
 
 using namespace mb;
@@ -313,6 +320,12 @@ int mstar_b200_linear_readout(void *handle, const float *x, int64_t x_stride, in
         check_device(token, "token");
         check_device(status, "status");
         cudaStream_t s = as_stream(stream);
+        if (h.wt && !h.wpg_override) {  // one launch: it writes the status itself
+            launch_readout(h, x, x_stride, queries, ln_weight, ln_bias, ln_eps, rounding, logits, token, status,
+                           suppressed, int64_t(suppressed_count), s);
+            cuda_check(cudaGetLastError(), "readout launch");
+            return 0;
+        }
         cuda_check(cudaMemsetAsync(status, 0, 4, s), "status reset");
         GemvArgs a = stage(h, x, x_stride, queries, rounding, ln_weight, ln_bias, ln_eps, status, s);
         a.out = logits;
@@ -344,6 +357,33 @@ int mstar_b200_q8_readout(void *handle, const float *x, float *out, int64_t *tok
                                      nullptr, nullptr, 0.0f, MSTAR_B200_Q8_ARM, stream, e, sizeof(e))
                ? EINVAL
                : 0;
+}
+
+int mstar_b200_linear_prepare_readout(void *handle, const void *blocks, uint64_t bytes, char *error,
+                                      size_t error_size) {
+    try {
+        require(handle, "missing linear handle");
+        auto &h = *static_cast<Linear *>(handle);
+        Busy busy(h.busy);
+        check_range({blocks, bytes}, uint64_t(h.rows) * h.nb * (h.q4 ? Q4_BYTES : Q8_BYTES), 1, "linear weights");
+        check_device(blocks, "linear weights");
+        require(readout_tiles_fit(h.rows, h.nb, h.q4), "readout width too large for the tile kernel");
+        if (!h.wt) {
+            cuda_check(cudaDeviceSynchronize(), "readout preparation");
+            const int64_t tiles = ceil_div(h.rows, 16);
+            h.wt = device_alloc<uint8_t>(size_t(tiles * h.nb * (h.q4 ? 288 : 544)), "readout tiles");
+            h.ro_flags = device_alloc<int>(1, "readout status bits");
+            cuda_check(cudaMemset(h.ro_flags, 0, sizeof(int)), "readout status reset");
+            launch_readout_repack(h.q4, static_cast<const uint8_t *>(blocks), h.wt, h.rows, h.nb, nullptr);
+            cuda_check(cudaGetLastError(), "readout repack");
+            cuda_check(cudaDeviceSynchronize(), "readout preparation");
+            h.tiles = tiles;
+        }
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
 }
 
 int mstar_b200_linear_prepare_gemm(void *handle, const void *blocks, uint64_t bytes, int64_t max_queries,

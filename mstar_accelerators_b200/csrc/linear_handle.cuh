@@ -32,11 +32,15 @@ struct Linear {
     __half *x16 = nullptr;        // fp16 dequantized activations [gemm_rows][width]
     int64_t gemm_rows = 0;
     CUtensorMap wmap{};
+    // vocab readout tile layout (readout.cu), built by prepare_readout
+    uint8_t *wt = nullptr;
+    int64_t tiles = 0;
+    int *ro_flags = nullptr;  // status bits of the readout in flight
     std::atomic_flag busy = ATOMIC_FLAG_INIT;
     uint64_t weight_bytes() const { return uint64_t(groups) * 8 * nb_pad * (q4 ? 18 : 34); }
     ~Linear() {
         for (void *p : {(void *)wq, (void *)ws, (void *)bias, (void *)xf, (void *)xs, (void *)xsum, (void *)status, (void *)keys,
-                        (void *)done, (void *)w16, (void *)x16})
+                        (void *)done, (void *)w16, (void *)x16, (void *)wt, (void *)ro_flags})
             if (p) cudaFree(p);
     }
 };

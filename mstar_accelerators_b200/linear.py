@@ -184,6 +184,7 @@ class BlockLinear:
         self.has_bias = bias_t is not None
         self.blocks = blocks  # canonical bytes stay available to callers (and tests)
         self.gemm_rows = 0
+        self.readout_tiles = False
 
     # ggml_mul_mat + epilogue -------------------------------------------------
     def __call__(self, x: torch.Tensor, *, out: torch.Tensor | None = None, residual: torch.Tensor | None = None,
@@ -220,6 +221,15 @@ class BlockLinear:
         check(self.lib.mstar_b200_linear_prepare_gemm(self.handle, self.blocks.data_ptr(), _nbytes(self.blocks),
                                                       int(max_queries), e, len(e)), e, "B200 GEMM preparation")
         self.gemm_rows = int(max_queries)
+
+    def prepare_readout(self) -> None:
+        """Build the vocab-readout tile layout; later readout calls use the tile kernel (synchronises)."""
+        if self.readout_tiles:
+            return
+        e = error_buffer()
+        check(self.lib.mstar_b200_linear_prepare_readout(self.handle, self.blocks.data_ptr(), _nbytes(self.blocks),
+                                                         e, len(e)), e, "B200 readout preparation")
+        self.readout_tiles = True
 
     def gemm(self, staged: torch.Tensor, *, out: torch.Tensor | None = None, out_format: str = "f32",
              residual: torch.Tensor | None = None, residual_period: int = 0, segments: tuple[int, int] = (0, 0),

@@ -43,6 +43,7 @@ SIGNATURES = {
     "mstar_b200_linear_close": (_int, [_vp, *_err]),
     "mstar_b200_linear_set_split": (_int, [_vp, _int, *_err]),
     "mstar_b200_linear_prepare_gemm": (_int, [_vp, _vp, _u64, _i64, *_err]),
+    "mstar_b200_linear_prepare_readout": (_int, [_vp, _vp, _u64, *_err]),
     "mstar_b200_linear_gemm": (_int, [_vp, _vp, _u64, _i64, _vp, _u64, _i64, C.c_int32, _vp, _u64, _i64, _i64, _i64,
                                       _i64, C.c_int32, C.c_int32, _vp, _vp, *_err]),
     "mstar_b200_tp_barrier": (_int, [_vp, _vp, C.c_int32, C.c_int32, _vp, _vp, _vp, *_err]),

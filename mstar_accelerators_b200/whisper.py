@@ -132,6 +132,7 @@ class WhisperDecoderB200:
         self.tok = W["decoder.embed_tokens.weight"]
         self.pos = W["decoder.embed_positions.weight"]
         self.head = BlockLinear(self.tok, fmt=readout_format)   # tied readout (proj_out == embed_tokens)
+        self.head.prepare_readout()
         self.suppressed = {k: torch.tensor(v, dtype=torch.int64, device=dev)
                            for k, v in (suppressed or {"prefill": [], "decode": []}).items()}
         self.shared_cross = shared_cross
