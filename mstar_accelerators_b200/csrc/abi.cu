@@ -321,6 +321,8 @@ int mstar_b200_linear_readout(void *handle, const float *x, int64_t x_stride, in
         check_device(status, "status");
         cudaStream_t s = as_stream(stream);
         if (h.wt && !h.wpg_override) {  // one launch: it writes the status itself
+            require(!ln_weight || (uintptr_t(ln_weight) % 16 == 0 && uintptr_t(ln_bias) % 16 == 0),
+                    "LayerNorm vectors must be 16-byte aligned");
             launch_readout(h, x, x_stride, queries, ln_weight, ln_bias, ln_eps, rounding, logits, token, status,
                            suppressed, int64_t(suppressed_count), s);
             cuda_check(cudaGetLastError(), "readout launch");

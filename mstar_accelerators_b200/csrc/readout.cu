@@ -9,9 +9,11 @@
 // tile chunk (all 16 rows' fragments and scales for up to RO_SLOT bytes of
 // blocks) into a warp's shared-memory ring.
 //
-// Per 16 x 8 x 32 block product the fp32 work is two packed f32x2 operations
-// per pair and scalar adds into the running sums (a packed add after a packed
-// multiply is fused into an fma by ptxas, which would change the rounding):
+// Per 16 x 8 x 32 block product the fp32 work is three packed f32x2
+// operations per pair (ptxas fuses a packed multiply into a packed add that
+// follows it, so each term is formed by an fma with a +0 addend, which equals
+// the rounded product up to the sign of a zero; a running sum that starts at
+// +0 never holds -0, so that sign never reaches a result):
 //   * the MMA accumulator starts at the bit pattern of 1.5 * 2^23, so the
 //     int32 result read as fp32 is 12582912 + sumi exactly (|sumi| < 2^22);
 //   * Q4_0 nibbles are unpacked as 16 * (n - 8) (signed), so no -8 * sum(x)
@@ -143,11 +145,47 @@ __device__ __forceinline__ void running_max(float &bv, uint32_t &bn, float v, ui
 // LayerNorm statistics of one row in launch_quantize_frag's reduction order
 // (virtual warps v of its 128 / 256-thread block, a warp reduction each, then
 // the partials in order), so the quantized queries are the ones the decode
-// GEMV path sees.
+// GEMV path sees. Lane l holds elements 32 k + l; element 32 k + l belongs to
+// virtual warp k mod (threads / 32), so each virtual warp's per-thread sum is
+// this lane's sum over those k in increasing order. KC > 0: a compile-time
+// width whose row is loaded into registers at once.
+template <int KC>
 __device__ __forceinline__ void row_stats(const float *xr, int64_t K, float eps, float &mean, float &rstd) {
     const int lane = threadIdx.x & 31;
-    const int vwarps = K >= 1024 ? 8 : 4, vthreads = 32 * vwarps;
-    float sum = 0.0f;
+    const int vwarps = K >= 1024 ? 8 : 4;
+    float sum = 0.0f, var = 0.0f;
+    if (KC) {
+        constexpr int NK = KC / 32 > 0 ? KC / 32 : 1;
+        constexpr int VW = KC >= 1024 ? 8 : 4;
+        float v[NK];
+#pragma unroll
+        for (int k = 0; k < NK; ++k) v[k] = xr[32 * k + lane];
+#pragma unroll
+        for (int w = 0; w < VW; ++w) {
+            float s = 0.0f;
+#pragma unroll
+            for (int k = w; k < NK; k += VW) s += v[k];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            sum += s;
+        }
+        mean = sum / float(KC ? KC : 1);
+#pragma unroll
+        for (int w = 0; w < VW; ++w) {
+            float s = 0.0f;
+#pragma unroll
+            for (int k = w; k < NK; k += VW) {
+                const float y = v[k] - mean;
+                s = fmaf(y, y, s);
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            var += s;
+        }
+        rstd = 1.0f / sqrtf(var / float(KC ? KC : 1) + eps);
+        return;
+    }
+    const int vthreads = 32 * vwarps;
     for (int w = 0; w < vwarps; ++w) {
         float s = 0.0f;
         for (int64_t i = 32 * w + lane; i < K; i += vthreads) s += xr[i];
@@ -156,7 +194,6 @@ __device__ __forceinline__ void row_stats(const float *xr, int64_t K, float eps,
         sum += s;
     }
     mean = sum / float(K);
-    float var = 0.0f;
     for (int w = 0; w < vwarps; ++w) {
         float s = 0.0f;
         for (int64_t i = 32 * w + lane; i < K; i += vthreads) {
@@ -173,9 +210,16 @@ __device__ __forceinline__ void row_stats(const float *xr, int64_t K, float eps,
 // Quantize the queries into shared-memory B fragments and fp32 scales (the
 // k_quantize_frag result: quantize_row_q8_0 with the selected rounding, after
 // the optional LayerNorm); rows >= m are zero. The LayerNorm statistics take
-// one warp per row (row_stats); the blocks then take one thread per
-// (row, block) pair, its 32 values in registers.
-template <int MT>
+// one warp per row (row_stats). The blocks go four at a time to a warp: one
+// coalesced 16-byte load per lane, the block maximum over its 8 lanes, and
+// each lane's four quants are exactly one word of the fragment layout. A warp
+// issues the loads of RO_QBATCH = 8 such tasks before it uses any of them; the
+// 32 block scales of the batch are divided one per lane. Scales are stored per
+// lane t of the B fragments: [block][t][n-tile][2] (queries 8 nt + 2 t + c).
+constexpr int RO_QBATCH = 8;
+static_assert(RO_QBATCH * 4 == 32, "one lane per block of a batch");
+
+template <int MT, int KC>
 __device__ __forceinline__ void stage_queries(const ReadoutArgs &a, int nb, uint4 *s_xf, float *s_xs,
                                               float2 *s_stats, int warps) {
     constexpr int MPAD = MT * 16;
@@ -184,64 +228,91 @@ __device__ __forceinline__ void stage_queries(const ReadoutArgs &a, int nb, uint
     if (a.ln_w) {
         for (int q = warp; q < a.m; q += warps) {
             float mean, rstd;
-            row_stats(a.x + int64_t(q) * a.ldx, K, a.eps, mean, rstd);
+            row_stats<KC>(a.x + int64_t(q) * a.ldx, K, a.eps, mean, rstd);
             if (lane == 0) s_stats[q] = make_float2(mean, rstd);
         }
         __syncthreads();
     }
     uint32_t *xw = reinterpret_cast<uint32_t *>(s_xf);
-    for (int p = threadIdx.x; p < MPAD * nb; p += blockDim.x) {
-        const int q = p / nb, b = p % nb;
-        float v[QK];
+    const int nchunk = (nb + 3) / 4, ntask = MPAD * nchunk, j = lane & 7;
+    // each phase runs over the whole batch, so the batch's shuffle and division
+    // chains overlap instead of following one another
+    for (int t0 = warp; t0 < ntask; t0 += RO_QBATCH * warps) {
+        float4 v[RO_QBATCH];
+        int qk[RO_QBATCH], bk[RO_QBATCH];
+        bool live[RO_QBATCH];
+#pragma unroll
+        for (int k = 0; k < RO_QBATCH; ++k) {
+            const int task = t0 + k * warps;
+            qk[k] = task / nchunk;
+            bk[k] = (task % nchunk) * 4 + (lane >> 3);
+            live[k] = task < ntask && qk[k] < a.m && bk[k] < nb;
+            v[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (live[k])
+                v[k] = *reinterpret_cast<const float4 *>(a.x + int64_t(qk[k]) * a.ldx + int64_t(bk[k]) * QK + 4 * j);
+        }
+        float amax[RO_QBATCH];
         bool finite = true;
-        if (q < a.m) {
-            const float4 *src = reinterpret_cast<const float4 *>(a.x + int64_t(q) * a.ldx + b * QK);
 #pragma unroll
-            for (int i = 0; i < QK / 4; ++i) {
-                const float4 f = src[i];
-                v[4 * i] = f.x;
-                v[4 * i + 1] = f.y;
-                v[4 * i + 2] = f.z;
-                v[4 * i + 3] = f.w;
-            }
-            if (a.ln_w) {
-                const float2 ms = s_stats[q];
-#pragma unroll
-                for (int i = 0; i < QK; ++i) {
-                    const int64_t e = int64_t(b) * QK + i;
-                    v[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i], ms.x), ms.y), __ldg(a.ln_w + e)),
-                                     __ldg(a.ln_b + e));
+        for (int k = 0; k < RO_QBATCH; ++k) {
+            if (live[k]) {
+                if (a.ln_w) {
+                    const int64_t e = int64_t(bk[k]) * QK + 4 * j;
+                    const float2 ms = s_stats[qk[k]];
+                    const float4 w = __ldg(reinterpret_cast<const float4 *>(a.ln_w + e));
+                    const float4 c = __ldg(reinterpret_cast<const float4 *>(a.ln_b + e));
+                    auto nf = [&](float x, float ww, float bb) {
+                        return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x, ms.x), ms.y), ww), bb);
+                    };
+                    v[k] = make_float4(nf(v[k].x, w.x, c.x), nf(v[k].y, w.y, c.y), nf(v[k].z, w.z, c.z),
+                                       nf(v[k].w, w.w, c.w));
                 }
+                finite = finite && isfinite(v[k].x) && isfinite(v[k].y) && isfinite(v[k].z) && isfinite(v[k].w);
             }
-#pragma unroll
-            for (int i = 0; i < QK; ++i) finite = finite && isfinite(v[i]);
-        } else {
-#pragma unroll
-            for (int i = 0; i < QK; ++i) v[i] = 0.0f;
+            amax[k] = fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w)));
         }
         if (!finite && blockIdx.x == 0) atomicOr(a.flags, 1);
-        float amax = 0.0f;
 #pragma unroll
-        for (int i = 0; i < QK; ++i) amax = fmaxf(amax, fabsf(v[i]));
-        const float d = __fdiv_rn(amax, 127.0f);
-        float id;
-        if (a.mode == 2) id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-        else id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        // word j holds elements 4j..4j+3: fragment lane 4g + (j & 3), register hi + 2 * (j >> 2)
-        const int mt = q / 16, r = q % 16, g = r & 7, hi = r >> 3;
-        uint32_t *dst = xw + ((b * MT + mt) * 32 + 4 * g) * 4 + hi;
+        for (int o = 1; o < 8; o <<= 1)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            uint32_t word = 0;
+            for (int k = 0; k < RO_QBATCH; ++k) amax[k] = fmaxf(amax[k], __shfl_xor_sync(0xffffffffu, amax[k], o));
+        // the batch holds 8 x 4 blocks: lane L divides for block (task L / 4, sub-block L % 4)
+        // once, instead of every lane of the warp dividing for its own block
+        float my_amax = 0.0f;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float sv = __fmul_rn(v[4 * j + e], id);
-                const int qv = a.mode == 0 ? int(roundf(sv)) : __float2int_rn(sv);
-                word |= (uint32_t(qv) & 0xffu) << (8 * e);
-            }
-            dst[(j & 3) * 4 + 2 * (j >> 2)] = word;
+        for (int k = 0; k < RO_QBATCH; ++k) {
+            const float m = __shfl_sync(0xffffffffu, amax[k], 8 * (lane & 3));
+            if ((lane >> 2) == k) my_amax = m;
         }
-        s_xs[b * MPAD + q] = __half2float(__float2half_rn(d));
+        const float my_d = __fdiv_rn(my_amax, 127.0f);
+        float my_id;
+        if (a.mode == 2) my_id = my_amax != 0.0f ? __fdiv_rn(127.0f, my_amax) : 0.0f;
+        else my_id = my_d != 0.0f ? __fdiv_rn(1.0f, my_d) : 0.0f;
+        {  // the block scale, stored by the lane that divided for it
+            const int k = lane >> 2, task = t0 + k * warps;
+            const int q = task / nchunk, b = (task % nchunk) * 4 + (lane & 3);
+            if (task < ntask && b < nb)
+                s_xs[b * MPAD + ((q & 7) >> 1) * (MPAD / 4) + (q >> 3) * 2 + (q & 1)] =
+                    __half2float(__float2half_rn(my_d));
+        }
+        float id[RO_QBATCH];
+#pragma unroll
+        for (int k = 0; k < RO_QBATCH; ++k) id[k] = __shfl_sync(0xffffffffu, my_id, 4 * k + (lane >> 3));
+#pragma unroll
+        for (int k = 0; k < RO_QBATCH; ++k) {
+            const int task = t0 + k * warps;
+            const int q = qk[k], b = bk[k];
+            if (task >= ntask || b >= nb) continue;  // lanes past the last block of the row hold nothing
+            auto quant = [&](float x) -> uint32_t {
+                const float sv = __fmul_rn(x, id[k]);
+                return uint32_t(a.mode == 0 ? int(roundf(sv)) : __float2int_rn(sv)) & 0xffu;
+            };
+            const uint32_t word =
+                quant(v[k].x) | (quant(v[k].y) << 8) | (quant(v[k].z) << 16) | (quant(v[k].w) << 24);
+            // word j holds elements 4j..4j+3: fragment lane 4g + (j & 3), register hi + 2 * (j >> 2)
+            const int mt = q / 16, r = q % 16, g = r & 7, hi = r >> 3;
+            xw[((b * MT + mt) * 32 + 4 * g + (j & 3)) * 4 + hi + 2 * (j >> 2)] = word;
+        }
     }
 }
 
@@ -295,7 +366,7 @@ __global__ void __launch_bounds__(RO_MAX_WARPS * 32, 1) k_readout(const ReadoutA
     for (int i = threadIdx.x; i < a.sup_words; i += blockDim.x) s_sup[i] = 0u;
     pdl_wait();
     pdl_trigger();  // the next kernel may launch now; it waits for this grid before reading
-    stage_queries<MT>(a, nb, s_xf, s_xs, s_stats, warps);
+    stage_queries<MT, NBC * QK>(a, nb, s_xf, s_xs, s_stats, warps);
     __syncthreads();  // bitmask zeroed before it is set
     for (int64_t i = threadIdx.x; i < a.nsup; i += blockDim.x) {
         const int64_t n = a.suppressed[i];
@@ -350,6 +421,20 @@ __global__ void __launch_bounds__(RO_MAX_WARPS * 32, 1) k_readout(const ReadoutA
                 c0 = mul2(s0, make_float2(-12582912.0f, -12582912.0f));
                 c1 = mul2(s1, make_float2(-12582912.0f, -12582912.0f));
             }
+            // this lane's query scales of the block: pairs (8 nt + 2 t, +1) for every n-tile
+            float2 dxs[NT];
+            if (NT == 1) {
+                dxs[0] = *reinterpret_cast<const float2 *>(s_xs + b * MPAD + t * (MPAD / 4));
+            } else {
+                const float4 *xs4 = reinterpret_cast<const float4 *>(s_xs + b * MPAD + t * (MPAD / 4));
+#pragma unroll
+                for (int i = 0; i < NT / 2; ++i) {
+                    const float4 f = xs4[i];
+                    dxs[2 * i] = make_float2(f.x, f.y);
+                    dxs[2 * i + 1] = make_float2(f.z, f.w);
+                }
+            }
+            const float2 zero = make_float2(0.0f, 0.0f);
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
                 const uint4 xf = s_xf[(b * MT + mt) * 32 + lane];
@@ -359,21 +444,21 @@ __global__ void __launch_bounds__(RO_MAX_WARPS * 32, 1) k_readout(const ReadoutA
                     if (nt >= NT) break;
                     int d[4];
                     mma_magic(d, a0, a1, a2, a3, h ? xf.y : xf.x, h ? xf.w : xf.z);
-                    const float2 dx = *reinterpret_cast<const float2 *>(s_xs + b * MPAD + 8 * nt + 2 * t);
+                    const float2 dx = dxs[nt];
+                    // each term is an fma with a +0 addend (exactly the product here, since a
+                    // running sum never holds -0): ptxas would fuse a packed multiply into the
+                    // packed add that follows it, an fma it cannot fuse
                     float2 lo, hi;
                     if (Q4) {
-                        lo = mul2(fma2(biased(d[0], d[1]), s0, c0), dx);
-                        hi = mul2(fma2(biased(d[2], d[3]), s1, c1), dx);
+                        lo = fma2(fma2(biased(d[0], d[1]), s0, c0), dx, zero);
+                        hi = fma2(fma2(biased(d[2], d[3]), s1, c1), dx, zero);
                     } else {
                         const float2 unbias = make_float2(-12582912.0f, -12582912.0f);  // exact
-                        lo = mul2(add2(biased(d[0], d[1]), unbias), mul2(s0, dx));
-                        hi = mul2(add2(biased(d[2], d[3]), unbias), mul2(s1, dx));
+                        lo = fma2(add2(biased(d[0], d[1]), unbias), mul2(s0, dx), zero);
+                        hi = fma2(add2(biased(d[2], d[3]), unbias), mul2(s1, dx), zero);
                     }
-                    // scalar adds: ptxas fuses a packed multiply and a packed add into one fma
-                    acc[nt][0].x = __fadd_rn(acc[nt][0].x, lo.x);
-                    acc[nt][0].y = __fadd_rn(acc[nt][0].y, lo.y);
-                    acc[nt][1].x = __fadd_rn(acc[nt][1].x, hi.x);
-                    acc[nt][1].y = __fadd_rn(acc[nt][1].y, hi.y);
+                    acc[nt][0] = add2(acc[nt][0], lo);
+                    acc[nt][1] = add2(acc[nt][1], hi);
                 }
             }
         };
