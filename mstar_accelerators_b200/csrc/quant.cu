@@ -253,6 +253,150 @@ __global__ void __launch_bounds__(256) k_quantize_frag(const float *__restrict__
     }
 }
 
+// The same result as k_quantize_frag, one warp per query row: the lanes load
+// the whole row at once (task t = elements 128 t .. 128 t + 127, one float4
+// per lane, so lane l holds elements 128 t + 4 l + c), and the LayerNorm sums
+// are formed in k_quantize_frag's order from registers: element e belongs to
+// its thread e mod VT (VT = 128 or 256 threads), which is thread
+// 128 (t mod VT/128) + 4 l + c, so each of those threads' running sums over t
+// is local to lane l; its warp reduction (butterfly over the thread's lane
+// bits 4..0) becomes a butterfly over lane bits 2..0 then over c, and the
+// warps' totals are added in thread order. Each lane then quantizes its four
+// elements of one block per task (block maxima over 8 lanes; one division per
+// lane for the row's blocks), so its four quants are one fragment word.
+constexpr int QW_MAX_TASKS = 12;  // rows up to 1536 wide
+constexpr int QW_WARPS = 2;
+
+template <int MODE, int NCH>
+__global__ void __launch_bounds__(QW_WARPS * 32) k_quantize_frag_warp(
+    const float *__restrict__ x, int64_t ldx, int64_t m, int64_t k, int64_t mpad, int64_t nb_pad,
+    const float *__restrict__ ln_w, const float *__restrict__ ln_b, float ln_eps, uint32_t *__restrict__ xf,
+    float *__restrict__ xs, int *__restrict__ xsum, int *__restrict__ status) {
+    const int lane = threadIdx.x & 31;
+    const int64_t q = int64_t(blockIdx.x) * QW_WARPS + (threadIdx.x >> 5);
+    pdl_wait();
+    pdl_trigger();
+    if (q >= mpad) return;  // warp-uniform
+    const int nb = int(k / QK), j = lane & 7, sb = lane >> 3;
+    const bool live_row = q < m;
+    const float *xr = x + q * ldx;
+    float4 v[NCH];
+#pragma unroll
+    for (int t = 0; t < NCH; ++t) {
+        v[t] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (live_row && 4 * t + sb < nb) v[t] = *reinterpret_cast<const float4 *>(xr + 128 * t + 4 * lane);
+    }
+    if (ln_w && live_row) {
+        constexpr int SL = NCH >= 8 ? 2 : 1;  // used only when VT = 256 (k >= 1024 needs NCH >= 8)
+        const int slabs = k >= 1024 ? 2 : 1;
+        auto stats = [&](auto term, float &total) {
+            float p[SL][4];
+#pragma unroll
+            for (int s2 = 0; s2 < SL; ++s2)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) p[s2][c] = 0.0f;
+#pragma unroll
+            for (int t = 0; t < NCH; ++t) {
+                if (4 * t + sb >= nb) continue;  // elements past the row: no term
+                const int s2 = SL == 2 ? (t & (slabs - 1)) : 0;
+                p[s2][0] = term(p[s2][0], v[t].x);
+                p[s2][1] = term(p[s2][1], v[t].y);
+                p[s2][2] = term(p[s2][2], v[t].z);
+                p[s2][3] = term(p[s2][3], v[t].w);
+            }
+            float tot[SL];
+#pragma unroll
+            for (int s2 = 0; s2 < SL; ++s2) {
+#pragma unroll
+                for (int o = 4; o; o >>= 1)  // thread lane bits 4, 3, 2 = this lane's bits 2, 1, 0
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) p[s2][c] += __shfl_xor_sync(0xffffffffu, p[s2][c], o);
+                float r[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) r[c] = p[s2][c] + p[s2][c ^ 2];  // thread lane bit 1
+                tot[s2] = r[0] + r[1];                                         // thread lane bit 0
+            }
+            float sum = 0.0f;  // the thread warps' totals in order: warp 4 s2 + (lane >> 3)
+#pragma unroll
+            for (int s2 = 0; s2 < SL; ++s2) {
+                if (s2 >= slabs) break;
+#pragma unroll
+                for (int w = 0; w < 4; ++w) sum += __shfl_sync(0xffffffffu, tot[s2], 8 * w);
+            }
+            total = sum;
+        };
+        float sum, var;
+        stats([](float acc, float e) { return acc + e; }, sum);
+        const float mean = sum / float(k);
+        stats([mean](float acc, float e) { const float y = e - mean; return fmaf(y, y, acc); }, var);
+        const float rstd = 1.0f / sqrtf(var / float(k) + ln_eps);
+#pragma unroll
+        for (int t = 0; t < NCH; ++t) {
+            if (4 * t + sb >= nb) continue;
+            const int64_t e = 128 * t + 4 * lane;
+            const float4 w = __ldg(reinterpret_cast<const float4 *>(ln_w + e));
+            const float4 c = __ldg(reinterpret_cast<const float4 *>(ln_b + e));
+            auto nf = [&](float xv, float ww, float bb) {
+                return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv, mean), rstd), ww), bb);
+            };
+            v[t] = make_float4(nf(v[t].x, w.x, c.x), nf(v[t].y, w.y, c.y), nf(v[t].z, w.z, c.z), nf(v[t].w, w.w, c.w));
+        }
+    }
+    if (live_row) {
+        bool finite = true;
+#pragma unroll
+        for (int t = 0; t < NCH; ++t)
+            if (4 * t + sb < nb)
+                finite = finite && isfinite(v[t].x) && isfinite(v[t].y) && isfinite(v[t].z) && isfinite(v[t].w);
+        if (!finite) atomicOr(status, 1);
+    }
+    float amax[NCH];
+#pragma unroll
+    for (int t = 0; t < NCH; ++t) amax[t] = fmaxf(fmaxf(fabsf(v[t].x), fabsf(v[t].y)), fmaxf(fabsf(v[t].z), fabsf(v[t].w)));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+        for (int t = 0; t < NCH; ++t) amax[t] = fmaxf(amax[t], __shfl_xor_sync(0xffffffffu, amax[t], o));
+    // one division per lane: lane L for blocks L and L + 32 (block b = 4 t + sub-block)
+    constexpr int NB2 = (4 * NCH + 31) / 32;
+    float my_id[NB2];
+#pragma unroll
+    for (int h = 0; h < NB2; ++h) {
+        const int b = 32 * h + lane;
+        float mine = 0.0f;
+#pragma unroll
+        for (int t = 0; t < NCH; ++t) {
+            const float mt = __shfl_sync(0xffffffffu, amax[t], 8 * (b & 3));
+            if ((b >> 2) == t) mine = mt;
+        }
+        const float d = __fdiv_rn(mine, 127.0f);
+        if (MODE == 2) my_id[h] = mine != 0.0f ? __fdiv_rn(127.0f, mine) : 0.0f;
+        else my_id[h] = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        if (b < nb_pad) xs[b * mpad + q] = __half2float(__float2half_rn(d));
+    }
+    const int64_t mtiles = mpad / 16, mt = q / 16;
+    const int r = int(q % 16), g = r & 7, hi = r >> 3;
+#pragma unroll
+    for (int t = 0; t < NCH; ++t) {
+        const int b = 4 * t + sb;
+        const float id = __shfl_sync(0xffffffffu, my_id[(4 * t) / 32 + 0], (4 * t + sb) & 31);
+        auto quant = [&](float xv) -> int {
+            const float sv = __fmul_rn(xv, id);
+            return MODE == 0 ? int(roundf(sv)) : __float2int_rn(sv);
+        };
+        const int q0 = quant(v[t].x), q1 = quant(v[t].y), q2 = quant(v[t].z), q3 = quant(v[t].w);
+        int qs = q0 + q1 + q2 + q3;
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
+        if (b >= nb_pad) continue;
+        const uint32_t word = (uint32_t(q0) & 0xffu) | ((uint32_t(q1) & 0xffu) << 8) | ((uint32_t(q2) & 0xffu) << 16) |
+                              ((uint32_t(q3) & 0xffu) << 24);
+        // word j holds elements 4j..4j+3: fragment lane 4g + (j & 3), register hi + 2 * (j >> 2)
+        xf[((b * mtiles + mt) * 32 + 4 * g + (j & 3)) * 4 + hi + 2 * (j >> 2)] = word;
+        if (j == 0) xsum[b * mpad + q] = qs;
+    }
+}
+
 // ------------------------------------------------------------------ launchers
 void launch_pack(const float *in, uint8_t *out, int64_t rows, int64_t width, int q4, int preround,
                  int fused, int *flags, cudaStream_t s) {
@@ -280,6 +424,37 @@ void launch_quantize_rows(int mode, const float *x, int64_t ldx, int64_t m, int6
     else k_quantize_rows<1><<<grid, 256, 0, s>>>(x, ldx, m, k, blocks, status);
 }
 
+template <int MODE, int NCH>
+static void quantize_warp_nch(cudaLaunchConfig_t &cfg, const float *x, int64_t ldx, int64_t m, int64_t k,
+                              int64_t mpad, int64_t nb_pad, const float *ln_w, const float *ln_b, float ln_eps,
+                              uint32_t *xf, float *xs, int *xsum, int *status) {
+    cudaLaunchKernelEx(&cfg, k_quantize_frag_warp<MODE, NCH>, x, ldx, m, k, mpad, nb_pad, ln_w, ln_b, ln_eps, xf,
+                       xs, xsum, status);
+}
+
+template <int MODE>
+static void quantize_warp_mode(int nch, cudaLaunchConfig_t &cfg, const float *x, int64_t ldx, int64_t m,
+                               int64_t k, int64_t mpad, int64_t nb_pad, const float *ln_w, const float *ln_b,
+                               float ln_eps, uint32_t *xf, float *xs, int *xsum, int *status) {
+#define QW_CASE(N)                                                                                          \
+    case N:                                                                                                 \
+        quantize_warp_nch<MODE, N>(cfg, x, ldx, m, k, mpad, nb_pad, ln_w, ln_b, ln_eps, xf, xs, xsum, status); \
+        break;
+    switch (nch) {
+        QW_CASE(1) QW_CASE(2) QW_CASE(3) QW_CASE(4) QW_CASE(5) QW_CASE(6)
+        QW_CASE(7) QW_CASE(8) QW_CASE(9) QW_CASE(10) QW_CASE(11) QW_CASE(12)
+    }
+#undef QW_CASE
+}
+
+static void launch_quantize_warp(int mode, int nch, cudaLaunchConfig_t &cfg, const float *x, int64_t ldx, int64_t m,
+                                 int64_t k, int64_t mpad, int64_t nb_pad, const float *ln_w, const float *ln_b,
+                                 float ln_eps, uint32_t *xf, float *xs, int *xsum, int *status) {
+    if (mode == 0) quantize_warp_mode<0>(nch, cfg, x, ldx, m, k, mpad, nb_pad, ln_w, ln_b, ln_eps, xf, xs, xsum, status);
+    else if (mode == 2) quantize_warp_mode<2>(nch, cfg, x, ldx, m, k, mpad, nb_pad, ln_w, ln_b, ln_eps, xf, xs, xsum, status);
+    else quantize_warp_mode<1>(nch, cfg, x, ldx, m, k, mpad, nb_pad, ln_w, ln_b, ln_eps, xf, xs, xsum, status);
+}
+
 void launch_quantize_frag(int mode, const float *x, int64_t ldx, int64_t m, int64_t k, int64_t mpad,
                           int64_t nb_pad, const float *ln_w, const float *ln_b, float ln_eps, uint32_t *xf,
                           float *xs, int *xsum, int *status, cudaStream_t s) {
@@ -292,6 +467,15 @@ void launch_quantize_frag(int mode, const float *x, int64_t ldx, int64_t m, int6
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    const int64_t nch = (k / QK + 3) / 4;
+    if (nch <= QW_MAX_TASKS && uintptr_t(x) % 16 == 0 && ldx % 4 == 0 &&
+        (!ln_w || (uintptr_t(ln_w) % 16 == 0 && uintptr_t(ln_b) % 16 == 0))) {
+        cfg.gridDim = dim3(unsigned(ceil_div(mpad, QW_WARPS)));
+        cfg.blockDim = dim3(QW_WARPS * 32);
+        launch_quantize_warp(mode, int(nch), cfg, x, ldx, m, k, mpad, nb_pad, ln_w, ln_b, ln_eps, xf, xs, xsum,
+                             status);
+        return;
+    }
     auto kernel = mode == 0 ? k_quantize_frag<0> : mode == 2 ? k_quantize_frag<2> : k_quantize_frag<1>;
     cudaLaunchKernelEx(&cfg, kernel, x, ldx, m, k, mpad, nb_pad, ln_w, ln_b, ln_eps, xf, xs, xsum, status);
 }
