@@ -119,6 +119,26 @@ MSTAR_B200_API int mstar_b200_linear_readout(void *handle, const float *x, int64
     uint64_t suppressed_count, const float *ln_weight, const float *ln_bias, float ln_eps,
     int rounding, void *stream, char *error, size_t error_size);
 MSTAR_B200_API int mstar_b200_linear_close(void *handle, char *error, size_t error_size);
+/* Q8_0 activation fragments of a handle's decode GEMV (the layout its
+ * quantizer writes: fragments [blocks][rows / 16][32][4] words, scales and
+ * quant sums [blocks][rows]), for a producer kernel that quantizes its own
+ * output straight into them (mstar_b200_attend_q8). */
+typedef struct mstar_b200_q8_frags {
+    void *fragments;
+    float *scales;
+    int32_t *sums;
+    int64_t blocks;    /* padded block count of the handle's width */
+    int64_t rows;      /* 16 or 32 */
+    int32_t rounding;  /* MSTAR_B200_Q8_REF / ARM / X86 */
+} mstar_b200_q8_frags;
+/* Describe the handle's fragment buffers for `queries` (1..32) rows. */
+MSTAR_B200_API int mstar_b200_linear_frags(void *handle, int64_t queries, int32_t rounding,
+    mstar_b200_q8_frags *frags, char *error, size_t error_size);
+/* The decode GEMV (+ bias / GELU / residual epilogue, flags as linear_run) on
+ * the fragments a producer wrote for `queries` rows: equal to linear_run on the
+ * producer's fp32 output (ggml_mul_mat + the same epilogue). */
+MSTAR_B200_API int mstar_b200_linear_run_frags(void *handle, int64_t queries, float *out, int64_t out_stride,
+    const float *residual, int flags, void *stream, char *error, size_t error_size);
 /* Prepare the vocab-readout tile layout of a handle (16 weight rows per tile,
  * the whole tile's fragments and scales contiguous): later linear_readout
  * calls on the handle use the tile kernel, bit-identical to the GEMV path.
@@ -338,6 +358,17 @@ MSTAR_B200_API int mstar_b200_attend(const float *q, int64_t q_stride, const flo
     int32_t batch, int32_t queries, const int64_t *begin, const int64_t *kv_length, int32_t causal,
     int32_t shared, float *out, int64_t out_stride, float scale, int32_t *status, void *workspace,
     uint64_t workspace_bytes, void *stream, char *error, size_t error_size);
+/* mstar_b200_attend that also writes the output rows (batch * queries <= 32)
+ * as the Q8_0 activation fragments of the linear that consumes them (out_proj
+ * after the attention, decoder.cpp:566-580): the quantization equals the one
+ * mstar_b200_linear_run performs on `out`, so mstar_b200_linear_run_frags on
+ * that handle gives the same bytes as mstar_b200_linear_run(out). frags comes
+ * from mstar_b200_linear_frags; NULL makes this mstar_b200_attend. */
+MSTAR_B200_API int mstar_b200_attend_q8(const float *q, int64_t q_stride, const float *k_new, const float *v_new,
+    int64_t kv_stride, void *k_plane, void *v_plane, int64_t capacity, int32_t heads, int32_t head_dim,
+    int32_t batch, int32_t queries, const int64_t *begin, const int64_t *kv_length, int32_t causal,
+    int32_t shared, float *out, int64_t out_stride, float scale, int32_t *status, void *workspace,
+    uint64_t workspace_bytes, const mstar_b200_q8_frags *frags, void *stream, char *error, size_t error_size);
 /* Cross K/V planes from the fused projection of the encoder states
  * (decoder.cpp:247-250, 322-330: one [3072 x 384] Q8_0 matrix for the four
  * layers' k/v; biases added, then stored fp16 like cross_bias_set_rows). */

@@ -267,6 +267,74 @@ int mstar_b200_linear_run(void *handle, const float *x, int64_t x_stride, int64_
     }
 }
 
+int mstar_b200_linear_frags(void *handle, int64_t queries, int32_t rounding, mstar_b200_q8_frags *frags,
+                            char *error, size_t error_size) {
+    try {
+        require(handle && frags, "missing linear handle or fragment descriptor");
+        auto &h = *static_cast<Linear *>(handle);
+        check_rounding(rounding);
+        require(queries >= 1 && queries <= CHUNK, "fragment staging takes 1..32 queries");
+        require(h.gemv_ok, "fragment staging needs a width of at most 4096");
+        frags->fragments = h.xf;
+        frags->scales = h.xs;
+        frags->sums = h.xsum;
+        frags->blocks = h.nb_pad;
+        frags->rows = queries <= 16 ? 16 : 32;
+        frags->rounding = rounding;
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+int mstar_b200_linear_run_frags(void *handle, int64_t queries, float *out, int64_t out_stride, const float *residual,
+                                int flags, void *stream, char *error, size_t error_size) {
+    try {
+        require(handle, "missing linear handle");
+        auto &h = *static_cast<Linear *>(handle);
+        Busy busy(h.busy);
+        require(queries >= 1 && queries <= CHUNK, "fragment GEMV takes 1..32 queries");
+        require(h.gemv_ok, "fragment GEMV needs a width of at most 4096");
+        require((flags & ~15) == 0 && !((flags & 2) && (flags & 8)), "invalid epilogue flags");
+        require(!(flags & 1) || h.bias, "bias epilogue without a prepared bias");
+        require(out_stride >= h.rows, "invalid row stride");
+        const uint64_t ob = uint64_t((queries - 1) * out_stride + h.rows) * 4;
+        check_range({out, ob}, ob, 4, "output");
+        check_device(out, "output");
+        if (flags & 4) {
+            check_range({residual, ob}, ob, 4, "residual");
+            require(residual == out || disjoint({residual, ob}, {out, ob}), "residual partially overlaps output");
+            check_device(residual, "residual");
+        } else require(!residual, "residual given without its epilogue flag");
+        GemvArgs a{};
+        a.status = h.status;
+        a.wq = h.wq;
+        a.ws = reinterpret_cast<const __half2 *>(h.ws);
+        a.xf = reinterpret_cast<const uint4 *>(h.xf);
+        a.xs = h.xs;
+        a.xsum = h.xsum;
+        a.groups = h.groups;
+        a.nb_pad = h.nb_pad;
+        a.nb = h.nb;
+        a.n = h.rows;
+        a.m = queries;
+        a.out = out;
+        a.ldo = out_stride;
+        a.bias = h.bias;
+        a.residual = (flags & 4) ? residual : nullptr;
+        a.flags = flags;
+        a.gelu = h.gelu;
+        a.wpg_override = h.wpg_override;
+        launch_gemv(h.q4, a, as_stream(stream));
+        cuda_check(cudaGetLastError(), "fragment GEMV launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
 int mstar_b200_linear_block_sums(void *handle, const float *x, int64_t queries, int32_t *sums,
                                  uint64_t sums_bytes, int rounding, void *stream, char *error, size_t error_size) {
     try {

@@ -2,7 +2,7 @@
 // Decode / prefill attention over fp16 K/V planes as device functions, shared
 // by the attention kernels (decoder.cu) and the persistent decode-step kernel
 // (step.cu).
-#include "common.cuh"
+#include "quant.cuh"
 
 namespace mb {
 
@@ -29,7 +29,63 @@ struct AttArgs {
     float scale;
     int *status;
     float *partial;  // splits > 1: [groups * heads][splits][rows][HEAD_DIM + 2] (O, max, sum)
+    Q8Frags frags;   // xf != null: also write the output rows as the next linear's Q8_0 fragments
 };
+
+// Q8_0 fragments of one output row of a head from the attention epilogue: lane
+// (g, t4) of the row's 4-lane group holds dims 8 j + 2 t4 + c, so block kb
+// (dims 32 kb ..) is j = 4 kb + jj with element 8 jj + 2 t4 + c. The block
+// maximum and quant sum take the 4 lanes; fragment word w = 2 jj + t4 / 2
+// (elements 4 w .. 4 w + 3) joins the bytes of lanes t4 and t4 + 1.
+template <int MODE>
+__device__ __forceinline__ void frag_head_row(const Q8Frags &f, const float (&v)[8][2], int64_t token, int h,
+                                              int t4, unsigned group, int *status) {
+    const int64_t mtiles = f.mpad / 16, mt = token / 16;
+    const int r = int(token % 16), gq = r & 7, hi = r >> 3;
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb) {
+        const int64_t b = 2 * h + kb;
+        float amax = 0.0f;
+        bool finite = true;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                amax = fmaxf(amax, fabsf(v[4 * kb + jj][c]));
+                finite = finite && isfinite(v[4 * kb + jj][c]);
+            }
+        if (!finite) atomicOr(status, 1);
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(group, amax, o));
+        const float d = __fdiv_rn(amax, 127.0f);
+        float id;
+        if (MODE == 2) id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        else id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        int qsum = 0;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+            int qv[2];
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const float sv = __fmul_rn(v[4 * kb + jj][c], id);
+                qv[c] = MODE == 0 ? int(roundf(sv)) : __float2int_rn(sv);
+                qsum += qv[c];
+            }
+            const uint32_t hw = (uint32_t(qv[0]) & 0xffu) | ((uint32_t(qv[1]) & 0xffu) << 8);
+            const uint32_t other = __shfl_xor_sync(group, hw, 1);
+            if ((t4 & 1) == 0) {
+                const int w = 2 * jj + (t4 >> 1);
+                f.xf[((b * mtiles + mt) * 32 + 4 * gq + (w & 3)) * 4 + hi + 2 * (w >> 2)] = hw | (other << 16);
+            }
+        }
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) qsum += __shfl_xor_sync(group, qsum, o);
+        if (t4 == 0) {
+            f.xs[b * f.mpad + token] = __half2float(__float2half_rn(d));
+            f.xsum[b * f.mpad + token] = qsum;
+        }
+    }
+}
 
 // D += A(16x16 f16, row) * B(16x8 f16, col), fp32 accumulate.
 __device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -255,10 +311,19 @@ __device__ __forceinline__ void attend_task(const AttArgs &a, int task, unsigned
             if (a.splits == 1) {  // one CTA saw every key: normalise and write the row
                 const float l = lrun[half], inv = l > 0.0f ? 1.0f / l : 0.0f;
                 float *dst = a.out + row_q(r) * a.out_stride + h * HEAD_DIM + 2 * t4;
+                float v[8][2];
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    *reinterpret_cast<float2 *>(dst + 8 * j) =
-                        make_float2(o[j][2 * half] * inv, o[j][2 * half + 1] * inv);
+                for (int j = 0; j < 8; ++j) {
+                    v[j][0] = o[j][2 * half] * inv;
+                    v[j][1] = o[j][2 * half + 1] * inv;
+                    *reinterpret_cast<float2 *>(dst + 8 * j) = make_float2(v[j][0], v[j][1]);
+                }
+                if (a.frags.xf) {  // the row's 4 lanes are live together
+                    const unsigned group = 0xFu << (lane & ~3);
+                    if (a.frags.mode == 0) frag_head_row<0>(a.frags, v, row_q(r), h, t4, group, a.status);
+                    else if (a.frags.mode == 2) frag_head_row<2>(a.frags, v, row_q(r), h, t4, group, a.status);
+                    else frag_head_row<1>(a.frags, v, row_q(r), h, t4, group, a.status);
+                }
             } else {
                 float *part = a.partial + ((int64_t(gh) * a.splits + split) * R + r) * (HEAD_DIM + 2);
 #pragma unroll
@@ -295,7 +360,16 @@ __device__ __forceinline__ void merge_task(const AttArgs &a, int task, int dd) {
         }
     }
     const int64_t qrow = a.shared ? int64_t(r) : int64_t(grp) * a.nq + r;
-    a.out[qrow * a.out_stride + h * HEAD_DIM + dd] = l > 0.0f ? o / l : 0.0f;
+    const float v = l > 0.0f ? o / l : 0.0f;
+    a.out[qrow * a.out_stride + h * HEAD_DIM + dd] = v;
+    if (a.frags.xf) {  // warp dd / 32 holds block 2 h + dd / 32 of the row
+        const Q8Frags &f = a.frags;
+        const int64_t b = 2 * h + dd / 32;
+        const int mtiles = int(f.mpad / 16);
+        if (f.mode == 0) frag_block<0>(v, true, b, int(qrow), mtiles, f.xf, f.xs, f.xsum, a.status);
+        else if (f.mode == 2) frag_block<2>(v, true, b, int(qrow), mtiles, f.xf, f.xs, f.xsum, a.status);
+        else frag_block<1>(v, true, b, int(qrow), mtiles, f.xf, f.xs, f.xsum, a.status);
+    }
 }
 
 

@@ -113,11 +113,12 @@ uint64_t mstar_b200_attend_workspace(int32_t heads, int32_t batch, int32_t queri
     return p.partial_bytes > 0 ? p.partial_bytes : 256;
 }
 
-int mstar_b200_attend(const float *q, int64_t q_stride, const float *k_new, const float *v_new, int64_t kv_stride,
-                      void *k_plane, void *v_plane, int64_t capacity, int32_t heads, int32_t head_dim,
-                      int32_t batch, int32_t queries, const int64_t *begin, const int64_t *kv_length, int32_t causal,
-                      int32_t shared, float *out, int64_t out_stride, float scale, int32_t *status, void *workspace,
-                      uint64_t workspace_bytes, void *stream, char *error, size_t error_size) {
+int mstar_b200_attend_q8(const float *q, int64_t q_stride, const float *k_new, const float *v_new, int64_t kv_stride,
+                         void *k_plane, void *v_plane, int64_t capacity, int32_t heads, int32_t head_dim,
+                         int32_t batch, int32_t queries, const int64_t *begin, const int64_t *kv_length,
+                         int32_t causal, int32_t shared, float *out, int64_t out_stride, float scale, int32_t *status,
+                         void *workspace, uint64_t workspace_bytes, const mstar_b200_q8_frags *frags, void *stream,
+                         char *error, size_t error_size) {
     try {
         require(head_dim == HEAD_DIM, "attention head_dim must be 64");
         require(queries >= 1 && queries <= MAX_Q && batch >= 1 && heads >= 1, "invalid attention geometry");
@@ -166,6 +167,20 @@ int mstar_b200_attend(const float *q, int64_t q_stride, const float *k_new, cons
         a.scale = scale;
         a.status = status;
         a.partial = static_cast<float *>(workspace);
+        if (frags) {
+            const int64_t rows = int64_t(batch) * queries;
+            require(frags->fragments && frags->scales && frags->sums, "missing fragment buffers");
+            require(rows <= frags->rows && (frags->rows == 16 || frags->rows == 32), "fragment rows too few");
+            require(frags->blocks >= int64_t(heads) * HEAD_DIM / QK, "fragment blocks fewer than the output width");
+            require(frags->rounding >= 0 && frags->rounding <= 2, "unknown Q8_0 activation rounding");
+            check_device(frags->fragments, "fragment buffer");
+            a.frags.xf = static_cast<uint32_t *>(frags->fragments);
+            a.frags.xs = frags->scales;
+            a.frags.xsum = frags->sums;
+            a.frags.nb_pad = frags->blocks;
+            a.frags.mpad = frags->rows;
+            a.frags.mode = frags->rounding;
+        }
         cudaStream_t s = as_stream(stream);
         const unsigned grid = unsigned(p.groups * heads * p.splits);
         const int threads = 32 * (p.rows > 64 ? (p.rows + 15) / 16 : 4);
@@ -178,6 +193,16 @@ int mstar_b200_attend(const float *q, int64_t q_stride, const float *k_new, cons
         message(error, error_size, e.what());
         return -1;
     }
+}
+
+int mstar_b200_attend(const float *q, int64_t q_stride, const float *k_new, const float *v_new, int64_t kv_stride,
+                      void *k_plane, void *v_plane, int64_t capacity, int32_t heads, int32_t head_dim,
+                      int32_t batch, int32_t queries, const int64_t *begin, const int64_t *kv_length, int32_t causal,
+                      int32_t shared, float *out, int64_t out_stride, float scale, int32_t *status, void *workspace,
+                      uint64_t workspace_bytes, void *stream, char *error, size_t error_size) {
+    return mstar_b200_attend_q8(q, q_stride, k_new, v_new, kv_stride, k_plane, v_plane, capacity, heads, head_dim,
+                                batch, queries, begin, kv_length, causal, shared, out, out_stride, scale, status,
+                                workspace, workspace_bytes, nullptr, stream, error, error_size);
 }
 
 int mstar_b200_fill_kv(const float *projected, int64_t stride, int64_t k_offset, int64_t v_offset,

@@ -43,6 +43,49 @@ struct GemvArgs {
     int ctas_per_sm;           // streamed (unsplit) launches: resident CTAs per SM (0: default)
 };
 
+// Quantizes one 32-element block (lane = element) of token `token` to Q8_0 and
+// writes it in the layout of k_quantize_frag: xf [nb_pad][mtiles][32][4 words], xs / xsum [nb_pad][mpad].
+template <int MODE>
+__device__ __forceinline__ void frag_block(float v, bool live, int64_t b, int token, int mtiles, uint32_t *xf,
+                                           float *xs, int *xsum, int *status) {
+    const int lane = threadIdx.x & 31;
+    if (live && !isfinite(v)) atomicOr(status, 1);
+    float amax = fabsf(v);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 127.0f);
+    float id;
+    if (MODE == 2) id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+    else id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float sv = __fmul_rn(v, id);
+    const int q = MODE == 0 ? int(roundf(sv)) : __float2int_rn(sv);
+    const int mt = token / 16, r = token % 16, g = r & 7, hi = r >> 3;
+    const int t = (lane & 15) >> 2, half = lane >> 4;
+    uint32_t byte = uint32_t(q) & 0xffu;
+    uint32_t word = byte;
+    word |= __shfl_down_sync(0xffffffffu, byte, 1) << 8;
+    word |= __shfl_down_sync(0xffffffffu, byte, 2) << 16;
+    word |= __shfl_down_sync(0xffffffffu, byte, 3) << 24;
+    if ((lane & 3) == 0) xf[((b * mtiles + mt) * 32 + (4 * g + t)) * 4 + hi + 2 * half] = word;
+    int qsum = q;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+    if (lane == 0) {
+        xs[b * mtiles * 16 + token] = __half2float(__float2half_rn(d));
+        xsum[b * mtiles * 16 + token] = qsum;
+    }
+}
+
+// A Q8_0 activation-fragment destination (the layout above) that a producer
+// kernel fills for the linear that consumes its output.
+struct Q8Frags {
+    uint32_t *xf;
+    float *xs;
+    int *xsum;
+    int64_t nb_pad, mpad;
+    int mode;  // Q8_0 activation rounding: 0 ref, 1 arm, 2 x86
+};
+
 bool gemv_supported(int64_t nb_pad);
 void launch_gemv(int q4, const GemvArgs &a, cudaStream_t s);
 

@@ -10,6 +10,8 @@ CPU computation in place of a kernel.
 """
 from __future__ import annotations
 
+import ctypes as C
+
 import torch
 
 from . import native
@@ -221,6 +223,37 @@ class BlockLinear:
         check(self.lib.mstar_b200_linear_prepare_gemm(self.handle, self.blocks.data_ptr(), _nbytes(self.blocks),
                                                       int(max_queries), e, len(e)), e, "B200 GEMM preparation")
         self.gemm_rows = int(max_queries)
+
+    def frags(self, queries: int, rounding: str = "arm") -> "native.Q8Frags":
+        """Descriptor of this handle's Q8_0 activation fragments for `queries` (1..32) rows,
+        for a producer that quantizes straight into them (attention with frags=)."""
+        key = (int(queries), rounding)
+        cache = self.__dict__.setdefault("_frags", {})
+        if key not in cache:
+            f = native.Q8Frags()
+            e = error_buffer()
+            check(self.lib.mstar_b200_linear_frags(self.handle, int(queries), native.ROUNDING[rounding],
+                                                   C.byref(f), e, len(e)), e, "B200 fragment descriptor")
+            cache[key] = f
+        return cache[key]
+
+    def run_frags(self, queries: int, *, out: torch.Tensor, residual: torch.Tensor | None = None, bias: bool = True,
+                  gelu: str | None = None) -> torch.Tensor:
+        """The decode GEMV + epilogue on fragments a producer wrote for `queries` rows."""
+        o2 = out.reshape(-1, self.rows)
+        flags = (BIAS if (bias and self.has_bias) else 0)
+        flags |= {None: 0, "tanh": GELU, "erf": GELU_ERF}[gelu]
+        r_ptr = None
+        if residual is not None:
+            r2 = residual.reshape(-1, self.rows)
+            if r2.stride() != o2.stride():
+                raise ValueError("residual layout differs from the output")
+            flags |= RESIDUAL
+            r_ptr = r2.data_ptr()
+        e = error_buffer()
+        check(self.lib.mstar_b200_linear_run_frags(self.handle, int(queries), o2.data_ptr(), o2.stride(0), r_ptr,
+                                                   flags, _stream(out.device), e, len(e)), e, "B200 fragment GEMV")
+        return out
 
     def prepare_readout(self) -> None:
         """Build the vocab-readout tile layout; later readout calls use the tile kernel (synchronises)."""

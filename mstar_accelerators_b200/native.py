@@ -25,6 +25,12 @@ BIAS, GELU, RESIDUAL, GELU_ERF = 1, 2, 4, 8
 ACT_F32, ACT_F16 = 0, 1
 OUT_F32, OUT_F16, OUT_STAGED = 0, 1, 2
 
+
+class Q8Frags(C.Structure):
+    """mstar_b200_q8_frags: a handle's Q8_0 activation-fragment buffers."""
+    _fields_ = [("fragments", C.c_void_p), ("scales", C.c_void_p), ("sums", C.c_void_p), ("blocks", C.c_int64),
+                ("rows", C.c_int64), ("rounding", C.c_int32)]
+
 _vp, _i64, _u64, _sz, _int = C.c_void_p, C.c_int64, C.c_uint64, C.c_size_t, C.c_int
 _err = [C.c_char_p, _sz]
 
@@ -44,6 +50,8 @@ SIGNATURES = {
     "mstar_b200_linear_set_split": (_int, [_vp, _int, *_err]),
     "mstar_b200_linear_prepare_gemm": (_int, [_vp, _vp, _u64, _i64, *_err]),
     "mstar_b200_linear_prepare_readout": (_int, [_vp, _vp, _u64, *_err]),
+    "mstar_b200_linear_frags": (_int, [_vp, _i64, C.c_int32, _vp, *_err]),
+    "mstar_b200_linear_run_frags": (_int, [_vp, _i64, _vp, _i64, _vp, _int, _vp, *_err]),
     "mstar_b200_linear_gemm": (_int, [_vp, _vp, _u64, _i64, _vp, _u64, _i64, C.c_int32, _vp, _u64, _i64, _i64, _i64,
                                       _i64, C.c_int32, C.c_int32, _vp, _vp, *_err]),
     "mstar_b200_tp_barrier": (_int, [_vp, _vp, C.c_int32, C.c_int32, _vp, _vp, _vp, *_err]),
@@ -60,6 +68,9 @@ SIGNATURES = {
     "mstar_b200_attend": (_int, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64, C.c_int32, C.c_int32, C.c_int32,
                                  C.c_int32, _vp, _vp, C.c_int32, C.c_int32, _vp, _i64, C.c_float, _vp, _vp, _u64,
                                  _vp, *_err]),
+    "mstar_b200_attend_q8": (_int, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64, C.c_int32, C.c_int32, C.c_int32,
+                                 C.c_int32, _vp, _vp, C.c_int32, C.c_int32, _vp, _i64, C.c_float, _vp, _vp, _u64,
+                                 _vp, _vp, *_err]),
     "mstar_b200_fill_kv": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _vp, *_err]),
     "mstar_b200_moe_route": (_int, [_vp, _i64, _i64, _vp, C.c_int32, C.c_int32, C.c_int32, _vp, _vp, _vp, _vp,
                                     *_err]),

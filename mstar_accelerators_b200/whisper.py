@@ -170,16 +170,21 @@ class WhisperDecoderB200:
                                         x.data_ptr(), self.status.data_ptr(), _stream(self.device), e, len(e)),
               e, "B200 embedding")
 
-    def _attend(self, q, q_stride, k_new, v_new, kv_stride, kp, vp, capacity, nq, begin, kv_len, causal, shared, out):
+    def _attend(self, q, q_stride, k_new, v_new, kv_stride, kp, vp, capacity, nq, begin, kv_len, causal, shared, out,
+                frags=None):
+        """Attention into out; with frags (a linear's fragment descriptor) the rows are also
+        quantized for that linear's run_frags."""
         ws = self._ws[(nq, capacity, bool(shared))]
         e = error_buffer()
-        check(self.lib.mstar_b200_attend(q.data_ptr(), q_stride, k_new.data_ptr() if k_new is not None else None,
-                                         v_new.data_ptr() if v_new is not None else None, kv_stride,
-                                         kp.data_ptr(), vp.data_ptr(), capacity, self.cfg.heads, 64, self.batch, nq,
-                                         begin.data_ptr() if begin is not None else None,
-                                         kv_len.data_ptr() if kv_len is not None else None, int(causal), int(shared),
-                                         out.data_ptr(), out.stride(0), 1.0 / math.sqrt(64), self.status.data_ptr(),
-                                         ws.data_ptr(), ws.numel(), _stream(self.device), e, len(e)),
+        check(self.lib.mstar_b200_attend_q8(q.data_ptr(), q_stride, k_new.data_ptr() if k_new is not None else None,
+                                            v_new.data_ptr() if v_new is not None else None, kv_stride,
+                                            kp.data_ptr(), vp.data_ptr(), capacity, self.cfg.heads, 64, self.batch,
+                                            nq, begin.data_ptr() if begin is not None else None,
+                                            kv_len.data_ptr() if kv_len is not None else None, int(causal),
+                                            int(shared), out.data_ptr(), out.stride(0), 1.0 / math.sqrt(64),
+                                            self.status.data_ptr(), ws.data_ptr(), ws.numel(),
+                                            C.byref(frags) if frags is not None else None, _stream(self.device),
+                                            e, len(e)),
               e, "B200 attention")
 
     def _body(self, x: torch.Tensor, nq: int, begin: torch.Tensor):
@@ -191,15 +196,23 @@ class WhisperDecoderB200:
         att = self._buf(f"att{nq}", (rows, d))
         cq = self._buf(f"cq{nq}", (rows, d))
         h = self._buf(f"h{nq}", (rows, cfg.ffn))
+        fused = rows <= 32  # attention quantizes its rows straight into the out-projections' fragments
         for i, Lr in enumerate(self.layers):
             Lr["qkv"](x, out=qkv, norm=Lr["ln1"], rounding=r)
             self._attend(qkv, qkv.stride(0), qkv[:, d:], qkv[:, 2 * d:], qkv.stride(0), self.self_k[i],
-                         self.self_v[i], cfg.target, nq, begin, None, True, False, att)
-            Lr["out"](att, out=x, residual=x, rounding=r)
+                         self.self_v[i], cfg.target, nq, begin, None, True, False, att,
+                         Lr["out"].frags(rows, r) if fused else None)
+            if fused:
+                Lr["out"].run_frags(rows, out=x, residual=x)
+            else:
+                Lr["out"](att, out=x, residual=x, rounding=r)
             Lr["cq"](x, out=cq, norm=Lr["ln2"], rounding=r)
             self._attend(cq, cq.stride(0), None, None, 0, self.cross_k[i], self.cross_v[i], cfg.source, nq, None,
-                         self.cross_len, False, self.shared_cross, att)
-            Lr["cout"](att, out=x, residual=x, rounding=r)
+                         self.cross_len, False, self.shared_cross, att, Lr["cout"].frags(rows, r) if fused else None)
+            if fused:
+                Lr["cout"].run_frags(rows, out=x, residual=x)
+            else:
+                Lr["cout"](att, out=x, residual=x, rounding=r)
             Lr["fc1"](x, out=h, norm=Lr["ln3"], gelu="tanh", rounding=r)
             Lr["fc2"](h, out=x, residual=x, rounding=r)
 

@@ -115,3 +115,56 @@ def test_per_sequence_lengths_and_invalid_rows():
     ref = reference(q.cpu().numpy(), kp.double().cpu().numpy(), vp.double().cpu().numpy(), lens, list(range(B)))
     np.testing.assert_allclose(got, ref, rtol=5e-5, atol=5e-5)
     assert np.all(got[3] == 0.0)
+
+
+def _attend_q8(lib, frags, q, kp, vp, capacity, batch, nq, causal, shared, begin=None, kv_len=None):
+    import ctypes as C
+    from mstar_accelerators_b200 import native
+    out = torch.empty((batch * nq, H * D), device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    n = int(lib.mstar_b200_attend_workspace(H, batch, nq, capacity, int(shared)))
+    ws = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    e = native.error_buffer()
+    native.check(lib.mstar_b200_attend_q8(
+        q.data_ptr(), q.stride(0), None, None, 0, kp.data_ptr(), vp.data_ptr(), capacity, H, D, batch, nq,
+        begin.data_ptr() if begin is not None else None, kv_len.data_ptr() if kv_len is not None else None,
+        int(causal), int(shared), out.data_ptr(), out.stride(0), 1.0 / math.sqrt(D), status.data_ptr(),
+        ws.data_ptr(), n, C.byref(frags), torch.cuda.current_stream().cuda_stream, e, len(e)), e, "attention")
+    return out, status
+
+
+@pytest.mark.parametrize("shared,batch", [(True, 32), (False, 32), (False, 5), (True, 12)])
+@pytest.mark.parametrize("rounding", ["arm", "x86", "ref"])
+def test_attention_output_fragments_equal_the_linear_quantizer(shared, batch, rounding):
+    """attend_q8 + run_frags on a Q8_0 out-projection gives the bytes of attend + linear_run."""
+    from mstar_accelerators_b200 import native
+    from mstar_accelerators_b200.linear import BlockLinear
+    lib = native.load()
+    g = torch.Generator(device="cuda").manual_seed(batch + int(shared))
+    cap = 1500 if shared else 448
+    nseq = 1 if shared else batch
+    kp = (torch.randn((nseq, cap, H * D), device="cuda", generator=g)).half()
+    vp = (torch.randn((nseq, cap, H * D), device="cuda", generator=g)).half()
+    q = torch.randn((batch, H * D), device="cuda", generator=g)
+    lin = BlockLinear(torch.randn((H * D, H * D), device="cuda", generator=g) * 0.02,
+                      bias=torch.randn(H * D, device="cuda", generator=g) * 0.1)
+    x = torch.randn((batch, H * D), device="cuda", generator=g)
+    if shared:
+        kv_len = torch.full((batch,), cap, dtype=torch.int64, device="cuda")
+        kv_len[0] = 77
+        args = dict(causal=False, shared=True, kv_len=kv_len)
+    else:
+        begin = torch.randint(0, 200, (batch,), device="cuda", generator=g)
+        args = dict(causal=True, shared=False, begin=begin)
+    att, st = _attend_q8(lib, lin.frags(batch, rounding), q, kp, vp, cap, batch, 1, **args)
+    got = lin.run_frags(batch, out=x.clone(), residual=None)
+    got_res = x.clone()
+    att2, _ = _attend_q8(lib, lin.frags(batch, rounding), q, kp, vp, cap, batch, 1, **args)
+    lin.run_frags(batch, out=got_res, residual=got_res)
+    ref = lin(att, rounding=rounding)
+    ref_res = lin(att, out=x.clone(), residual=x.clone(), rounding=rounding)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    assert torch.equal(att, att2)
+    assert torch.equal(got, ref) and torch.equal(got_res, ref_res)
+    lin.close()
