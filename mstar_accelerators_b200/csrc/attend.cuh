@@ -12,7 +12,8 @@ constexpr int TILE_KEYS = 64;        // keys per shared-memory tile
 constexpr int ATT_THREADS = 128;      // CTA size for up to 4 row tiles
 constexpr int ATT_MAX_THREADS = 256;  // one warp per 16-row tile up to 128 rows
 constexpr int ATT_MAX_ROWS = 128;    // query rows one CTA attends (all B*NQ rows when the planes are shared)
-constexpr int SHARED_SPLITS = 24;    // key splits per head over shared planes (6 heads -> 144 CTAs)
+constexpr int SHARED_SPLITS = 8;     // key splits per head over shared planes (one thread-block cluster per head)
+constexpr int ATT_PRE = 4;           // key tiles a CTA loads into shared memory at once
 
 struct AttArgs {
     const float *q;
@@ -99,6 +100,22 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) { return half
 
 constexpr int ATT_LD = HEAD_DIM + 8;  // fp16 row stride of the shared tiles (72 halves: conflict-free fragment loads)
 
+// Warps per 16-row tile of attend_task ("tile lanes", key tiles processed side
+// by side): a function of the row count only, so every caller (its own block
+// size permitting mtiles * lanes warps) computes the same bits.
+__host__ __device__ constexpr int att_tile_lanes(int rows) {
+    return (rows + 15) / 16 <= 2 ? 4 : (rows + 15) / 16 <= 4 ? 2 : 1;
+}
+__host__ __device__ constexpr int att_threads(int rows) { return 32 * ((rows + 15) / 16) * att_tile_lanes(rows); }
+
+// Shared memory of attend_task for `rows` query rows: fp16 Q hi / lo, ATT_PRE K
+// tiles and V tiles, the per-row key limits (the tile buffers hold the lanes'
+// states for the final merge).
+__host__ __device__ constexpr size_t att_smem_bytes(int rows) {
+    return (2 * size_t((rows + 15) / 16 * 16) + 2 * size_t(ATT_PRE) * TILE_KEYS) * ATT_LD * 2 +
+           size_t((rows + 15) / 16 * 16) * 4;
+}
+
 // Decode / prefill attention over the fp16 K/V planes, flash-attention style
 // on the tensor cores (mma.sync m16n8k16, fp16 operands, fp32 accumulation).
 // CTA (group g, head h, split s) walks its key tiles of 64: S = Q K^T, online
@@ -114,14 +131,20 @@ constexpr int ATT_LD = HEAD_DIM + 8;  // fp16 row stride of the shared tiles (72
 // writes their K/V rows to the planes (fp16, ggml_set_rows,
 // decoder.cpp:566-567). Warp w owns the 16-row tile w (the CTA has
 // max(4, row tiles) warps).
+//
+// A CTA loads up to ATT_PRE of its key tiles at once (one round of loads for
+// the group), then runs the tiles' math in order. With part_dst (splits > 1)
+// the split's partial rows go to that shared-memory array instead of the
+// global partial buffer.
 template <bool CAUSAL>
-__device__ __forceinline__ void attend_task(const AttArgs &a, int task, unsigned char *att_smem) {
+__device__ __forceinline__ void attend_task(const AttArgs &a, int task, unsigned char *att_smem,
+                                            float *part_dst = nullptr) {
     const int R = a.rows, mtiles = (R + 15) / 16;
     __half *qs = reinterpret_cast<__half *>(att_smem);            // [mtiles*16][72] fp16(q)
     __half *ql = qs + mtiles * 16 * ATT_LD;                       // [mtiles*16][72] fp16(q - fp16(q))
-    __half *ks = ql + mtiles * 16 * ATT_LD;                       // [64 keys][72]
-    __half *vt = ks + TILE_KEYS * ATT_LD;                         // [64 dims][72] (V transposed)
-    int *lim = reinterpret_cast<int *>(vt + HEAD_DIM * ATT_LD);   // [mtiles*16]
+    __half *ks0 = ql + mtiles * 16 * ATT_LD;                      // [ATT_PRE][64 keys][72]
+    __half *vs0 = ks0 + ATT_PRE * TILE_KEYS * ATT_LD;             // [ATT_PRE][64 keys][72]
+    int *lim = reinterpret_cast<int *>(vs0 + ATT_PRE * TILE_KEYS * ATT_LD);  // [mtiles*16]
     __shared__ int maxlim;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t4 = lane & 3;
@@ -168,46 +191,59 @@ __device__ __forceinline__ void attend_task(const AttArgs &a, int task, unsigned
     }
     __syncthreads();
 
-    // this warp's 16-row tile: O [16 x 64] (8 n-tiles x 4), running max / sum of rows g, g+8
-    const int mt = warp;
+    // this warp's 16-row tile mt and tile lane tl: the warps of a row tile take the key tiles of a
+    // group in turn (tile gi goes to lane gi mod TL), each with its own O [16 x 64] (8 n-tiles x 4)
+    // and running max / sum of rows g, g+8; the lanes' states are merged in lane order at the end
+    const int TL = att_tile_lanes(R);
+    const int mt = warp % mtiles, tl = warp / mtiles;
+    const bool active = tl < TL;
     float o[8][4];
     float mrun[2] = {-INFINITY, -INFINITY}, lrun[2] = {0.0f, 0.0f};
 #pragma unroll
     for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
     const int64_t t_begin = int64_t(split) * a.tiles_per_split;
-    for (int64_t t = t_begin; t < t_begin + a.tiles_per_split && t * TILE_KEYS < maxlim; ++t) {
-        const int64_t c0 = t * TILE_KEYS;
-        // K tile [key][dim] and transposed V tile [dim][key], fp16; new rows from knew/vnew
-        for (int e = tid; e < TILE_KEYS * HEAD_DIM / 8; e += blockDim.x) {
-            const int jj = e / (HEAD_DIM / 8), d8 = (e % (HEAD_DIM / 8)) * 8;
-            const int64_t j = c0 + jj;
-            uint4 kr = make_uint4(0u, 0u, 0u, 0u), vr = kr;
-            if (j < maxlim) {  // keys past every row's length stay zero (never stale plane bytes)
-                const int64_t b0 = CAUSAL && a.knew ? a.begin[grp] : -1;
-                if (CAUSAL && a.knew && b0 >= 0 && j >= b0 && j < b0 + a.nq && b0 + a.nq <= a.capacity) {
-                    const int64_t src = (int64_t(grp) * a.nq + (j - b0)) * a.kv_stride + h * HEAD_DIM + d8;
-                    __half kh[8], vh[8];
+    int64_t t_end = t_begin + a.tiles_per_split;
+    if (t_end * TILE_KEYS > maxlim) t_end = (int64_t(maxlim) + TILE_KEYS - 1) / TILE_KEYS;  // tiles past every row
+    for (int64_t tg = t_begin; tg < t_end; tg += ATT_PRE) {
+      const int ng = int(t_end - tg < ATT_PRE ? t_end - tg : ATT_PRE);
+      // K and V tiles [key][dim] of the group, fp16, by 16-byte asynchronous copies all in flight at
+      // once; keys past every row's length are zero-filled (never stale plane bytes); the new
+      // rows of a causal step come from knew / vnew and are written to the planes as well
+      for (int e = tid; e < ng * TILE_KEYS * HEAD_DIM / 8; e += blockDim.x) {
+            const int gi = e / (TILE_KEYS * HEAD_DIM / 8), ee = e % (TILE_KEYS * HEAD_DIM / 8);
+            const int jj = ee / (HEAD_DIM / 8), d8 = (ee % (HEAD_DIM / 8)) * 8;
+            const int64_t j = (tg + gi) * TILE_KEYS + jj;
+            __half *ks = ks0 + gi * TILE_KEYS * ATT_LD + jj * ATT_LD + d8;
+            __half *vs = vs0 + gi * TILE_KEYS * ATT_LD + jj * ATT_LD + d8;
+            const bool live = j < maxlim;
+            const int64_t b0 = CAUSAL && a.knew ? a.begin[grp] : -1;
+            if (live && CAUSAL && a.knew && b0 >= 0 && j >= b0 && j < b0 + a.nq && b0 + a.nq <= a.capacity) {
+                const int64_t src = (int64_t(grp) * a.nq + (j - b0)) * a.kv_stride + h * HEAD_DIM + d8;
+                __half kh[8], vh[8];
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        kh[u] = __float2half_rn(a.knew[src + u]);
-                        vh[u] = __float2half_rn(a.vnew[src + u]);
-                    }
-                    memcpy(&kr, kh, 16);
-                    memcpy(&vr, vh, 16);
-                    *reinterpret_cast<uint4 *>(kp + j * width + d8) = kr;
-                    *reinterpret_cast<uint4 *>(vp + j * width + d8) = vr;
-                } else {
-                    kr = *reinterpret_cast<const uint4 *>(kp + j * width + d8);
-                    vr = *reinterpret_cast<const uint4 *>(vp + j * width + d8);
+                for (int u = 0; u < 8; ++u) {
+                    kh[u] = __float2half_rn(a.knew[src + u]);
+                    vh[u] = __float2half_rn(a.vnew[src + u]);
                 }
+                uint4 kr, vr;
+                memcpy(&kr, kh, 16);
+                memcpy(&vr, vh, 16);
+                *reinterpret_cast<uint4 *>(kp + j * width + d8) = kr;
+                *reinterpret_cast<uint4 *>(vp + j * width + d8) = vr;
+                *reinterpret_cast<uint4 *>(ks) = kr;
+                *reinterpret_cast<uint4 *>(vs) = vr;
+            } else {
+                const int64_t jr = live ? j : 0;  // a valid row address; nothing is read when not live
+                cp_async16(ks, kp + jr * width + d8, live ? 16 : 0);
+                cp_async16(vs, vp + jr * width + d8, live ? 16 : 0);
             }
-            *reinterpret_cast<uint4 *>(ks + jj * ATT_LD + d8) = kr;
-            const __half *vh = reinterpret_cast<const __half *>(&vr);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) vt[(d8 + u) * ATT_LD + jj] = vh[u];
-        }
-        __syncthreads();
-        if (mt < mtiles) {
+      }
+      cp_async_wait_all();
+      __syncthreads();
+      for (int gi = tl; gi < ng; gi += TL) {
+        const int64_t c0 = (tg + gi) * TILE_KEYS;
+        const __half *ks = ks0 + gi * TILE_KEYS * ATT_LD, *vs = vs0 + gi * TILE_KEYS * ATT_LD;
+        if (active) {
             const int r0 = mt * 16 + g, r1 = r0 + 8;
             // S = Q K^T over the 64 dims (4 k-steps) for the 8 key n-tiles
             float sc[8][4];
@@ -292,18 +328,63 @@ __device__ __forceinline__ void attend_task(const AttArgs &a, int task, unsigned
             for (int kk = 0; kk < TILE_KEYS / 16; ++kk) {
                 const uint32_t af[4] = {pf[2 * kk][0], pf[2 * kk][1], pf[2 * kk + 1][0], pf[2 * kk + 1][1]};
                 const uint32_t al[4] = {pl[2 * kk][0], pl[2 * kk][1], pl[2 * kk + 1][0], pl[2 * kk + 1][1]};
+                // B fragments of V (16 keys x 8 dims) for n-tiles 2 jp and 2 jp + 1, transposed from
+                // the row-major tile: thread 8 m + r addresses key 16 kk + r + 8 (m & 1), dims 8 (2 jp + m / 2)
+#pragma unroll
+                for (int jp = 0; jp < 4; ++jp) {
+                    uint32_t vb[4];
+                    ldmatrix_x4_trans(vb, vs + (kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * ATT_LD +
+                                              8 * (2 * jp + (lane >> 4)));
+                    mma_f16(o[2 * jp], af, vb[0], vb[1]);
+                    mma_f16(o[2 * jp], al, vb[0], vb[1]);
+                    mma_f16(o[2 * jp + 1], af, vb[2], vb[3]);
+                    mma_f16(o[2 * jp + 1], al, vb[2], vb[3]);
+                }
+            }
+        }
+      }
+      __syncthreads();
+    }
+    const int used = int(t_end - t_begin < TL ? (t_end > t_begin ? t_end - t_begin : 0) : TL);  // lanes that saw a tile
+    if (used > 1) {  // lanes 1.. leave their states in the (now free) tile buffers; lane 0 merges them in order
+        float *st = reinterpret_cast<float *>(ks0);  // [mtiles][TL - 1][16 rows][HEAD_DIM + 2]
+        if (active && tl > 0 && tl < used) {
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                float *row = st + ((mt * (TL - 1) + tl - 1) * 16 + g + 8 * half) * (HEAD_DIM + 2);
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    const __half *vb = vt + (8 * j + g) * ATT_LD + kk * 16 + 2 * t4;
-                    const uint32_t b0 = *reinterpret_cast<const uint32_t *>(vb), b1 = *reinterpret_cast<const uint32_t *>(vb + 8);
-                    mma_f16(o[j], af, b0, b1);
-                    mma_f16(o[j], al, b0, b1);
+                    row[8 * j + 2 * t4] = o[j][2 * half];
+                    row[8 * j + 2 * t4 + 1] = o[j][2 * half + 1];
+                }
+                if (t4 == 0) {
+                    row[HEAD_DIM] = mrun[half];
+                    row[HEAD_DIM + 1] = lrun[half];
                 }
             }
         }
         __syncthreads();
+        if (active && tl == 0) {
+            for (int l2 = 1; l2 < used; ++l2) {
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    const float *row = st + ((mt * (TL - 1) + l2 - 1) * 16 + g + 8 * half) * (HEAD_DIM + 2);
+                    const float mb = row[HEAD_DIM], lb = row[HEAD_DIM + 1];
+                    const float M = fmaxf(mrun[half], mb);
+                    const float wa = M == -INFINITY || mrun[half] == -INFINITY ? 0.0f : __expf(mrun[half] - M);
+                    const float wb = M == -INFINITY || mb == -INFINITY ? 0.0f : __expf(mb - M);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        o[j][2 * half] = fmaf(row[8 * j + 2 * t4], wb, o[j][2 * half] * wa);
+                        o[j][2 * half + 1] = fmaf(row[8 * j + 2 * t4 + 1], wb, o[j][2 * half + 1] * wa);
+                    }
+                    lrun[half] = fmaf(lb, wb, lrun[half] * wa);
+                    mrun[half] = M;
+                }
+            }
+        }
     }
-    if (mt < mtiles) {
+    if (active && tl == 0) {
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
             const int r = mt * 16 + g + 8 * half;
@@ -325,7 +406,8 @@ __device__ __forceinline__ void attend_task(const AttArgs &a, int task, unsigned
                     else frag_head_row<1>(a.frags, v, row_q(r), h, t4, group, a.status);
                 }
             } else {
-                float *part = a.partial + ((int64_t(gh) * a.splits + split) * R + r) * (HEAD_DIM + 2);
+                float *part = part_dst ? part_dst + int64_t(r) * (HEAD_DIM + 2)
+                                       : a.partial + ((int64_t(gh) * a.splits + split) * R + r) * (HEAD_DIM + 2);
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     part[8 * j + 2 * t4] = o[j][2 * half];

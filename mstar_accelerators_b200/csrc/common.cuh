@@ -189,6 +189,22 @@ __device__ __forceinline__ void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// ---- 16-byte asynchronous global -> shared copies (cp.async, no TMA) ---------
+// src_bytes 0 zero-fills the destination without reading the source.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Four 8x8 fp16 matrices from shared memory, transposed (ldmatrix .trans):
+// thread 8 m + r gives the address of row r of matrix m.
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void *row) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_addr(row)));
+}
+
 // Q4_0 nibbles of 4 bytes -> (elements 4t..4t+3, elements 16+4t..) as unsigned
 // nibbles; the -8 offset is applied after the dot as -8 * (sum of the block's
 // activation quants), which keeps the integer result exact.

@@ -5,6 +5,8 @@
 // the new self-attention K/V rows appended first (ggml_set_rows,
 // decoder.cpp:566-567). Attention math is fp32 (scores, split softmax, weighted
 // sums); K/V are stored fp16 like the reference's F16 plain storage.
+#include <cooperative_groups.h>
+
 #include "../../include/mstar_b200.h"
 #include "attend.cuh"
 #include "quant.cuh"
@@ -46,10 +48,55 @@ __global__ void __launch_bounds__(HEAD_DIM) k_attend_merge(const AttArgs a) {
     merge_task(a, blockIdx.x, threadIdx.x);
 }
 
-static size_t tiles_smem_bytes(int rows) {
-    const size_t padded = size_t(rows + 15) / 16 * 16;
-    return (2 * padded + TILE_KEYS + HEAD_DIM) * ATT_LD * 2 + padded * 4;
+// Attention over shared planes with the key splits of a head as one thread-block
+// cluster (cluster rank = split): every CTA keeps its partial rows (O, max,
+// sum) in shared memory; after a cluster barrier CTA k merges rows
+// k * R / splits .. through distributed shared memory, in split order exactly
+// as k_attend_merge, writes them (and their Q8_0 fragments when asked) and
+// waits at a second barrier so that no partial is read after its CTA exits.
+__global__ void __launch_bounds__(ATT_MAX_THREADS) k_attend_cluster(const AttArgs a) {
+    namespace cg = cooperative_groups;
+    extern __shared__ __align__(16) unsigned char att_smem[];
+    cg::cluster_group cluster = cg::this_cluster();
+    float *part = reinterpret_cast<float *>(att_smem + att_smem_bytes(a.rows));  // [rows][HEAD_DIM + 2]
+    pdl_wait();
+    pdl_trigger();
+    attend_task<false>(a, blockIdx.x, att_smem, part);
+    cluster.sync();
+    const int R = a.rows, S = a.splits, k = int(cluster.block_rank());
+    const int h = int(blockIdx.x) / S % a.heads;
+    const int per = (R + S - 1) / S, r0 = k * per, r1 = r0 + per < R ? r0 + per : R;
+    const int lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    for (int pair = int(threadIdx.x >> 5); pair < (r1 - r0) * 2; pair += nwarps) {  // (row, 32-dim block) per warp
+        const int r = r0 + pair / 2, dd = (pair % 2) * 32 + lane;
+        float M = -INFINITY;
+        for (int sp = 0; sp < S; ++sp) M = fmaxf(M, cluster.map_shared_rank(part, sp)[r * (HEAD_DIM + 2) + HEAD_DIM]);
+        float o = 0.0f, l = 0.0f;
+        if (M != -INFINITY) {
+#pragma unroll 4
+            for (int sp = 0; sp < S; ++sp) {
+                const float *pr = cluster.map_shared_rank(part, sp) + r * (HEAD_DIM + 2);
+                const float m = pr[HEAD_DIM];
+                const float w = m == -INFINITY ? 0.0f : __expf(m - M);
+                o = fmaf(w, pr[dd], o);
+                l = fmaf(w, pr[HEAD_DIM + 1], l);
+            }
+        }
+        const float v = l > 0.0f ? o / l : 0.0f;
+        a.out[int64_t(r) * a.out_stride + h * HEAD_DIM + dd] = v;
+        if (a.frags.xf) {
+            const Q8Frags &f = a.frags;
+            const int64_t b = 2 * h + dd / 32;
+            const int mtiles = int(f.mpad / 16);
+            if (f.mode == 0) frag_block<0>(v, true, b, r, mtiles, f.xf, f.xs, f.xsum, a.status);
+            else if (f.mode == 2) frag_block<2>(v, true, b, r, mtiles, f.xf, f.xs, f.xsum, a.status);
+            else frag_block<1>(v, true, b, r, mtiles, f.xf, f.xs, f.xsum, a.status);
+        }
+    }
+    cluster.sync();
 }
+
+static size_t tiles_smem_bytes(int rows) { return att_smem_bytes(rows); }
 
 struct SplitPlan {
     int groups, rows, splits, tiles_per_split;
@@ -134,8 +181,12 @@ int mstar_b200_attend_q8(const float *q, int64_t q_stride, const float *k_new, c
                 "attention workspace must be mstar_b200_attend_workspace() bytes, 256-byte aligned");
         check_device(workspace, "attention workspace");
         const size_t smem = tiles_smem_bytes(p.rows);
+        const size_t cluster_smem = smem + size_t(p.rows) * (HEAD_DIM + 2) * 4;
         static bool configured = false;
         if (!configured) {
+            cuda_check(cudaFuncSetAttribute(k_attend_cluster, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            int(tiles_smem_bytes(ATT_MAX_ROWS) + ATT_MAX_ROWS * (HEAD_DIM + 2) * 4)),
+                       "attention shared-memory attribute");
             cuda_check(cudaFuncSetAttribute(k_attend_tiles<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             int(tiles_smem_bytes(ATT_MAX_ROWS))),
                        "attention shared-memory attribute");
@@ -183,10 +234,29 @@ int mstar_b200_attend_q8(const float *q, int64_t q_stride, const float *k_new, c
         }
         cudaStream_t s = as_stream(stream);
         const unsigned grid = unsigned(p.groups * heads * p.splits);
-        const int threads = 32 * (p.rows > 64 ? (p.rows + 15) / 16 : 4);
-        if (causal) launch_pdl(k_attend_tiles<true>, dim3(grid), dim3(threads), smem, s, a);
-        else launch_pdl(k_attend_tiles<false>, dim3(grid), dim3(threads), smem, s, a);
-        if (p.splits > 1) launch_pdl(k_attend_merge, dim3(unsigned(p.groups * heads * p.rows)), dim3(HEAD_DIM), 0, s, a);
+        const int threads = att_threads(p.rows);
+        if (p.splits > 1 && !causal) {  // one cluster of p.splits CTAs per (group, head); merge inside
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(grid);
+            cfg.blockDim = dim3(unsigned(threads));
+            cfg.dynamicSmemBytes = cluster_smem;
+            cfg.stream = s;
+            cudaLaunchAttribute attr[2];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            attr[1].id = cudaLaunchAttributeClusterDimension;
+            attr[1].val.clusterDim.x = unsigned(p.splits);
+            attr[1].val.clusterDim.y = 1;
+            attr[1].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 2;
+            cuda_check(cudaLaunchKernelEx(&cfg, k_attend_cluster, a), "attention cluster launch");
+        } else {
+            if (causal) launch_pdl(k_attend_tiles<true>, dim3(grid), dim3(threads), smem, s, a);
+            else launch_pdl(k_attend_tiles<false>, dim3(grid), dim3(threads), smem, s, a);
+            if (p.splits > 1)
+                launch_pdl(k_attend_merge, dim3(unsigned(p.groups * heads * p.rows)), dim3(HEAD_DIM), 0, s, a);
+        }
         cuda_check(cudaGetLastError(), "attention launch");
         return 0;
     } catch (const std::exception &e) {

@@ -579,7 +579,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_decode_step(const StepArgs 
 // ------------------------------------------------------------------ host side
 static size_t step_smem_bytes(int64_t ffn, int mt) {
     const int64_t nbp_max = (ffn / QK + 3) / 4 * 4;
-    return size_t(nbp_max) * mt * 32 * 16 * 2 + size_t(nbp_max) * mt * 16 * 4 * 2 + 32 * 8;
+    const size_t gemv = size_t(nbp_max) * mt * 32 * 16 * 2 + size_t(nbp_max) * mt * 16 * 4 * 2 + 32 * 8;
+    const size_t att = att_smem_bytes(mt * 16);  // attention over up to mt * 16 shared rows
+    return gemv > att ? gemv : att;
 }
 
 struct DecodeStep {
