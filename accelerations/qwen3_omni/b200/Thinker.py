@@ -9,8 +9,11 @@ select_expert_kernels is a no-op off ROCm), after which
 install_thinker_experts gives each MoE layer a ThinkerExpertsBackend: router
 top-8 ids/weights -> counting-sort permutation -> gate/up GEMM with the SwiGLU
 epilogue -> down GEMM with the routing-weight epilogue -> slot-ordered combine,
-with the bf16 rounding points of thinker_moe.py:17-101. No torch.compile: the
-program is captured in CUDA graphs instead.
+with the bf16 rounding points of thinker_moe.py:17-101; then
+install_thinker_attention_linears makes the plain nn.Linear attention
+projections (q/k/v/o_proj) and lm_head Q8_0 contractions (thinker_model.py:106-148,
+the 48-layer stack's "linears in Q8_0"). No torch.compile: the program is
+captured in CUDA graphs instead.
 
 Requires the M* runtime (mstar); it is exercised through
 python -m mstar_accelerators.testing --registry accelerations/qwen3_omni/b200.
@@ -31,6 +34,7 @@ from mstar_accelerators import Acceleration, Eq, Implementation, Range, TensorFo
 from mstar_accelerators.backends.torch.tensor_forward import tensor_resource_requests
 from mstar_accelerators_b200.conditions import SM100aAvailable
 from mstar_accelerators_b200.moe import install_thinker_experts
+from mstar_accelerators_b200.thinker import install_thinker_attention_linears
 
 
 @dataclass(frozen=True)
@@ -74,6 +78,9 @@ def build_thinker_b200(binding):
     program = build_thinker(binding)
     if install_thinker_experts(program) == 0:
         raise ValueError("no thinker MoE layer of the expected geometry was found")
+    # attention-prologue projections and lm_head as Q8_0 contractions (plain nn.Linear only;
+    # tensor-parallel linears keep their own path)
+    install_thinker_attention_linears(program)
     return program
 
 

@@ -54,7 +54,8 @@ bool readout_tiles_fit(int64_t rows, int64_t nb, int q4);
 void launch_readout_repack(int q4, const uint8_t *blocks, uint8_t *wt, int64_t rows, int64_t nb, cudaStream_t s);
 void launch_readout(const Linear &h, const float *x, int64_t ldx, int64_t m, const float *ln_w,
                     const float *ln_b, float eps, int mode, float *logits, int64_t *token, int *status,
-                    const int64_t *suppressed, int64_t nsup, cudaStream_t s);
+                    const int64_t *suppressed, int64_t nsup, cudaStream_t s, int64_t ldo = 0,
+                    const float *bias = nullptr, const float *residual = nullptr);
 
 }  // namespace mb
 
@@ -247,7 +248,16 @@ int mstar_b200_linear_run(void *handle, const float *x, int64_t x_stride, int64_
             return 0;
         }
         require(h.gemv_ok, "width beyond 4096 needs the prepared GEMM and at least 64 queries without LayerNorm");
+        const bool tiles = h.wt && !h.wpg_override && !(flags & (2 | 8)) &&
+                           (!ln_weight || (uintptr_t(ln_weight) % 16 == 0 && uintptr_t(ln_bias) % 16 == 0));
         for (int64_t m0 = 0; m0 < queries; m0 += CHUNK) {
+            const int64_t mc = queries - m0 < CHUNK ? queries - m0 : CHUNK;
+            if (tiles) {  // the tile GEMV (prepare_readout): query quantization inside, one launch per chunk
+                launch_readout(h, x + m0 * x_stride, x_stride, mc, ln_weight, ln_bias, ln_eps, rounding,
+                               out + m0 * out_stride, nullptr, h.status, nullptr, 0, s, out_stride,
+                               (flags & 1) ? h.bias : nullptr, (flags & 4) ? residual + m0 * out_stride : nullptr);
+                continue;
+            }
             const int64_t m = queries - m0 < CHUNK ? queries - m0 : CHUNK;
             GemvArgs a = stage(h, x + m0 * x_stride, x_stride, m, rounding, ln_weight, ln_bias, ln_eps, h.status, s);
             a.out = out + m0 * out_stride;

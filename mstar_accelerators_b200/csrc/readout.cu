@@ -44,6 +44,7 @@ constexpr int RO_SLOT = 4096;      // bytes of one ring slot (one chunk of a til
 constexpr int RO_MAX_WARPS = 16;
 constexpr size_t RO_SMEM_LIMIT = 220 * 1024;
 constexpr uint32_t RO_MAGIC = 0x4B400000u;  // 1.5 * 2^23
+constexpr int64_t RO_SELF_QUANT_BLOCKS = 32;  // rows up to 1024 wide are quantized inside the kernel
 
 __host__ __device__ constexpr int ro_block_bytes(bool q4) { return q4 ? 288 : 544; }  // 16 rows of one block
 __host__ __device__ constexpr int ro_quant_bytes(bool q4) { return q4 ? 256 : 512; }
@@ -101,13 +102,17 @@ struct ReadoutArgs {
     int ring;               // slots per warp
     int sup_words;          // words of the per-CTA suppression bitmask
     const float *x;         // [m][ldx] fp32 query rows
+    const uint4 *pre_xf;    // non-null: queries already quantized by launch_quantize_frag ([nb_pad][mt][32] fragments,
+    const float *pre_xs;    //           [nb_pad][mpad] scales), copied instead of quantized here
     int64_t ldx, m;
     const float *ln_w, *ln_b;  // optional LayerNorm applied before quantization
     float eps;
     int mode;               // Q8_0 activation rounding (0 ref, 1 arm, 2 x86)
     float *out;             // [m][ldo]
     int64_t ldo;
-    unsigned long long *keys;  // [32] running per-query maxima, zero between calls
+    const float *bias;      // [rows] or null (added before the residual, as the GEMV epilogue)
+    const float *residual;  // [m][ldo] or null
+    unsigned long long *keys;  // [32] running per-query maxima, zero between calls; null: logits only
     unsigned int *done;        // CTA completion counter, zero between calls
     int *flags;                // status bits of the call in flight, zero between calls
     int64_t *token;
@@ -366,7 +371,15 @@ __global__ void __launch_bounds__(RO_MAX_WARPS * 32, 1) k_readout(const ReadoutA
     for (int i = threadIdx.x; i < a.sup_words; i += blockDim.x) s_sup[i] = 0u;
     pdl_wait();
     pdl_trigger();  // the next kernel may launch now; it waits for this grid before reading
-    stage_queries<MT, NBC * QK>(a, nb, s_xf, s_xs, s_stats, warps);
+    if (a.pre_xf) {  // wide rows: one quantization for the whole grid, each CTA copies the 8-bit fragments
+        for (int i = threadIdx.x; i < nb * MT * 32; i += blockDim.x) s_xf[i] = a.pre_xf[i];
+        for (int i = threadIdx.x; i < nb * MPAD; i += blockDim.x) {
+            const int b = i / MPAD, q = i % MPAD;
+            s_xs[b * MPAD + ((q & 7) >> 1) * (MPAD / 4) + (q >> 3) * 2 + (q & 1)] = a.pre_xs[i];
+        }
+    } else {
+        stage_queries<MT, NBC * QK>(a, nb, s_xf, s_xs, s_stats, warps);
+    }
     __syncthreads();  // bitmask zeroed before it is set
     for (int64_t i = threadIdx.x; i < a.nsup; i += blockDim.x) {
         const int64_t n = a.suppressed[i];
@@ -386,6 +399,7 @@ __global__ void __launch_bounds__(RO_MAX_WARPS * 32, 1) k_readout(const ReadoutA
         for (int nt = 0; nt < NT; ++nt) bv[nt][0] = bv[nt][1] = -INFINITY, bn[nt][0] = bn[nt][1] = n0;
     }
     const bool all_queries = a.m == 8 * NT;
+    const bool argmax = a.keys != nullptr;
 
     int64_t st = 0;
     bool failed = false;
@@ -498,7 +512,29 @@ __global__ void __launch_bounds__(RO_MAX_WARPS * 32, 1) k_readout(const ReadoutA
             z1 = suppressed(n1);
         }
         float *o0 = a.out + n0, *o1 = a.out + n1;
-        if (all_queries && (tile + 1) * 16 <= a.rows) {  // full tile, every query live: no predicates
+        if (!argmax) {  // plain linear: bias, then residual (the GEMV epilogue order)
+            const float b0 = a.bias && n0 < a.rows ? a.bias[n0] : 0.0f, b1 = a.bias && n1 < a.rows ? a.bias[n1] : 0.0f;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {
+                    const int64_t q = 8 * nt + 2 * t + cc;
+                    if (q >= a.m) continue;
+                    float v0 = cc ? acc[nt][0].y : acc[nt][0].x, v1 = cc ? acc[nt][1].y : acc[nt][1].x;
+                    if (a.bias) {
+                        v0 = __fadd_rn(v0, b0);
+                        v1 = __fadd_rn(v1, b1);
+                    }
+                    if (n0 < a.rows) {
+                        if (a.residual) v0 = __fadd_rn(a.residual[q * a.ldo + n0], v0);
+                        o0[q * a.ldo] = v0;
+                    }
+                    if (n1 < a.rows) {
+                        if (a.residual) v1 = __fadd_rn(a.residual[q * a.ldo + n1], v1);
+                        o1[q * a.ldo] = v1;
+                    }
+                }
+        } else if (all_queries && (tile + 1) * 16 <= a.rows) {  // full tile, every query live: no predicates
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -538,6 +574,7 @@ __global__ void __launch_bounds__(RO_MAX_WARPS * 32, 1) k_readout(const ReadoutA
 
     // keys: per warp over the 8 lanes sharing t, per CTA over the warps (in
     // shared memory), across CTAs with one 64-bit atomic max per query
+    if (argmax) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -550,9 +587,10 @@ __global__ void __launch_bounds__(RO_MAX_WARPS * 32, 1) k_readout(const ReadoutA
             }
             if (g == 0) s_keys[warp * 32 + 8 * nt + 2 * t + cc] = key;
         }
+    }
     __shared__ bool last;
     __syncthreads();
-    if (threadIdx.x < a.m) {
+    if (argmax && threadIdx.x < a.m) {
         unsigned long long best = 0ull;
         for (int w = 0; w < warps; ++w) {
             const unsigned long long k = s_keys[w * 32 + threadIdx.x];
@@ -566,7 +604,7 @@ __global__ void __launch_bounds__(RO_MAX_WARPS * 32, 1) k_readout(const ReadoutA
     __syncthreads();
     if (last) {
         __threadfence();
-        if (threadIdx.x < a.m) {
+        if (argmax && threadIdx.x < a.m) {
             const unsigned long long k = atomicExch(a.keys + threadIdx.x, 0ull);
             a.token[threadIdx.x] = int64_t(0xFFFFFFFFu - uint32_t(k & 0xFFFFFFFFull));
         }
@@ -654,7 +692,8 @@ static void launch_nt(const ReadoutArgs &a, const ReadoutPlan &p, cudaStream_t s
 // status, for 1..32 query rows.
 void launch_readout(const Linear &h, const float *x, int64_t ldx, int64_t m, const float *ln_w,
                     const float *ln_b, float eps, int mode, float *logits, int64_t *token, int *status,
-                    const int64_t *suppressed, int64_t nsup, cudaStream_t s) {
+                    const int64_t *suppressed, int64_t nsup, cudaStream_t s, int64_t ldo, const float *bias,
+                    const float *residual) {
     const int nt = m <= 8 ? 1 : m <= 16 ? 2 : 4;
     const int mt = (nt + 1) / 2;
     const ReadoutPlan p = plan_readout(h.tiles, h.nb, h.q4, mt);
@@ -670,13 +709,21 @@ void launch_readout(const Linear &h, const float *x, int64_t ldx, int64_t m, con
     a.x = x;
     a.ldx = ldx;
     a.m = m;
+    if (h.nb > RO_SELF_QUANT_BLOCKS) {  // every CTA quantizing wide rows would re-read them from L2 148 times
+        launch_quantize_frag(mode, x, ldx, m, h.width, mt * 16, h.nb_pad, ln_w, ln_b, eps, h.xf, h.xs, h.xsum,
+                             h.ro_flags, s);
+        a.pre_xf = reinterpret_cast<const uint4 *>(h.xf);
+        a.pre_xs = h.xs;
+    }
     a.ln_w = ln_w;
     a.ln_b = ln_b;
     a.eps = eps;
     a.mode = mode;
     a.out = logits;
-    a.ldo = h.rows;
-    a.keys = h.keys;
+    a.ldo = ldo > 0 ? ldo : h.rows;
+    a.bias = bias;
+    a.residual = residual;
+    a.keys = token ? h.keys : nullptr;
     a.done = h.done;
     a.flags = h.ro_flags;
     a.token = token;

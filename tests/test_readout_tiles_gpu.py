@@ -154,3 +154,33 @@ def test_tile_readout_status_and_fused_layernorm(L, fmt):
     assert host(tiles.readout(dev(x))[2])[0] == 0
     tiles.close()
     plain.close()
+
+
+@pytest.mark.parametrize("m", [1, 17, 32, 40])
+def test_tile_gemv_equals_the_split_gemv(L, m):
+    """linear_run on a handle with the tile layout (the logits-only tile kernel) gives the bytes of
+    the fragment-layout GEMV: bias, residual and the fused LayerNorm included."""
+    rng = np.random.default_rng(40 + m)
+    n, k = 1000, 2048
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    bias = rng.standard_normal(n).astype(np.float32)
+    blocks = O.pack_weights(w, "q8_0")
+    plain = L.BlockLinear(blocks=dev(blocks), fmt="q8_0", rows=n, width=k, bias=dev(bias))
+    tiles = L.BlockLinear(blocks=dev(blocks), fmt="q8_0", rows=n, width=k, bias=dev(bias))
+    tiles.prepare_readout()
+    x = (rng.standard_normal((m, k)) * 2).astype(np.float32)
+    res = rng.standard_normal((m, n)).astype(np.float32)
+    lw = rng.uniform(0.5, 1.5, k).astype(np.float32)
+    lb = (rng.standard_normal(k) * 0.1).astype(np.float32)
+    for kw in ({}, {"norm": (dev(lw), dev(lb), 1e-5)}):
+        a = host(plain(dev(x), **kw))
+        b = host(tiles(dev(x), **kw))
+        assert np.array_equal(a, b)
+        ra = dev(res.copy())
+        rb = dev(res.copy())
+        plain(dev(x), out=ra, residual=ra, **kw)
+        tiles(dev(x), out=rb, residual=rb, **kw)
+        assert np.array_equal(host(ra), host(rb))
+    assert np.array_equal(host(tiles(dev(x), bias=False)), O.mul_mat(blocks, x, "q8_0"))
+    plain.close()
+    tiles.close()
