@@ -317,9 +317,10 @@ def run_b200(args):
                    "sample": f"{n} decode steps of the 33 block-quantized linears (batch 32) through the "
                              "vendored ggml x86 kernels on the host cores; attention/LayerNorm excluded"}
         clk = clocks.summary()
-        # embedding; per layer 4 linears (quantize + GEMV) and 2 GEMVs on fragments the attention wrote,
-        # self attention, cross attention (tiles + merge); readout (one launch)
-        launches_per_step = 1 + cfg.layers * (4 * 2 + 2 + 1 + 2) + 1
+        # embedding; per layer: qkv, cq (quantize + GEMV), fc1 (quantize + GEMV writing fc2's fragments),
+        # out, cout, fc2 (GEMV on fragments written by their producer), self attention (1), cross attention
+        # (one cluster launch); readout (one launch)
+        launches_per_step = 1 + cfg.layers * (3 * 2 + 3 + 1 + 1) + 1
         line = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,

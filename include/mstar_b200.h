@@ -134,6 +134,15 @@ typedef struct mstar_b200_q8_frags {
 /* Describe the handle's fragment buffers for `queries` (1..32) rows. */
 MSTAR_B200_API int mstar_b200_linear_frags(void *handle, int64_t queries, int32_t rounding,
     mstar_b200_q8_frags *frags, char *error, size_t error_size);
+/* mstar_b200_linear_run (Q8_0 weights, 1..32 queries, rows a multiple of 32)
+ * that also quantizes its outputs into `next` (from mstar_b200_linear_frags of
+ * the linear that consumes them, e.g. fc2 after fc1 with GELU,
+ * decoder.cpp:580): the bytes mstar_b200_linear_run on `out` would produce, so
+ * mstar_b200_linear_run_frags on the next handle needs no quantize launch. */
+MSTAR_B200_API int mstar_b200_linear_run_q8out(void *handle, const float *x, int64_t x_stride, int64_t queries,
+    float *out, int64_t out_stride, const float *residual, int flags, const float *ln_weight,
+    const float *ln_bias, float ln_eps, int rounding, const mstar_b200_q8_frags *next, void *stream,
+    char *error, size_t error_size);
 /* The decode GEMV (+ bias / GELU / residual epilogue, flags as linear_run) on
  * the fragments a producer wrote for `queries` rows: equal to linear_run on the
  * producer's fp32 output (ggml_mul_mat + the same epilogue). */

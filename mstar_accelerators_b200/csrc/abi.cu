@@ -277,6 +277,58 @@ int mstar_b200_linear_run(void *handle, const float *x, int64_t x_stride, int64_
     }
 }
 
+int mstar_b200_linear_run_q8out(void *handle, const float *x, int64_t x_stride, int64_t queries, float *out,
+                                int64_t out_stride, const float *residual, int flags, const float *ln_weight,
+                                const float *ln_bias, float ln_eps, int rounding, const mstar_b200_q8_frags *next,
+                                void *stream, char *error, size_t error_size) {
+    try {
+        require(handle && next, "missing linear handle or fragment descriptor");
+        auto &h = *static_cast<Linear *>(handle);
+        Busy busy(h.busy);
+        check_rounding(rounding);
+        require(!h.q4, "fragment output needs Q8_0 weights");
+        require(queries >= 1 && queries <= CHUNK, "fragment output takes 1..32 queries");
+        require(h.gemv_ok && h.rows % 32 == 0, "fragment output needs whole 32-output blocks");
+        require((flags & ~15) == 0 && !((flags & 2) && (flags & 8)), "invalid epilogue flags");
+        require(!(flags & 1) || h.bias, "bias epilogue without a prepared bias");
+        validate_run(h, x, x_stride, queries, out, out_stride);
+        validate_norm(h, ln_weight, ln_bias, ln_eps);
+        if (flags & 4) {
+            const uint64_t rb = uint64_t((queries - 1) * out_stride + h.rows) * 4;
+            check_range({residual, rb}, rb, 4, "residual");
+            require(residual == out || disjoint({residual, rb}, {out, rb}), "residual partially overlaps output");
+            check_device(residual, "residual");
+        } else require(!residual, "residual given without its epilogue flag");
+        require(next->fragments && next->scales && next->sums, "missing fragment buffers");
+        require(next->rows == (queries <= 16 ? 16 : 32), "fragment rows differ from the query count");
+        require(next->blocks >= h.rows / QK, "fragment blocks fewer than the output width");
+        require(next->rounding >= 0 && next->rounding <= 2, "unknown Q8_0 activation rounding");
+        require(gemv_frag_smem_bytes(h.nb_pad, queries <= 16 ? 1 : 2) <= 200 * 1024, "input too wide");
+        check_device(next->fragments, "fragment buffer");
+        cudaStream_t s = as_stream(stream);
+        GemvArgs a = stage(h, x, x_stride, queries, rounding, ln_weight, ln_bias, ln_eps, h.status, s);
+        a.out = out;
+        a.ldo = out_stride;
+        a.bias = h.bias;
+        a.residual = (flags & 4) ? residual : nullptr;
+        a.flags = flags;
+        a.gelu = h.gelu;
+        Q8Frags f{};
+        f.xf = static_cast<uint32_t *>(next->fragments);
+        f.xs = next->scales;
+        f.xsum = next->sums;
+        f.nb_pad = next->blocks;
+        f.mpad = next->rows;
+        f.mode = next->rounding;
+        launch_gemv_frag(a, f, s);
+        cuda_check(cudaGetLastError(), "fragment-output GEMV launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
 int mstar_b200_linear_frags(void *handle, int64_t queries, int32_t rounding, mstar_b200_q8_frags *frags,
                             char *error, size_t error_size) {
     try {

@@ -533,6 +533,141 @@ static void launch_variant(GemvArgs a, cudaStream_t s) {
 
 bool gemv_supported(int64_t nb_pad) { return gemv_smem_bytes(nb_pad, 2, 1) <= SMEM_LIMIT; }
 
+// Split-K GEMV over Q8_0 weights whose CTA owns FRAG_GROUPS = 4 row groups: 32
+// consecutive outputs, one Q8_0 block of the next linear's input. After the
+// block-order fold and the epilogue (bias, GELU, residual; the values stored
+// to `out`), every query row's 32 outputs are quantized into the next linear's
+// activation fragments (frag_block: the quantization launch_quantize_frag would
+// apply to `out`), so that linear needs no quantize launch (the decoder's fc1
+// feeding fc2). Warp w takes group w / wpg and the w % wpg-th part of its chunks.
+constexpr int FRAG_GROUPS = 4;
+
+template <int MT, int MODE>
+__global__ void __launch_bounds__(FRAG_GROUPS * GEMV_THREADS / 2, 1) k_gemv_frag(const GemvArgs a, const Q8Frags f) {
+    constexpr int BPC = 2;  // Q8_0 blocks per 16-byte chunk
+    constexpr int MPAD = MT * 16;
+    constexpr int RING = CHUNKS_IN_FLIGHT;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, t = lane & 3;
+    const int nb_pad = int(a.nb_pad), nb = int(a.nb), m_live = int(a.m), wpg = a.wpg;
+    const int chunks = nb_pad / BPC;
+    const int gi = warp / wpg, wp = warp % wpg;
+    const int64_t G = int64_t(blockIdx.x) * FRAG_GROUPS + gi;
+    const int cpw = (chunks + wpg - 1) / wpg;
+    const int c_begin = wp * cpw < chunks ? wp * cpw : chunks;
+    const int c_len = (c_begin + cpw < chunks ? c_begin + cpw : chunks) - c_begin;
+    const int total = G < a.groups ? c_len : 0;
+
+    GemvSmem s;
+    s.xf = reinterpret_cast<uint4 *>(smem_raw);
+    s.xs = reinterpret_cast<float *>(s.xf + nb_pad * MT * 32);
+    s.xsum = reinterpret_cast<int *>(s.xs + nb_pad * MPAD);
+    float *tile = reinterpret_cast<float *>(s.xsum + nb_pad * MPAD);  // [MPAD][32] epilogue outputs
+    float4 *terms = reinterpret_cast<float4 *>(tile + MPAD * 32) + size_t(gi) * nb_pad * MT * 32;
+
+    uint4 w[RING];
+    __half2 sc[RING][BPC];
+    int ld = 0;
+    auto load_next = [&](int u) {
+        if (ld < total) {
+            const int c = c_begin + ld;
+            w[u] = ldg_stream(a.wq + (G * chunks + c) * 32 + lane);
+            const __half2 *sp = a.ws + G * int64_t(nb_pad) * 4 + t + c * BPC * 4;
+#pragma unroll
+            for (int j = 0; j < BPC; ++j) sc[u][j] = __ldg(sp + j * 4);
+            ++ld;
+        }
+    };
+#pragma unroll
+    for (int u = 0; u < RING; ++u) load_next(u);  // immutable weights: before waiting on x's producer
+    pdl_wait();
+    pdl_trigger();
+    stage_activations<MT>(a, s);
+
+    bool hi_live[MT];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) hi_live[mt] = mt * 16 + 8 < m_live;
+    for (int s0 = 0; s0 < total; s0 += RING) {
+#pragma unroll
+        for (int u = 0; u < RING; ++u) {
+            if (s0 + u >= total) break;
+            const int c = c_begin + s0 + u;
+#pragma unroll
+            for (int j = 0; j < BPC; ++j) {
+                const int b = c * BPC + j;
+                const uint32_t b0 = word(w[u], 2 * j), b1 = word(w[u], 2 * j + 1);
+                const float2 dw = __half22float2(sc[u][j]);
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    int d[4];
+                    mma_q<false>(d, s.xf[(b * MT + mt) * 32 + lane], b0, b1, s.xsum + b * MPAD + mt * 16 + (lane >> 2));
+                    const float dx0 = s.xs[b * MPAD + mt * 16 + (lane >> 2)], dx1 = s.xs[b * MPAD + mt * 16 + (lane >> 2) + 8];
+                    float2 lo_t, hi_t = make_float2(0.0f, 0.0f);
+                    block_terms<false>(d, dw, dx0, dx1, hi_live[mt], lo_t, hi_t);
+                    terms[(b * MT + mt) * 32 + lane] = make_float4(lo_t.x, lo_t.y, hi_t.x, hi_t.y);
+                }
+            }
+            load_next(u);
+        }
+    }
+    __syncthreads();
+    // in-order fold of the per-block terms, epilogue, stores: one thread per output element
+    for (int o = threadIdx.x; o < FRAG_GROUPS * MT * 128; o += blockDim.x) {
+        const int g2 = o / (MT * 128), rem = o % (MT * 128);
+        const int mt = rem / 128, ln = (rem / 4) % 32, i = rem % 4;
+        const int m = mt * 16 + (ln >> 2) + 8 * (i >> 1);
+        const int col = g2 * 8 + 2 * (ln & 3) + (i & 1);
+        const int64_t n = int64_t(blockIdx.x) * 32 + col;
+        float v = 0.0f;
+        if (m < m_live && n < a.n) {
+            const float *tg = reinterpret_cast<const float *>(reinterpret_cast<float4 *>(tile + MPAD * 32) +
+                                                              size_t(g2) * nb_pad * MT * 32) +
+                              (mt * 32 + ln) * 4 + i;
+            for (int b = 0; b < nb; ++b) v = __fadd_rn(v, tg[b * MT * 128]);
+            v = finish<false>(a, m, n, v);
+        }
+        tile[m * 32 + col] = v;
+    }
+    __syncthreads();
+    const int nwarps = blockDim.x >> 5;
+    for (int q = warp; q < MPAD; q += nwarps)  // lane = column of the block
+        frag_block<MODE>(tile[q * 32 + lane], q < m_live, blockIdx.x, q, MT, f.xf, f.xs, f.xsum, a.status);
+}
+
+template <int MT, int MODE>
+static void launch_frag_mode(const GemvArgs &a, const Q8Frags &f, cudaStream_t s) {
+    const size_t smem = size_t(a.nb_pad) * MT * 512 + 2 * size_t(a.nb_pad) * MT * 16 * 4 + MT * 16 * 32 * 4 +
+                        size_t(FRAG_GROUPS) * a.nb_pad * MT * 512;
+    auto kernel = k_gemv_frag<MT, MODE>;
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_LIMIT + 8192));
+        configured = true;
+    }
+    launch_pdl(kernel, dim3(unsigned(a.n / 32)), dim3(unsigned(FRAG_GROUPS * a.wpg * 32)), smem, s, a, f);
+}
+
+size_t gemv_frag_smem_bytes(int64_t nb_pad, int mt) {
+    return size_t(nb_pad) * mt * 512 + 2 * size_t(nb_pad) * mt * 16 * 4 + mt * 16 * 32 * 4 +
+           size_t(FRAG_GROUPS) * nb_pad * mt * 512;
+}
+
+// Q8_0 weights, n a multiple of 32, m <= 32 (f.mpad = 16 for m <= 16, else 32).
+void launch_gemv_frag(GemvArgs a, const Q8Frags &f, cudaStream_t s) {
+    const int mt = a.m <= 16 ? 1 : 2;
+    const int64_t chunks = a.nb_pad / 2;
+    a.wpg = int(chunks / 2 < 4 ? (chunks / 2 > 0 ? chunks / 2 : 1) : 4);  // about two chunks per warp
+    if (mt == 1) {
+        if (f.mode == 0) launch_frag_mode<1, 0>(a, f, s);
+        else if (f.mode == 2) launch_frag_mode<1, 2>(a, f, s);
+        else launch_frag_mode<1, 1>(a, f, s);
+    } else {
+        if (f.mode == 0) launch_frag_mode<2, 0>(a, f, s);
+        else if (f.mode == 2) launch_frag_mode<2, 2>(a, f, s);
+        else launch_frag_mode<2, 1>(a, f, s);
+    }
+}
+
 void launch_gemv(int q4, const GemvArgs &a, cudaStream_t s) {
     const int mt = a.m <= 16 ? 1 : 2;
     if (q4) {

@@ -87,6 +87,10 @@ struct Q8Frags {
 };
 
 bool gemv_supported(int64_t nb_pad);
+// split-K GEMV (Q8_0 weights, n % 32 == 0, m <= 32) that also writes the next
+// linear's Q8_0 fragments of its outputs (gemv.cu)
+void launch_gemv_frag(GemvArgs a, const Q8Frags &f, cudaStream_t s);
+size_t gemv_frag_smem_bytes(int64_t nb_pad, int mt);
 void launch_gemv(int q4, const GemvArgs &a, cudaStream_t s);
 
 }  // namespace mb

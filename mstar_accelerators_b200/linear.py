@@ -191,8 +191,9 @@ class BlockLinear:
     # ggml_mul_mat + epilogue -------------------------------------------------
     def __call__(self, x: torch.Tensor, *, out: torch.Tensor | None = None, residual: torch.Tensor | None = None,
                  bias: bool = True, gelu: str | None = None, norm: tuple | None = None,
-                 rounding: str = "arm") -> torch.Tensor:
-        """ggml_mul_mat(W, [LayerNorm](x)) + epilogue; norm = (weight, bias, eps) fuses the LayerNorm."""
+                 rounding: str = "arm", next_frags: "native.Q8Frags | None" = None) -> torch.Tensor:
+        """ggml_mul_mat(W, [LayerNorm](x)) + epilogue; norm = (weight, bias, eps) fuses the LayerNorm.
+        next_frags (another handle's frags(rows)) also quantizes the outputs for that handle's run_frags."""
         _require_cuda(x, "activations", torch.float32)
         lead = x.shape[:-1]
         x2 = _rows(x, self.width)
@@ -211,6 +212,13 @@ class BlockLinear:
             r_ptr = r2.data_ptr()
         lw, lb, eps = _norm(norm)
         e = error_buffer()
+        if next_frags is not None:
+            check(self.lib.mstar_b200_linear_run_q8out(self.handle, x2.data_ptr(), x2.stride(0), m, o2.data_ptr(),
+                                                       o2.stride(0), r_ptr, flags, lw, lb, eps,
+                                                       native.ROUNDING[rounding], C.byref(next_frags),
+                                                       _stream(x.device), e, len(e)),
+                  e, "B200 linear with fragment output")
+            return out
         check(self.lib.mstar_b200_linear_run(self.handle, x2.data_ptr(), x2.stride(0), m, o2.data_ptr(), o2.stride(0),
                                              r_ptr, flags, lw, lb, eps, native.ROUNDING[rounding], _stream(x.device),
                                              e, len(e)),

@@ -52,6 +52,8 @@ SIGNATURES = {
     "mstar_b200_linear_prepare_readout": (_int, [_vp, _vp, _u64, *_err]),
     "mstar_b200_linear_frags": (_int, [_vp, _i64, C.c_int32, _vp, *_err]),
     "mstar_b200_linear_run_frags": (_int, [_vp, _i64, _vp, _i64, _vp, _int, _vp, *_err]),
+    "mstar_b200_linear_run_q8out": (_int, [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _int, _vp, _vp, C.c_float, _int,
+                                           _vp, _vp, *_err]),
     "mstar_b200_linear_gemm": (_int, [_vp, _vp, _u64, _i64, _vp, _u64, _i64, C.c_int32, _vp, _u64, _i64, _i64, _i64,
                                       _i64, C.c_int32, C.c_int32, _vp, _vp, *_err]),
     "mstar_b200_tp_barrier": (_int, [_vp, _vp, C.c_int32, C.c_int32, _vp, _vp, _vp, *_err]),

@@ -213,8 +213,12 @@ class WhisperDecoderB200:
                 Lr["cout"].run_frags(rows, out=x, residual=x)
             else:
                 Lr["cout"](att, out=x, residual=x, rounding=r)
-            Lr["fc1"](x, out=h, norm=Lr["ln3"], gelu="tanh", rounding=r)
-            Lr["fc2"](h, out=x, residual=x, rounding=r)
+            if fused:  # fc1's epilogue quantizes its GELU outputs straight into fc2's fragments
+                Lr["fc1"](x, out=h, norm=Lr["ln3"], gelu="tanh", rounding=r, next_frags=Lr["fc2"].frags(rows, r))
+                Lr["fc2"].run_frags(rows, out=x, residual=x)
+            else:
+                Lr["fc1"](x, out=h, norm=Lr["ln3"], gelu="tanh", rounding=r)
+                Lr["fc2"](h, out=x, residual=x, rounding=r)
 
     def _readout(self, last: torch.Tensor, walk: str, logits, token):
         sup = self.suppressed.get(walk)

@@ -168,3 +168,32 @@ def test_attention_output_fragments_equal_the_linear_quantizer(shared, batch, ro
     assert torch.equal(att, att2)
     assert torch.equal(got, ref) and torch.equal(got_res, ref_res)
     lin.close()
+
+
+@pytest.mark.parametrize("m", [1, 9, 16, 32])
+@pytest.mark.parametrize("rounding", ["arm", "ref", "x86"])
+def test_fc1_fragment_output_equals_the_fc2_quantizer(m, rounding):
+    """fc1 (LayerNorm, bias, GELU) with next_frags + fc2.run_frags gives the bytes of fc1 then fc2."""
+    from mstar_accelerators_b200.linear import BlockLinear
+    g = torch.Generator(device="cuda").manual_seed(m)
+    d, f = 384, 1536
+    fc1 = BlockLinear(torch.randn((f, d), device="cuda", generator=g) * 0.05,
+                      bias=torch.randn(f, device="cuda", generator=g) * 0.1)
+    fc2 = BlockLinear(torch.randn((d, f), device="cuda", generator=g) * 0.05,
+                      bias=torch.randn(d, device="cuda", generator=g) * 0.1)
+    x = torch.randn((m, d), device="cuda", generator=g) * 2
+    lw = torch.rand(d, device="cuda", generator=g) + 0.5
+    lb = torch.randn(d, device="cuda", generator=g) * 0.1
+    norm = (lw, lb, 1e-5)
+    h_ref = fc1(x, norm=norm, gelu="tanh", rounding=rounding)
+    xr = x.clone()
+    fc2(h_ref, out=xr, residual=xr, rounding=rounding)
+    h = torch.empty_like(h_ref)
+    fc1(x, out=h, norm=norm, gelu="tanh", rounding=rounding, next_frags=fc2.frags(m, rounding))
+    xg = x.clone()
+    fc2.run_frags(m, out=xg, residual=xg)
+    torch.cuda.synchronize()
+    assert torch.equal(h, h_ref)
+    assert torch.equal(xg, xr)
+    fc1.close()
+    fc2.close()
