@@ -351,6 +351,7 @@ __device__ __forceinline__ void attend_task(const AttArgs &a, int task, unsigned
         if (active && tl > 0 && tl < used) {
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
+                if (mt * 16 + g + 8 * half >= R) continue;  // only live rows are merged
                 float *row = st + ((mt * (TL - 1) + tl - 1) * 16 + g + 8 * half) * (HEAD_DIM + 2);
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
@@ -368,6 +369,7 @@ __device__ __forceinline__ void attend_task(const AttArgs &a, int task, unsigned
             for (int l2 = 1; l2 < used; ++l2) {
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
+                    if (mt * 16 + g + 8 * half >= R) continue;
                     const float *row = st + ((mt * (TL - 1) + l2 - 1) * 16 + g + 8 * half) * (HEAD_DIM + 2);
                     const float mb = row[HEAD_DIM], lb = row[HEAD_DIM + 1];
                     const float M = fmaxf(mrun[half], mb);
