@@ -3,6 +3,7 @@
     python -m mstar_accelerators_b200.cases readout-q4-b32
     python -m mstar_accelerators_b200.cases decode-step-b32
     python -m mstar_accelerators_b200.cases encoder-large-b16
+    python -m mstar_accelerators_b200.cases moe-prefill-4096
 
 Each case builds its inputs from fixed seeds, runs a few calls, synchronises
 and prints "ok". The ncu summaries under profiles/ name the case they used.
@@ -77,9 +78,30 @@ def encoder_large_b16():
     _encoder(LARGE_V3, 16, 2)
 
 
+def moe_prefill_4096(fmt: str = "bf16"):
+    """Qwen3-Omni thinker MoE layer (128 experts, I 768, H 2048, top-8) over 4096 tokens, three calls."""
+    from .moe import ThinkerMoEB200, route
+    g = torch.Generator(device="cuda").manual_seed(5)
+    E, I, H, K, T = 128, 768, 2048, 8, 4096
+    w1 = (torch.randn((E, 2 * I, H), device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn((E, H, I), device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    wr = (torch.randn((E, H), device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn((T, H), device="cuda", generator=g).to(torch.bfloat16)
+    layer = ThinkerMoEB200(w1, w2, fmt=fmt, top_k=K, max_tokens=T)
+    w, ids = route(x, wr, top_k=K)
+    for _ in range(3):
+        layer(x, w, ids)
+
+
+def moe_prefill_4096_q8():
+    """The same layer with Q8_0 experts."""
+    moe_prefill_4096("q8_0")
+
+
 CASES = {"readout-q4-b32": readout_q4_b32, "decode-step-b32": decode_step_b32,
          "gemm-q8-8192x5120x1280": gemm_q8_8192x5120x1280, "encoder-tiny-b1": encoder_tiny_b1,
-         "encoder-large-b16": encoder_large_b16}
+         "encoder-large-b16": encoder_large_b16, "moe-prefill-4096": moe_prefill_4096,
+         "moe-prefill-4096-q8": moe_prefill_4096_q8}
 
 
 def main(argv):

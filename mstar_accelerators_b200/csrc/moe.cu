@@ -191,30 +191,37 @@ __global__ void k_moe_count(const int32_t *__restrict__ ids, int P, int E, int *
     atomicAdd(counts + e, 1);
 }
 
-// single CTA: exclusive scan of counts, per-expert cursors, 128-row tile list
+// single CTA: exclusive scans of the counts and of the 128-row tile counts
+// (one thread, in shared memory), then every expert's offsets, cursor and tile
+// entries written in parallel; the tile list is in expert order, cut at max_tiles
 __global__ void k_moe_plan(MoePlan p, int E, int max_tiles) {
-    __shared__ int cnt[1024], mt[1024];
+    __shared__ int cnt[1024], off[1024], toff[1024];
     const int tid = threadIdx.x;
-    for (int e = tid; e < E; e += blockDim.x) {
-        cnt[e] = p.counts[e];
-        mt[e] = (cnt[e] + MOE_BM - 1) / MOE_BM;
-    }
+    for (int e = tid; e < E; e += blockDim.x) cnt[e] = p.counts[e];
     __syncthreads();
     if (tid == 0) {
-        int off = 0, tiles = 0;
+        int o = 0, t = 0;
         for (int e = 0; e < E; ++e) {
-            p.offsets[e] = off;
-            p.cursor[e] = 0;
-            for (int j = 0; j < mt[e] && tiles < max_tiles; ++j, ++tiles) {
-                p.tiles[3 * tiles] = e;
-                p.tiles[3 * tiles + 1] = off + j * MOE_BM;
-                const int end = off + (j + 1) * MOE_BM;
-                p.tiles[3 * tiles + 2] = end < off + cnt[e] ? end : off + cnt[e];
-            }
-            off += cnt[e];
+            off[e] = o;
+            toff[e] = t;
+            o += cnt[e];
+            t += (cnt[e] + MOE_BM - 1) / MOE_BM;
         }
-        *p.num_tiles = tiles;
-        *p.valid = off;
+        *p.num_tiles = t < max_tiles ? t : max_tiles;
+        *p.valid = o;
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += blockDim.x) {
+        p.offsets[e] = off[e];
+        p.cursor[e] = 0;
+        const int mt = (cnt[e] + MOE_BM - 1) / MOE_BM;
+        for (int j = 0; j < mt && toff[e] + j < max_tiles; ++j) {
+            const int tile = toff[e] + j;
+            p.tiles[3 * tile] = e;
+            p.tiles[3 * tile + 1] = off[e] + j * MOE_BM;
+            const int end = off[e] + (j + 1) * MOE_BM;
+            p.tiles[3 * tile + 2] = end < off[e] + cnt[e] ? end : off[e] + cnt[e];
+        }
     }
 }
 
@@ -259,6 +266,77 @@ __global__ void k_moe_gather(const __nv_bfloat16 *__restrict__ x, const int *__r
         const float sv = __fmul_rn(v, id);
         const int q = rounding == 0 ? int(roundf(sv)) : __float2int_rn(sv);
         dst[b * QK + lane] = __float2half_rn(__fmul_rn(float(q), __half2float(__float2half_rn(d))));
+    }
+}
+
+// k_moe_gather with 16-byte rows pieces (x 16-byte aligned, H a multiple of
+// 128): bf16 rows as one uint4 per thread and pass; Q8_0 rows four blocks per
+// warp and pass (8 lanes per block, 4 elements per lane), the same quantization.
+__global__ void __launch_bounds__(256) k_moe_gather_vec(const __nv_bfloat16 *__restrict__ x,
+                                                        const int *__restrict__ perm, const int *__restrict__ valid,
+                                                        int P, int H, int topk, int q8, int rounding,
+                                                        void *__restrict__ xp) {
+    const int pos = blockIdx.x;
+    if (pos >= P || pos >= *valid) return;
+    const int64_t t = perm[pos] / topk;
+    const __nv_bfloat16 *src = x + t * H;
+    if (!q8) {
+        const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
+        uint4 *d4 = reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(xp) + int64_t(pos) * H);
+        for (int i = threadIdx.x; i < H / 8; i += blockDim.x) d4[i] = s4[i];
+        return;
+    }
+    __half *dst = static_cast<__half *>(xp) + int64_t(pos) * H;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    for (int c = warp; c < H / 128; c += nwarps) {  // 128 elements = 4 blocks per warp and pass
+        const int e0 = c * 128 + 4 * lane;
+        const uint2 raw = *reinterpret_cast<const uint2 *>(src + e0);
+        __nv_bfloat162 p0, p1;
+        memcpy(&p0, &raw.x, 4);
+        memcpy(&p1, &raw.y, 4);
+        const float2 f0 = __bfloat1622float2(p0), f1 = __bfloat1622float2(p1);
+        float amax = fmaxf(fmaxf(fabsf(f0.x), fabsf(f0.y)), fmaxf(fabsf(f1.x), fabsf(f1.y)));
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float d = __fdiv_rn(amax, 127.0f);
+        float id;
+        if (rounding == 2) id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        else id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        const float dh = __half2float(__float2half_rn(d));
+        auto qd = [&](float v) {
+            const float sv = __fmul_rn(v, id);
+            const int q = rounding == 0 ? int(roundf(sv)) : __float2int_rn(sv);
+            return __float2half_rn(__fmul_rn(float(q), dh));
+        };
+        __half2 h0 = __halves2half2(qd(f0.x), qd(f0.y)), h1 = __halves2half2(qd(f1.x), qd(f1.y));
+        uint2 o;
+        memcpy(&o.x, &h0, 4);
+        memcpy(&o.y, &h1, 4);
+        *reinterpret_cast<uint2 *>(dst + e0) = o;
+    }
+}
+
+// k_moe_combine with 8 outputs per thread (y and out 16-byte aligned, H a multiple of 8)
+__global__ void k_moe_combine_vec(const __nv_bfloat16 *__restrict__ y, const int *__restrict__ inv, int T, int H,
+                                  int topk, __nv_bfloat16 *__restrict__ out) {
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    int rows[MOE_MAX_TOPK];
+    for (int s = 0; s < topk; ++s) rows[s] = inv[t * topk + s];
+    for (int n8 = threadIdx.x; n8 < H / 8; n8 += blockDim.x) {
+        float acc[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        for (int s = 0; s < topk; ++s) {
+            if (rows[s] < 0) continue;
+            const uint4 v = *reinterpret_cast<const uint4 *>(y + int64_t(rows[s]) * H + 8 * n8);
+            const __nv_bfloat16 *b = reinterpret_cast<const __nv_bfloat16 *>(&v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __bfloat162float(b[i]));
+        }
+        uint4 o;
+        __nv_bfloat16 *ob = reinterpret_cast<__nv_bfloat16 *>(&o);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ob[i] = __float2bfloat16_rn(acc[i]);
+        *reinterpret_cast<uint4 *>(out + int64_t(t) * H + 8 * n8) = o;
     }
 }
 
@@ -445,11 +523,18 @@ __global__ void __launch_bounds__(MOE_THREADS, 1)
                             mid[j] = bf16r(silu_bf16(gv) * uv);
                         }
                         const int64_t col = int64_t(nt) * 128 + c * 32;
-                        if (!a.q8) {
-                            __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(a.mid) + int64_t(row) * a.I + col;
+                        if (!a.q8) {  // 16-byte stores: 4 per row chunk
+                            uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(a.mid) +
+                                                                   int64_t(row) * a.I + col);
 #pragma unroll
-                            for (int j = 0; j < 32; j += 2)
-                                *reinterpret_cast<__nv_bfloat162 *>(dst + j) = __floats2bfloat162_rn(mid[j], mid[j + 1]);
+                            for (int j = 0; j < 32; j += 8) {
+                                uint4 v;
+                                __nv_bfloat162 h[4];
+#pragma unroll
+                                for (int u = 0; u < 4; ++u) h[u] = __floats2bfloat162_rn(mid[j + 2 * u], mid[j + 2 * u + 1]);
+                                memcpy(&v, h, 16);
+                                dst[j / 8] = v;
+                            }
                         } else {
                             // this thread's 32 values are one Q8_0 block of the row
                             float amax = 0.0f;
@@ -460,12 +545,19 @@ __global__ void __launch_bounds__(MOE_THREADS, 1)
                             if (a.rounding == 2) id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
                             else id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
                             const float dh = __half2float(__float2half_rn(d));
-                            __half *dst = static_cast<__half *>(a.mid) + int64_t(row) * a.I + col;
+                            uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__half *>(a.mid) + int64_t(row) * a.I + col);
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) {
-                                const float sv = __fmul_rn(mid[j], id);
-                                const int qv = a.rounding == 0 ? int(roundf(sv)) : __float2int_rn(sv);
-                                dst[j] = __float2half_rn(__fmul_rn(float(qv), dh));
+                            for (int j = 0; j < 32; j += 8) {
+                                __half hv[8];
+#pragma unroll
+                                for (int u = 0; u < 8; ++u) {
+                                    const float sv = __fmul_rn(mid[j + u], id);
+                                    const int qv = a.rounding == 0 ? int(roundf(sv)) : __float2int_rn(sv);
+                                    hv[u] = __float2half_rn(__fmul_rn(float(qv), dh));
+                                }
+                                uint4 v;
+                                memcpy(&v, hv, 16);
+                                dst[j / 8] = v;
                             }
                         }
                     }
@@ -475,13 +567,20 @@ __global__ void __launch_bounds__(MOE_THREADS, 1)
                 for (int c = 0; c < MOE_BN / 32; ++c) {
                     uint32_t r[32];
                     tmem_ld32(tb0 + uint32_t(c * 32), r);
-                    if (row < r1) {
-                        __nv_bfloat16 *dst = a.y + int64_t(row) * (int64_t(a.n_tiles) * MOE_BN) +
-                                             int64_t(nt) * MOE_BN + c * 32;
+                    if (row < r1) {  // 16-byte stores: 4 per row chunk
+                        uint4 *dst = reinterpret_cast<uint4 *>(a.y + int64_t(row) * (int64_t(a.n_tiles) * MOE_BN) +
+                                                               int64_t(nt) * MOE_BN + c * 32);
 #pragma unroll
-                        for (int j = 0; j < 32; j += 2)
-                            *reinterpret_cast<__nv_bfloat162 *>(dst + j) =
-                                __floats2bfloat162_rn(__uint_as_float(r[j]) * w, __uint_as_float(r[j + 1]) * w);
+                        for (int j = 0; j < 32; j += 8) {
+                            __nv_bfloat162 h[4];
+#pragma unroll
+                            for (int u = 0; u < 4; ++u)
+                                h[u] = __floats2bfloat162_rn(__uint_as_float(r[j + 2 * u]) * w,
+                                                             __uint_as_float(r[j + 2 * u + 1]) * w);
+                            uint4 v;
+                            memcpy(&v, h, 16);
+                            dst[j / 8] = v;
+                        }
                     }
                 }
             }
@@ -731,8 +830,13 @@ int mstar_b200_moe_run(void *handle, const void *x, int64_t tokens, const float 
         k_moe_count<<<unsigned(ceil_div(P, 256)), 256, 0, s>>>(topk_ids, P, m.E, m.plan.counts, status);
         k_moe_plan<<<1, 256, 0, s>>>(m.plan, m.E, m.max_tiles);
         k_moe_scatter<<<unsigned(ceil_div(P, 256)), 256, 0, s>>>(topk_ids, P, m.E, m.plan);
-        k_moe_gather<<<unsigned(P), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), m.plan.perm, m.plan.valid, P, m.H, m.topk,
-                                                 m.q8, rounding, m.xp);
+        const bool vec = uintptr_t(x) % 16 == 0 && uintptr_t(out) % 16 == 0 && m.H % 128 == 0;
+        if (vec)
+            k_moe_gather_vec<<<unsigned(P), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), m.plan.perm,
+                                                         m.plan.valid, P, m.H, m.topk, m.q8, rounding, m.xp);
+        else
+            k_moe_gather<<<unsigned(P), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), m.plan.perm,
+                                                     m.plan.valid, P, m.H, m.topk, m.q8, rounding, m.xp);
         MoeGemmArgs g{};
         g.tiles = m.plan.tiles;
         g.num_tiles = m.plan.num_tiles;
@@ -756,8 +860,12 @@ int mstar_b200_moe_run(void *handle, const void *x, int64_t tokens, const float 
         g.y = m.y;
         if (m.q8) launch_moe_gemm<MOE_DOWN, false>(m.map_mid, m.map_w2, g, m.max_tiles, s);
         else launch_moe_gemm<MOE_DOWN, true>(m.map_mid, m.map_w2, g, m.max_tiles, s);
-        k_moe_combine<<<unsigned(tokens), 256, 0, s>>>(m.y, m.plan.inv, int(tokens), m.H, m.topk,
-                                                        static_cast<__nv_bfloat16 *>(out));
+        if (vec)
+            k_moe_combine_vec<<<unsigned(tokens), 256, 0, s>>>(m.y, m.plan.inv, int(tokens), m.H, m.topk,
+                                                               static_cast<__nv_bfloat16 *>(out));
+        else
+            k_moe_combine<<<unsigned(tokens), 256, 0, s>>>(m.y, m.plan.inv, int(tokens), m.H, m.topk,
+                                                           static_cast<__nv_bfloat16 *>(out));
         cuda_check(cudaGetLastError(), "MoE launch");
         return 0;
     } catch (const std::exception &e) {
