@@ -87,7 +87,13 @@ def moe_prefill_4096(fmt: str = "bf16"):
     w2 = (torch.randn((E, H, I), device="cuda", generator=g) * 0.02).to(torch.bfloat16)
     wr = (torch.randn((E, H), device="cuda", generator=g) * 0.02).to(torch.bfloat16)
     x = torch.randn((T, H), device="cuda", generator=g).to(torch.bfloat16)
-    layer = ThinkerMoEB200(w1, w2, fmt=fmt, top_k=K, max_tokens=T)
+    if fmt == "q8_0":  # canonical Q8_0 expert bytes
+        from .linear import pack
+        w1 = pack(w1.float().reshape(-1, H), "q8_0", preround=False).reshape(E, 2 * I, -1)
+        w2 = pack(w2.float().reshape(-1, I), "q8_0", preround=False).reshape(E, H, -1)
+        layer = ThinkerMoEB200(w1, w2, fmt=fmt, top_k=K, max_tokens=T, intermediate=I, hidden=H)
+    else:
+        layer = ThinkerMoEB200(w1, w2, fmt=fmt, top_k=K, max_tokens=T)
     w, ids = route(x, wr, top_k=K)
     for _ in range(3):
         layer(x, w, ids)
