@@ -4,10 +4,11 @@ Each of the W ranks holds experts [r*E/W, (r+1)*E/W) (16 of 128 at W = 8) and
 the full routing of its own tokens. One forward:
 
   1. dispatch: the (token, slot) pairs are ordered by owning rank (stable, so
-     slot order inside a rank is kept); send counts are exchanged with one
-     all_to_all of W int64 and read on the host (the split sizes of the next
-     collectives); token rows (bf16), local expert ids and routing weights
-     travel with all_to_all_single;
+     slot order inside a rank is kept); send counts and an invalid-id flag are
+     exchanged with one all_to_all and read on the host in the call's one
+     synchronisation (the split sizes of the next collectives; an invalid id on
+     any rank makes every rank raise there); token rows (bf16) and the (local
+     expert id, routing weight) pairs travel with two all_to_all_single;
   2. every rank runs its local experts on the received pairs as a top-1 MoE
      whose routing weight is the pair's weight, so each returned row is
      y_s = bf16((mid . w_down) * w_s) exactly as in down_vector_reduce
@@ -78,21 +79,28 @@ class ExpertParallelMoE:
         k = self.top_k
         per = self.experts // self.world
         ids = topk_ids.reshape(-1).long()
-        if ids.numel() and (int(ids.min()) < 0 or int(ids.max()) >= self.experts):
-            raise ValueError("expert id outside [0, experts)")
-        dest = ids // per
+        bad = ((ids < 0) | (ids >= self.experts)).any().to(torch.int64).reshape(1)
+        dest = (ids // per).clamp_(0, self.world - 1)
         order = torch.sort(dest, stable=True).indices          # send position -> pair index
         counts = torch.bincount(dest, minlength=self.world)
-        recv_counts_t = torch.empty_like(counts)
-        dist.all_to_all_single(recv_counts_t, counts, group=self.group)
-        both = torch.stack([counts, recv_counts_t]).cpu()  # the one host synchronisation: split sizes
-        send_counts, recv_counts = both[0].tolist(), both[1].tolist()
+        # one exchange of (count, invalid-id flag) per peer and one host synchronisation: the split
+        # sizes of the next collectives, and an invalid id on any rank stops every rank here
+        meta = torch.stack([counts, bad.expand(self.world)], dim=1).reshape(-1).contiguous()
+        recv_meta = torch.empty_like(meta)
+        dist.all_to_all_single(recv_meta, meta, group=self.group)
+        host = torch.stack([meta, recv_meta]).cpu().view(2, self.world, 2)
+        if int(host[1, :, 1].max()) != 0:
+            raise ValueError("expert id outside [0, experts)")
+        send_counts, recv_counts = host[0, :, 0].tolist(), host[1, :, 0].tolist()
         rows = x[order // k]
+        # local expert id and routing weight travel together as two 32-bit words per pair
         local_ids = (ids[order] - dest[order] * per).to(torch.int32)
         weights = topk_weights.reshape(-1)[order].to(torch.float32)
+        pairs = torch.stack([local_ids, weights.view(torch.int32)], dim=1).contiguous()
         r_rows = self._exchange(rows.contiguous(), send_counts, recv_counts)
-        r_ids = self._exchange(local_ids.contiguous(), send_counts, recv_counts)
-        r_w = self._exchange(weights.contiguous(), send_counts, recv_counts)
+        r_pairs = self._exchange(pairs, send_counts, recv_counts)
+        r_ids = r_pairs[:, 0].contiguous()
+        r_w = r_pairs[:, 1].contiguous().view(torch.float32)
         y_local = self.local(r_rows, r_w, r_ids)               # [received, H] bf16, one row per pair
         y_back = self._exchange(y_local.contiguous(), recv_counts, send_counts)
         inverse = torch.empty_like(order)

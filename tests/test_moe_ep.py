@@ -95,3 +95,30 @@ def test_owned_experts_split():
     assert owned_experts(128, 8, 3) == range(48, 64)
     with pytest.raises(ValueError):
         owned_experts(10, 4, 0)
+
+
+def _bad_worker(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from mstar_accelerators_b200.moe_ep import ExpertParallelMoE
+        layer = ExpertParallelMoE(lambda r, w, i: r, lambda y, rows, k: y, experts=E, top_k=K)
+        x, w, ids = _tokens(rank)
+        if rank == 1:
+            ids[2, 1] = E + 3                       # one invalid id on one rank only
+        try:
+            layer(x, w, ids)
+            results[rank] = "no error"
+        except ValueError as err:
+            results[rank] = "raised" if "expert id" in str(err) else str(err)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_an_invalid_id_on_one_rank_stops_every_rank():
+    world = 2
+    with mp.Manager() as manager:
+        results = manager.dict()
+        mp.spawn(_bad_worker, args=(world, _port(), results), nprocs=world, join=True)
+        assert dict(results) == {0: "raised", 1: "raised"}
