@@ -228,6 +228,20 @@ MSTAR_B200_API int mstar_b200_moe_close(void *handle, char *error, size_t error_
  * nothing), out bf16 [tokens][hidden]. */
 MSTAR_B200_API int mstar_b200_moe_combine(const void *y, int64_t y_rows, const int32_t *rows, int64_t tokens,
     int32_t top_k, int64_t hidden, void *out, void *stream, char *error, size_t error_size);
+/* Expert-parallel dispatch plan (the send side of an all_to_all MoE over
+ * `ranks` ranks, each owning experts/ranks consecutive experts; the reference
+ * runs all experts in one process, thinker_moe.py:104-188, so this has no
+ * direct counterpart there). The tokens*top_k (token, slot) pairs are put in
+ * send order: grouped by owning rank d = clamp(floor(id / (experts/ranks)), 0,
+ * ranks-1), pair order inside a rank. Writes meta int64 [ranks][2] = (pairs for
+ * rank d, 1 if any id is outside [0, experts)); rows bf16 [pairs][hidden] =
+ * x[pair / top_k] in send order; pairs int32 [pairs][2] = (id - d*(experts/
+ * ranks), bits of the fp32 weight) in send order; inverse int32 [pairs] = the
+ * send position of each pair (the rows argument of mstar_b200_moe_combine).
+ * tokens may be 0 (meta only). No host synchronisation. */
+MSTAR_B200_API int mstar_b200_moe_dispatch(const void *x, int64_t tokens, int64_t hidden,
+    const float *topk_weights, const int32_t *topk_ids, int32_t top_k, int32_t experts, int32_t ranks,
+    int64_t *meta, void *rows, int32_t *pairs, int32_t *inverse, void *stream, char *error, size_t error_size);
 
 
 /* --- encoder graph staging (backends/cpu_ggml/encoder.cpp:400-754) ------------------

@@ -372,6 +372,147 @@ __global__ void k_moe_combine_rows(const __nv_bfloat16 *__restrict__ y, int64_t 
     }
 }
 
+// k_moe_combine_rows with 8 outputs per thread (y and out 16-byte aligned, H a multiple of 8)
+__global__ void k_moe_combine_rows_vec(const __nv_bfloat16 *__restrict__ y, int64_t y_rows,
+                                       const int *__restrict__ rows, int T, int H, int topk,
+                                       __nv_bfloat16 *__restrict__ out) {
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    int r[MOE_MAX_TOPK];
+    for (int s = 0; s < topk; ++s) r[s] = rows[int64_t(t) * topk + s];
+    for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+        for (int s = 0; s < topk; ++s) {
+            if (r[s] < 0 || r[s] >= y_rows) continue;
+            const uint4 v = reinterpret_cast<const uint4 *>(y + int64_t(r[s]) * H)[c];
+            const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 f = __bfloat1622float2(h[j]);
+                acc[2 * j] = __fadd_rn(acc[2 * j], f.x);
+                acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], f.y);
+            }
+        }
+        uint4 o;
+        __nv_bfloat162 *oh = reinterpret_cast<__nv_bfloat162 *>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+        reinterpret_cast<uint4 *>(out + int64_t(t) * H)[c] = o;
+    }
+}
+
+// ------------------------------------------------------------------ expert-parallel dispatch
+// Send order of the T*k (token, slot) pairs for W expert-owning ranks: the
+// pairs grouped by owning rank d = clamp(floor(id / per), 0, W - 1), in pair
+// order inside a rank (a stable counting sort). One CTA of 32 warps. Pass 1
+// counts the pairs per rank with warp ballots. Pass 2 walks the pairs in
+// rounds of 1024: each pair's place among its warp's pairs for the same rank
+// comes from a ballot, the warps' counts become offsets through one warp-level
+// scan per rank, and the pair's send position (inverse), local expert id and
+// routing weight bits (pairs) are written. meta [W][2] = (pairs for rank d,
+// 1 if any id lies outside [0, E)).
+constexpr int EP_THREADS = 1024, EP_MAX_RANKS = 32;
+
+__device__ __forceinline__ int ep_rank_of(int id, int per, int W) {
+    if (id < 0) return 0;
+    const int d = id / per;
+    return d < W ? d : W - 1;
+}
+
+__global__ void __launch_bounds__(EP_THREADS) k_ep_plan(const int32_t *__restrict__ ids,
+                                                        const float *__restrict__ w, int P, int per, int E, int W,
+                                                        int64_t *__restrict__ meta, int32_t *__restrict__ pairs,
+                                                        int32_t *__restrict__ inverse) {
+    __shared__ int warp_off[32][EP_MAX_RANKS + 1];
+    __shared__ int base[EP_MAX_RANKS];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const unsigned below = (1u << lane) - 1u;
+    if (tid < EP_MAX_RANKS) base[tid] = 0;
+    __syncthreads();
+    int mine = 0, bad = 0;  // lane d of a warp counts that warp's pairs for rank d
+    for (int r0 = 0; r0 < P; r0 += EP_THREADS) {
+        const int p = r0 + tid;
+        int d = -1;
+        if (p < P) {
+            const int id = ids[p];
+            bad |= id < 0 || id >= E;
+            d = ep_rank_of(id, per, W);
+        }
+        for (int dd = 0; dd < W; ++dd) {
+            const unsigned m = __ballot_sync(0xffffffffu, d == dd);
+            if (lane == dd) mine += __popc(m);
+        }
+    }
+    if (lane < W) atomicAdd(&base[lane], mine);
+    bad = __syncthreads_or(bad);
+    if (tid == 0) {  // totals -> meta, and the exclusive scan over ranks as running offsets
+        int o = 0;
+        for (int d = 0; d < W; ++d) {
+            const int c = base[d];
+            meta[2 * d] = c;
+            meta[2 * d + 1] = bad ? 1 : 0;
+            base[d] = o;
+            o += c;
+        }
+    }
+    __syncthreads();
+    for (int r0 = 0; r0 < P; r0 += EP_THREADS) {
+        const int p = r0 + tid;
+        int id = 0, d = -1;
+        if (p < P) {
+            id = ids[p];
+            d = ep_rank_of(id, per, W);
+        }
+        int place = 0, count = 0;
+        for (int dd = 0; dd < W; ++dd) {
+            const unsigned m = __ballot_sync(0xffffffffu, d == dd);
+            if (d == dd) place = __popc(m & below);
+            if (lane == dd) count = __popc(m);
+        }
+        if (lane < W) warp_off[warp][lane] = count;
+        __syncthreads();
+        if (warp < W) {  // warp d: offsets of the 32 warps' pairs for rank d
+            const int c = warp_off[lane][warp];
+            int incl = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            const int start = base[warp];
+            warp_off[lane][warp] = start + incl - c;
+            __syncwarp();
+            if (lane == 31) base[warp] = start + incl;
+        }
+        __syncthreads();
+        if (d >= 0) {
+            const int pos = warp_off[warp][d] + place;
+            inverse[p] = pos;
+            pairs[2 * pos] = id - d * per;
+            pairs[2 * pos + 1] = __float_as_int(w[p]);
+        }
+        __syncthreads();  // warp_off is rewritten by the next round
+    }
+}
+
+// rows[inverse[p]] = x[p / k]; vec: 16-byte pieces (x and rows 16-byte aligned, H a multiple of 8)
+__global__ void __launch_bounds__(256) k_ep_rows(const __nv_bfloat16 *__restrict__ x,
+                                                 const int32_t *__restrict__ inverse, int P, int H, int topk,
+                                                 int vec, __nv_bfloat16 *__restrict__ rows) {
+    const int p = blockIdx.x;
+    if (p >= P) return;
+    const __nv_bfloat16 *src = x + int64_t(p / topk) * H;
+    __nv_bfloat16 *dst = rows + int64_t(inverse[p]) * H;
+    if (vec) {
+        for (int i = threadIdx.x; i < H / 8; i += blockDim.x)
+            reinterpret_cast<uint4 *>(dst)[i] = reinterpret_cast<const uint4 *>(src)[i];
+    } else {
+        for (int i = threadIdx.x; i < H; i += blockDim.x) dst[i] = src[i];
+    }
+}
+
 // ------------------------------------------------------------------ grouped GEMM
 struct MoeGemmArgs {
     const int *tiles;      // [num_tiles][3]
@@ -885,10 +1026,52 @@ int mstar_b200_moe_combine(const void *y, int64_t y_rows, const int32_t *rows, i
         check_device(rows, "slot rows");
         check_device(out, "combined output");
         cudaStream_t s = as_stream(stream);
-        k_moe_combine_rows<<<unsigned(tokens), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(y), y_rows, rows,
-                                                            int(tokens), int(hidden), top_k,
-                                                            static_cast<__nv_bfloat16 *>(out));
+        if (uintptr_t(y) % 16 == 0 && uintptr_t(out) % 16 == 0 && hidden % 8 == 0)
+            k_moe_combine_rows_vec<<<unsigned(tokens), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(y), y_rows,
+                                                                    rows, int(tokens), int(hidden), top_k,
+                                                                    static_cast<__nv_bfloat16 *>(out));
+        else
+            k_moe_combine_rows<<<unsigned(tokens), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(y), y_rows, rows,
+                                                                int(tokens), int(hidden), top_k,
+                                                                static_cast<__nv_bfloat16 *>(out));
         cuda_check(cudaGetLastError(), "combine launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+int mstar_b200_moe_dispatch(const void *x, int64_t tokens, int64_t hidden, const float *topk_weights,
+                            const int32_t *topk_ids, int32_t top_k, int32_t experts, int32_t ranks, int64_t *meta,
+                            void *rows, int32_t *pairs, int32_t *inverse, void *stream, char *error,
+                            size_t error_size) {
+    try {
+        require(tokens >= 0 && tokens <= (int64_t(1) << 24) && top_k >= 1 && top_k <= MOE_MAX_TOPK &&
+                    hidden >= 1 && hidden <= 65536,
+                "invalid dispatch geometry");
+        require(ranks >= 1 && ranks <= EP_MAX_RANKS && experts >= ranks && experts % ranks == 0,
+                "experts must divide evenly over 1..32 ranks");
+        require(meta, "missing dispatch meta");
+        check_device(meta, "dispatch meta");
+        cudaStream_t s = as_stream(stream);
+        const int P = int(tokens) * top_k;
+        if (P > 0) {
+            require(x && topk_weights && topk_ids && rows && pairs && inverse, "missing dispatch operand");
+            for (const void *q : {x, (const void *)topk_weights, (const void *)topk_ids, (const void *)rows,
+                                  (const void *)pairs, (const void *)inverse})
+                check_device(q, "dispatch operand");
+            const uint64_t xb = uint64_t(tokens) * hidden * 2, rb = uint64_t(P) * hidden * 2;
+            require(disjoint({x, xb}, {rows, rb}), "dispatch rows overlap x");
+        }
+        k_ep_plan<<<1, EP_THREADS, 0, s>>>(topk_ids, topk_weights, P, experts / ranks, experts, ranks, meta, pairs,
+                                            inverse);
+        if (P > 0) {
+            const int vec = uintptr_t(x) % 16 == 0 && uintptr_t(rows) % 16 == 0 && hidden % 8 == 0;
+            k_ep_rows<<<unsigned(P), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), inverse, P, int(hidden),
+                                                  top_k, vec, static_cast<__nv_bfloat16 *>(rows));
+        }
+        cuda_check(cudaGetLastError(), "dispatch launch");
         return 0;
     } catch (const std::exception &e) {
         message(error, error_size, e.what());

@@ -4,7 +4,8 @@ Each of the W ranks holds experts [r*E/W, (r+1)*E/W) (16 of 128 at W = 8) and
 the full routing of its own tokens. One forward:
 
   1. dispatch: the (token, slot) pairs are ordered by owning rank (stable, so
-     slot order inside a rank is kept); send counts and an invalid-id flag are
+     slot order inside a rank is kept; on B200 one counting-sort CTA and one
+     row-copy launch, mstar_b200_moe_dispatch); send counts and an invalid-id flag are
      exchanged with one all_to_all and read on the host in the call's one
      synchronisation (the split sizes of the next collectives; an invalid id on
      any rank makes every rank raise there); token rows (bf16) and the (local
@@ -31,6 +32,33 @@ import torch.distributed as dist
 
 LocalExperts = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
 Combine = Callable[[torch.Tensor, torch.Tensor, int], torch.Tensor]
+# (x, topk_weights, topk_ids, top_k, experts, ranks) -> meta int64 [2W], rows [P, H],
+# pairs int32 [P, 2], inverse int32 [P] (the send-side plan; mstar_b200_moe_dispatch)
+Dispatch = Callable[[torch.Tensor, torch.Tensor, torch.Tensor, int, int, int],
+                    tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]]
+
+
+def torch_dispatch(x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor, top_k: int, experts: int,
+                   ranks: int):
+    """The send-side plan in torch operations (the host-logic tests on CPU ranks):
+    pairs grouped by owning rank clamp(floor(id / per), 0, W - 1), pair order
+    inside a rank; meta [W][2] = (pairs for rank d, 1 if any id is outside
+    [0, experts)); rows = x[pair / k], pairs = (local id, weight bits) and inverse
+    = each pair's send position."""
+    per = experts // ranks
+    ids = topk_ids.reshape(-1).long()
+    bad = ((ids < 0) | (ids >= experts)).any().to(torch.int64).reshape(1)
+    dest = torch.div(ids, per, rounding_mode="floor").clamp_(0, ranks - 1)
+    order = torch.sort(dest, stable=True).indices          # send position -> pair index
+    counts = torch.bincount(dest, minlength=ranks)
+    meta = torch.stack([counts, bad.expand(ranks)], dim=1).reshape(-1).contiguous()
+    rows = x[order // top_k].contiguous()
+    local_ids = (ids[order] - dest[order] * per).to(torch.int32)
+    weights = topk_weights.reshape(-1)[order].to(torch.float32)
+    pairs = torch.stack([local_ids, weights.view(torch.int32)], dim=1).contiguous()
+    inverse = torch.empty_like(order)
+    inverse[order] = torch.arange(order.numel(), device=order.device)
+    return meta, rows, pairs, inverse.to(torch.int32)
 
 
 def owned_experts(experts: int, world: int, rank: int) -> range:
@@ -43,7 +71,8 @@ def owned_experts(experts: int, world: int, rank: int) -> range:
 class ExpertParallelMoE:
     """One thinker MoE layer sharded by experts over ``group``."""
 
-    def __init__(self, local_experts: LocalExperts, combine: Combine, *, experts: int, top_k: int, group=None):
+    def __init__(self, local_experts: LocalExperts, combine: Combine, *, experts: int, top_k: int, group=None,
+                 dispatch: Dispatch = torch_dispatch):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -51,6 +80,7 @@ class ExpertParallelMoE:
         self.owned = owned_experts(experts, self.world, self.rank)
         self.local = local_experts
         self.combine = combine
+        self.dispatch = dispatch
 
     @classmethod
     def b200(cls, w1: torch.Tensor, w2: torch.Tensor, *, experts: int, top_k: int = 8, group=None,
@@ -64,8 +94,9 @@ class ExpertParallelMoE:
         own = owned_experts(experts, world, rank)
         local = ThinkerMoEB200(w1[own.start:own.stop].contiguous(), w2[own.start:own.stop].contiguous(), fmt="bf16",
                                top_k=1, max_tokens=capacity)
-        return cls(b200_local_experts(local, capacity), b200_combine(native.require_capability()), experts=experts,
-                   top_k=top_k, group=group)
+        lib = native.require_capability()
+        return cls(b200_local_experts(local, capacity), b200_combine(lib), experts=experts, top_k=top_k, group=group,
+                   dispatch=b200_dispatch(lib))
 
     def _exchange(self, send: torch.Tensor, send_counts: list[int], recv_counts: list[int]) -> torch.Tensor:
         recv = send.new_empty((sum(recv_counts),) + tuple(send.shape[1:]))
@@ -75,37 +106,23 @@ class ExpertParallelMoE:
 
     def __call__(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
         """x [T, H] bf16, topk_weights [T, k] fp32, topk_ids [T, k] -> [T, H] bf16."""
-        T, H = x.shape
         k = self.top_k
-        per = self.experts // self.world
-        ids = topk_ids.reshape(-1).long()
-        bad = ((ids < 0) | (ids >= self.experts)).any().to(torch.int64).reshape(1)
-        dest = (ids // per).clamp_(0, self.world - 1)
-        order = torch.sort(dest, stable=True).indices          # send position -> pair index
-        counts = torch.bincount(dest, minlength=self.world)
+        meta, rows, pairs, inverse = self.dispatch(x, topk_weights, topk_ids, k, self.experts, self.world)
         # one exchange of (count, invalid-id flag) per peer and one host synchronisation: the split
         # sizes of the next collectives, and an invalid id on any rank stops every rank here
-        meta = torch.stack([counts, bad.expand(self.world)], dim=1).reshape(-1).contiguous()
         recv_meta = torch.empty_like(meta)
         dist.all_to_all_single(recv_meta, meta, group=self.group)
         host = torch.stack([meta, recv_meta]).cpu().view(2, self.world, 2)
         if int(host[1, :, 1].max()) != 0:
             raise ValueError("expert id outside [0, experts)")
         send_counts, recv_counts = host[0, :, 0].tolist(), host[1, :, 0].tolist()
-        rows = x[order // k]
-        # local expert id and routing weight travel together as two 32-bit words per pair
-        local_ids = (ids[order] - dest[order] * per).to(torch.int32)
-        weights = topk_weights.reshape(-1)[order].to(torch.float32)
-        pairs = torch.stack([local_ids, weights.view(torch.int32)], dim=1).contiguous()
-        r_rows = self._exchange(rows.contiguous(), send_counts, recv_counts)
-        r_pairs = self._exchange(pairs, send_counts, recv_counts)
+        r_rows = self._exchange(rows, send_counts, recv_counts)
+        r_pairs = self._exchange(pairs, send_counts, recv_counts)  # (local expert id, weight bits)
         r_ids = r_pairs[:, 0].contiguous()
         r_w = r_pairs[:, 1].contiguous().view(torch.float32)
         y_local = self.local(r_rows, r_w, r_ids)               # [received, H] bf16, one row per pair
         y_back = self._exchange(y_local.contiguous(), recv_counts, send_counts)
-        inverse = torch.empty_like(order)
-        inverse[order] = torch.arange(order.numel(), device=order.device)
-        return self.combine(y_back, inverse.to(torch.int32), k)
+        return self.combine(y_back, inverse, k)
 
 
 def b200_local_experts(moe, capacity: int) -> LocalExperts:
@@ -117,6 +134,35 @@ def b200_local_experts(moe, capacity: int) -> LocalExperts:
             p1 = min(p0 + capacity, rows.shape[0])
             moe(rows[p0:p1], weights[p0:p1].view(-1, 1), ids[p0:p1].view(-1, 1), out=out[p0:p1])
         return out
+    return run
+
+
+def b200_dispatch(lib) -> Dispatch:
+    """The send-side plan on the device (mstar_b200_moe_dispatch): one counting-sort
+    CTA and one row-copy launch, no host synchronisation."""
+    from .linear import _stream
+    from .native import check, error_buffer
+
+    def run(x, topk_weights, topk_ids, top_k, experts, ranks):
+        T, H = x.shape
+        P = T * top_k
+        dev = x.device
+        ids = topk_ids.reshape(-1)
+        if ids.dtype != torch.int32:  # ids outside int32 stay outside [0, experts)
+            ids = ids.clamp(-1, experts).to(torch.int32)
+        ids = ids.contiguous()
+        w = topk_weights.reshape(-1).to(torch.float32).contiguous()
+        xc = x.contiguous()
+        meta = torch.empty(2 * ranks, dtype=torch.int64, device=dev)
+        rows = torch.empty((P, H), dtype=torch.bfloat16, device=dev)
+        pairs = torch.empty((P, 2), dtype=torch.int32, device=dev)
+        inverse = torch.empty(P, dtype=torch.int32, device=dev)
+        e = error_buffer()
+        ptr = (lambda t: t.data_ptr() if t.numel() else None)
+        check(lib.mstar_b200_moe_dispatch(ptr(xc), T, H, ptr(w), ptr(ids), top_k, experts, ranks, meta.data_ptr(),
+                                          ptr(rows), ptr(pairs), ptr(inverse), _stream(dev), e, len(e)), e,
+              "B200 MoE dispatch")
+        return meta, rows, pairs, inverse
     return run
 
 
