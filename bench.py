@@ -46,18 +46,60 @@ def env_rank():
 
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples during the timed region (200 ms period)."""
+    """SM clock and clock-event reasons sampled while the timed region runs.
+
+    NVML (nvidia-ml-py) is read in-process every ~0.5 ms from a thread, so even a
+    timed region of a few milliseconds gets samples; the GPU is matched by UUID
+    (CUDA_VISIBLE_DEVICES-safe). Without NVML, nvidia-smi at its 200 ms period."""
 
     FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown", 0x8),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap", 0x4))
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self.samples = []          # (sm MHz, max sm MHz, reason bits) from NVML
+        self.nvml = self.handle = None
+        self.stop = threading.Event()
+        self.thread = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            try:
+                uuid = str(torch.cuda.get_device_properties(gpu_index).uuid)
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(gpu_index)
+            self.nvml = pynvml
+            self.max_sm = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self.nvml = self.handle = None
+
+    def _sample(self):
+        n = self.nvml
+        sm = float(n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM))
+        self.samples.append((sm, self.max_sm, int(n.nvmlDeviceGetCurrentClocksEventReasons(self.handle))))
+
+    def _poll(self):
+        while not self.stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(0.0005)
 
     def __enter__(self):
+        if self.nvml is not None:
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return self
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
@@ -72,6 +114,9 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
         if self.proc:
             self.proc.terminate()
             try:
@@ -81,7 +126,17 @@ class ClockSampler:
 
     def summary(self):
         sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        if self.samples:
+            for clock, top, bits in self.samples:
+                sm.append(clock)
+                mx.append(top)
+                for name, const, value in self.REASONS:
+                    if bits & int(getattr(self.nvml, const, value)):
+                        reasons.add(name)
+            source = "nvml"
+        else:
+            source = "nvidia-smi"
+        names = [r[0] for r in self.REASONS]
         for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
@@ -95,9 +150,9 @@ class ClockSampler:
                 if flag.lower() == "active":
                     reasons.add(name)
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "source": None}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": source}
 
 
 # ----------------------------------------------------------------------------- peaks
@@ -335,7 +390,7 @@ def run_b200(args):
                              "algorithmic_bytes_per_launch": alg_bytes,
                              "launch_us": round(launch_s * 1e6, 3), "traffic": committed_traffic()},
                 "cpu_baseline": cpu,
-                "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")}}
+                "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons", "samples", "source")}}
     for gd in graphs:
         gd.graph = None
     rg = None
