@@ -48,8 +48,9 @@ def env_rank():
 class ClockSampler:
     """SM clock and clock-event reasons sampled while the timed region runs.
 
-    NVML (nvidia-ml-py) is read in-process every ~0.5 ms from a thread, so even a
-    timed region of a few milliseconds gets samples; the GPU is matched by UUID
+    NVML (nvidia-ml-py) is read in-process every ~0.5 ms from a thread and, while
+    the host waits for the timed work to finish, from the waiting thread, so even
+    a timed region of a few milliseconds gets samples; the GPU is matched by UUID
     (CUDA_VISIBLE_DEVICES-safe). Without NVML, nvidia-smi at its 200 ms period."""
 
     FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
@@ -108,6 +109,19 @@ class ClockSampler:
         except OSError:
             self.proc = None
         return self
+
+    def wait(self, event) -> None:
+        """Sample on the calling thread until the GPU reaches ``event`` (the end of the timed
+        work): the launching thread would otherwise hold the interpreter lock for most of a
+        short region, starving the polling thread."""
+        if self.nvml is None:
+            return
+        while not event.query():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(0.0002)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -291,6 +305,7 @@ def run_b200(args):
         start.record(stream)
         run_steps(args.steps)
         end.record(stream)
+        clocks.wait(end)
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
