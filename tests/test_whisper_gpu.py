@@ -2,7 +2,7 @@
 the reference graph (oracle/whisper_oracle.py).
 
 Fidelity bar: logits within 1e-2 relative to the oracle's largest |logit|
-(the north-star tolerance on logits) and greedy tokens accepted by the
+(the stated fidelity bar for logits) and greedy tokens accepted by the
 reference harness's policy (testing/generation.py:25-89: the same token, or
 reciprocal top-5, compared through the first divergence). Sequences are
 teacher-forced with the oracle's tokens so every step is compared.
