@@ -372,11 +372,13 @@ __global__ void __launch_bounds__(RO_MAX_WARPS * 32, 1) k_readout(const ReadoutA
     pdl_wait();
     pdl_trigger();  // the next kernel may launch now; it waits for this grid before reading
     if (a.pre_xf) {  // wide rows: one quantization for the whole grid, each CTA copies the 8-bit fragments
-        for (int i = threadIdx.x; i < nb * MT * 32; i += blockDim.x) s_xf[i] = a.pre_xf[i];
+        // (asynchronous 16-byte copies: all of a thread's copies in flight at once)
+        for (int i = threadIdx.x; i < nb * MT * 32; i += blockDim.x) cp_async16(s_xf + i, a.pre_xf + i, 16);
         for (int i = threadIdx.x; i < nb * MPAD; i += blockDim.x) {
             const int b = i / MPAD, q = i % MPAD;
             s_xs[b * MPAD + ((q & 7) >> 1) * (MPAD / 4) + (q >> 3) * 2 + (q & 1)] = a.pre_xs[i];
         }
+        cp_async_wait_all();
     } else {
         stage_queries<MT, NBC * QK>(a, nb, s_xf, s_xs, s_stats, warps);
     }
