@@ -274,10 +274,22 @@ __global__ void __launch_bounds__(QW_WARPS * 32) k_quantize_frag_warp(
     float *__restrict__ xs, int *__restrict__ xsum, int *__restrict__ status) {
     const int lane = threadIdx.x & 31;
     const int64_t q = int64_t(blockIdx.x) * QW_WARPS + (threadIdx.x >> 5);
+    const int nb = int(k / QK), j = lane & 7, sb = lane >> 3;
+    // narrow rows: the LayerNorm weights are parameters, not the previous kernel's output,
+    // so they are loaded before waiting on it (their latency hides behind its tail)
+    constexpr bool PRE_LN = NCH <= 4;
+    float4 pw[PRE_LN ? NCH : 1], pb[PRE_LN ? NCH : 1];
+    if (PRE_LN && ln_w && q < m) {
+#pragma unroll
+        for (int t = 0; t < (PRE_LN ? NCH : 1); ++t)
+            if (4 * t + sb < nb) {
+                pw[t] = __ldg(reinterpret_cast<const float4 *>(ln_w + 128 * t + 4 * lane));
+                pb[t] = __ldg(reinterpret_cast<const float4 *>(ln_b + 128 * t + 4 * lane));
+            }
+    }
     pdl_wait();
     pdl_trigger();
     if (q >= mpad) return;  // warp-uniform
-    const int nb = int(k / QK), j = lane & 7, sb = lane >> 3;
     const bool live_row = q < m;
     const float *xr = x + q * ldx;
     float4 v[NCH];
@@ -334,8 +346,8 @@ __global__ void __launch_bounds__(QW_WARPS * 32) k_quantize_frag_warp(
         for (int t = 0; t < NCH; ++t) {
             if (4 * t + sb >= nb) continue;
             const int64_t e = 128 * t + 4 * lane;
-            const float4 w = __ldg(reinterpret_cast<const float4 *>(ln_w + e));
-            const float4 c = __ldg(reinterpret_cast<const float4 *>(ln_b + e));
+            const float4 w = PRE_LN ? pw[PRE_LN ? t : 0] : __ldg(reinterpret_cast<const float4 *>(ln_w + e));
+            const float4 c = PRE_LN ? pb[PRE_LN ? t : 0] : __ldg(reinterpret_cast<const float4 *>(ln_b + e));
             auto nf = [&](float xv, float ww, float bb) {
                 return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv, mean), rstd), ww), bb);
             };
