@@ -193,7 +193,7 @@ def committed_traffic():
 
 
 # ----------------------------------------------------------------------------- cpu arm
-def cpu_reference_step_rate(seconds: float = 10.0, max_steps: int = 200):
+def cpu_reference_step_rate(seconds: float = 10.0, max_steps: int = 200, warmup: int = 1):
     """The reference's CPU arithmetic for one decode step's linears at batch 32:
     vendored ggml x86 quantize_row_q8_0 + vec_dot (oracle/_ref), all host threads.
     Returns (steps/s, steps timed, cores)."""
@@ -218,7 +218,8 @@ def cpu_reference_step_rate(seconds: float = 10.0, max_steps: int = 200):
             O.ref_mul_mat(blocks, xs[k], fmt, threads=cores)
         O.ref_mul_mat(head, xs[d], "q4_0", threads=cores)
 
-    step()  # warm
+    for _ in range(max(1, warmup)):  # untimed warm-up steps
+        step()
     t0 = time.perf_counter()
     n = 0
     while n < max_steps and time.perf_counter() - t0 < seconds:
@@ -233,10 +234,10 @@ def run_reference(args):
     if rank != 0:
         return 0
     rate, n, cores = cpu_reference_step_rate(seconds=min(60.0, 2.0 + 0.5 * args.steps),
-                                             max_steps=max(args.steps, 1))
+                                             max_steps=max(args.steps, 1), warmup=args.warmup)
     value = rate * BATCH
     line = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": n, "warmup": 1, "ms_per_step": round(1e3 / rate, 3), "higher_is_better": True,
+            "steps": n, "warmup": args.warmup, "ms_per_step": round(1e3 / rate, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "q8_0/q4_0 x q8_0 -> f32", "data": "synthetic",
             "config": CONFIG, "impl": "reference",
             "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": cores, "kind": "reference",
@@ -382,7 +383,7 @@ def run_b200(args):
     if rank == 0:
         cpu = None
         if world == 1:
-            rate, n, cores = cpu_reference_step_rate(seconds=10.0, max_steps=50)
+            rate, n, cores = cpu_reference_step_rate(seconds=10.0, max_steps=50, warmup=3)
             cpu = {"value": round(rate * BATCH, 2), "unit": "tokens/s", "cores": cores, "kind": "reference",
                    "sample": f"{n} decode steps of the 33 block-quantized linears (batch 32) through the "
                              "vendored ggml x86 kernels on the host cores; attention/LayerNorm excluded"}
