@@ -173,6 +173,8 @@ def b200_combine(lib) -> Combine:
     def run(y, rows, top_k):
         T = rows.numel() // top_k
         out = torch.empty((T, y.shape[1]), dtype=torch.bfloat16, device=rows.device)
+        if T == 0:  # a rank that routed no tokens this step: nothing to sum
+            return out
         e = error_buffer()
         check(lib.mstar_b200_moe_combine(y.data_ptr() if y.numel() else rows.data_ptr(), y.shape[0],
                                          rows.contiguous().data_ptr(), T, top_k, y.shape[1], out.data_ptr(),

@@ -6,7 +6,9 @@ the slot-ordered combine) is exercised with the oracle as the local expert
 computation (oracle/moe_oracle.py, top-1 per received pair) and a numpy
 slot-ordered combine. Every rank's output must equal, bit for bit, the
 single-process oracle layer over all experts for that rank's tokens. Includes a
-rank whose tokens all route to the other rank's experts.
+rank whose tokens all route to the other rank's experts, and a rank with no
+tokens at all in the step (it still takes every collective step and serves the
+other rank's pairs).
 """
 import os
 import socket
@@ -42,7 +44,7 @@ def _tokens(rank):
     return x, w.float(), ids.to(torch.int32)
 
 
-def _worker(rank, world, port, results):
+def _worker(rank, world, port, results, empty_rank=-1):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -69,9 +71,14 @@ def _worker(rank, world, port, results):
 
         layer = ExpertParallelMoE(local, combine, experts=E, top_k=K)
         x, w, ids = _tokens(rank)
+        if rank == empty_rank:  # this step routes no tokens from this rank; it still serves its experts
+            x, w, ids = x[:0], w[:0], ids[:0]
         got = layer(x, w, ids).float().numpy()
-        ref = M.experts_bf16(x.float().numpy(), w1f, w2f, w.numpy(), ids.numpy())
-        results[rank] = bool(np.array_equal(got, ref))
+        if x.shape[0]:
+            ref = M.experts_bf16(x.float().numpy(), w1f, w2f, w.numpy(), ids.numpy())
+        else:
+            ref = np.zeros((0, H), np.float32)
+        results[rank] = bool(got.shape == ref.shape and np.array_equal(got, ref))
     finally:
         dist.destroy_process_group()
 
@@ -88,6 +95,20 @@ def test_expert_parallel_matches_single_process_oracle():
         results = manager.dict()
         mp.spawn(_worker, args=(world, _port(), results), nprocs=world, join=True)
         assert dict(results) == {0: True, 1: True}
+
+
+def test_a_rank_with_no_tokens_still_serves_its_experts():
+    world = 2
+    with mp.Manager() as manager:
+        results = manager.dict()
+        mp.spawn(_worker, args=(world, _port(), results, 1), nprocs=world, join=True)
+        assert dict(results) == {0: True, 1: True}
+
+
+def test_b200_combine_of_no_tokens_launches_nothing():
+    from mstar_accelerators_b200.moe_ep import b200_combine
+    out = b200_combine(None)(torch.empty((0, H), dtype=torch.bfloat16), torch.empty(0, dtype=torch.int32), K)
+    assert out.shape == (0, H) and out.dtype == torch.bfloat16
 
 
 def test_owned_experts_split():
