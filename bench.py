@@ -1,24 +1,32 @@
-"""Throughput of the block-quantized decode path on B200.
+"""Throughput of the block-quantized Whisper encoder path on B200.
 
-Workload (the decode-bound Whisper-tiny configuration): 4 pre-LN decoder
-blocks, d=384, 6 heads, FFN 1536, Q8_0 linears, tied Q4_0 readout 51865x384,
-self-attention KV cache and cross-attention over seeded encoder states
-[1,1500,384] ~ N(0,1); 4 prompt tokens per sequence, then greedy decode at
-batch 32. One step = one greedy decode step of all 32 sequences through the
-whole layer stack and readout (32 tokens). Weights are seeded synthetic
-(N(0,0.02), fp16 pre-round, Q8_0/Q4_0); token ids uniform.
+Workload (the Whisper-large-v3-shaped encoder): log-mel input [16, 128, 3000]
+fp32 ~ U(-1.5, 1.0); two convolution stems (128 -> 1280 kernel 3, 1280 -> 1280
+kernel 3 stride 2) with GELU, + positions; 32 pre-LN layers of width 1280,
+20 heads of 64, FFN 5120 with GELU; final LayerNorm -> encoder states
+[16, 1500, 1280] fp32. Every linear and both convolutions are Q8_0 (seeded
+N(0, 0.02) weights, fp16 pre-round). One step = one forward of the whole
+batch: 16 x 1500 = 24,000 tokens through the 32-layer stack.
 
-L2 policy: 8 independent weight replicas (8 x 20 MB > 126 MB L2) rotate
-step by step, so every step streams its weights from HBM.
+--gpus 1 runs the encoder on one GPU (tensor parallelism 1). Under torchrun
+with N ranks the same forward runs tensor-parallel over N GPUs (QKV and fc1
+column-parallel by heads / FFN columns; out_proj and fc2 row-parallel with the
+reduction over NVLink peer memory), so the total work per step is fixed:
+``scaling: strong``, ``value`` = 24,000 tokens per step / step time (max over
+ranks).
 
---impl reference times the reference's own CPU arithmetic for the same step
-(the vendored ggml x86 quantizer + vec_dot kernels compiled from the
-reference sources into oracle/_ref, driven row-parallel over every host core)
-on a bounded number of steps.
+L2 policy: the inputs exceed L2 (the 24,000 x 1280 fp32 residual stream is
+123 MB and each forward streams 668 MB of weights through the 126 MB L2).
+
+--impl reference times the reference's own CPU arithmetic for the same encoder
+on the host cores (oracle/encoder_cpu_baseline.py: the vendored ggml x86
+quantizer + vec_dot kernels compiled from the reference sources into
+oracle/_ref for every contraction), one utterance of the batch per step.
 """
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import os
 import statistics
@@ -31,13 +39,15 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-BATCH = 32
-PROMPT = 4
-REPLICAS = 8
-METRIC = "tokens/s per layer stack (Whisper-tiny decoder, Q8_0 body + Q4_0 readout, greedy decode)"
-CONFIG = {"workload": "whisper-tiny decoder decode step: 4 layers d384 h6 ffn1536, Q8_0 linears, "
-                      "Q4_0 tied readout 51865x384, cross-attention over [1,1500,384]",
-          "batch": BATCH, "prompt_tokens": PROMPT, "l2": f"{REPLICAS} rotating weight replicas (> L2)"}
+BATCH = 16
+POSITIONS = 1500
+LAYERS = 32
+TOKENS = BATCH * POSITIONS
+METRIC = "tokens/s per layer stack (Whisper-large-v3-shaped encoder, Q8_0)"
+CONFIG = {"workload": "whisper-large-v3-shaped encoder: conv stems 128->1280->1280, 32 pre-LN layers d1280 h20 "
+                      "ffn5120, Q8_0 linears and convolutions, log-mel [16,128,3000] -> states [16,1500,1280]",
+          "batch": BATCH, "positions": POSITIONS, "layers": LAYERS,
+          "l2": "inputs larger than L2 (123 MB fp32 residual stream, 668 MB of Q8_0 weights per forward)"}
 
 
 def env_rank():
@@ -169,92 +179,187 @@ class ClockSampler:
                 "samples": len(sm), "source": source}
 
 
-# ----------------------------------------------------------------------------- peaks
+# ----------------------------------------------------------------------------- peaks / traffic
 def measured_peaks():
+    """(peaks dict, "measured" | "fallback") from the pool's measured peak file."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return d.get("hbm_gbs", 6650.0), "measured"
-    return 6650.0, "fallback"
+        return {"hbm_gbs": d.get("hbm_gbs", 6650.0), "bf16_tflops": d.get("bf16_tflops", 1590.0),
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", 1400.0)}, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def committed_traffic():
-    """Per-launch DRAM bytes (read + write) of the readout kernel from the committed ncu summary."""
-    p = ROOT / "profiles" / "readout_q4_vocab51865_b32.md"
-    if not p.exists():
-        return None
-    for line in p.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
-            try:
-                return int(line.split(":")[1].strip())
-            except ValueError:
-                return None
-    return None
+GEMM_SOURCE = ROOT / "mstar_accelerators_b200" / "csrc" / "gemm.cu"
+GEMM_PROFILE = ROOT / "profiles" / "gemm_encoder_large_b16.md"
+
+
+def gemm_traffic():
+    """DRAM bytes (read + write) per GEMM launch of one encoder layer, from the ncu capture
+    summarised in profiles/gemm_encoder_large_b16.md, or None when that capture was taken
+    on another revision of the GEMM kernel (the summary records the source's SHA-256)."""
+    if not GEMM_PROFILE.exists():
+        return None, "no ncu capture committed"
+    fields = {}
+    for line in GEMM_PROFILE.read_text().splitlines():
+        if ":" in line and line.split(":")[0].strip() in ("gemm_cu_sha256", "traffic_bytes_per_launch"):
+            k, v = line.split(":", 1)
+            fields[k.strip()] = v.strip().strip("`")
+    sha = hashlib.sha256(GEMM_SOURCE.read_bytes()).hexdigest()
+    if fields.get("gemm_cu_sha256") != sha:
+        return None, "the committed ncu capture is of another revision of gemm.cu"
+    try:
+        return int(fields["traffic_bytes_per_launch"]), "ncu capture of this gemm.cu revision (" + GEMM_PROFILE.name + ")"
+    except (KeyError, ValueError):
+        return None, "capture summary unreadable"
 
 
 # ----------------------------------------------------------------------------- cpu arm
-def cpu_reference_step_rate(seconds: float = 10.0, max_steps: int = 200, warmup: int = 1):
-    """The reference's CPU arithmetic for one decode step's linears at batch 32:
-    vendored ggml x86 quantize_row_q8_0 + vec_dot (oracle/_ref), all host threads.
-    Returns (steps/s, steps timed, cores)."""
-    import numpy as np
-    from oracle import oracle as O
-    if O.ref_lib() is None:
-        O.build()
-    cores = O.cpu_cores()
-    rng = np.random.default_rng(1)
-    d, f, V = 384, 1536, 51865
-    mats = []
-    for _ in range(4):
-        mats += [(O.pack_weights((rng.standard_normal((3 * d, d)) * 0.02).astype(np.float32)), "q8_0", d)]
-        mats += [(O.pack_weights((rng.standard_normal((d, d)) * 0.02).astype(np.float32)), "q8_0", d)] * 3
-        mats += [(O.pack_weights((rng.standard_normal((f, d)) * 0.02).astype(np.float32)), "q8_0", d)]
-        mats += [(O.pack_weights((rng.standard_normal((d, f)) * 0.02).astype(np.float32)), "q8_0", f)]
-    head = O.pack_weights((rng.standard_normal((V, d)) * 0.02).astype(np.float32), "q4_0")
-    xs = {k: rng.standard_normal((BATCH, k)).astype(np.float32) for k in (d, f)}
+def cpu_sample(sample_layers: int):
+    from oracle.encoder_cpu_baseline import CpuEncoderSample
+    return CpuEncoderSample(mels=128, width=1280, heads=20, layers=LAYERS, positions=POSITIONS,
+                            sample_layers=sample_layers, seed=1)
 
-    def step():
-        for blocks, fmt, k in mats:
-            O.ref_mul_mat(blocks, xs[k], fmt, threads=cores)
-        O.ref_mul_mat(head, xs[d], "q4_0", threads=cores)
 
-    for _ in range(max(1, warmup)):  # untimed warm-up steps
-        step()
-    t0 = time.perf_counter()
-    n = 0
-    while n < max_steps and time.perf_counter() - t0 < seconds:
-        step()
-        n += 1
-    dt = time.perf_counter() - t0
-    return n / dt, n, cores
+def cpu_rate(sample, steps: int, warmup: int):
+    """Tokens/s of the CPU encoder sample: `warmup` untimed, then `steps` timed forwards."""
+    for _ in range(warmup):
+        sample.forward_seconds()
+    secs = [sample.forward_seconds() for _ in range(steps)]
+    return POSITIONS * len(secs) / sum(secs), secs
 
 
 def run_reference(args):
     rank, world, _ = env_rank()
     if rank != 0:
         return 0
-    rate, n, cores = cpu_reference_step_rate(seconds=min(60.0, 2.0 + 0.5 * args.steps),
-                                             max_steps=max(args.steps, 1), warmup=args.warmup)
-    value = rate * BATCH
+    # each step is one utterance through the stems, a few layers and the final norm; fewer
+    # sampled layers for long runs so the whole run stays within a few minutes
+    sample = cpu_sample(2 if args.steps + args.warmup <= 40 else 1)
+    value, secs = cpu_rate(sample, args.steps, args.warmup)
     line = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": n, "warmup": args.warmup, "ms_per_step": round(1e3 / rate, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "q8_0/q4_0 x q8_0 -> f32", "data": "synthetic",
-            "config": CONFIG, "impl": "reference",
-            "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": cores, "kind": "reference",
-                             "sample": f"{n} decode steps of the 33 block-quantized linears (batch 32) through "
-                                       "the vendored ggml x86 kernels; attention/LayerNorm excluded"},
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * sum(secs) / len(secs), 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "q8_0 x q8_0 -> f32", "data": "synthetic", "config": CONFIG, "impl": "reference",
+            "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": sample.threads,
+                             "kind": "reference", "sample": sample.sample_text()},
             "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
 
 # ----------------------------------------------------------------------------- b200 arm
+def time_calls(calls, reps, stream):
+    """Average device microseconds of each named call list: events around `reps` rounds."""
+    import torch
+    out = {}
+    for name, fns in calls.items():
+        for f in fns:   # warm
+            f()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            for f in fns:
+                f()
+        b.record(stream)
+        b.synchronize()
+        out[name] = a.elapsed_time(b) * 1e3 / (reps * len(fns))
+    return out
+
+
+def gemm_roofline(enc, tp: bool, stream):
+    """Live CUDA-event timing of the encoder's GEMM launches (the dominant kernel), one
+    layer's four shapes over 8 rotating layers (8 x 39 MB of fp16 weights > L2)."""
+    import torch
+    from mstar_accelerators_b200.linear import stage_rows
+    cfg = enc.cfg
+    M = BATCH * POSITIONS
+    d = cfg.width
+    st = enc.status
+    layers = enc.layers[:8]
+    x = torch.randn((M, d), device="cuda")
+    a_d = stage_rows(x)
+    if tp:
+        dl, fl = enc.d_local, enc.f_local
+        a_dl = stage_rows(torch.randn((M, dl), device="cuda"))
+        h = torch.empty((M, fl), dtype=torch.float16, device="cuda")
+        qkv = enc.qkv16
+        part = enc.part[:M * d].view(M, d)
+        calls = {
+            "qkv": [lambda L=L: L["qkv"].gemm(a_d, out=qkv, out_format="f16", segments=(POSITIONS, cfg.padded_keys),
+                                             status=st) for L in layers],
+            "out_proj": [lambda L=L: L["out"].gemm(a_dl, out=part, bias=False, status=st) for L in layers],
+            "fc1": [lambda L=L: L["fc1"].gemm(a_d, out=h, out_format="staged", gelu="tanh", status=st)
+                    for L in layers],
+            "fc2": [lambda L=L: L["fc2"].gemm(h, out=part, bias=False, status=st) for L in layers]}
+        flops = {"qkv": 2 * M * 3 * dl * d, "out_proj": 2 * M * d * dl, "fc1": 2 * M * fl * d, "fc2": 2 * M * d * fl}
+    else:
+        f = cfg.ffn
+        h = enc.hidden16[:M]
+        qkv = enc.qkv16[:BATCH]
+        xs = enc.x[:M]
+        calls = {
+            "qkv": [lambda L=L: L["qkv"].gemm(a_d, out=qkv, out_format="f16", segments=(POSITIONS, cfg.padded_keys),
+                                             status=st) for L in layers],
+            "out_proj": [lambda L=L: L["out"].gemm(a_d, out=xs, residual=xs, status=st) for L in layers],
+            "fc1": [lambda L=L: L["fc1"].gemm(a_d, out=h, out_format="staged", gelu="tanh", status=st)
+                    for L in layers],
+            "fc2": [lambda L=L: L["fc2"].gemm(h, out=xs, residual=xs, status=st) for L in layers]}
+        flops = {"qkv": 2 * M * 3 * d * d, "out_proj": 2 * M * d * d, "fc1": 2 * M * f * d, "fc2": 2 * M * d * f}
+    us = time_calls(calls, 4, stream)
+    per = {k: {"us": round(us[k], 2), "tflops": round(flops[k] / us[k] / 1e6, 1)} for k in us}
+    tot_flops, tot_us = sum(flops.values()), sum(us.values())
+    return tot_flops / len(us), tot_us / len(us), per
+
+
+def decode_secondary(steps: int, warmup: int):
+    """Whisper-tiny decode (Q8_0 body, tied Q4_0 readout 51865 x 384) at batch 32, one greedy
+    step per CUDA-graph replay over 8 rotating weight replicas (> L2): the decode-bound line."""
+    import torch
+    from mstar_accelerators_b200.whisper import GraphDecoder, WhisperConfig, WhisperDecoderB200, synthetic_weights
+    cfg, batch, prompt_len, replicas = WhisperConfig(), 32, 4, 8
+    weights = synthetic_weights(cfg, seed=1, device="cuda")
+    g = torch.Generator().manual_seed(2)
+    enc = torch.randn((1, cfg.source, cfg.d_model), generator=g).cuda()
+    prompt = torch.randint(0, cfg.vocab, (batch, prompt_len), generator=torch.Generator().manual_seed(3)).cuda()
+    decs, graphs = [], []
+    for _ in range(replicas):
+        dec = WhisperDecoderB200(weights, cfg, batch=batch)
+        _, tok = dec.prefill(prompt, enc)
+        gd = GraphDecoder(dec)
+        gd.tokens.copy_(tok)
+        gd.positions.fill_(prompt_len)
+        gd.capture()
+        decs.append(dec)
+        graphs.append(gd)
+    steps = min(steps, (cfg.target - prompt_len - 2) * replicas - warmup)
+    for i in range(warmup):
+        graphs[i % replicas].graph.replay()
+    stream = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record(stream)
+    for i in range(steps):
+        graphs[(warmup + i) % replicas].graph.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    weight_bytes = 8_767_488 + 11_202_840   # Q8_0 body + Q4_0 readout per step
+    for gd in graphs:
+        gd.graph = None
+    for d in decs:
+        d.close()
+    return {"workload": "whisper-tiny decoder, batch 32, greedy decode step (4 layers d384, Q8_0 body, Q4_0 "
+                        "readout 51865x384, cross-attention over 1500 positions), 8 rotating weight replicas",
+            "value": round(batch / (ms / 1e3), 2), "unit": "tokens/s", "ms_per_step": round(ms, 4),
+            "steps": steps, "weight_gbs": round(weight_bytes / (ms / 1e3) / 1e9, 1)}
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
     from mstar_accelerators_b200 import native
-    from mstar_accelerators_b200.linear import BlockLinear
-    from mstar_accelerators_b200.whisper import GraphDecoder, WhisperConfig, WhisperDecoderB200, synthetic_weights
+    from mstar_accelerators_b200.encoder import LARGE_V3, WhisperEncoderB200, synthetic_mel, synthetic_weights
 
     rank, world, local = env_rank()
     torch.cuda.set_device(local)
@@ -262,170 +367,118 @@ def run_b200(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     native.require_capability()
-    cfg = WhisperConfig()
-    weights = synthetic_weights(cfg, seed=1, device="cuda")
-    g = torch.Generator().manual_seed(2)
-    enc = torch.randn((1, cfg.source, cfg.d_model), generator=g).cuda()
-    g3 = torch.Generator().manual_seed(3 + rank)
-    prompt = torch.randint(0, cfg.vocab, (BATCH, PROMPT), generator=g3).cuda()
+    cfg = LARGE_V3
+    weights = synthetic_weights(cfg, seed=1)
+    mel_host = synthetic_mel(cfg, BATCH, seed=2).pin_memory()
+    mel = mel_host.cuda()
+    if world > 1:
+        from mstar_accelerators_b200.encoder_tp import WhisperEncoderTP
+        enc = WhisperEncoderTP(weights, cfg, max_batch=BATCH)
+    else:
+        enc = WhisperEncoderB200(weights, cfg, max_batch=BATCH)
+    del weights
+    states = torch.empty((BATCH, POSITIONS, cfg.width), dtype=torch.float32, device="cuda")
 
-    decs, graphs = [], []
-    for r in range(REPLICAS):
-        dec = WhisperDecoderB200(weights, cfg, batch=BATCH)
-        _, tok = dec.prefill(prompt, enc)
-        gd = GraphDecoder(dec)
-        gd.tokens.copy_(tok)
-        gd.positions.fill_(PROMPT)
-        gd.capture()
-        decs.append(dec)
-        graphs.append(gd)
-    torch.cuda.synchronize()
+    def step():
+        enc(mel, out=states)
 
-    # positions must stay inside the 448-token self-attention capacity
-    max_steps = cfg.target - PROMPT - 1
-
-    def reset():
-        for gd in graphs:
-            gd.positions.fill_(PROMPT)
-
-    def run_steps(k):
-        for i in range(k):
-            graphs[i % REPLICAS].graph.replay()
-
-    per_replica = (args.warmup + args.steps + REPLICAS - 1) // REPLICAS + 1
-    if per_replica > max_steps:
-        raise SystemExit(f"--steps/--warmup exceed the {max_steps}-step context per replica")
-    reset()
-    run_steps(args.warmup)
     stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        step()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
         start.record(stream)
-        run_steps(args.steps)
+        for _ in range(args.steps):
+            step()
         end.record(stream)
         clocks.wait(end)
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    ms = start.elapsed_time(end)
-    t = torch.tensor([ms], device="cuda")
+    t = torch.tensor([start.elapsed_time(end)], device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    value = BATCH * args.steps * world / (ms_max / 1e3)
+    value = TOKENS * args.steps / (ms_max / 1e3)
+    status = int(enc.status.item())
 
-    # e2e through the public step API with host buffers: H2D tokens, replay, D2H next tokens
-    reset()
-    host_in = torch.zeros(BATCH, dtype=torch.int64).pin_memory()
-    host_out = torch.zeros(BATCH, dtype=torch.int64).pin_memory()
-    for gd in graphs:
-        host_in.copy_(gd.tokens.cpu())
-    e2e_steps = args.steps
+    # e2e through the public forward with host buffers: pinned mel in, states back to pinned host memory
+    states_host = torch.empty((BATCH, POSITIONS, cfg.width), dtype=torch.float32).pin_memory()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record(stream)
-    for i in range(e2e_steps):
-        gd = graphs[i % REPLICAS]
-        gd.tokens.copy_(host_in, non_blocking=True)
-        gd.graph.replay()
-        host_out.copy_(gd.tokens, non_blocking=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        mel.copy_(mel_host, non_blocking=True)
+        enc(mel, out=states)
+        states_host.copy_(states, non_blocking=True)
         stream.synchronize()
-        host_in.copy_(host_out)
-    e_end.record(stream)
+    e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = torch.tensor([e_start.elapsed_time(e_end)], device="cuda")
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], device="cuda")
     if world > 1:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = BATCH * e2e_steps * world / (float(e2e_ms.item()) / 1e3)
+    e2e_value = TOKENS * args.steps / (float(e2e_ms.item()) / 1e3)
 
-    # roofline of the dominant kernel: the Q4_0 vocab readout (one launch: query quantization,
-    # tile GEMV, suppression, argmax), timed alone with events over rotating replicas
-    # tile weights of 16 heads (180 MB) rotate through the 126 MB L2
-    heads = [d.head for d in decs]
-    heads += [BlockLinear(blocks=h.blocks, fmt=h.fmt, rows=h.rows, width=h.width) for h in heads]
-    for h in heads:
-        h.prepare_readout()
-    x = torch.randn((BATCH, cfg.d_model), device="cuda")
-    lg = torch.empty((BATCH, cfg.vocab), device="cuda")
-    tk = torch.empty(BATCH, dtype=torch.int64, device="cuda")
-    st = torch.zeros(1, dtype=torch.int32, device="cuda")
-    cap_stream = torch.cuda.Stream()
-    cap_stream.wait_stream(stream)
-    with torch.cuda.stream(cap_stream):
-        for h in heads:
-            h.readout(x, logits=lg, token=tk, status=st)
-    stream.wait_stream(cap_stream)
-    rg = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(rg, stream=cap_stream):
-        for i in range(2 * len(heads)):
-            heads[i % len(heads)].readout(x, logits=lg, token=tk, status=st)
-    for _ in range(3):
-        rg.replay()
-    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = max(5, args.steps // 4)
-    r0.record(stream)
-    for _ in range(reps):
-        rg.replay()
-    r1.record(stream)
-    torch.cuda.synchronize()
-    launch_s = r0.elapsed_time(r1) / 1e3 / (reps * 2 * len(heads))
-    weight_bytes = cfg.vocab * (cfg.d_model // 32) * 18
-    alg_bytes = weight_bytes + BATCH * cfg.d_model * 4 + BATCH * cfg.vocab * 4
-    peak, peak_kind = measured_peaks()
-    achieved = alg_bytes / launch_s / 1e9
+    # roofline of the dominant kernel (the tcgen05 GEMM), timed live on this stream
+    flops_per_launch, us_per_launch, per_shape = gemm_roofline(enc, world > 1, stream)
+    peaks, peak_kind = measured_peaks()
+    achieved = flops_per_launch / us_per_launch / 1e6   # TFLOP/s
+    traffic, traffic_src = gemm_traffic()
+    launches = enc.launches_per_forward() * args.steps
 
     line = None
     if rank == 0:
         cpu = None
+        secondary = None
         if world == 1:
-            rate, n, cores = cpu_reference_step_rate(seconds=10.0, max_steps=50, warmup=3)
-            cpu = {"value": round(rate * BATCH, 2), "unit": "tokens/s", "cores": cores, "kind": "reference",
-                   "sample": f"{n} decode steps of the 33 block-quantized linears (batch 32) through the "
-                             "vendored ggml x86 kernels on the host cores; attention/LayerNorm excluded"}
+            sample = cpu_sample(2)
+            cpu_value, secs = cpu_rate(sample, 2, 1)
+            cpu = {"value": round(cpu_value, 2), "unit": "tokens/s", "cores": sample.threads, "kind": "reference",
+                   "sample": sample.sample_text() + f"; {len(secs)} timed forwards"}
+            if not args.no_decode:
+                secondary = decode_secondary(64, 8)
         clk = clocks.summary()
-        # embedding; per layer: qkv, cq (quantize + GEMV), fc1 (quantize + GEMV writing fc2's fragments),
-        # out, cout, fc2 (GEMV on fragments written by their producer), self attention (1), cross attention
-        # (one cluster launch); readout (one launch)
-        launches_per_step = 1 + cfg.layers * (3 * 2 + 3 + 1 + 1) + 1
         line = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "q8_0/q4_0 x q8_0 -> f32", "data": "synthetic",
-                "config": dict(CONFIG, parallelism=f"replicas x{world}" if world > 1 else "single GPU"),
-                "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": BATCH * 8,
-                        "d2h_bytes_per_step": BATCH * 8},
-                "gpu_launches": launches_per_step * args.steps,
-                "roofline": {"bound": "hbm", "kernel": "Q4_0 vocab readout (one launch: query quantization, tile GEMV, suppression, argmax)",
-                             "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                             "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                             "algorithmic_bytes_per_launch": alg_bytes,
-                             "launch_us": round(launch_s * 1e6, 3), "traffic": committed_traffic()},
-                "cpu_baseline": cpu,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "q8_0 x q8_0 -> f32 (tensor cores on fp16(q*d) operands, fp32 accumulation)",
+                "data": "synthetic", "config": dict(CONFIG, parallelism=f"tp{world}"),
+                "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s",
+                        "h2d_bytes_per_step": mel_host.numel() * 4, "d2h_bytes_per_step": states_host.numel() * 4},
+                "gpu_launches": launches,
+                "roofline": {"bound": "tensor", "kernel": "k_gemm_f16 (tcgen05 GEMM of the encoder linears; "
+                                                          "average over one layer's four shapes)",
+                             "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                             "frac": round(achieved / peaks["bf16_tflops"], 4),
+                             "peak_kind": peak_kind + " (burst bf16: the GEMMs are timed alone)",
+                             "flops_per_launch": flops_per_launch, "launch_us": round(us_per_launch, 2),
+                             "per_shape": per_shape, "traffic": traffic, "traffic_source": traffic_src},
+                "cpu_baseline": cpu, "status": status,
                 "clocks": {k: clk[k] for k in ("sm_mhz", "sm_max_mhz", "reasons", "samples", "source")}}
-    for gd in graphs:
-        gd.graph = None
-    rg = None
+        if secondary is not None:
+            line["secondary_decode"] = secondary
     if world > 1:
         dist.barrier()
+    enc.close()
+    if world > 1:
         dist.destroy_process_group()
     if line is not None:
         print(json.dumps(line), flush=True)
-    for d in decs:
-        d.close()
-    return 0
+    return 0 if status == 0 else 1
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
-    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-decode", action="store_true", help="skip the secondary Whisper-tiny decode line")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")

@@ -209,6 +209,12 @@ class WhisperEncoderB200:
 
     __call__ = forward
 
+    def launches_per_forward(self) -> int:
+        """This library's kernel launches in one forward: two convolution stagings and GEMMs;
+        per layer three stagings (two with the LayerNorm) and four GEMMs; the final LayerNorm.
+        The attention between them is torch's."""
+        return 4 + 7 * len(self.layers) + 1
+
     def close(self) -> None:
         for lin in [self.conv1, self.conv2] + [L[k] for L in self.layers for k in ("qkv", "out", "fc1", "fc2")]:
             lin.close()

@@ -182,9 +182,9 @@ class WhisperEncoderTP:
     # rows) and the barrier after each reduction (the staged rows are complete
     # before the next column-parallel GEMM reads them, and every owner has read
     # the partials before any rank overwrites its partial buffer).
-    def forward(self, mel: torch.Tensor) -> torch.Tensor:
+    def forward(self, mel: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """mel fp32 [batch, mels, 2 * positions] (the same on every rank) ->
-        encoder_states fp32 [batch, positions, width] on every rank."""
+        encoder_states fp32 [batch, positions, width] on every rank (into ``out`` when given)."""
         cfg, r = self.cfg, self.rounding
         B = mel.shape[0]
         if B > self.max_batch or mel.shape[1:] != (cfg.mels, 2 * cfg.positions):
@@ -233,9 +233,20 @@ class WhisperEncoderTP:
         if owned:
             layer_norm(self.x_own[:owned], w, b, eps, out=mine[:owned])
         dist.all_gather_into_tensor(states, mine, group=self.group)
+        if out is not None:
+            out.view(M, d).copy_(states[:M])
+            return out
         return states[:M].view(B, T, d)
 
     __call__ = forward
+
+    def launches_per_forward(self) -> int:
+        """This library's kernel launches in one forward: the replicated stems (two stagings,
+        two GEMMs), the first LayerNorm staging, per layer two column-parallel GEMMs, the
+        attention staging, two row-parallel partial GEMMs, two reductions and four peer
+        barriers, then the final LayerNorm. The attention, the row copy and the closing
+        all-gather are torch / NCCL."""
+        return 4 + 1 + 11 * len(self.layers) + 1
 
     def close(self):
         for lin in [self.conv1, self.conv2] + [L[k] for L in self.layers for k in ("qkv", "out", "fc1", "fc2")]:

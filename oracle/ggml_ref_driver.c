@@ -68,21 +68,35 @@ float ref_vec_dot(int q4, int generic, int k, const void *w, const void *xq) {
 }
 
 /* out[m][n] = W[n] . quantize_q8_0_x86(x[m]); W ggml row-major blocks.
- * xq_scratch holds m * (k/32) * 34 bytes. threads <= 0 uses every OpenMP thread. */
+ * xq_scratch holds m * (k/32) * 34 bytes. threads <= 0 uses every OpenMP thread.
+ *
+ * Work split in the manner of ggml_compute_forward_mul_mat (ggml-cpu.c:1255,
+ * ggml_compute_forward_mul_mat_one_chunk): the (weight row, activation row)
+ * plane is cut into 64 x 64 chunks dealt dynamically to the threads, and each
+ * chunk is walked in 16 x 16 blocks, one vec_dot per (row, column) pair, so a
+ * block's weight rows and quantized activation rows stay in cache. */
 void ref_mul_mat(const void *w, int q4, const float *x, float *out, int64_t m, int64_t n,
                  int64_t k, void *xq_scratch, int threads) {
     const int64_t nb = k / 32, xrow = nb * 34, wrow = nb * (q4 ? 18 : 34);
     uint8_t *xq = (uint8_t *)xq_scratch;
     const int nt = threads > 0 ? threads : omp_get_max_threads();
     const uint8_t *wb = (const uint8_t *)w;
+    const int64_t CH = 64, BL = 16;
+    const int64_t cn = (n + CH - 1) / CH, cm = (m + CH - 1) / CH;
 #pragma omp parallel for schedule(static) num_threads(nt)
     for (int64_t i = 0; i < m; ++i) quantize_row_q8_0(x + i * k, xq + i * xrow, k);
-#pragma omp parallel for schedule(static) num_threads(nt)
-    for (int64_t r = 0; r < n; ++r)
-        for (int64_t i = 0; i < m; ++i) {
-            float s = 0.0f;
-            if (q4) ggml_vec_dot_q4_0_q8_0((int)k, &s, 0, wb + r * wrow, 0, xq + i * xrow, 0, 1);
-            else ggml_vec_dot_q8_0_q8_0((int)k, &s, 0, wb + r * wrow, 0, xq + i * xrow, 0, 1);
-            out[i * n + r] = s;
-        }
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nt)
+    for (int64_t c = 0; c < cn * cm; ++c) {
+        const int64_t r0 = (c % cn) * CH, i0 = (c / cn) * CH;
+        const int64_t r1 = r0 + CH < n ? r0 + CH : n, i1 = i0 + CH < m ? i0 + CH : m;
+        for (int64_t bi = i0; bi < i1; bi += BL)
+            for (int64_t br = r0; br < r1; br += BL)
+                for (int64_t i = bi; i < bi + BL && i < i1; ++i)
+                    for (int64_t r = br; r < br + BL && r < r1; ++r) {
+                        float s = 0.0f;
+                        if (q4) ggml_vec_dot_q4_0_q8_0((int)k, &s, 0, wb + r * wrow, 0, xq + i * xrow, 0, 1);
+                        else ggml_vec_dot_q8_0_q8_0((int)k, &s, 0, wb + r * wrow, 0, xq + i * xrow, 0, 1);
+                        out[i * n + r] = s;
+                    }
+    }
 }

@@ -21,6 +21,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "liboracle.so"
 REF_LIB = HERE / "_ref" / "libggml_quant_ref.so"
+REF_LIB_512 = HERE / "_ref" / "libggml_quant_ref_avx512.so"   # AVX-512 VNNI build of the same sources
 
 Q8_REF, Q8_ARM, Q8_X86 = 0, 1, 2
 MODES = {"ref": Q8_REF, "arm": Q8_ARM, "x86": Q8_X86}
@@ -68,11 +69,21 @@ def lib():
     return _lib
 
 
+def _host_has_avx512_vnni() -> bool:
+    try:
+        flags = Path("/proc/cpuinfo").read_text()
+    except OSError:
+        return False
+    return all(f in flags for f in ("avx512f", "avx512bw", "avx512vl", "avx512dq", "avx512_vnni", "avx_vnni"))
+
+
 def ref_lib():
-    """The reference's ggml quantizers/dots; None when they were not built."""
+    """The reference's ggml quantizers/dots (the AVX-512 VNNI build where the host has
+    it, as ggml built with -march=native would be; else AVX2); None when not built."""
     global _ref
-    if _ref is None and REF_LIB.exists():
-        L = C.CDLL(str(REF_LIB))
+    path = REF_LIB_512 if REF_LIB_512.exists() and _host_has_avx512_vnni() else REF_LIB
+    if _ref is None and path.exists():
+        L = C.CDLL(str(path))
         for name in ("ref_quantize_q8_0_ref", "ref_quantize_q8_0_x86", "ref_quantize_q4_0_ref"):
             getattr(L, name).argtypes = [_f32p, _u8p, C.c_int64]
         L.ref_vec_dot.argtypes = [C.c_int, C.c_int, C.c_int, _u8p, _u8p]

@@ -235,14 +235,22 @@ void orc_mul_mat(const uint8_t *w, int q4, const float *x, float *out,
                  int64_t m, int64_t n, int64_t k, int mode, uint8_t *xq_scratch) {
     const int64_t nb = k / QK;
     const int64_t wrow = nb * (q4 ? Q4_BLOCK_BYTES : Q8_BLOCK_BYTES);
+    const int64_t CH = 64, cn = (n + CH - 1) / CH, cm = (m + CH - 1) / CH;
+#pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < m; ++i)
         orc_quantize_row_q8_0(x + i * k, xq_scratch + i * nb * Q8_BLOCK_BYTES, k, mode);
-#pragma omp parallel for schedule(static)
-    for (int64_t r = 0; r < n; ++r)
-        for (int64_t i = 0; i < m; ++i) {
+    /* 64 x 64 (weight row, activation row) chunks so both operands stay in cache;
+     * every output is one generic-order dot, so the split never changes a bit */
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t c = 0; c < cn * cm; ++c) {
+        const int64_t r0 = (c % cn) * CH, i0 = (c / cn) * CH;
+        const int64_t r1 = r0 + CH < n ? r0 + CH : n, i1 = i0 + CH < m ? i0 + CH : m;
+        for (int64_t i = i0; i < i1; ++i) {
             const uint8_t *xr = xq_scratch + i * nb * Q8_BLOCK_BYTES;
-            out[i * n + r] = q4 ? orc_vec_dot_q4_0(w + r * wrow, xr, nb) : orc_vec_dot_q8_0(w + r * wrow, xr, nb);
+            for (int64_t r = r0; r < r1; ++r)
+                out[i * n + r] = q4 ? orc_vec_dot_q4_0(w + r * wrow, xr, nb) : orc_vec_dot_q8_0(w + r * wrow, xr, nb);
         }
+    }
 }
 
 /* ---------------- readout ------------------------------------------------------

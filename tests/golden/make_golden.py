@@ -22,6 +22,7 @@ Sources of truth, all from the reference itself:
 from __future__ import annotations
 
 import importlib.util
+import os
 import struct
 import sys
 import types
@@ -31,7 +32,8 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REFERENCE = Path("/root/reference")
+# the reference checkout: MSTAR_REFERENCE in the environment, else its usual place here
+REFERENCE = Path(os.environ.get("MSTAR_REFERENCE", "/root/reference"))
 sys.path.insert(0, str(REPO))
 
 from oracle import oracle as O  # noqa: E402
