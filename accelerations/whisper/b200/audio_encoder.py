@@ -22,11 +22,11 @@ import torch
 from mstar.model.whisper.results import EncoderResult
 from mstar.model.whisper.submodules import WhisperEncoderSubmodule
 from mstar_accelerators import Acceleration, Eq, Implementation, PreparedImplementation, Range, When
-from mstar_accelerators.backends.torch import TorchProgram, prepare_torch_programs
 from mstar_accelerators.backends.weights import prepare_weights
 from mstar_accelerators.compiler import bind_default_call, default_resource_requests
 from mstar_accelerators_b200.conditions import SM100aAvailable
 from mstar_accelerators_b200.encoder import TINY, WhisperEncoderB200
+from mstar_accelerators_b200.programs import DeviceProgram, prepare_device_programs
 
 MAX_ROWS = 16
 
@@ -59,15 +59,22 @@ def prepare(binding, resources):
     weights = prepare_weights(binding, "encoder.", dtype=torch.float32)
     encoder = WhisperEncoderB200(weights, TINY, max_batch=MAX_ROWS, device=binding.device)
 
-    def run(call):
+    def run(call):  # enqueued on execution.stream by the device program
         features = torch.stack([f.to(binding.device, torch.float32) for f in call.inputs.audio_features])
         states = encoder(features)
         for owned, row in zip(call.outputs.encoder_states, states):
             owned.copy_(row)
         return {'encoder_states': call.outputs.encoder_states}
 
-    program = prepare_torch_programs(binding, resources, {"prefill": TorchProgram(run, slots=1)},
-                                     call_binding=defaults)
+    # the reference's CPU helper refuses a CUDA binding; its device twin enqueues run()
+    # and the owned-output copies on execution.stream. The encoder's device memory is
+    # released if the binding fails (pi_cpu/audio_encoder.py:45-52).
+    try:
+        program = prepare_device_programs(binding, resources, {"prefill": DeviceProgram(run, slots=1)},
+                                          call_binding=defaults)
+    except BaseException:
+        encoder.close()
+        raise
 
     def close():
         program.close()

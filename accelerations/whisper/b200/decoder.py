@@ -11,12 +11,12 @@ python -m mstar_accelerators.testing --registry accelerations/whisper/b200.
 import torch
 
 from mstar.model.whisper.submodules import WhisperDecoderSubmodule
-from mstar_accelerators import Acceleration, AllRows, Eq, Implementation, Or, Range, When
-from mstar_accelerators.backends.torch import TorchProgram, prepare_torch_programs
+from mstar_accelerators import Acceleration, AllRows, Eq, Implementation, Or, PreparedImplementation, Range, When
 from mstar_accelerators.backends.weights import prepare_weights
 from mstar_accelerators.compiler import bind_default_call
 from mstar_accelerators.implementations.whisper.decoder_call import Call, Inputs, Plans, Resources
 from mstar_accelerators_b200.conditions import SM100aAvailable
+from mstar_accelerators_b200.programs import DeviceProgram, prepare_device_programs
 from mstar_accelerators_b200.whisper import WhisperConfig, WhisperDecoderB200
 
 
@@ -29,30 +29,32 @@ def prepare(binding, resources):
 
     def owner(rows):
         if rows not in owners:
+            # every row brings its own encoder states, so each row has its own cross planes
             owners[rows] = WhisperDecoderB200(weights, WhisperConfig(), batch=rows, suppressed=suppressed,
-                                              device=binding.device)
+                                              shared_cross=False, device=binding.device)
         return owners[rows]
 
     def run(call):
         ids = torch.stack([t.to(binding.device) for t in call.inputs.input_ids])
         dec = owner(ids.shape[0])
         if call.graph_walk == "prefill":
-            enc = torch.stack([e for e in call.inputs.encoder_states if e is not None])
+            enc = torch.stack([e for e in call.inputs.encoder_states if e is not None]).to(binding.device, torch.float32)
             _, tokens = dec.prefill(ids, enc)
-        else:
-            positions = torch.stack([call.plan_results.positions[k] for k in sorted(call.plan_results.positions)])
-            _, tokens = dec.decode(ids.reshape(-1), positions.reshape(-1).to(binding.device))
+        else:  # the position plan's rows follow the call's rows (cpu_ggml_decoder.py:213)
+            positions = call.plan_results.positions["main"].to(binding.device).reshape(ids.shape[0], -1)[:, -1]
+            _, tokens = dec.decode(ids.reshape(-1), positions)
         return {"tokens": tokens}
 
-    program = prepare_torch_programs(binding, resources,
-                                     {walk: TorchProgram(run) for walk in ("prefill", "decode")},
-                                     call_binding=defaults)
+    # the reference's CPU helper refuses a CUDA binding; its device twin enqueues run()
+    # and the owned-output copies on execution.stream
+    program = prepare_device_programs(binding, resources,
+                                      {walk: DeviceProgram(run) for walk in ("prefill", "decode")},
+                                      call_binding=defaults)
 
     def close():
         program.close()
         for dec in owners.values():
             dec.close()
-    from mstar_accelerators import PreparedImplementation
     return PreparedImplementation(program.materialize, program.primitive, program.acquire, close)
 
 

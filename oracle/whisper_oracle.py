@@ -51,16 +51,20 @@ class WhisperDecoderOracle:
         return out
 
     def _att(self, q, K, V, lens):
-        # q [nq, d]; K/V [T, d] fp16-rounded; query i sees keys [0, lens[i])
+        # q [nq, d]; K/V [T, d] fp16-rounded; query i sees keys [0, lens[i]); fp32 scores,
+        # softmax and weighted sum per head (all heads of a query at once)
         cfg = self.cfg
         H, hd = cfg.heads, cfg.d_model // cfg.heads
         out = np.zeros_like(q)
-        for h in range(H):
-            sl = slice(h * hd, (h + 1) * hd)
-            for i in range(q.shape[0]):
-                s = (K[:lens[i], sl] @ q[i, sl]).astype(np.float32) * np.float32(1.0 / np.sqrt(hd))
-                p = np.exp(s - s.max()).astype(np.float32)
-                out[i, sl] = (p @ V[:lens[i], sl]) / p.sum()
+        Kh = K.reshape(K.shape[0], H, hd)
+        Vh = V.reshape(V.shape[0], H, hd)
+        scale = np.float32(1.0 / np.sqrt(hd))
+        for i in range(q.shape[0]):
+            n = int(lens[i])
+            s = np.einsum("thd,hd->ht", Kh[:n], q[i].reshape(H, hd)).astype(np.float32) * scale
+            p = np.exp(s - s.max(-1, keepdims=True)).astype(np.float32)
+            o = np.einsum("ht,thd->hd", p, Vh[:n]).astype(np.float32) / p.sum(-1, keepdims=True)
+            out[i] = o.reshape(-1)
         return out
 
     def set_cross(self, enc):
