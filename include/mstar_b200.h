@@ -296,6 +296,28 @@ MSTAR_B200_API int mstar_b200_tp_reduce(const float *const *part_ptrs, int32_t w
     void *const *staged_ptrs, int64_t row0, int32_t rounding, int32_t *status, void *stream, char *error,
     size_t error_size);
 
+/* --- bounded device waits (no reference counterpart: the reference's native
+ * backends run on the CPU and never wait on a device flag) ---
+ * Every spin or mbarrier wait in this library gives up after a bounded number of
+ * polls and reports it in the call's status word instead of hanging the GPU:
+ * bit value 2 for an mbarrier of a TMA / MMA pipeline, 16 for tp_barrier, 32 for
+ * the persistent decode step's grid barrier.
+ * set_wait_limits: process-wide poll limits for tp_barrier (polls of ~100 ns;
+ * default 2^26, about 7 s) and for the decode step's grid barrier (polls of
+ * ~64 ns; default 2^24, about 1 s; read when a decode-step handle is created);
+ * 0 restores a default. Kernels launched afterwards use them.
+ * wait_selftest: makes one wait run out on purpose, on the calling stream, with
+ * `limit` polls: MSTAR_B200_WAIT_MBARRIER waits on an mbarrier nothing arrives at
+ * (status |= 2); MSTAR_B200_WAIT_GRID_BARRIER runs the grid barrier in a grid of
+ * two CTAs one of which never arrives (status |= 32; words: 2 device uint32 the
+ * call zeroes first). The context stays usable afterwards. */
+#define MSTAR_B200_WAIT_MBARRIER 0
+#define MSTAR_B200_WAIT_GRID_BARRIER 1
+MSTAR_B200_API int mstar_b200_set_wait_limits(int64_t tp_barrier_polls, int64_t grid_barrier_polls, char *error,
+    size_t error_size);
+MSTAR_B200_API int mstar_b200_wait_selftest(int32_t kind, int64_t limit, uint32_t *words, int32_t *status,
+    void *stream, char *error, size_t error_size);
+
 /* --- the whole decoder step as one persistent kernel ------------------------------
  * One greedy decode step of the Whisper decoder graph (decoder.cpp:489-600,
  * 683-696) for `batch` sequences (one new token each) as a single cooperative

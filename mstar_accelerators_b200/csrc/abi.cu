@@ -61,6 +61,27 @@ void launch_readout(const Linear &h, const float *x, int64_t ldx, int64_t m, con
 
 using namespace mb;
 
+namespace mb {
+WaitLimits &wait_limits() {
+    static WaitLimits limits;
+    return limits;
+}
+void launch_grid_barrier_selftest(unsigned int *bar, int *status, long long limit, cudaStream_t s);
+
+// An mbarrier that nothing arrives at: mbar_wait_bounded (the wait every TMA /
+// MMA pipeline here uses) must give up after `limit` polls and report status
+// bit value 2, leaving the context usable.
+__global__ void k_mbarrier_selftest(int *status, uint32_t limit) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && !mbar_wait_bounded(&bar, 0, limit)) atomicOr(status, 2);
+}
+}  // namespace mb
+
 extern "C" {
 
 int mstar_b200_abi(void) { return 1; }
@@ -243,7 +264,7 @@ int mstar_b200_linear_run(void *handle, const float *x, int64_t x_stride, int64_
             g.out_mode = GEMM_OUT_F32;
             g.rounding = rounding;
             g.status = h.status;
-            launch_gemm(xmap, h.wmap, g, s);
+            launch_gemm(xmap, h.wmap, h.wmap_pair, g, s);
             cuda_check(cudaGetLastError(), "GEMM launch");
             return 0;
         }
@@ -533,6 +554,7 @@ int mstar_b200_linear_prepare_gemm(void *handle, const void *blocks, uint64_t by
             launch_dequant_weights(static_cast<const uint8_t *>(blocks), h.w16, h.rows, h.nb, h.q4, nullptr);
             cuda_check(cudaGetLastError(), "weight dequantization");
             make_fp16_map(&h.wmap, h.w16, h.rows, h.width, GEMM_TILE_N);
+            make_fp16_map(&h.wmap_pair, h.w16, h.rows, h.width, GEMM_PAIR_TILE_N);
         }
         if (max_queries > h.gemm_rows) {
             if (h.x16) cudaFree(h.x16);
@@ -616,7 +638,7 @@ int mstar_b200_linear_gemm(void *handle, const void *staged, uint64_t staged_byt
                      : out_format == MSTAR_B200_OUT_F16 ? GEMM_OUT_F16 : GEMM_OUT_Q8;
         g.rounding = rounding;
         g.status = status;
-        launch_gemm(xmap, h.wmap, g, s);
+        launch_gemm(xmap, h.wmap, h.wmap_pair, g, s);
         cuda_check(cudaGetLastError(), "GEMM launch");
         return 0;
     } catch (const std::exception &e) {
@@ -647,6 +669,45 @@ int mstar_b200_linear_close(void *handle, char *error, size_t error_size) {
             cudaDeviceSynchronize();
             delete h;
         }
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+int mstar_b200_set_wait_limits(int64_t tp_barrier_polls, int64_t grid_barrier_polls, char *error,
+                               size_t error_size) {
+    try {
+        require(tp_barrier_polls >= 0 && grid_barrier_polls >= 0, "wait limits must not be negative");
+        wait_limits().tp_barrier = tp_barrier_polls;
+        wait_limits().grid_barrier = grid_barrier_polls;
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+int mstar_b200_wait_selftest(int32_t kind, int64_t limit, uint32_t *words, int32_t *status, void *stream,
+                             char *error, size_t error_size) {
+    try {
+        require(mstar_b200_capability() == 1, "sm_100a device capability is unavailable");
+        require(limit > 0 && limit <= (int64_t(1) << 30), "selftest wait limit out of range");
+        require(status != nullptr, "status word missing");
+        check_device(status, "status word");
+        cudaStream_t s = as_stream(stream);
+        if (kind == MSTAR_B200_WAIT_MBARRIER) {
+            k_mbarrier_selftest<<<1, 32, 0, s>>>(status, uint32_t(limit));
+        } else if (kind == MSTAR_B200_WAIT_GRID_BARRIER) {
+            require(words != nullptr, "barrier words missing");
+            check_device(words, "barrier words");
+            cuda_check(cudaMemsetAsync(words, 0, 2 * sizeof(uint32_t), s), "barrier words");
+            launch_grid_barrier_selftest(words, status, limit, s);
+        } else {
+            require(false, "unknown wait kind");
+        }
+        cuda_check(cudaGetLastError(), "wait selftest launch");
         return 0;
     } catch (const std::exception &e) {
         message(error, error_size, e.what());

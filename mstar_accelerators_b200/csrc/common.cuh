@@ -85,6 +85,15 @@ inline cudaStream_t as_stream(void *s) { return static_cast<cudaStream_t>(s); }
 
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Process-wide limits of the bounded device waits, in polls (0 = the built-in
+// default). Set through mstar_b200_set_wait_limits; kernels launched afterwards
+// use them (a decode-step handle reads them when it is created).
+struct WaitLimits {
+    long long tp_barrier = 0;    // k_tp_barrier: polls of ~100 ns
+    long long grid_barrier = 0;  // persistent decode step: polls of ~64 ns
+};
+WaitLimits &wait_limits();
+
 }  // namespace mb
 
 // ---------------------------------------------------------------- device side

@@ -53,6 +53,112 @@ constexpr size_t gemm_smem_bytes() {
     return size_t(STAGES) * GEMM_STAGE_BYTES + 1024 + 256 + (GELU_TABLE ? GELU_TABLE_BYTES : 0);
 }
 
+// Epilogue of one row's 32-column block (one Q8_0 block of the output): bias, GELU,
+// residual, then the output mode. `r` holds the fp32 accumulators of columns
+// nc .. nc + 31 of output row `orow_i` (residual row `rrow_i`).
+template <bool GELU_TABLE>
+__device__ __forceinline__ void epilogue_block(const GemmArgs &a, const uint32_t (&r)[32], int64_t orow_i,
+                                               int64_t rrow_i, int64_t nc, const uint16_t *gelu_smem) {
+    void *const obase = a.out;
+    const float *rrow = a.residual ? a.residual + rrow_i * a.ldr : nullptr;
+    if (nc + 32 <= a.N) {
+        // whole 32-column block: bias, activation, residual, then the output mode
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (a.flags & 1) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+                const float4 bb = *reinterpret_cast<const float4 *>(a.bias + nc + j);
+                v[j] = __fadd_rn(v[j], bb.x); v[j + 1] = __fadd_rn(v[j + 1], bb.y);
+                v[j + 2] = __fadd_rn(v[j + 2], bb.z); v[j + 3] = __fadd_rn(v[j + 3], bb.w);
+            }
+        }
+        if (GELU_TABLE && (a.flags & 2)) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = gelu_ggml(v[j], gelu_smem);
+        } else if (a.flags & 8) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+        }
+        if (a.flags & 4) {
+            if ((reinterpret_cast<uintptr_t>(rrow + nc) & 15) == 0) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    const float4 rr = *reinterpret_cast<const float4 *>(rrow + nc + j);
+                    v[j] = __fadd_rn(rr.x, v[j]); v[j + 1] = __fadd_rn(rr.y, v[j + 1]);
+                    v[j + 2] = __fadd_rn(rr.z, v[j + 2]); v[j + 3] = __fadd_rn(rr.w, v[j + 3]);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(rrow[nc + j], v[j]);
+            }
+        }
+        if (a.out_mode == GEMM_OUT_F32) {
+            float *o = static_cast<float *>(obase) + orow_i * a.ldo + nc;
+            if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4 *>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) o[j] = v[j];
+            }
+    } else {
+            if (a.out_mode == GEMM_OUT_Q8) {
+                float amax = 0.0f;
+                bool finite = true;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    amax = fmaxf(amax, fabsf(v[j]));
+                    finite = finite && isfinite(v[j]);
+                }
+                if (!finite && a.status) atomicOr(a.status, 1);
+                const float d = __fdiv_rn(amax, 127.0f);
+                const float id = a.rounding == 2 ? (amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f)
+                                                 : (d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f);
+                const float dh = __half2float(__float2half_rn(d));
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float sv = __fmul_rn(v[j], id);
+                    const int qv = a.rounding == 0 ? int(roundf(sv)) : __float2int_rn(sv);
+                    v[j] = __fmul_rn(float(qv), dh);
+                }
+            }
+            __half *o = static_cast<__half *>(obase) + orow_i * a.ldo + nc;
+            if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) {
+                    uint4 pk;
+                    pk.x = half2_bits(__floats2half2_rn(v[j], v[j + 1]));
+                    pk.y = half2_bits(__floats2half2_rn(v[j + 2], v[j + 3]));
+                    pk.z = half2_bits(__floats2half2_rn(v[j + 4], v[j + 5]));
+                    pk.w = half2_bits(__floats2half2_rn(v[j + 6], v[j + 7]));
+                    *reinterpret_cast<uint4 *>(o + j) = pk;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) o[j] = __float2half_rn(v[j]);
+            }
+        }
+    } else {
+        // ragged last block (fp32 / fp16 output only; Q8_0 staging needs N % 32 == 0)
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int64_t n = nc + j;
+            if (n < a.N) {
+                float v = __uint_as_float(r[j]);
+                if (a.flags & 1) v = __fadd_rn(v, a.bias[n]);
+                if (GELU_TABLE && (a.flags & 2)) v = gelu_ggml(v, gelu_smem);
+                else if (a.flags & 8) v = gelu_erf(v);
+                if (a.flags & 4) v = __fadd_rn(rrow[n], v);
+                if (a.out_mode == GEMM_OUT_F32) static_cast<float *>(obase)[orow_i * a.ldo + n] = v;
+                else static_cast<__half *>(obase)[orow_i * a.ldo + n] = __float2half_rn(v);
+            }
+        }
+    }
+}
+
 template <int GEMM_STAGES, bool GELU_TABLE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_f16(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const GemmArgs a) {
@@ -171,110 +277,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const int64_t row = m0 + 32 * q + lane;
             const int64_t orow_i = a.seg_rows ? (row / a.seg_rows) * a.out_seg_rows + row % a.seg_rows : row;
             const int64_t rrow_i = a.res_period ? row % a.res_period : row;
-            void *const obase = a.out;
             for (int c = c0; c < c0 + GEMM_BN / 32 / (GEMM_EPI_WARPS / 4); ++c) {
                 uint32_t r[32];
                 tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(buf * GEMM_BN + c * 32), r);
-                if (row < a.M) {
-                    const float *rrow = a.residual ? a.residual + rrow_i * a.ldr : nullptr;
-                    const int64_t nc = n0 + c * 32;
-                    if (nc + 32 <= a.N) {
-                        // whole 32-column block: bias, activation, residual, then the output mode
-                        float v[32];
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-                        if (a.flags & 1) {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 4) {
-                                const float4 bb = *reinterpret_cast<const float4 *>(a.bias + nc + j);
-                                v[j] = __fadd_rn(v[j], bb.x); v[j + 1] = __fadd_rn(v[j + 1], bb.y);
-                                v[j + 2] = __fadd_rn(v[j + 2], bb.z); v[j + 3] = __fadd_rn(v[j + 3], bb.w);
-                            }
-                        }
-                        if (GELU_TABLE && (a.flags & 2)) {
-#pragma unroll
-                            for (int j = 0; j < 32; ++j) v[j] = gelu_ggml(v[j], gelu_smem);
-                        } else if (a.flags & 8) {
-#pragma unroll
-                            for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-                        }
-                        if (a.flags & 4) {
-                            if ((reinterpret_cast<uintptr_t>(rrow + nc) & 15) == 0) {
-#pragma unroll
-                                for (int j = 0; j < 32; j += 4) {
-                                    const float4 rr = *reinterpret_cast<const float4 *>(rrow + nc + j);
-                                    v[j] = __fadd_rn(rr.x, v[j]); v[j + 1] = __fadd_rn(rr.y, v[j + 1]);
-                                    v[j + 2] = __fadd_rn(rr.z, v[j + 2]); v[j + 3] = __fadd_rn(rr.w, v[j + 3]);
-                                }
-                            } else {
-#pragma unroll
-                                for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(rrow[nc + j], v[j]);
-                            }
-                        }
-                        if (a.out_mode == GEMM_OUT_F32) {
-                            float *o = static_cast<float *>(obase) + orow_i * a.ldo + nc;
-                            if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-#pragma unroll
-                                for (int j = 0; j < 32; j += 4)
-                                    *reinterpret_cast<float4 *>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                            } else {
-#pragma unroll
-                                for (int j = 0; j < 32; ++j) o[j] = v[j];
-                            }
-                        } else {
-                            if (a.out_mode == GEMM_OUT_Q8) {
-                                float amax = 0.0f;
-                                bool finite = true;
-#pragma unroll
-                                for (int j = 0; j < 32; ++j) {
-                                    amax = fmaxf(amax, fabsf(v[j]));
-                                    finite = finite && isfinite(v[j]);
-                                }
-                                if (!finite && a.status) atomicOr(a.status, 1);
-                                const float d = __fdiv_rn(amax, 127.0f);
-                                const float id = a.rounding == 2 ? (amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f)
-                                                                 : (d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f);
-                                const float dh = __half2float(__float2half_rn(d));
-#pragma unroll
-                                for (int j = 0; j < 32; ++j) {
-                                    const float sv = __fmul_rn(v[j], id);
-                                    const int qv = a.rounding == 0 ? int(roundf(sv)) : __float2int_rn(sv);
-                                    v[j] = __fmul_rn(float(qv), dh);
-                                }
-                            }
-                            __half *o = static_cast<__half *>(obase) + orow_i * a.ldo + nc;
-                            if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-#pragma unroll
-                                for (int j = 0; j < 32; j += 8) {
-                                    uint4 pk;
-                                    pk.x = half2_bits(__floats2half2_rn(v[j], v[j + 1]));
-                                    pk.y = half2_bits(__floats2half2_rn(v[j + 2], v[j + 3]));
-                                    pk.z = half2_bits(__floats2half2_rn(v[j + 4], v[j + 5]));
-                                    pk.w = half2_bits(__floats2half2_rn(v[j + 6], v[j + 7]));
-                                    *reinterpret_cast<uint4 *>(o + j) = pk;
-                                }
-                            } else {
-#pragma unroll
-                                for (int j = 0; j < 32; ++j) o[j] = __float2half_rn(v[j]);
-                            }
-                        }
-                    } else {
-                        // ragged last block (fp32 / fp16 output only; Q8_0 staging needs N % 32 == 0)
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int64_t n = nc + j;
-                            if (n < a.N) {
-                                float v = __uint_as_float(r[j]);
-                                if (a.flags & 1) v = __fadd_rn(v, a.bias[n]);
-                                if (GELU_TABLE && (a.flags & 2)) v = gelu_ggml(v, gelu_smem);
-                                else if (a.flags & 8) v = gelu_erf(v);
-                                if (a.flags & 4) v = __fadd_rn(rrow[n], v);
-                                if (a.out_mode == GEMM_OUT_F32) static_cast<float *>(obase)[orow_i * a.ldo + n] = v;
-                                else static_cast<__half *>(obase)[orow_i * a.ldo + n] = __float2half_rn(v);
-                            }
-                        }
-                    }
-                }
+                if (row < a.M) epilogue_block<GELU_TABLE>(a, r, orow_i, rrow_i, n0 + c * 32, gelu_smem);
             }
             tc_fence_before();
             __syncwarp();
@@ -287,6 +293,174 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(GEMM_TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// CTA-pair GEMM (cta_group::2) ----------------------------------------------------
+// Two CTAs of a cluster compute one 256 x 256 output tile: each loads its own
+// 128 rows of A and 128 of the tile's 256 rows of B (32 KB per stage instead of
+// 48 KB per CTA for the same MMA work), the leader issues tcgen05.mma
+// cta_group::2 (M = 256, N = 256, K = 16) reading both CTAs' shared memory, and
+// each CTA's TMEM receives its own 128 rows, which its own epilogue warps drain
+// (the same per-row epilogue as the single-CTA kernel). Barriers:
+//   full[s]    leader only: the leader producer's expect_tx arrival plus both
+//              CTAs' TMA bytes (each load names the leader's barrier);
+//   empty[s]   both CTAs: the leader's MMA commit arrives on both (multicast
+//              commit; no load uses multicast);
+//   acc_full   both CTAs: the same multicast commit after a tile's last MMA;
+//   acc_empty  leader only: one arrival per epilogue warp of both CTAs.
+// Every wait is bounded; a timeout sets status bit value 2. Both CTAs meet at a
+// cluster barrier before any remote arrival and again before they exit.
+constexpr int PAIR_A_BYTES = GEMM_BM * GEMM_BK * 2;          // this CTA's 128 rows of A
+constexpr int PAIR_B_BYTES = (GEMM_BN / 2) * GEMM_BK * 2;    // this CTA's 128 of the tile's 256 rows of B
+constexpr int PAIR_STAGE_BYTES = PAIR_A_BYTES + PAIR_B_BYTES;
+constexpr int PAIR_BM = 2 * GEMM_BM;                          // output rows per CTA pair
+constexpr int PAIR_GROUP_M = 4;                               // pair row tiles per group (1024 rows)
+// instruction descriptor: D f32, A/B f16, K-major, N = 256, M = 256 (the pair)
+constexpr uint32_t PAIR_IDESC = (1u << 4) | (uint32_t(GEMM_BN >> 3) << 17) | (uint32_t(PAIR_BM >> 4) << 24);
+template <int STAGES, bool GELU_TABLE>
+constexpr size_t pair_smem_bytes() {
+    return size_t(STAGES) * PAIR_STAGE_BYTES + 1024 + 256 + (GELU_TABLE ? GELU_TABLE_BYTES : 0);
+}
+
+template <int STAGES, bool GELU_TABLE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm_pair(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const GemmArgs a) {
+    extern __shared__ __align__(1024) unsigned char gemm_smem[];
+    unsigned char *base = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(gemm_smem) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(base + STAGES * PAIR_STAGE_BYTES);
+    uint64_t *empty = full + STAGES;
+    uint64_t *acc_full = empty + STAGES;   // [2]
+    uint64_t *acc_empty = acc_full + 2;    // [2] (the leader's counts both CTAs' epilogue warps)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    uint16_t *gelu_smem = reinterpret_cast<uint16_t *>(base + STAGES * PAIR_STAGE_BYTES + 256);
+    __shared__ int failed;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    if (GELU_TABLE)
+        for (int i = threadIdx.x; i < int(GELU_TABLE_BYTES / 16); i += blockDim.x)
+            reinterpret_cast<uint4 *>(gelu_smem)[i] = __ldg(reinterpret_cast<const uint4 *>(a.gelu) + i);
+    const int kt = int((a.K + GEMM_BK - 1) / GEMM_BK);
+    const int64_t tiles_n = (a.N + GEMM_BN - 1) / GEMM_BN, tiles_m = (a.M + PAIR_BM - 1) / PAIR_BM;
+    const int64_t tiles = tiles_n * tiles_m;
+    const int64_t cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
+    auto tile_coords = [&](int64_t tile, int64_t &m0, int64_t &n0) {  // grouped order, as the single-CTA kernel
+        const int64_t per_group = int64_t(PAIR_GROUP_M) * tiles_n;
+        const int64_t first_m = (tile / per_group) * PAIR_GROUP_M;
+        const int64_t gsz = tiles_m - first_m < PAIR_GROUP_M ? tiles_m - first_m : PAIR_GROUP_M;
+        const int64_t r = tile % per_group;
+        m0 = (first_m + r % gsz) * PAIR_BM;
+        n0 = (r / gsz) * GEMM_BN;
+    };
+
+    if (threadIdx.x == 0) {
+        failed = 0;
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(acc_full + b, 1);
+            mbar_init(acc_empty + b, 2 * GEMM_EPI_WARPS);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(GEMM_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    cluster_sync();   // both CTAs' barriers exist before any load or arrival names them
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int64_t it = 0;
+            for (int64_t tile = cluster; tile < tiles && !failed; tile += clusters) {
+                int64_t m0, n0;
+                tile_coords(tile, m0, n0);
+                const int row = int(m0) + int(rank) * GEMM_BM, col = int(n0) + int(rank) * (GEMM_BN / 2);
+                for (int i = 0; i < kt; ++i, ++it) {
+                    const int s = int(it % STAGES);
+                    if (!mbar_wait_bounded(empty + s, uint32_t(((it / STAGES) & 1) ^ 1))) {
+                        atomicOr(&failed, 1);
+                        break;
+                    }
+                    unsigned char *sa = base + s * PAIR_STAGE_BYTES;
+                    if (leader) mbar_expect_tx(full + s, 2 * PAIR_STAGE_BYTES);
+                    const uint32_t bar = cluster_smem(full + s, 0);
+                    tma_load_2d_pair(sa, &ta, i * GEMM_BK, row, bar);
+                    tma_load_2d_pair(sa + PAIR_A_BYTES, &tb, i * GEMM_BK, col, bar);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (leader && lane == 0) {
+            int64_t it = 0, local = 0;
+            for (int64_t tile = cluster; tile < tiles && !failed; tile += clusters, ++local) {
+                const int buf = int(local & 1);
+                if (!mbar_wait_bounded(acc_empty + buf, uint32_t(((local >> 1) & 1) ^ 1))) {
+                    atomicOr(&failed, 1);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t acc = tmem + uint32_t(buf * GEMM_BN);
+                for (int i = 0; i < kt; ++i, ++it) {
+                    const int s = int(it % STAGES);
+                    if (!mbar_wait_bounded(full + s, uint32_t((it / STAGES) & 1))) {
+                        atomicOr(&failed, 1);
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_addr(base + s * PAIR_STAGE_BYTES);
+                    const uint64_t da = sw128_desc(sa), db = sw128_desc(sa + PAIR_A_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < GEMM_BK / 16; ++kk)
+                        umma_f16_pair(acc, da + uint64_t(2 * kk), db + uint64_t(2 * kk), PAIR_IDESC, (i | kk) != 0);
+                    umma_commit_pair(empty + s);
+                }
+                umma_commit_pair(acc_full + buf);
+            }
+        }
+    } else {
+        const int q = warp & 3;
+        const int c0 = ((warp - 2) / 4) * (GEMM_BN / 32 / (GEMM_EPI_WARPS / 4));
+        const uint32_t leader_acc_empty[2] = {cluster_smem(acc_empty, 0), cluster_smem(acc_empty + 1, 0)};
+        int64_t local = 0;
+        for (int64_t tile = cluster; tile < tiles; tile += clusters, ++local) {
+            const int buf = int(local & 1);
+            if (!mbar_wait_bounded(acc_full + buf, uint32_t((local >> 1) & 1))) {
+                atomicOr(&failed, 1);
+                break;
+            }
+            tc_fence_after();
+            int64_t m0, n0;
+            tile_coords(tile, m0, n0);
+            const int64_t row = m0 + int64_t(rank) * GEMM_BM + 32 * q + lane;
+            const int64_t orow_i = a.seg_rows ? (row / a.seg_rows) * a.out_seg_rows + row % a.seg_rows : row;
+            const int64_t rrow_i = a.res_period ? row % a.res_period : row;
+            for (int c = c0; c < c0 + GEMM_BN / 32 / (GEMM_EPI_WARPS / 4); ++c) {
+                uint32_t r[32];
+                tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(buf * GEMM_BN + c * 32), r);
+                if (row < a.M) epilogue_block<GELU_TABLE>(a, r, orow_i, rrow_i, n0 + c * 32, gelu_smem);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(leader_acc_empty[buf]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();   // no CTA leaves while its partner may still signal its barriers
+    if (threadIdx.x == 0 && failed && a.status) atomicOr(a.status, 2);
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(GEMM_TMEM_COLS)
                      : "memory");
     }
 }
@@ -370,8 +544,13 @@ void launch_dequant_act(int mode, const float *x, int64_t ldx, int64_t m, int64_
     else k_dequant_act<1><<<grid, 256, 0, s>>>(x, ldx, m, k, out, status);
 }
 
-void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &a, cudaStream_t s) {
+// Pair kernel shapes: 6 stages (192 KB) without GELU, 4 stages + the 75 KB GELU table with it.
+constexpr int PAIR_STAGES = 6, PAIR_STAGES_GELU = 4;
+
+void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tb_pair, const GemmArgs &a,
+                 cudaStream_t s) {
     static bool configured = false;
+    static int pair_clusters = 0, pair_clusters_gelu = 0;
     if (!configured) {
         cuda_check(cudaFuncSetAttribute(k_gemm_f16<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         int(gemm_smem_bytes<4, false>())),
@@ -379,6 +558,29 @@ void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &a
         cuda_check(cudaFuncSetAttribute(k_gemm_f16<3, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         int(gemm_smem_bytes<3, true>())),
                    "GEMM shared-memory attribute");
+        cuda_check(cudaFuncSetAttribute(k_gemm_pair<PAIR_STAGES, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(pair_smem_bytes<PAIR_STAGES, false>())),
+                   "pair GEMM shared-memory attribute");
+        cuda_check(cudaFuncSetAttribute(k_gemm_pair<PAIR_STAGES_GELU, true>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(pair_smem_bytes<PAIR_STAGES_GELU, true>())),
+                   "pair GEMM shared-memory attribute");
+        // persistent grid: as many CTA pairs as can be resident at once
+        auto clusters = [](const void *fn, size_t smem) {
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(2, 1, 1);
+            cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
+            cfg.dynamicSmemBytes = smem;
+            cfg.numAttrs = 0;   // the kernel's own cluster dimensions (2, 1, 1) apply
+            int n = 0;
+            cuda_check(cudaOccupancyMaxActiveClusters(&n, fn, &cfg), "pair GEMM occupancy");
+            return n;
+        };
+        pair_clusters = clusters(reinterpret_cast<const void *>(k_gemm_pair<PAIR_STAGES, false>),
+                                 pair_smem_bytes<PAIR_STAGES, false>());
+        pair_clusters_gelu = clusters(reinterpret_cast<const void *>(k_gemm_pair<PAIR_STAGES_GELU, true>),
+                                      pair_smem_bytes<PAIR_STAGES_GELU, true>());
+        require(pair_clusters > 0 && pair_clusters_gelu > 0, "pair GEMM cannot be resident");
         configured = true;
     }
     static int sms = 0;
@@ -387,6 +589,19 @@ void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &a
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (sms <= 0) sms = 148;
+    }
+    if (a.M > GEMM_BM) {
+        const int64_t tiles = ceil_div(a.N, GEMM_BN) * ceil_div(a.M, PAIR_BM);
+        const bool gelu = (a.flags & 2) != 0;
+        const int64_t resident = gelu ? pair_clusters_gelu : pair_clusters;
+        const unsigned grid = unsigned(2 * (tiles < resident ? tiles : resident));
+        if (gelu)
+            k_gemm_pair<PAIR_STAGES_GELU, true><<<grid, GEMM_THREADS, pair_smem_bytes<PAIR_STAGES_GELU, true>(), s>>>(
+                ta, tb_pair, a);
+        else
+            k_gemm_pair<PAIR_STAGES, false><<<grid, GEMM_THREADS, pair_smem_bytes<PAIR_STAGES, false>(), s>>>(
+                ta, tb_pair, a);
+        return;
     }
     const int64_t tiles = ceil_div(a.N, GEMM_BN) * ceil_div(a.M, GEMM_BM);
     const unsigned grid = unsigned(tiles < sms ? tiles : sms);  // persistent: one CTA per SM

@@ -41,8 +41,11 @@ void launch_stage_conv(int mode, const float *src, int time_major, int64_t batch
                        cudaStream_t s);
 void launch_layer_norm(const float *x, int64_t ldx, int64_t rows, int64_t k, const float *w, const float *b, float eps,
                        float *out, int64_t ldo, cudaStream_t s);
-void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &a, cudaStream_t s);
+// tb: weights with 256-row boxes (single-CTA kernel, M <= 128); tb_pair: the same
+// weights with 128-row boxes (the CTA-pair kernel used above 128 rows)
+void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tb_pair, const GemmArgs &a,
+                 cudaStream_t s);
 
-constexpr int GEMM_TILE_M = 128, GEMM_TILE_N = 256;
+constexpr int GEMM_TILE_M = 128, GEMM_TILE_N = 256, GEMM_PAIR_TILE_N = 128;
 
 }  // namespace mb

@@ -31,7 +31,8 @@ struct Linear {
     __half *w16 = nullptr;        // fp16(q * d) weights [rows][width]
     __half *x16 = nullptr;        // fp16 dequantized activations [gemm_rows][width]
     int64_t gemm_rows = 0;
-    CUtensorMap wmap{};
+    CUtensorMap wmap{};       // 256-row boxes (single-CTA GEMM)
+    CUtensorMap wmap_pair{};  // 128-row boxes (CTA-pair GEMM)
     // vocab readout tile layout (readout.cu), built by prepare_readout
     uint8_t *wt = nullptr;
     int64_t tiles = 0;

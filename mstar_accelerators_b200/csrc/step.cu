@@ -65,6 +65,7 @@ struct StepArgs {
     unsigned long long *keys;  // [32] argmax keys, zero between steps
     unsigned int *bar;         // [2] arrivals, generation
     int *status;
+    long long spin_limit;      // polls of a grid barrier before it gives up
     const uint16_t *gelu;
 };
 
@@ -74,7 +75,7 @@ struct StepArgs {
 // generation, the others watch it. Every wait is bounded; a timeout sets status
 // bit value 32. (One arrival slot per CTA watched by CTA 0 measured slower:
 // about 4.5 us against 3 us per barrier.)
-__device__ __forceinline__ void grid_barrier(unsigned int *bar, unsigned int &gen, int *status) {
+__device__ __forceinline__ void grid_barrier(unsigned int *bar, unsigned int &gen, int *status, long long limit) {
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
@@ -89,7 +90,7 @@ __device__ __forceinline__ void grid_barrier(unsigned int *bar, unsigned int &ge
             for (;;) {
                 asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar + 1) : "memory");
                 if (v != g) break;
-                if (++n > STEP_SPIN_LIMIT) {
+                if (++n > limit) {
                     atomicOr(status, 32);
                     break;
                 }
@@ -100,6 +101,19 @@ __device__ __forceinline__ void grid_barrier(unsigned int *bar, unsigned int &ge
         gen = g + 1;
     }
     __syncthreads();
+}
+
+// Self-test of the barrier's timeout: a grid of two CTAs where CTA 1 leaves
+// without arriving, so CTA 0's wait runs out after `limit` polls and sets
+// status bit value 32 (bar: two zeroed words).
+__global__ void k_grid_barrier_selftest(unsigned int *bar, int *status, long long limit) {
+    if (blockIdx.x != 0) return;
+    unsigned int gen = 0;
+    grid_barrier(bar, gen, status, limit);
+}
+
+void launch_grid_barrier_selftest(unsigned int *bar, int *status, long long limit, cudaStream_t s) {
+    k_grid_barrier_selftest<<<2, 32, 0, s>>>(bar, status, limit);
 }
 
 // ------------------------------------------------------------------ activations -> A fragments
@@ -428,16 +442,16 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_decode_step(const StepArgs 
         }
         a.x[e] = __fadd_rn(a.tok[id * d + i], a.pos[p * d + i]);
     }
-    grid_barrier(a.bar, gen, a.status);
+    grid_barrier(a.bar, gen, a.status, a.spin_limit);
 
     for (int li = 0; li < a.L; ++li) {
         const StepLayer &Ly = a.layer[li];
         // self attention block
         phase_quant<MODE>(a, a.x, d, Ly.ln[0], Ly.ln[1], Ly.lin[L_QKV].nb_pad);
         prefetch_gemv(Ly.lin[L_QKV], pre);
-        grid_barrier(a.bar, gen, a.status);
+        grid_barrier(a.bar, gen, a.status, a.spin_limit);
         phase_gemv<MT>(a, Ly.lin[L_QKV], Epi{a.qkv, 3 * d, nullptr, false}, s, pre);
-        grid_barrier(a.bar, gen, a.status);
+        grid_barrier(a.bar, gen, a.status, a.spin_limit);
         {
             AttArgs at{};
             at.q = a.qkv;
@@ -473,15 +487,15 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_decode_step(const StepArgs 
             }
         }
         prefetch_gemv(Ly.lin[L_OUT], pre);
-        grid_barrier(a.bar, gen, a.status);
+        grid_barrier(a.bar, gen, a.status, a.spin_limit);
         phase_gemv<MT>(a, Ly.lin[L_OUT], Epi{a.x, d, a.x, false}, s, pre);
-        grid_barrier(a.bar, gen, a.status);
+        grid_barrier(a.bar, gen, a.status, a.spin_limit);
         // cross attention block
         phase_quant<MODE>(a, a.x, d, Ly.ln[2], Ly.ln[3], Ly.lin[L_CQ].nb_pad);
         prefetch_gemv(Ly.lin[L_CQ], pre);
-        grid_barrier(a.bar, gen, a.status);
+        grid_barrier(a.bar, gen, a.status, a.spin_limit);
         phase_gemv<MT>(a, Ly.lin[L_CQ], Epi{a.cq, d, nullptr, false}, s, pre);
-        grid_barrier(a.bar, gen, a.status);
+        grid_barrier(a.bar, gen, a.status, a.spin_limit);
         {
             AttArgs at{};
             at.q = a.cq;
@@ -518,7 +532,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_decode_step(const StepArgs 
                 }
             }
             if (a.shared) {
-                grid_barrier(a.bar, gen, a.status);
+                grid_barrier(a.bar, gen, a.status, a.spin_limit);
                 // merge of the key splits and the Q8_0 quantization of the two blocks, one warp per (head, row)
                 const int64_t W = int64_t(gridDim.x) * STEP_WARPS;
                 for (int64_t task = int64_t(blockIdx.x) * STEP_WARPS + warp; task < int64_t(a.B) * a.heads; task += W) {
@@ -548,28 +562,28 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_decode_step(const StepArgs 
             }
         }
         prefetch_gemv(Ly.lin[L_COUT], pre);
-        grid_barrier(a.bar, gen, a.status);
+        grid_barrier(a.bar, gen, a.status, a.spin_limit);
         phase_gemv<MT>(a, Ly.lin[L_COUT], Epi{a.x, d, a.x, false}, s, pre);
-        grid_barrier(a.bar, gen, a.status);
+        grid_barrier(a.bar, gen, a.status, a.spin_limit);
         // feed-forward block
         phase_quant<MODE>(a, a.x, d, Ly.ln[4], Ly.ln[5], Ly.lin[L_FC1].nb_pad);
         prefetch_gemv(Ly.lin[L_FC1], pre);
-        grid_barrier(a.bar, gen, a.status);
+        grid_barrier(a.bar, gen, a.status, a.spin_limit);
         phase_gemv<MT>(a, Ly.lin[L_FC1], Epi{a.h, a.ffn, nullptr, true}, s, pre);
-        grid_barrier(a.bar, gen, a.status);
+        grid_barrier(a.bar, gen, a.status, a.spin_limit);
         phase_quant<MODE>(a, a.h, a.ffn, nullptr, nullptr, Ly.lin[L_FC2].nb_pad);
         prefetch_gemv(Ly.lin[L_FC2], pre);
-        grid_barrier(a.bar, gen, a.status);
+        grid_barrier(a.bar, gen, a.status, a.spin_limit);
         phase_gemv<MT>(a, Ly.lin[L_FC2], Epi{a.x, d, a.x, false}, s, pre);
-        grid_barrier(a.bar, gen, a.status);
+        grid_barrier(a.bar, gen, a.status, a.spin_limit);
     }
     // final LayerNorm + readout + argmax
     phase_quant<MODE>(a, a.x, d, a.lnf_w, a.lnf_b, a.head.nb_pad);
     RoPre first;
     load_group<HEAD_Q4>(a.head, int64_t(blockIdx.x) * STEP_WARPS + warp, first);
-    grid_barrier(a.bar, gen, a.status);
+    grid_barrier(a.bar, gen, a.status, a.spin_limit);
     phase_readout<MT, HEAD_Q4>(a, s, first);
-    grid_barrier(a.bar, gen, a.status);
+    grid_barrier(a.bar, gen, a.status, a.spin_limit);
     if (blockIdx.x == 0 && tid < a.B) {
         const unsigned long long k = atomicExch(a.keys + tid, 0ull);
         a.next[tid] = int64_t(0xFFFFFFFFu - uint32_t(k & 0xFFFFFFFFull));
@@ -681,6 +695,7 @@ void *mstar_b200_decode_step_create(const mstar_b200_decode_step_config *c, char
         a.shared = c->shared_cross ? 1 : 0;
         a.mtiles = c->batch <= 16 ? 1 : 2;
         a.rounding = c->rounding;
+        a.spin_limit = wait_limits().grid_barrier > 0 ? wait_limits().grid_barrier : STEP_SPIN_LIMIT;
         a.eps = c->eps;
         a.scale = 1.0f / sqrtf(float(HEAD_DIM));
         a.tok = c->token_table;

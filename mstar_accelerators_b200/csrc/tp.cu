@@ -29,7 +29,8 @@ constexpr int TP_MAX_CHUNKS = 12;  // float4 chunks per lane: rows up to 1536 wi
 constexpr int TP_MAX_WORLD = 8;
 constexpr long long TP_SPIN_LIMIT = 1ll << 26;  // polls (with 100 ns sleeps) before a barrier gives up
 
-__global__ void k_tp_barrier(int *const *flags, int *mine, int rank, int world, int *counter, int *status) {
+__global__ void k_tp_barrier(int *const *flags, int *mine, int rank, int world, int *counter, int *status,
+                             long long limit) {
     const int p = threadIdx.x;
     __shared__ int gen;
     if (p == 0) {  // this rank's barrier count (device-resident, so captured graphs replay correctly)
@@ -50,7 +51,7 @@ __global__ void k_tp_barrier(int *const *flags, int *mine, int rank, int world, 
         for (;;) {
             asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine + p) : "memory");
             if (v - generation >= 0) break;
-            if (++n > TP_SPIN_LIMIT) {
+            if (++n > limit) {
                 atomicOr(status, 16);
                 break;
             }
@@ -160,7 +161,8 @@ int mstar_b200_tp_barrier(int32_t *const *flag_ptrs, int32_t *my_flags, int32_t 
     try {
         require(world >= 1 && world <= TP_MAX_WORLD && rank >= 0 && rank < world, "invalid rank / world");
         require(flag_ptrs && my_flags && counter && status, "missing barrier operand");
-        k_tp_barrier<<<1, 32, 0, as_stream(stream)>>>(flag_ptrs, my_flags, rank, world, counter, status);
+        const long long limit = wait_limits().tp_barrier > 0 ? wait_limits().tp_barrier : TP_SPIN_LIMIT;
+        k_tp_barrier<<<1, 32, 0, as_stream(stream)>>>(flag_ptrs, my_flags, rank, world, counter, status, limit);
         cuda_check(cudaGetLastError(), "barrier launch");
         return 0;
     } catch (const std::exception &e) {
