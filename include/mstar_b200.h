@@ -295,6 +295,15 @@ MSTAR_B200_API int mstar_b200_tp_reduce(const float *const *part_ptrs, int32_t w
     int64_t width, const float *bias, float *x, const float *ln_weight, const float *ln_bias, float ln_eps,
     void *const *staged_ptrs, int64_t row0, int32_t rounding, int32_t *status, void *stream, char *error,
     size_t error_size);
+/* tp_reduce_multicast: tp_reduce where the partial buffers and the staged operands
+ * are also bound to an NVLink multicast object (NVSwitch NVLS): mc_part and
+ * mc_staged are the multicast addresses (16-byte aligned). Each 16 bytes of an
+ * owned row's partial sum over all ranks is one multimem.ld_reduce (the switch
+ * adds the ranks' partials, in its own fp32 order), and each staged row chunk is
+ * one multimem.st that lands in every rank's staged operand. */
+MSTAR_B200_API int mstar_b200_tp_reduce_multicast(const float *mc_part, int32_t world, int64_t owned, int64_t width,
+    const float *bias, float *x, const float *ln_weight, const float *ln_bias, float ln_eps, void *mc_staged,
+    int64_t row0, int32_t rounding, int32_t *status, void *stream, char *error, size_t error_size);
 
 /* --- bounded device waits (no reference counterpart: the reference's native
  * backends run on the CPU and never wait on a device flag) ---

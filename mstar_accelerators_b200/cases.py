@@ -3,6 +3,7 @@
     python -m mstar_accelerators_b200.cases readout-q4-b32
     python -m mstar_accelerators_b200.cases decode-step-b32
     python -m mstar_accelerators_b200.cases encoder-large-b16
+    python -m mstar_accelerators_b200.cases gemm-encoder-large-layer
     python -m mstar_accelerators_b200.cases moe-prefill-4096
 
 Each case builds its inputs from fixed seeds, runs a few calls, synchronises
@@ -57,6 +58,32 @@ def gemm_q8_8192x5120x1280():
         lin(x, out=out)
 
 
+def gemm_encoder_large_layer():
+    """The four GEMMs of one Whisper-large-v3-shaped encoder layer at the bench's 24,000 rows, each
+    in its encoder mode (QKV fp16 into padded planes; out_proj fp32 + residual; fc1 GELU + Q8_0-staged
+    fp16; fc2 fp32 + residual), two rounds: 8 launches, the second four the ones to profile."""
+    from .encoder import LARGE_V3
+    from .linear import BlockLinear, stage_rows
+    g = torch.Generator(device="cuda").manual_seed(1)
+    d, f, M, T, P = LARGE_V3.width, LARGE_V3.ffn, 24000, 1500, LARGE_V3.padded_keys
+
+    def lin(n, k):
+        L = BlockLinear(torch.randn(n, k, device="cuda", generator=g) * 0.02,
+                        bias=torch.randn(n, device="cuda", generator=g) * 0.02)
+        L.prepare_gemm(M)
+        return L
+    qkv, out, fc1, fc2 = lin(3 * d, d), lin(d, d), lin(f, d), lin(d, f)
+    a = stage_rows(torch.randn(M, d, device="cuda", generator=g))
+    planes = torch.zeros((M // T, P, 3 * d), dtype=torch.float16, device="cuda")
+    x = torch.randn(M, d, device="cuda", generator=g)
+    h = torch.empty((M, f), dtype=torch.float16, device="cuda")
+    for _ in range(2):
+        qkv.gemm(a, out=planes, out_format="f16", segments=(T, P))
+        out.gemm(a, out=x, residual=x)
+        fc1.gemm(a, out=h, out_format="staged", gelu="tanh")
+        fc2.gemm(h, out=x, residual=x)
+
+
 def _encoder(cfg, batch, calls):
     from .encoder import WhisperEncoderB200, synthetic_mel, synthetic_weights
     w = {k: v.cuda() for k, v in synthetic_weights(cfg, seed=1).items()}
@@ -105,7 +132,8 @@ def moe_prefill_4096_q8():
 
 
 CASES = {"readout-q4-b32": readout_q4_b32, "decode-step-b32": decode_step_b32,
-         "gemm-q8-8192x5120x1280": gemm_q8_8192x5120x1280, "encoder-tiny-b1": encoder_tiny_b1,
+         "gemm-q8-8192x5120x1280": gemm_q8_8192x5120x1280, "gemm-encoder-large-layer": gemm_encoder_large_layer,
+         "encoder-tiny-b1": encoder_tiny_b1,
          "encoder-large-b16": encoder_large_b16, "moe-prefill-4096": moe_prefill_4096,
          "moe-prefill-4096-q8": moe_prefill_4096_q8}
 

@@ -8,7 +8,7 @@
 // reorder + fp16-rounding tolerance (the decode GEMV keeps the exact integer
 // path).
 //
-// Kernel: persistent (one CTA per SM walking 128 x 256 output tiles), 10 warps:
+// Kernel: persistent (one CTA per SM walking 128 x 256 output tiles), 18 warps:
 //   warp 0  TMA producer: 2-D tiled bulk tensor copies (128B swizzle) of the
 //           A (128 x 64) and B (256 x 64) K-slices into a 4-stage ring (3 stages
 //           when the epilogue applies GELU: the fourth stage's room holds
@@ -17,13 +17,17 @@
 //           one thread issues tcgen05.mma kind::f16 (M=128, N=256, K=16) into
 //           the free accumulator, commits each stage back to the producer and
 //           each finished tile to the epilogue;
-//   warps 2-9 epilogue: two warps per TMEM lane quarter (warp % 4), each
-//           taking half of the 256 columns: tcgen05.ld 32x32b.x32
+//   warps 2-17 epilogue: four warps per TMEM lane quarter (warp % 4), each
+//           taking a quarter of the 256 columns: tcgen05.ld 32x32b.x32
 //           (one thread = one row x 32 columns = one Q8_0 block), bias / GELU /
 //           residual, then fp32 or fp16 stores, or the block's Q8_0
 //           quantization stored as fp16(q * d) (the next GEMM's staged A
 //           operand); then release the accumulator, so tile i's epilogue
-//           overlaps tile i+1's MMAs.
+//           overlaps tile i+1's MMAs. The epilogue is the long pole of the GELU /
+//           Q8_0-staging shapes (about 30 instructions per output before packing),
+//           so it has four warps per scheduler to hide its latencies.
+// Above 128 rows the CTA-pair kernel (k_gemm_pair) takes over with the same
+// warp roles and epilogue.
 // Every mbarrier wait is bounded; a timeout sets status bit value 2 and the
 // CTA skips to the end (TMEM is still released).
 #include <cuda.h>
@@ -39,7 +43,7 @@ constexpr int GEMM_BM = 128, GEMM_BN = 256, GEMM_BK = 64;
 constexpr int GEMM_A_BYTES = GEMM_BM * GEMM_BK * 2;
 constexpr int GEMM_B_BYTES = GEMM_BN * GEMM_BK * 2;
 constexpr int GEMM_STAGE_BYTES = GEMM_A_BYTES + GEMM_B_BYTES;
-constexpr int GEMM_EPI_WARPS = 8;  // two warps per TMEM lane quarter, each owning half the columns
+constexpr int GEMM_EPI_WARPS = 16;  // four warps per TMEM lane quarter, each owning a quarter of the columns
 constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 constexpr int GEMM_GROUP_M = 8;
 constexpr uint32_t GEMM_TMEM_COLS = 512;  // two 256-column fp32 accumulators
@@ -51,6 +55,17 @@ constexpr uint32_t GEMM_IDESC = (1u << 4) | (uint32_t(GEMM_BN >> 3) << 17) | (ui
 template <int STAGES, bool GELU_TABLE>
 constexpr size_t gemm_smem_bytes() {
     return size_t(STAGES) * GEMM_STAGE_BYTES + 1024 + 256 + (GELU_TABLE ? GELU_TABLE_BYTES : 0);
+}
+
+// The residual rows a thread's epilogue will read for tile (m0, n0): requested into
+// L2 while the epilogue still waits for that tile's MMAs, so the residual read
+// does not stall on DRAM latency (one 128-byte line per 32-column block).
+__device__ __forceinline__ void prefetch_residual(const GemmArgs &a, int64_t row, int64_t n0, int c0, int chunks) {
+    if (!a.residual || row >= a.M) return;
+    const int64_t rrow_i = a.res_period ? row % a.res_period : row;
+    const float *base = a.residual + rrow_i * a.ldr + n0;
+    for (int c = c0; c < c0 + chunks; ++c)
+        if (n0 + c * 32 < a.N) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + c * 32));
 }
 
 // Epilogue of one row's 32-column block (one Q8_0 block of the output): bias, GELU,
@@ -104,25 +119,33 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs &a, const uint32_t
 #pragma unroll
                 for (int j = 0; j < 32; ++j) o[j] = v[j];
             }
-    } else {
+        } else {
             if (a.out_mode == GEMM_OUT_Q8) {
-                float amax = 0.0f;
-                bool finite = true;
+                // amax as ggml takes it (fmaxf skips a NaN); a NaN-propagating max flags any
+                // nonfinite input of the block in one instruction per element
+                float amax = 0.0f, bad = 0.0f;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     amax = fmaxf(amax, fabsf(v[j]));
-                    finite = finite && isfinite(v[j]);
+                    asm("max.NaN.f32 %0, %0, %1;" : "+f"(bad) : "f"(fabsf(v[j])));
                 }
-                if (!finite && a.status) atomicOr(a.status, 1);
+                if (!isfinite(bad) && a.status) atomicOr(a.status, 1);
                 const float d = __fdiv_rn(amax, 127.0f);
                 const float id = a.rounding == 2 ? (amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f)
                                                  : (d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f);
                 const float dh = __half2float(__float2half_rn(d));
+                if (a.rounding == 0) {   // roundf: half away from zero
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float sv = __fmul_rn(v[j], id);
-                    const int qv = a.rounding == 0 ? int(roundf(sv)) : __float2int_rn(sv);
-                    v[j] = __fmul_rn(float(qv), dh);
+                    for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(float(int(roundf(__fmul_rn(v[j], id)))), dh);
+                } else {
+                    // round to nearest even without the conversion pipe: |x * id| <= 127.5 < 2^22,
+                    // so adding 1.5 * 2^23 (unit in the last place 1) rounds it to an integer in one
+                    // scalar IEEE add and subtracting gives it back exactly
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float t = __fsub_rn(__fadd_rn(__fmul_rn(v[j], id), 12582912.0f), 12582912.0f);
+                        v[j] = __fmul_rn(t, dh);
+                    }
                 }
             }
             __half *o = static_cast<__half *>(obase) + orow_i * a.ldo + nc;
@@ -267,14 +290,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         int64_t local = 0;
         for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
             const int buf = int(local & 1);
+            int64_t m0, n0;
+            tile_coords(tile, m0, n0);
+            const int64_t row = m0 + 32 * q + lane;
+            prefetch_residual(a, row, n0, c0, GEMM_BN / 32 / (GEMM_EPI_WARPS / 4));
             if (!mbar_wait_bounded(acc_full + buf, uint32_t((local >> 1) & 1))) {
                 atomicOr(&failed, 1);
                 break;
             }
             tc_fence_after();
-            int64_t m0, n0;
-            tile_coords(tile, m0, n0);
-            const int64_t row = m0 + 32 * q + lane;
             const int64_t orow_i = a.seg_rows ? (row / a.seg_rows) * a.out_seg_rows + row % a.seg_rows : row;
             const int64_t rrow_i = a.res_period ? row % a.res_period : row;
             for (int c = c0; c < c0 + GEMM_BN / 32 / (GEMM_EPI_WARPS / 4); ++c) {
@@ -434,14 +458,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         int64_t local = 0;
         for (int64_t tile = cluster; tile < tiles; tile += clusters, ++local) {
             const int buf = int(local & 1);
+            int64_t m0, n0;
+            tile_coords(tile, m0, n0);
+            const int64_t row = m0 + int64_t(rank) * GEMM_BM + 32 * q + lane;
+            prefetch_residual(a, row, n0, c0, GEMM_BN / 32 / (GEMM_EPI_WARPS / 4));
             if (!mbar_wait_bounded(acc_full + buf, uint32_t((local >> 1) & 1))) {
                 atomicOr(&failed, 1);
                 break;
             }
             tc_fence_after();
-            int64_t m0, n0;
-            tile_coords(tile, m0, n0);
-            const int64_t row = m0 + int64_t(rank) * GEMM_BM + 32 * q + lane;
             const int64_t orow_i = a.seg_rows ? (row / a.seg_rows) * a.out_seg_rows + row % a.seg_rows : row;
             const int64_t rrow_i = a.res_period ? row % a.res_period : row;
             for (int c = c0; c < c0 + GEMM_BN / 32 / (GEMM_EPI_WARPS / 4); ++c) {

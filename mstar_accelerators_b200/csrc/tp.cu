@@ -17,6 +17,13 @@
 // Remote reads and writes are whole 512-byte warp segments; a row-per-thread
 // push of the partials from the GEMM epilogue instead splits every row into
 // 16-byte remote stores.
+// Where the buffers are also bound to an NVLink multicast object (NVSwitch
+// NVLS), k_tp_reduce<MODE, true> reads each owned row's sum over all ranks with
+// one multimem.ld_reduce per 16 bytes (the switch adds the W partials, so an
+// owner receives M/W rows instead of (W-1) M/W rows of partials) and writes the
+// staged rows to every rank with one multimem.st (the switch replicates them).
+// The switch's fp32 addition order is its own, so the sum may differ from the
+// rank-order sum in the last bit.
 #include <cmath>
 
 #include "../../include/mstar_b200.h"
@@ -60,13 +67,28 @@ __global__ void k_tp_barrier(int *const *flags, int *mine, int rank, int world, 
     }
 }
 
-// One warp per owned row. parts[p]: rank p's [M][n] fp32 partial product;
-// x: [owned][n] fp32 residual rows of this owner (updated in place).
-template <int MODE>
+__device__ __forceinline__ float4 mc_ld_reduce_add(const float *p) {
+    float4 v;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ void mc_store8(void *p, uint2 u) {
+    asm volatile("multimem.st.relaxed.sys.global.v2.f16x2 [%0], {%1, %2};" ::"l"(p), "r"(u.x), "r"(u.y) : "memory");
+}
+
+// One warp per owned row. parts[p]: rank p's [M][n] fp32 partial product, or
+// (MC) mc_part: the partial buffer's multicast address; x: [owned][n] fp32
+// residual rows of this owner (updated in place); staged[p]: rank p's staged
+// operand, or (MC) mc_staged: its multicast address.
+template <int MODE, bool MC>
 __global__ void __launch_bounds__(TP_WARPS * 32)
-    k_tp_reduce(const float *const *parts, int world, int64_t owned, int64_t n, const float *__restrict__ bias,
-                float *__restrict__ x, const float *__restrict__ ln_w, const float *__restrict__ ln_b, float eps,
-                __half *const *staged, int64_t row0, int *status) {
+    k_tp_reduce(const float *const *parts, const float *mc_part, int world, int64_t owned, int64_t n,
+                const float *__restrict__ bias, float *__restrict__ x, const float *__restrict__ ln_w,
+                const float *__restrict__ ln_b, float eps, __half *const *staged, __half *mc_staged, int64_t row0,
+                int *status) {
     const int lane = threadIdx.x & 31;
     const int64_t r = int64_t(blockIdx.x) * TP_WARPS + (threadIdx.x >> 5);
     if (r >= owned) return;
@@ -78,13 +100,18 @@ __global__ void __launch_bounds__(TP_WARPS * 32)
         const int64_t c = int64_t(i) * 32 + lane;
         v[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         if (c < chunks) {
-            float4 acc = *reinterpret_cast<const float4 *>(parts[0] + (row0 + r) * n + 4 * c);
-            for (int s = 1; s < world; ++s) {
-                const float4 p = *reinterpret_cast<const float4 *>(parts[s] + (row0 + r) * n + 4 * c);
-                acc.x = __fadd_rn(acc.x, p.x);
-                acc.y = __fadd_rn(acc.y, p.y);
-                acc.z = __fadd_rn(acc.z, p.z);
-                acc.w = __fadd_rn(acc.w, p.w);
+            float4 acc;
+            if (MC) {
+                acc = mc_ld_reduce_add(mc_part + (row0 + r) * n + 4 * c);
+            } else {
+                acc = *reinterpret_cast<const float4 *>(parts[0] + (row0 + r) * n + 4 * c);
+                for (int s = 1; s < world; ++s) {
+                    const float4 p = *reinterpret_cast<const float4 *>(parts[s] + (row0 + r) * n + 4 * c);
+                    acc.x = __fadd_rn(acc.x, p.x);
+                    acc.y = __fadd_rn(acc.y, p.y);
+                    acc.z = __fadd_rn(acc.z, p.z);
+                    acc.w = __fadd_rn(acc.w, p.w);
+                }
             }
             const float4 b = *reinterpret_cast<const float4 *>(bias + 4 * c);
             float4 *xr = reinterpret_cast<float4 *>(x + r * n + 4 * c);
@@ -144,10 +171,29 @@ __global__ void __launch_bounds__(TP_WARPS * 32)
             uint2 u;
             u.x = half2_bits(__floats2half2_rn(q(y.x), q(y.y)));
             u.y = half2_bits(__floats2half2_rn(q(y.z), q(y.w)));
-            for (int p = 0; p < world; ++p)
-                *reinterpret_cast<uint2 *>(staged[p] + (row0 + r) * n + 4 * c) = u;
+            if (MC) mc_store8(mc_staged + (row0 + r) * n + 4 * c, u);
+            else
+                for (int p = 0; p < world; ++p)
+                    *reinterpret_cast<uint2 *>(staged[p] + (row0 + r) * n + 4 * c) = u;
         }
     }
+}
+
+template <bool MC>
+static void launch_tp_reduce(const float *const *parts, const float *mc_part, int world, int64_t owned, int64_t width,
+                             const float *bias, float *x, const float *ln_w, const float *ln_b, float eps,
+                             __half *const *staged, __half *mc_staged, int64_t row0, int rounding, int *status,
+                             cudaStream_t s) {
+    const unsigned grid = unsigned(ceil_div(owned, TP_WARPS));
+    if (rounding == 0)
+        k_tp_reduce<0, MC><<<grid, TP_WARPS * 32, 0, s>>>(parts, mc_part, world, owned, width, bias, x, ln_w, ln_b,
+                                                         eps, staged, mc_staged, row0, status);
+    else if (rounding == 2)
+        k_tp_reduce<2, MC><<<grid, TP_WARPS * 32, 0, s>>>(parts, mc_part, world, owned, width, bias, x, ln_w, ln_b,
+                                                         eps, staged, mc_staged, row0, status);
+    else
+        k_tp_reduce<1, MC><<<grid, TP_WARPS * 32, 0, s>>>(parts, mc_part, world, owned, width, bias, x, ln_w, ln_b,
+                                                         eps, staged, mc_staged, row0, status);
 }
 
 }  // namespace mb
@@ -188,18 +234,38 @@ int mstar_b200_tp_reduce(const float *const *part_ptrs, int32_t world, int64_t o
         }
         check_device(x, "owned rows");
         if (owned == 0) return 0;
-        const unsigned grid = unsigned(ceil_div(owned, TP_WARPS));
-        auto *dst = reinterpret_cast<__half *const *>(staged_ptrs);
-        cudaStream_t s = as_stream(stream);
-        if (rounding == 0)
-            k_tp_reduce<0><<<grid, TP_WARPS * 32, 0, s>>>(part_ptrs, world, owned, width, bias, x, ln_weight, ln_bias,
-                                                         ln_eps, dst, row0, status);
-        else if (rounding == 2)
-            k_tp_reduce<2><<<grid, TP_WARPS * 32, 0, s>>>(part_ptrs, world, owned, width, bias, x, ln_weight, ln_bias,
-                                                         ln_eps, dst, row0, status);
-        else
-            k_tp_reduce<1><<<grid, TP_WARPS * 32, 0, s>>>(part_ptrs, world, owned, width, bias, x, ln_weight, ln_bias,
-                                                         ln_eps, dst, row0, status);
+        launch_tp_reduce<false>(part_ptrs, nullptr, world, owned, width, bias, x, ln_weight, ln_bias, ln_eps,
+                                reinterpret_cast<__half *const *>(staged_ptrs), nullptr, row0, rounding, status,
+                                as_stream(stream));
+        cuda_check(cudaGetLastError(), "reduction launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+int mstar_b200_tp_reduce_multicast(const float *mc_part, int32_t world, int64_t owned, int64_t width,
+                                   const float *bias, float *x, const float *ln_weight, const float *ln_bias,
+                                   float ln_eps, void *mc_staged, int64_t row0, int32_t rounding, int32_t *status,
+                                   void *stream, char *error, size_t error_size) {
+    try {
+        require(world >= 1 && world <= TP_MAX_WORLD, "invalid world size");
+        require(owned >= 0 && row0 >= 0, "invalid owned rows");
+        require(width >= 4 && width % 32 == 0 && width <= 4 * 32 * TP_MAX_CHUNKS, "width must be 32..1536, /32");
+        require(mc_part && bias && x && status, "missing reduction operand");
+        require(uintptr_t(mc_part) % 16 == 0, "multicast partial buffer must be 16-byte aligned");
+        require(uintptr_t(x) % 16 == 0 && uintptr_t(bias) % 16 == 0, "reduction operands must be 16-byte aligned");
+        require(rounding >= 0 && rounding <= 2, "unknown Q8_0 activation rounding");
+        if (ln_weight) {
+            require(ln_bias && mc_staged && std::isfinite(ln_eps) && ln_eps >= 0.0f, "invalid LayerNorm staging");
+            require(uintptr_t(mc_staged) % 16 == 0, "multicast staged buffer must be 16-byte aligned");
+            require(uintptr_t(ln_weight) % 16 == 0 && uintptr_t(ln_bias) % 16 == 0, "LayerNorm vectors unaligned");
+        }
+        check_device(x, "owned rows");
+        if (owned == 0) return 0;
+        launch_tp_reduce<true>(nullptr, mc_part, world, owned, width, bias, x, ln_weight, ln_bias, ln_eps, nullptr,
+                               static_cast<__half *>(mc_staged), row0, rounding, status, as_stream(stream));
         cuda_check(cudaGetLastError(), "reduction launch");
         return 0;
     } catch (const std::exception &e) {

@@ -21,6 +21,11 @@ encoder block):
     layer's first LayerNorm;
   * the final LayerNorm runs on each owner's rows; ``forward`` all-gathers the
     rows (NCCL) so every rank returns the full encoder states.
+Where NVSwitch multicast (NVLS) is available, the reduction instead reads each
+owned row's sum over all ranks with multimem loads that add in the switch, and
+writes the staged rows once through the multicast address to every rank
+(mstar_b200_tp_reduce_multicast): an owner then moves its own rows over NVLink,
+not the W - 1 other ranks' partials of them.
 Q8_0 blocks lie along K and every shard boundary is a multiple of 32, so each
 rank's weights are exactly sub-blocks of the single-GPU weights.
 """
@@ -79,7 +84,11 @@ def shard_weights(weights: dict, cfg: EncoderConfig, world: int, rank: int) -> d
 class WhisperEncoderTP:
     """This rank's part of a tensor-parallel encoder for up to ``max_batch`` utterances."""
 
-    def __init__(self, weights: dict, cfg: EncoderConfig, *, max_batch: int = 1, group=None, rounding: str = "arm"):
+    def __init__(self, weights: dict, cfg: EncoderConfig, *, max_batch: int = 1, group=None, rounding: str = "arm",
+                 multicast: bool | None = None):
+        """multicast: reduce through the NVSwitch multicast object of the symmetric buffers
+        (multimem loads that sum in the switch, multimem stores to every rank); None uses it
+        where the platform offers it, False keeps the peer loads and stores."""
         import torch.distributed._symmetric_memory as symm
         self.lib = native.require_capability()
         self.group = group
@@ -152,6 +161,15 @@ class WhisperEncoderTP:
         def ptrs(h):
             return torch.tensor(h.buffer_ptrs, dtype=torch.int64, device=dev)
         self.part_ptrs, self.staged_ptrs, self.flag_ptrs = (ptrs(h) for h in self._h)
+        mc = [int(getattr(h, "multicast_ptr", 0) or 0) for h in self._h[:2]]
+        available = self.world > 1 and all(mc)
+        if multicast and not available:
+            raise ValueError("the symmetric buffers have no multicast object on this platform")
+        # every rank must take the same path: use multicast only if all ranks have it
+        flag = torch.tensor([1 if available and multicast is not False else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+        self.multicast = bool(flag.item())
+        self.mc_part, self.mc_staged = mc
         dist.barrier(group=group)
 
     # ------------------------------------------------------------------ pieces
@@ -169,6 +187,13 @@ class WhisperEncoderTP:
     def _reduce(self, owner_rows: int, owned: int, bias: torch.Tensor, norm):
         lw, lb, eps = (norm[0].data_ptr(), norm[1].data_ptr(), float(norm[2])) if norm else (None, None, 0.0)
         e = error_buffer()
+        if self.multicast:
+            check(self.lib.mstar_b200_tp_reduce_multicast(self.mc_part, self.world, owned, self.cfg.width,
+                                                          bias.data_ptr(), self.x_own.data_ptr(), lw, lb, eps,
+                                                          self.mc_staged if norm else None, self.rank * owner_rows,
+                                                          native.ROUNDING[self.rounding], self.status.data_ptr(),
+                                                          _stream(self.device), e, len(e)), e, "B200 TP reduce")
+            return
         check(self.lib.mstar_b200_tp_reduce(self.part_ptrs.data_ptr(), self.world, owned, self.cfg.width,
                                             bias.data_ptr(), self.x_own.data_ptr(), lw, lb, eps,
                                             self.staged_ptrs.data_ptr() if norm else None, self.rank * owner_rows,

@@ -23,7 +23,7 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 
-def _worker(rank, world, port, results):
+def _worker(rank, world, port, results, multicast):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
@@ -34,7 +34,7 @@ def _worker(rank, world, port, results):
         from mstar_accelerators_b200.encoder_tp import WhisperEncoderTP
         w = synthetic_weights(TINY, seed=1)
         mel = synthetic_mel(TINY, 2, seed=2).cuda()
-        tp = WhisperEncoderTP(w, TINY, max_batch=2)
+        tp = WhisperEncoderTP(w, TINY, max_batch=2, multicast=multicast)
         got = tp(mel)
         assert int(tp.status.item()) == 0
         ref = WhisperEncoderB200({k: v.cuda() for k, v in w.items()}, TINY, max_batch=2)(mel)
@@ -44,7 +44,7 @@ def _worker(rank, world, port, results):
         scale = ref.abs().max().item()
         diff = (got - ref).abs()
         results[rank] = (bool(all(torch.equal(o, got) for o in others)), diff.max().item() / scale,
-                         diff.mean().item() / scale)
+                         diff.mean().item() / scale, tp.multicast)
         tp.close()
     finally:
         dist.destroy_process_group()
@@ -57,12 +57,18 @@ def _port():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_tensor_parallel_encoder_matches_single_gpu():
+@pytest.mark.parametrize("multicast", [False, None])
+def test_tensor_parallel_encoder_matches_single_gpu(multicast):
+    """multicast False: peer loads and stores; None: the NVSwitch multicast path where the
+    platform offers it (the result records which path ran)."""
     world = 2
     ctx = mp.get_context("spawn")
     with ctx.Manager() as manager:
         results = manager.dict()
-        mp.start_processes(_worker, args=(world, _port(), results), nprocs=world, join=True, start_method="spawn")
+        mp.start_processes(_worker, args=(world, _port(), results, multicast), nprocs=world, join=True,
+                           start_method="spawn")
         for rank in range(world):
-            same, mx, mean = results[rank]
-            assert same and mx <= 3e-2 and mean <= 2e-3, (rank, mx, mean)
+            same, mx, mean, used = results[rank]
+            assert same and mx <= 3e-2 and mean <= 2e-3, (rank, mx, mean, used)
+            if multicast is False:
+                assert not used
