@@ -89,8 +89,10 @@ def _encoder(cfg, batch, calls):
     w = {k: v.cuda() for k, v in synthetic_weights(cfg, seed=1).items()}
     mel = synthetic_mel(cfg, batch, seed=2).cuda()
     enc = WhisperEncoderB200(w, cfg, max_batch=batch)
-    for _ in range(calls):
+    for i in range(calls):   # NVTX range per forward, so a profiler can keep one forward's launches only
+        torch.cuda.nvtx.range_push(f"forward{i}")
         enc(mel)
+        torch.cuda.nvtx.range_pop()
 
 
 def encoder_tiny_b1():

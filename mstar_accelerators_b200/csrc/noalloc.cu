@@ -48,21 +48,36 @@ struct NoAllocScratch {
 
 static __device__ __align__(256) NoAllocScratch g_noalloc_scratch;
 
-// Address of this device's copy of the array, resolved once per device.
-static NoAllocScratch *noalloc_scratch(int device) {
+// This device's copy of the array and its SM count, resolved once per device
+// under one lock (the first call on a device does it; make that call before any
+// stream capture).
+struct NoAllocDevice {
+    NoAllocScratch *scratch = nullptr;
+    int sms = 0;
+};
+
+static bool noalloc_device(int device, NoAllocDevice &out) {
     static std::mutex lock;
-    static NoAllocScratch *address[NOALLOC_MAX_DEVICES] = {};
-    if (device < 0 || device >= NOALLOC_MAX_DEVICES) return nullptr;
+    static NoAllocDevice known[NOALLOC_MAX_DEVICES] = {};
+    if (device < 0 || device >= NOALLOC_MAX_DEVICES) return false;
     std::lock_guard<std::mutex> guard(lock);
-    if (!address[device]) {
+    NoAllocDevice &d = known[device];
+    if (!d.scratch) {
         void *p = nullptr;
         if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) {
             cudaGetLastError();
-            return nullptr;
+            return false;
         }
-        address[device] = static_cast<NoAllocScratch *>(p);
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || sms <= 0) {
+            cudaGetLastError();
+            sms = 148;
+        }
+        d.sms = sms;
+        d.scratch = static_cast<NoAllocScratch *>(p);
     }
-    return address[device];
+    out = d;
+    return true;
 }
 
 __device__ __forceinline__ float block_scale(const uint8_t *block) {
@@ -160,8 +175,9 @@ int mstar_b200_q8_readout_noalloc(const void *blocks, size_t bytes, int64_t rows
         cudaGetLastError();
         return EIO;
     }
-    NoAllocScratch *s = noalloc_scratch(device);
-    if (!s) return EIO;
+    NoAllocDevice dev;
+    if (!noalloc_device(device, dev)) return EIO;
+    NoAllocScratch *s = dev.scratch;
     cudaStream_t st = as_stream(stream);
     const int64_t nb = k / QK, nb_pad = (nb + 1) / 2 * 2;
     // the argmax state and the caller's status start at zero
@@ -172,14 +188,9 @@ int mstar_b200_q8_readout_noalloc(const void *blocks, size_t bytes, int64_t rows
     }
     launch_quantize_frag(MSTAR_B200_Q8_ARM, x, k, 1, k, 16, nb_pad, nullptr, nullptr, 0.0f,
                          reinterpret_cast<uint32_t *>(s->xf), s->xs, s->xsum, status, st);
-    static int sms = 0;
-    if (!sms) {
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-        if (sms <= 0) sms = 148;
-    }
     const int64_t groups = (rows + 7) / 8;
     int64_t grid = (groups + 7) / 8;
-    if (grid > int64_t(sms) * 8) grid = int64_t(sms) * 8;
+    if (grid > int64_t(dev.sms) * 8) grid = int64_t(dev.sms) * 8;
     k_readout_canonical<<<unsigned(grid), 256, 0, st>>>(static_cast<const uint8_t *>(blocks), rows, int(nb), s, out,
                                                         token, suppressed, int64_t(suppressed_count));
     if (cudaGetLastError() != cudaSuccess) return EIO;

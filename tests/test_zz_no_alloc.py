@@ -36,18 +36,20 @@ def _call_both(lib, handle, blocks, rows, k, x, suppressed, stream):
     return (ref, ref_tok, ref_st), (out, tok, st)
 
 
-def test_noalloc_readout_equals_handle_readout_on_consecutive_calls():
+@pytest.mark.parametrize("rows,k", [(51865, 384), (1000, 416), (5, 4096)])
+def test_noalloc_readout_equals_handle_readout_on_consecutive_calls(rows, k):
+    """Vocabulary width with an even block count (384: 12 blocks), an odd block count
+    (416: 13, so the quantizer writes a padding block into the shared array), and the
+    widest activation the array holds (4096), with and without suppression."""
     from mstar_accelerators_b200 import linear, native
     lib = native.load()
     native.require_capability(lib)
     torch.cuda.set_device(0)
-    rows, k = 51865, 384
-    g = torch.Generator(device="cuda").manual_seed(7)
+    g = torch.Generator(device="cuda").manual_seed(7 + k)
     blocks = linear.pack(torch.randn(rows, k, device="cuda", generator=g) * 0.02, "q8_0")
     head = linear.BlockLinear(blocks=blocks, fmt="q8_0", rows=rows, width=k)
     stream = torch.cuda.current_stream().cuda_stream
-    suppression = [None, torch.tensor([3, 77, 50000, rows - 1], dtype=torch.int64, device="cuda")]
-    free_after_first = None
+    suppression = [None, torch.tensor(sorted({3 % rows, 77 % rows, rows - 1}), dtype=torch.int64, device="cuda")]
     for call, sup in enumerate(suppression):
         x = torch.randn(k, device="cuda", generator=g)
         (ref, ref_tok, ref_st), (out, tok, st) = _call_both(lib, head.handle, blocks, rows, k, x, sup, stream)
@@ -56,11 +58,18 @@ def test_noalloc_readout_equals_handle_readout_on_consecutive_calls():
         assert int(st) == 0 and int(ref_st) == 0
         if sup is not None:
             assert torch.isinf(out[sup]).all()
-        free_now = torch.cuda.mem_get_info()[0]
-        if free_after_first is None:
-            free_after_first = free_now
-        else:
-            assert free_now == free_after_first, "a later call changed free device memory"
+    # free device memory is read right around a lone no-allocation call whose every
+    # operand exists beforehand: the call itself must not change it
+    x = torch.randn(k, device="cuda", generator=g)
+    out = torch.empty(rows, device="cuda")
+    tok = torch.empty(1, dtype=torch.int64, device="cuda")
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    before = torch.cuda.mem_get_info()[0]
+    assert lib.mstar_b200_q8_readout_noalloc(blocks.data_ptr(), blocks.numel(), rows, k, x.data_ptr(),
+                                             out.data_ptr(), tok.data_ptr(), st.data_ptr(), None, 0, stream) == 0
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == before, "the call changed free device memory"
     head.close()
 
 
