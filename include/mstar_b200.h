@@ -305,6 +305,22 @@ MSTAR_B200_API int mstar_b200_tp_reduce_multicast(const float *mc_part, int32_t 
     const float *bias, float *x, const float *ln_weight, const float *ln_bias, float ln_eps, void *mc_staged,
     int64_t row0, int32_t rounding, int32_t *status, void *stream, char *error, size_t error_size);
 
+/* --- categorical sampling of readout logits (backends/pi/docs/categorical.md, the
+ * Graph.categorical operation; scalar oracle backends/pi/torch/tests/categorical_reference.py) ---
+ * philox4x32-10-gumbel23-v1: for row r and vocabulary entry j, Philox4x32-10 with
+ * key (seeds[r] lo, hi) and counter (offsets[r] lo, hi, j, 0) gives u = ((word0 >> 9)
+ * + 0.5) * 2^-23, and tokens[r] is the lowest j maximizing centered_j / T - log(-log(u_j))
+ * (centered_j = 0 at the row maximum, else (logit_j - max) / T, each step an fp32
+ * rounding); -1 for a row with a NaN, nothing above -inf, or a temperature that is not
+ * positive and finite; +inf logits restrict the draw to themselves. Seeds and offsets
+ * are read as full 64-bit words and never written. logits: [rows][ld] fp32 device rows
+ * (vocab <= INT32_MAX entries used of each); workspace: categorical_workspace(rows)
+ * bytes of device memory (16-byte aligned), overwritten. Stream-ordered. */
+MSTAR_B200_API uint64_t mstar_b200_categorical_workspace(int64_t rows);
+MSTAR_B200_API int mstar_b200_categorical(const float *logits, int64_t rows, int64_t vocab, int64_t ld,
+    const int64_t *seeds, const int64_t *offsets, const float *temperatures, int64_t *tokens, void *workspace,
+    uint64_t workspace_bytes, void *stream, char *error, size_t error_size);
+
 /* --- bounded device waits (no reference counterpart: the reference's native
  * backends run on the CPU and never wait on a device flag) ---
  * Every spin or mbarrier wait in this library gives up after a bounded number of

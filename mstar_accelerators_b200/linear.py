@@ -137,6 +137,33 @@ def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: f
     return out
 
 
+def categorical(logits: torch.Tensor, seeds: torch.Tensor, offsets: torch.Tensor, temperatures: torch.Tensor,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """Positive-temperature categorical draws of fp32 logits [rows, vocab] (the reference's
+    philox4x32-10-gumbel23-v1 operation): int64 seeds / offsets and fp32 temperatures per row;
+    returns int64 tokens [rows], -1 for an invalid row (a NaN, nothing above -inf, or a
+    temperature that is not positive and finite)."""
+    lib = native.require_capability()
+    _require_cuda(logits, "logits", torch.float32)
+    if logits.ndim != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be [rows, vocab] with unit column stride")
+    rows, vocab = logits.shape
+    for t, name, dt in ((seeds, "seeds", torch.int64), (offsets, "offsets", torch.int64),
+                        (temperatures, "temperatures", torch.float32)):
+        _require_cuda(t, name, dt)
+        if t.shape != (rows,) or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous [rows] tensor")
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int64, device=logits.device)
+    ws_bytes = int(lib.mstar_b200_categorical_workspace(rows))
+    ws = torch.empty((ws_bytes + 15) // 16 * 4, dtype=torch.float32, device=logits.device)
+    e = error_buffer()
+    check(lib.mstar_b200_categorical(logits.data_ptr(), rows, vocab, logits.stride(0), seeds.data_ptr(),
+                                     offsets.data_ptr(), temperatures.data_ptr(), out.data_ptr(), ws.data_ptr(),
+                                     ws_bytes, _stream(logits.device), e, len(e)), e, "B200 categorical sampling")
+    return out
+
+
 def _rows(x: torch.Tensor, width: int) -> torch.Tensor:
     """[..., width] -> a 2-D view with unit inner stride and 16-byte aligned rows."""
     x2 = x.reshape(-1, width)

@@ -65,6 +65,11 @@ def lib():
         L.orc_gelu_ggml_rows.argtypes = [_f32p, _f32p, C.c_int64]
         L.orc_gelu_ggml_rows.restype = None
         L.orc_gelu_ggml.restype = C.c_float
+        _u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+        L.orc_philox4x32_10.argtypes = [_u32p, _u32p, _u32p]
+        L.orc_philox4x32_10.restype = None
+        L.orc_categorical.argtypes = [_f32p, C.c_int64, C.c_int64, _i64p, _i64p, _f32p, _i64p]
+        L.orc_categorical.restype = None
         _lib = L
     return _lib
 
@@ -157,6 +162,24 @@ def argmax(logits, suppressed=()) -> tuple[np.ndarray, int]:
     s = np.ascontiguousarray(np.asarray(suppressed, np.int64).reshape(-1))
     tok = lib().orc_argmax(l, l.size, s, s.size)
     return l, int(tok)
+
+
+def philox4x32_10(counter, key) -> tuple[int, ...]:
+    """Random123 Philox4x32-10 of four counter and two key words."""
+    out = np.zeros(4, np.uint32)
+    lib().orc_philox4x32_10(np.asarray(counter, np.uint32), np.asarray(key, np.uint32), out)
+    return tuple(int(v) for v in out)
+
+
+def categorical(logits, seeds, offsets, temperatures) -> np.ndarray:
+    """philox4x32-10-gumbel23-v1 draws of each row of fp32 logits [rows, vocab] (-1: invalid row)."""
+    x = _f32(logits)
+    rows, vocab = x.shape
+    out = np.zeros(rows, np.int64)
+    lib().orc_categorical(x.reshape(-1), rows, vocab, np.ascontiguousarray(seeds, np.int64).reshape(-1),
+                          np.ascontiguousarray(offsets, np.int64).reshape(-1),
+                          _f32(temperatures).reshape(-1), out)
+    return out
 
 
 def fp16_round(x) -> np.ndarray:

@@ -280,3 +280,69 @@ float orc_gelu_ggml(float x) {
 void orc_gelu_ggml_rows(const float *x, float *y, int64_t n) {
     for (int64_t i = 0; i < n; ++i) y[i] = orc_gelu_ggml(x[i]);
 }
+
+/* ---------------- categorical sampling (readout epilogue) ------------------------
+ * philox4x32-10-gumbel23-v1 (backends/pi/docs/categorical.md; its scalar test
+ * oracle backends/pi/torch/tests/categorical_reference.py:18-64): Philox4x32-10
+ * (Random123: ten rounds, multipliers 0xD2511F53 / 0xCD9E8D57, Weyl key steps
+ * 0x9E3779B9 / 0xBB67AE85) with key = (seed lo, seed hi), counter = (offset lo,
+ * offset hi, token, 0); u = ((word0 >> 9) + 0.5) * 2^-23; score = centered / T -
+ * log(-log(u)), each step rounded to fp32 (the logarithms evaluated in double
+ * and rounded, as that oracle does), centered = 0 for a row maximum, else
+ * fp32(logit - max) / T; the lowest index of the highest score wins. A NaN
+ * logit, an all -inf row or a temperature that is not positive and finite give
+ * -1; with a +inf logit only the +inf entries compete. */
+void orc_philox4x32_10(const uint32_t counter[4], const uint32_t key[2], uint32_t out[4]) {
+    uint32_t c0 = counter[0], c1 = counter[1], c2 = counter[2], c3 = counter[3];
+    uint32_t k0 = key[0], k1 = key[1];
+    for (int r = 0; r < 10; ++r) {
+        const uint64_t a = (uint64_t)0xD2511F53u * c0, b = (uint64_t)0xCD9E8D57u * c2;
+        const uint32_t n0 = (uint32_t)(b >> 32) ^ c1 ^ k0, n1 = (uint32_t)b;
+        const uint32_t n2 = (uint32_t)(a >> 32) ^ c3 ^ k1, n3 = (uint32_t)a;
+        c0 = n0; c1 = n1; c2 = n2; c3 = n3;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
+}
+
+static float orc_uniform(uint64_t seed, uint64_t offset, uint32_t token) {
+    const uint32_t ctr[4] = {(uint32_t)offset, (uint32_t)(offset >> 32), token, 0};
+    const uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
+    uint32_t w[4];
+    orc_philox4x32_10(ctr, key, w);
+    return ((float)(w[0] >> 9) + 0.5f) * 0x1p-23f;
+}
+
+int64_t orc_categorical_row(const float *logits, int64_t vocab, uint64_t seed, uint64_t offset, float temperature) {
+    if (vocab <= 0 || !isfinite(temperature) || !(temperature > 0.0f)) return -1;
+    float m = -INFINITY;
+    for (int64_t j = 0; j < vocab; ++j) {
+        if (isnan(logits[j])) return -1;
+        if (logits[j] > m) m = logits[j];
+    }
+    if (m == -INFINITY) return -1;
+    int64_t best = -1;
+    float best_score = -INFINITY;
+    for (int64_t j = 0; j < vocab; ++j) {
+        const float v = logits[j];
+        if (v == -INFINITY || (m == INFINITY && v != m)) continue;
+        const float centered = v == m ? 0.0f : (float)(v - m) / temperature;
+        const float u = orc_uniform(seed, offset, (uint32_t)j);
+        const float inner = (float)log((double)u);
+        const float noise = (float)log((double)(-inner));
+        const float score = centered - noise;
+        if (best < 0 || score > best_score) {
+            best = j;
+            best_score = score;
+        }
+    }
+    return best;
+}
+
+void orc_categorical(const float *logits, int64_t rows, int64_t vocab, const int64_t *seeds, const int64_t *offsets,
+                     const float *temperatures, int64_t *tokens) {
+    for (int64_t r = 0; r < rows; ++r)
+        tokens[r] = orc_categorical_row(logits + r * vocab, vocab, (uint64_t)seeds[r], (uint64_t)offsets[r],
+                                        temperatures[r]);
+}

@@ -127,10 +127,54 @@ def mul_mat():
     np.savez(HERE / "mul_mat.npz", **out)
 
 
+def reference_categorical():
+    """The reference's own scalar categorical oracle, imported from the checkout
+    (backends/pi/torch/tests/categorical_reference.py; it imports only the standard library)."""
+    path = REFERENCE / "backends/pi/torch/tests/categorical_reference.py"
+    spec = importlib.util.spec_from_file_location("_reference_categorical", path)
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+def categorical():
+    """Draws of the reference's scalar oracle on seeded rows: ordinary finite rows at
+    several temperatures, 64-bit seeds and offsets, exact ties, -inf masks, +inf
+    entries, a NaN row, an all -inf row and invalid temperatures."""
+    ref = reference_categorical()
+    ref.known_answers()
+    rng = np.random.default_rng(31)
+    V = 257
+    rows = [rng.standard_normal(V).astype(np.float32) * s for s in (0.5, 2.0, 8.0, 0.1)]
+    r = np.zeros(V, np.float32); r[[3, 100, 200]] = 5.0; rows.append(r)                    # tied maxima
+    r = rng.standard_normal(V).astype(np.float32); r[::2] = -np.inf; rows.append(r)         # masked entries
+    r = rng.standard_normal(V).astype(np.float32); r[[7, 150]] = np.inf; rows.append(r)    # +inf entries
+    r = rng.standard_normal(V).astype(np.float32); r[42] = np.nan; rows.append(r)          # NaN
+    rows.append(np.full(V, -np.inf, np.float32))                                          # nothing to draw
+    rows.append(rng.standard_normal(V).astype(np.float32))                                # invalid temperature
+    rows.append(rng.standard_normal(V).astype(np.float32))                                # invalid temperature
+    logits = np.stack(rows)
+    n = len(rows)
+    seeds = rng.integers(-(1 << 63), (1 << 63) - 1, n, dtype=np.int64)
+    offsets = rng.integers(-(1 << 63), (1 << 63) - 1, n, dtype=np.int64)
+    temps = np.array([1.0, 0.8, 2.5, 1e-5, 1.0, 0.7, 1.0, 1.0, 1.0, 0.0, -1.0], np.float32)
+    tokens = np.array([ref.categorical_row(logits[i].tolist(), int(seeds[i]) & ((1 << 64) - 1),
+                                           int(offsets[i]) & ((1 << 64) - 1), float(temps[i]))
+                       for i in range(n)], np.int64)
+    # many draws of one row, for the statistics of the sampler
+    many_logits = (rng.standard_normal(16) * 1.5).astype(np.float32)
+    many_offsets = np.arange(2000, dtype=np.int64)
+    many_tokens = np.array([ref.categorical_row(many_logits.tolist(), 12345, int(o), 0.9) for o in many_offsets],
+                           np.int64)
+    np.savez(HERE / "categorical.npz", logits=logits, seeds=seeds, offsets=offsets, temperatures=temps,
+             tokens=tokens, many_logits=many_logits, many_offsets=many_offsets, many_tokens=many_tokens)
+
+
 if __name__ == "__main__":
     O.build()
     q8_kat()
     q8_pack()
     q4_pack()
     mul_mat()
+    categorical()
     print("golden vectors written to", HERE)
