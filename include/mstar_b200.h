@@ -305,6 +305,24 @@ MSTAR_B200_API int mstar_b200_tp_reduce_multicast(const float *mc_part, int32_t 
     const float *bias, float *x, const float *ln_weight, const float *ln_bias, float ln_eps, void *mc_staged,
     int64_t row0, int32_t rounding, int32_t *status, void *stream, char *error, size_t error_size);
 
+/* --- thinker attention prologue (implementations/qwen3_omni/amd/qknorm_rope.py:9-53, the
+ * fused QK RMSNorm + prepared MRoPE op; KV write as cp_kernels.py:16-58) ---
+ * qknorm_rope: for every token t and head of 128 bf16 values: x = q or k head row,
+ * n = bf16((x * (1 / sqrt(sum(x^2) / 128 + eps))) * w) with w the q / k norm weight,
+ * y = bf16(bf16(n * cos[t]) + bf16(rotate_half(n) * sin[t])) (products rounded to bf16
+ * when round_products, else summed in fp32). q heads are written to out_q [tokens,
+ * q_heads, 128]; k heads to k_cache row slots[t] (or t without a slot table), and v
+ * heads, when v is given, copied unchanged to v_cache at the same row; a row is
+ * cache_slot_stride elements holding kv_heads x 128. A slot outside [0, num_slots)
+ * skips the token's k / v and sets status bit value 1. All tensors bf16 on the device;
+ * strides in elements; head_dim must be 128. */
+MSTAR_B200_API int mstar_b200_qknorm_rope(const void *q, int64_t q_s0, int64_t q_s1, const void *k, int64_t k_s0,
+    int64_t k_s1, const void *v, int64_t v_s0, int64_t v_s1, const void *q_weight, const void *k_weight,
+    const void *cos, int64_t cos_s0, const void *sin, int64_t sin_s0, int64_t tokens, int32_t q_heads,
+    int32_t kv_heads, int32_t head_dim, float eps, int32_t round_products, void *out_q, void *k_cache,
+    void *v_cache, int64_t cache_slot_stride, const int64_t *slots, int64_t num_slots, int32_t *status, void *stream,
+    char *error, size_t error_size);
+
 /* --- categorical sampling of readout logits (backends/pi/docs/categorical.md, the
  * Graph.categorical operation; scalar oracle backends/pi/torch/tests/categorical_reference.py) ---
  * philox4x32-10-gumbel23-v1: for row r and vocabulary entry j, Philox4x32-10 with

@@ -1,0 +1,174 @@
+// Thinker attention prologue after the QKV projection, in one launch: per-head
+// QK RMSNorm, the prepared (M)RoPE rotation and the KV-cache write.
+//
+// Arithmetic of the reference's fused op (implementations/qwen3_omni/amd/
+// qknorm_rope.py:9-53, bf16 boundaries, no fused multiply-add):
+//   x = fp32(bf16 head row of 128), r = 1 / sqrt(sum(x^2) / 128 + eps)
+//   n = bf16((x * r) * w)                          (w: q_norm or k_norm weight)
+//   rot = rotate_half(n): rot[d] = -n[d + 64] for d < 64, n[d - 64] after
+//   a = n * cos[t], b = rot * sin[t]  (each rounded to bf16 when round_products)
+//   y = bf16(a + b)
+// cos / sin are the token's prepared rows [128] (the MRoPE sections already
+// interleaved by the caller, as for the reference op). q heads go to out_q; k
+// heads go to k_cache at the token's slot, and (when v is given) the token's v
+// heads are copied to v_cache at the same slot (the KV write of the code
+// predictor's prologue, cp_kernels.py:16-58). One warp per (token, head), four
+// elements per lane; the rotation partner is lane ^ 16. The sum of squares is a
+// fixed butterfly in fp32, so a result can sit one bf16 step from another
+// summation order's where it lands on a rounding boundary.
+#include <cmath>
+
+#include <cuda_bf16.h>
+
+#include "../../include/mstar_b200.h"
+#include "common.cuh"
+
+namespace mb {
+
+constexpr int QK_HEAD_DIM = 128;
+constexpr int QK_WARPS = 8;
+
+struct QkArgs {
+    const __nv_bfloat16 *q, *k, *v;      // [T, heads, 128] rows with strides (elements)
+    int64_t q_s0, q_s1, k_s0, k_s1, v_s0, v_s1;
+    const __nv_bfloat16 *qw, *kw;        // [128]
+    const __nv_bfloat16 *cos, *sin;      // [T, 128] rows
+    int64_t cs0, ss0;
+    int64_t tokens;
+    int qh, kh;
+    float eps;
+    int round_products;
+    __nv_bfloat16 *out_q;                // [T, qh, 128] contiguous
+    __nv_bfloat16 *k_cache, *v_cache;    // [slots, kh, 128] contiguous rows of slot stride
+    int64_t cache_s0;                    // elements between slots
+    const int64_t *slots;                // [T] slot of each token (k / v destination row)
+    int64_t num_slots;
+    int *status;                         // bit value 1: a slot outside [0, num_slots) (token skipped)
+};
+
+__device__ __forceinline__ float bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__global__ void __launch_bounds__(QK_WARPS * 32) k_qknorm_rope(const QkArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int64_t item = int64_t(blockIdx.x) * QK_WARPS + (threadIdx.x >> 5);
+    const int heads = a.qh + a.kh;
+    if (item >= a.tokens * heads) return;
+    const int64_t t = item / heads;
+    const int h = int(item % heads);
+    const bool is_q = h < a.qh;
+    const __nv_bfloat16 *src = is_q ? a.q + t * a.q_s0 + int64_t(h) * a.q_s1 : a.k + t * a.k_s0 + int64_t(h - a.qh) * a.k_s1;
+    const __nv_bfloat16 *w = is_q ? a.qw : a.kw;
+    const int d0 = 4 * lane;
+    float x[4], ww[4], c[4], s[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        x[i] = __bfloat162float(src[d0 + i]);
+        ww[i] = __bfloat162float(w[d0 + i]);
+        c[i] = __bfloat162float(a.cos[t * a.cs0 + d0 + i]);
+        s[i] = __bfloat162float(a.sin[t * a.ss0 + d0 + i]);
+    }
+    float ss = __fadd_rn(__fadd_rn(__fmul_rn(x[0], x[0]), __fmul_rn(x[1], x[1])),
+                         __fadd_rn(__fmul_rn(x[2], x[2]), __fmul_rn(x[3], x[3])));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(QK_HEAD_DIM)), a.eps)));
+    float n[4], p[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) n[i] = bf(__fmul_rn(__fmul_rn(x[i], r), ww[i]));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) p[i] = __shfl_xor_sync(0xffffffffu, n[i], 16);  // element d +- 64
+    const float sign = lane < 16 ? -1.0f : 1.0f;
+    __align__(8) __nv_bfloat16 y[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float av = __fmul_rn(n[i], c[i]), bv = __fmul_rn(sign * p[i], s[i]);
+        if (a.round_products) {
+            av = bf(av);
+            bv = bf(bv);
+        }
+        y[i] = __float2bfloat16_rn(__fadd_rn(av, bv));
+    }
+    if (is_q) {
+        *reinterpret_cast<uint2 *>(a.out_q + (t * a.qh + h) * QK_HEAD_DIM + d0) = *reinterpret_cast<const uint2 *>(y);
+        return;
+    }
+    const int hk = h - a.qh;
+    const int64_t slot = a.slots ? a.slots[t] : t;
+    if (slot < 0 || slot >= a.num_slots) {
+        if (lane == 0 && a.status) atomicOr(a.status, 1);
+        return;
+    }
+    __nv_bfloat16 *kd = a.k_cache + slot * a.cache_s0 + int64_t(hk) * QK_HEAD_DIM + d0;
+    *reinterpret_cast<uint2 *>(kd) = *reinterpret_cast<const uint2 *>(y);
+    if (a.v) {
+        const __nv_bfloat16 *vs = a.v + t * a.v_s0 + int64_t(hk) * a.v_s1 + d0;
+        __nv_bfloat16 *vd = a.v_cache + slot * a.cache_s0 + int64_t(hk) * QK_HEAD_DIM + d0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) vd[i] = vs[i];
+    }
+}
+
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" {
+
+int mstar_b200_qknorm_rope(const void *q, int64_t q_s0, int64_t q_s1, const void *k, int64_t k_s0, int64_t k_s1,
+                           const void *v, int64_t v_s0, int64_t v_s1, const void *q_weight, const void *k_weight,
+                           const void *cos, int64_t cos_s0, const void *sin, int64_t sin_s0, int64_t tokens,
+                           int32_t q_heads, int32_t kv_heads, int32_t head_dim, float eps, int32_t round_products,
+                           void *out_q, void *k_cache, void *v_cache, int64_t cache_slot_stride,
+                           const int64_t *slots, int64_t num_slots, int32_t *status, void *stream, char *error,
+                           size_t error_size) {
+    try {
+        require(head_dim == QK_HEAD_DIM, "head_dim must be 128");
+        require(tokens >= 0 && q_heads >= 1 && kv_heads >= 1 && q_heads + kv_heads <= 1024, "invalid head counts");
+        require(std::isfinite(eps) && eps >= 0.0f, "invalid RMSNorm epsilon");
+        require(q && k && q_weight && k_weight && cos && sin && out_q && k_cache, "missing prologue operand");
+        require(!v == !v_cache, "v and v_cache come together");
+        require(q_s1 >= QK_HEAD_DIM && k_s1 >= QK_HEAD_DIM && q_s0 >= q_s1 * q_heads && k_s0 >= k_s1 * kv_heads &&
+                    cos_s0 >= QK_HEAD_DIM && sin_s0 >= QK_HEAD_DIM,
+                "row strides smaller than the rows");
+        require(cache_slot_stride >= int64_t(kv_heads) * QK_HEAD_DIM && num_slots >= 1, "invalid KV cache layout");
+        require(slots || num_slots >= tokens, "without a slot table the cache needs a slot per token");
+        const int64_t strides[] = {q_s0, q_s1, k_s0, k_s1, cos_s0, sin_s0, cache_slot_stride};
+        for (int64_t st : strides) require(st % 4 == 0, "strides must keep 8-byte alignment");
+        if (v) require(v_s1 >= QK_HEAD_DIM && v_s0 >= v_s1 * kv_heads, "v row strides smaller than the rows");
+        const void *ptrs[] = {q, k, out_q, k_cache, cos, sin};
+        for (const void *p : ptrs) require(uintptr_t(p) % 8 == 0, "prologue tensors must be 8-byte aligned");
+        check_device(q, "q");
+        check_device(out_q, "out_q");
+        check_device(k_cache, "k_cache");
+        if (tokens == 0) return 0;
+        QkArgs a{};
+        a.q = static_cast<const __nv_bfloat16 *>(q);
+        a.k = static_cast<const __nv_bfloat16 *>(k);
+        a.v = static_cast<const __nv_bfloat16 *>(v);
+        a.q_s0 = q_s0; a.q_s1 = q_s1; a.k_s0 = k_s0; a.k_s1 = k_s1; a.v_s0 = v_s0; a.v_s1 = v_s1;
+        a.qw = static_cast<const __nv_bfloat16 *>(q_weight);
+        a.kw = static_cast<const __nv_bfloat16 *>(k_weight);
+        a.cos = static_cast<const __nv_bfloat16 *>(cos);
+        a.sin = static_cast<const __nv_bfloat16 *>(sin);
+        a.cs0 = cos_s0; a.ss0 = sin_s0;
+        a.tokens = tokens; a.qh = q_heads; a.kh = kv_heads;
+        a.eps = eps;
+        a.round_products = round_products ? 1 : 0;
+        a.out_q = static_cast<__nv_bfloat16 *>(out_q);
+        a.k_cache = static_cast<__nv_bfloat16 *>(k_cache);
+        a.v_cache = static_cast<__nv_bfloat16 *>(v_cache);
+        a.cache_s0 = cache_slot_stride;
+        a.slots = slots;
+        a.num_slots = num_slots;
+        a.status = status;
+        const int64_t items = tokens * (q_heads + kv_heads);
+        k_qknorm_rope<<<unsigned(ceil_div(items, QK_WARPS)), QK_WARPS * 32, 0, as_stream(stream)>>>(a);
+        cuda_check(cudaGetLastError(), "QK norm / RoPE launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+}  // extern "C"

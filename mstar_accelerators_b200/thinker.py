@@ -14,7 +14,9 @@ bit-exact; the tcgen05 GEMM on fp16(q * d) operands for prefill-sized calls.
 swaps the plain ``nn.Linear`` projections (q_proj, k_proj, v_proj, qkv_proj, o_proj and
 lm_head) of a thinker module for it and returns how many it replaced. Tensor-parallel
 linears (which own a collective) are not plain ``nn.Linear`` and are left alone.
-QK-RMSNorm, RoPE and the attention itself stay with the module.
+``qknorm_rope`` is the next step of the prologue in one launch: per-head QK RMSNorm, the
+prepared MRoPE rotation and the KV-cache write, with the bf16 rounding points of the
+reference's fused op (qknorm_rope.py:9-53).
 """
 from __future__ import annotations
 
@@ -65,6 +67,45 @@ class Q8LinearB200(nn.Module):
 
     def close(self) -> None:
         self.lin.close()
+
+
+def qknorm_rope(q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor,
+                cos: torch.Tensor, sin: torch.Tensor, *, eps: float = 1e-6, round_products: bool = True,
+                v: torch.Tensor | None = None, k_cache: torch.Tensor | None = None,
+                v_cache: torch.Tensor | None = None, slots: torch.Tensor | None = None,
+                status: torch.Tensor | None = None):
+    """The thinker's QK RMSNorm + prepared MRoPE (+ KV write) in one launch (the reference's
+    fused op, qknorm_rope.py:9-53). q [T, Hq, 128], k / v [T, Hkv, 128], weights [128], cos / sin
+    [T, 128], all bf16. Returns (q_out [T, Hq, 128], k_cache); without a cache the normed, roped
+    k comes back as a fresh [T, Hkv, 128] tensor. slots [T] int64 picks each token's cache row."""
+    from . import native
+    from .linear import _stream
+    from .native import check, error_buffer
+    lib = native.require_capability()
+    T, Hq, D = q.shape
+    Hkv = k.shape[1]
+    for t in (q, k, q_weight, k_weight, cos, sin) + ((v,) if v is not None else ()):
+        if t.dtype != torch.bfloat16 or not t.is_cuda or t.stride(-1) != 1:
+            raise ValueError("bf16 CUDA tensors with unit last stride expected")
+    out_q = torch.empty((T, Hq, D), dtype=torch.bfloat16, device=q.device)
+    if k_cache is None:
+        k_cache = torch.empty((T, Hkv, D), dtype=torch.bfloat16, device=q.device)
+    slot_stride = k_cache.stride(0)
+    if v is not None and (v_cache is None or v_cache.stride(0) != slot_stride):
+        raise ValueError("v needs a v_cache laid out like k_cache")
+    if slots is not None and (slots.dtype != torch.int64 or slots.shape != (T,)):
+        raise ValueError("slots must be int64 [T]")
+    st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=q.device)
+    e = error_buffer()
+    check(lib.mstar_b200_qknorm_rope(
+        q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), k.stride(1),
+        v.data_ptr() if v is not None else None, v.stride(0) if v is not None else 0,
+        v.stride(1) if v is not None else 0, q_weight.data_ptr(), k_weight.data_ptr(), cos.data_ptr(), cos.stride(0),
+        sin.data_ptr(), sin.stride(0), T, Hq, Hkv, D, float(eps), int(round_products), out_q.data_ptr(),
+        k_cache.data_ptr(), v_cache.data_ptr() if v is not None else None, slot_stride,
+        slots.data_ptr() if slots is not None else None, k_cache.shape[0], st.data_ptr(), _stream(q.device),
+        e, len(e)), e, "B200 QK norm / RoPE")
+    return out_q, k_cache
 
 
 def thinker_linear_targets(module: nn.Module) -> list[tuple[nn.Module, str, nn.Linear]]:
