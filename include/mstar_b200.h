@@ -305,6 +305,27 @@ MSTAR_B200_API int mstar_b200_tp_reduce_multicast(const float *mc_part, int32_t 
     const float *bias, float *x, const float *ln_weight, const float *ln_bias, float ln_eps, void *mc_staged,
     int64_t row0, int32_t rounding, int32_t *status, void *stream, char *error, size_t error_size);
 
+/* --- exact Q8_0 GEMM (ggml_vec_dot_q8_0_q8_0 generic order, ggml-cpu/quants.c:451-480, at
+ * prefill row counts; the tcgen05 int8 tensor pipe computes each block's integer dot) ---
+ * q8_exact_weights: canonical Q8_0 blocks [rows][width/32] -> int8 quants [rows][width]
+ * (weights_i8, rows * width bytes, 16-byte aligned) and fp32 scales [width/32][pad]
+ * (scales, pad = q8_exact_pad(rows), rows beyond `rows` zero).
+ * q8_exact_activations: fp32 rows [rows][x_stride] -> their Q8_0 quantization (rounding
+ * as MSTAR_B200_Q8_*) as int8 quants [rows][width] and fp32 scales [rows][width/32]
+ * (each d rounded through fp16, as the block stores it); status bit 1: a nonfinite input.
+ * gemm_q8_exact: out[r][n] = sum over blocks b, in order, of float(sumi) * (d_w * d_x)
+ * (+ bias[n] after the sum), fp32 [rows][out_stride]; bit-identical to the decode GEMV
+ * and to ggml's generic order for every row count. status bit 2: a bounded pipeline
+ * wait timed out. Stream-ordered; operands from the two calls above. */
+MSTAR_B200_API int64_t mstar_b200_q8_exact_pad(int64_t rows);
+MSTAR_B200_API int mstar_b200_q8_exact_weights(const void *blocks, uint64_t bytes, int64_t rows, int64_t width,
+    void *weights_i8, float *scales, void *stream, char *error, size_t error_size);
+MSTAR_B200_API int mstar_b200_q8_exact_activations(const float *x, int64_t x_stride, int64_t rows, int64_t width,
+    int32_t rounding, void *x_i8, float *scales, int32_t *status, void *stream, char *error, size_t error_size);
+MSTAR_B200_API int mstar_b200_gemm_q8_exact(const void *x_i8, const float *x_scales, int64_t rows, const void *w_i8,
+    const float *w_scales, int64_t out_features, int64_t width, const float *bias, float *out, int64_t out_stride,
+    int32_t *status, void *stream, char *error, size_t error_size);
+
 /* --- thinker attention prologue (implementations/qwen3_omni/amd/qknorm_rope.py:9-53, the
  * fused QK RMSNorm + prepared MRoPE op; KV write as cp_kernels.py:16-58) ---
  * qknorm_rope: for every token t and head of 128 bf16 values: x = q or k head row,

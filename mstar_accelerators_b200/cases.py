@@ -84,6 +84,22 @@ def gemm_encoder_large_layer():
         fc2.gemm(h, out=x, residual=x)
 
 
+def gemm_fc1_exact_and_f16():
+    """The Whisper-large-v3 fc1 shape (N=5120, K=1280) at 24,000 rows, fp32 output, through the
+    exact int8-tensor-pipe GEMM and through the fp16-staged GEMM, two calls each (launch order:
+    exact activation quantization, exact GEMM, fp16 staging, fp16 GEMM, twice)."""
+    from .linear import BlockLinear, stage_rows
+    g = torch.Generator(device="cuda").manual_seed(1)
+    lin = BlockLinear(torch.randn(5120, 1280, device="cuda", generator=g) * 0.02)
+    lin.prepare_gemm(24000)
+    lin.prepare_exact()
+    x = torch.randn(24000, 1280, device="cuda", generator=g)
+    out = torch.empty(24000, 5120, device="cuda")
+    for _ in range(2):
+        lin.exact(x, out=out)
+        lin.gemm(stage_rows(x), out=out)
+
+
 def _encoder(cfg, batch, calls):
     from .encoder import WhisperEncoderB200, synthetic_mel, synthetic_weights
     w = {k: v.cuda() for k, v in synthetic_weights(cfg, seed=1).items()}
@@ -135,6 +151,7 @@ def moe_prefill_4096_q8():
 
 CASES = {"readout-q4-b32": readout_q4_b32, "decode-step-b32": decode_step_b32,
          "gemm-q8-8192x5120x1280": gemm_q8_8192x5120x1280, "gemm-encoder-large-layer": gemm_encoder_large_layer,
+         "gemm-fc1-exact-and-f16": gemm_fc1_exact_and_f16,
          "encoder-tiny-b1": encoder_tiny_b1,
          "encoder-large-b16": encoder_large_b16, "moe-prefill-4096": moe_prefill_4096,
          "moe-prefill-4096-q8": moe_prefill_4096_q8}

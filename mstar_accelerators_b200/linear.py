@@ -211,6 +211,7 @@ class BlockLinear:
             raise native.NativeError("B200 linear preparation: " + e.value.decode(errors="replace"))
         self.handle = handle
         self.has_bias = bias_t is not None
+        self.bias_t = bias_t
         self.blocks = blocks  # canonical bytes stay available to callers (and tests)
         self.gemm_rows = 0
         self.readout_tiles = False
@@ -344,6 +345,49 @@ class BlockLinear:
                                               native.ROUNDING[rounding], status.data_ptr(), _stream(staged.device),
                                               e, len(e)),
               e, "B200 GEMM")
+        return out
+
+    def prepare_exact(self) -> None:
+        """Lay the Q8_0 weights out for the exact int8-tensor-pipe GEMM (int8 quants + fp32 scales)."""
+        if self.fmt != "q8_0":
+            raise ValueError("the exact GEMM takes Q8_0 weights")
+        if getattr(self, "_exact", None) is not None:
+            return
+        pad = int(self.lib.mstar_b200_q8_exact_pad(self.rows))
+        wq = torch.empty((self.rows, self.width), dtype=torch.int8, device=self.device)
+        ws = torch.zeros((self.width // 32, pad), dtype=torch.float32, device=self.device)
+        e = error_buffer()
+        check(self.lib.mstar_b200_q8_exact_weights(self.blocks.data_ptr(), _nbytes(self.blocks), self.rows, self.width,
+                                                   wq.data_ptr(), ws.data_ptr(), _stream(self.device), e, len(e)),
+              e, "B200 exact GEMM weights")
+        self._exact = (wq, ws)
+
+    def exact(self, x: torch.Tensor, *, out: torch.Tensor | None = None, bias: bool = True,
+              rounding: str = "arm", status: torch.Tensor | None = None) -> torch.Tensor:
+        """ggml_mul_mat(W, x) (+ bias) in ggml's generic block order for any row count: x's rows are
+        Q8_0-quantized, every block's integer dot runs on the int8 tensor pipe and the blocks are
+        rescaled and summed in order (bit-identical to the decode GEMV); slower than the fp16 GEMM."""
+        self.prepare_exact()
+        _require_cuda(x, "activations", torch.float32)
+        x2 = _rows(x, self.width)
+        m = x2.shape[0]
+        if out is None:
+            out = torch.empty((m, self.rows), dtype=torch.float32, device=x.device)
+        if status is None:
+            status = torch.zeros(1, dtype=torch.int32, device=x.device)
+        xq = torch.empty((m, self.width), dtype=torch.int8, device=x.device)
+        xs = torch.empty((m, self.width // 32), dtype=torch.float32, device=x.device)
+        wq, ws = self._exact
+        e = error_buffer()
+        check(self.lib.mstar_b200_q8_exact_activations(x2.data_ptr(), x2.stride(0), m, self.width,
+                                                       native.ROUNDING[rounding], xq.data_ptr(), xs.data_ptr(),
+                                                       status.data_ptr(), _stream(x.device), e, len(e)),
+              e, "B200 exact GEMM activations")
+        check(self.lib.mstar_b200_gemm_q8_exact(xq.data_ptr(), xs.data_ptr(), m, wq.data_ptr(), ws.data_ptr(), self.rows,
+                                                self.width, self.bias_t.data_ptr() if (bias and self.has_bias) else None,
+                                                out.data_ptr(), out.stride(0), status.data_ptr(), _stream(x.device),
+                                                e, len(e)),
+              e, "B200 exact GEMM")
         return out
 
     def set_split(self, warps: int) -> None:

@@ -61,6 +61,10 @@ SIGNATURES = {
                                               C.c_int32, _vp, _vp, *_err]),
     "mstar_b200_set_wait_limits": (_int, [_i64, _i64, *_err]),
     "mstar_b200_categorical_workspace": (_u64, [_i64]),
+    "mstar_b200_q8_exact_pad": (_i64, [_i64]),
+    "mstar_b200_q8_exact_weights": (_int, [_vp, _u64, _i64, _i64, _vp, _vp, _vp, *_err]),
+    "mstar_b200_q8_exact_activations": (_int, [_vp, _i64, _i64, _i64, C.c_int32, _vp, _vp, _vp, _vp, *_err]),
+    "mstar_b200_gemm_q8_exact": (_int, [_vp, _vp, _i64, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, *_err]),
     "mstar_b200_qknorm_rope": (_int, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _i64,
                                       _i64, C.c_int32, C.c_int32, C.c_int32, C.c_float, C.c_int32, _vp, _vp, _vp, _i64,
                                       _vp, _i64, _vp, _vp, *_err]),
