@@ -100,6 +100,31 @@ def gemm_fc1_exact_and_f16():
         lin.gemm(stage_rows(x), out=out)
 
 
+def thinker_stack_48():
+    """The Qwen3-Omni thinker 48-layer stack (Q8_0 linears and experts) on one GPU: 32 sequences of
+    1024 synthetic prompt tokens, then 128 greedy decode steps; prints the device times."""
+    import json
+    from .thinker_stack import ThinkerStackB200, ThinkerStackConfig
+    cfg = ThinkerStackConfig()
+    stack = ThinkerStackB200(cfg, max_seqs=32, max_len=1024 + 128)
+    g = torch.Generator().manual_seed(3)
+    prompt = torch.randint(0, cfg.vocab, (32, 1024), generator=g).cuda()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    torch.cuda.synchronize()
+    ev[0].record()
+    _, tok = stack.prefill(prompt)
+    ev[1].record()
+    for _ in range(128):
+        _, tok = stack.decode(tok)
+    ev[2].record()
+    torch.cuda.synchronize()
+    pre, dec = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    print(json.dumps({"prefill_ms": round(pre, 2), "prefill_tokens_per_s": round(32 * 1024 / (pre / 1e3), 1),
+                      "decode_ms_per_step": round(dec / 128, 3), "decode_tokens_per_s": round(32 * 128 / (dec / 1e3), 1),
+                      "status": int(stack.status.item())}))
+    stack.close()
+
+
 def _encoder(cfg, batch, calls):
     from .encoder import WhisperEncoderB200, synthetic_mel, synthetic_weights
     w = {k: v.cuda() for k, v in synthetic_weights(cfg, seed=1).items()}
@@ -151,7 +176,7 @@ def moe_prefill_4096_q8():
 
 CASES = {"readout-q4-b32": readout_q4_b32, "decode-step-b32": decode_step_b32,
          "gemm-q8-8192x5120x1280": gemm_q8_8192x5120x1280, "gemm-encoder-large-layer": gemm_encoder_large_layer,
-         "gemm-fc1-exact-and-f16": gemm_fc1_exact_and_f16,
+         "gemm-fc1-exact-and-f16": gemm_fc1_exact_and_f16, "thinker-stack-48": thinker_stack_48,
          "encoder-tiny-b1": encoder_tiny_b1,
          "encoder-large-b16": encoder_large_b16, "moe-prefill-4096": moe_prefill_4096,
          "moe-prefill-4096-q8": moe_prefill_4096_q8}

@@ -1,0 +1,210 @@
+"""Qwen3-Omni thinker decoder stack on B200 with Q8_0 linears (the 48-layer workload).
+
+The layer is the reference's thinker layer (implementations/qwen3_omni/amd/
+thinker_model.py:106-148, transformers' Qwen3OmniMoeThinkerTextDecoderLayer):
+    h = RMSNorm(x); q, k, v = Wq h, Wk h, Wv h
+    q, k = QK-RMSNorm + RoPE(q, k); K/V appended to the cache
+    x = x + Wo attention(q, K, V)              (GQA, causal)
+    h = RMSNorm(x); x = x + MoE(h)             (router top-8, SwiGLU experts, slot-order combine)
+and the stack ends with the final RMSNorm and the lm_head with greedy argmax.
+Every linear is this library's block-quantized contraction: the fused QKV and o_proj
+as Q8_0 (split-K GEMV for <= 32 rows, bit-exact with ggml's generic order; the
+tcgen05 GEMM for prefill rows), the experts as the grouped tcgen05 MoE kernels
+(Q8_0 or bf16 experts), lm_head as the one-launch tile readout (GEMV + argmax).
+QK-RMSNorm + RoPE + the KV write are one launch (mstar_b200_qknorm_rope). RMSNorm,
+the embedding lookup and attention (torch SDPA over the bf16 cache, GQA) are torch,
+as the reference leaves them to its runtime. Text-only positions: the MRoPE sections
+all take the same position, so the prepared cos / sin rows are the plain rotary ones
+(theta 1e6). bf16 residual stream, as transformers runs the layer.
+
+One process, one GPU (tensor / expert parallelism 1): the weights of the 48 Q8_0
+layers (~31 GB, ~60 GB with the experts' fp16 GEMM operands) fit one B200.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from .linear import BlockLinear, pack
+from .moe import ThinkerMoEB200, route
+from .thinker import qknorm_rope
+
+
+@dataclass(frozen=True)
+class ThinkerStackConfig:
+    hidden: int = 2048
+    layers: int = 48
+    q_heads: int = 32
+    kv_heads: int = 4
+    head_dim: int = 128
+    experts: int = 128
+    top_k: int = 8
+    moe_intermediate: int = 768
+    vocab: int = 151936
+    rope_theta: float = 1e6
+    eps: float = 1e-6
+
+
+def layer_weights(cfg: ThinkerStackConfig, layer: int, seed: int = 1, device="cuda") -> dict:
+    """Seeded random weights of one layer, bf16: matrices N(0, 0.02), norm weights 1 + N(0, 0.02)."""
+    g = torch.Generator(device=device).manual_seed(seed * 1000 + layer)
+    H, D, E, I = cfg.hidden, cfg.head_dim, cfg.experts, cfg.moe_intermediate
+
+    def n(*shape, one=False):
+        t = torch.randn(shape, generator=g, device=device) * 0.02
+        return (t + 1.0 if one else t).to(torch.bfloat16)
+
+    return {"ln1": n(H, one=True), "q": n(cfg.q_heads * D, H), "k": n(cfg.kv_heads * D, H), "v": n(cfg.kv_heads * D, H),
+            "q_norm": n(D, one=True), "k_norm": n(D, one=True), "o": n(H, cfg.q_heads * D), "ln2": n(H, one=True),
+            "router": n(E, H), "w1": n(E, 2 * I, H), "w2": n(E, H, I)}
+
+
+def head_weights(cfg: ThinkerStackConfig, seed: int = 1, device="cuda") -> dict:
+    g = torch.Generator(device=device).manual_seed(seed * 1000 + 999)
+    return {"embed": (torch.randn((cfg.vocab, cfg.hidden), generator=g, device=device) * 0.02).to(torch.bfloat16),
+            "norm": (1.0 + torch.randn(cfg.hidden, generator=g, device=device) * 0.02).to(torch.bfloat16),
+            "lm_head": (torch.randn((cfg.vocab, cfg.hidden), generator=g, device=device) * 0.02).to(torch.bfloat16)}
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """transformers' Qwen3OmniMoeThinkerTextRMSNorm: fp32 normalisation, bf16 before the weight."""
+    h = x.float()
+    h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + eps)
+    return w * h.to(x.dtype)
+
+
+def rotary(positions: torch.Tensor, cfg: ThinkerStackConfig):
+    """Prepared cos / sin rows [T, head_dim] (bf16) of the plain rotary embedding."""
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, cfg.head_dim, 2, device=positions.device, dtype=torch.float32)
+                                    / cfg.head_dim))
+    f = positions.float()[:, None] * inv[None, :]
+    emb = torch.cat([f, f], dim=-1)
+    return emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+
+
+class ThinkerStackB200:
+    """The thinker stack for up to ``max_seqs`` sequences of ``max_len`` positions on one GPU."""
+
+    def __init__(self, cfg: ThinkerStackConfig = ThinkerStackConfig(), *, max_seqs: int = 32, max_len: int = 1152,
+                 seed: int = 1, experts: str = "q8_0", gemm_rows: int = 4096, weights=None, device="cuda"):
+        self.cfg, self.max_seqs, self.max_len = cfg, max_seqs, max_len
+        self.device = torch.device(device)
+        self.gemm_rows = gemm_rows
+        H, D = cfg.hidden, cfg.head_dim
+        self.layers = []
+        for i in range(cfg.layers):
+            w = weights(i) if weights is not None else layer_weights(cfg, i, seed, self.device)
+            qkv = BlockLinear(torch.cat([w["q"], w["k"], w["v"]]).float().contiguous(), fmt="q8_0")
+            o = BlockLinear(w["o"].float().contiguous(), fmt="q8_0")
+            qkv.prepare_gemm(gemm_rows)
+            o.prepare_gemm(gemm_rows)
+            if experts == "q8_0":
+                I = cfg.moe_intermediate
+                b1 = pack(w["w1"].float().reshape(-1, H), "q8_0", preround=False).reshape(cfg.experts, 2 * I, -1)
+                b2 = pack(w["w2"].float().reshape(-1, I), "q8_0", preround=False).reshape(cfg.experts, H, -1)
+                moe = ThinkerMoEB200(b1, b2, fmt="q8_0", top_k=cfg.top_k, max_tokens=gemm_rows, intermediate=I,
+                                     hidden=H)
+                del b1, b2
+            else:
+                moe = ThinkerMoEB200(w["w1"], w["w2"], fmt="bf16", top_k=cfg.top_k, max_tokens=gemm_rows)
+            self.layers.append({"ln1": w["ln1"], "ln2": w["ln2"], "q_norm": w["q_norm"], "k_norm": w["k_norm"],
+                                "router": w["router"].contiguous(), "qkv": qkv, "o": o, "moe": moe})
+            del w
+        hw = head_weights(cfg, seed, self.device)
+        self.embed, self.final_norm = hw["embed"], hw["norm"]
+        self.lm_head = BlockLinear(hw["lm_head"].float().contiguous(), fmt="q8_0")
+        self.lm_head.prepare_readout()
+        slots = max_seqs * max_len
+        self.k_cache = [torch.zeros((slots, cfg.kv_heads, D), dtype=torch.bfloat16, device=self.device)
+                        for _ in range(cfg.layers)]
+        self.v_cache = [torch.zeros_like(c) for c in self.k_cache]
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.length = 0
+
+    # ------------------------------------------------------------------ pieces
+    def _linear(self, lin: BlockLinear, x: torch.Tensor) -> torch.Tensor:
+        x = x.float().contiguous()
+        out = torch.empty((x.shape[0], lin.rows), dtype=torch.float32, device=x.device)
+        step = self.gemm_rows if x.shape[0] >= 64 else max(x.shape[0], 1)
+        for r0 in range(0, x.shape[0], step):
+            lin(x[r0:r0 + step], out=out[r0:r0 + step])
+        return out
+
+    def _moe(self, L, h: torch.Tensor) -> torch.Tensor:
+        out = torch.empty_like(h)
+        for r0 in range(0, h.shape[0], self.gemm_rows):
+            part = h[r0:r0 + self.gemm_rows]
+            w, ids = route(part, L["router"], top_k=self.cfg.top_k)
+            out[r0:r0 + self.gemm_rows] = L["moe"](part, w, ids)
+        return out
+
+    def _layer(self, i: int, x: torch.Tensor, S: int, n: int, start: int) -> torch.Tensor:
+        """x [S * n, H] bf16: n new positions start .. start + n - 1 of each of S sequences."""
+        cfg, L = self.cfg, self.layers[i]
+        D, Hq, Hk = cfg.head_dim, cfg.q_heads, cfg.kv_heads
+        T = S * n
+        h = rms_norm(x, L["ln1"], cfg.eps)
+        qkv = self._linear(L["qkv"], h).to(torch.bfloat16)
+        q = qkv[:, :Hq * D].view(T, Hq, D)
+        k = qkv[:, Hq * D:(Hq + Hk) * D].view(T, Hk, D)
+        v = qkv[:, (Hq + Hk) * D:].view(T, Hk, D)
+        pos = torch.arange(start, start + n, device=x.device).repeat(S)
+        cos, sin = rotary(pos, cfg)
+        slots = (torch.arange(S, device=x.device).repeat_interleave(n) * self.max_len + pos).to(torch.int64)
+        q, _ = qknorm_rope(q, k, L["q_norm"], L["k_norm"], cos, sin, eps=cfg.eps, v=v, k_cache=self.k_cache[i],
+                           v_cache=self.v_cache[i], slots=slots, status=self.status)
+        ctx = start + n
+        kk = self.k_cache[i].view(self.max_seqs, self.max_len, Hk, D)[:S, :ctx].transpose(1, 2)
+        vv = self.v_cache[i].view(self.max_seqs, self.max_len, Hk, D)[:S, :ctx].transpose(1, 2)
+        qq = q.view(S, n, Hq, D).transpose(1, 2)
+        if n == 1:
+            att = F.scaled_dot_product_attention(qq, kk, vv, scale=D ** -0.5, enable_gqa=True)
+        elif start == 0:
+            att = F.scaled_dot_product_attention(qq, kk, vv, is_causal=True, scale=D ** -0.5, enable_gqa=True)
+        else:
+            mask = torch.ones((n, ctx), dtype=torch.bool, device=x.device).tril(ctx - n)
+            att = F.scaled_dot_product_attention(qq, kk, vv, attn_mask=mask, scale=D ** -0.5, enable_gqa=True)
+        att = att.transpose(1, 2).reshape(T, Hq * D)
+        x = x + self._linear(L["o"], att).to(torch.bfloat16)
+        h = rms_norm(x, L["ln2"], cfg.eps)
+        return x + self._moe(L, h)
+
+    def _readout(self, last: torch.Tensor):
+        h = rms_norm(last, self.final_norm, self.cfg.eps).float().contiguous()
+        logits = torch.empty((h.shape[0], self.cfg.vocab), dtype=torch.float32, device=h.device)
+        tokens = torch.empty(h.shape[0], dtype=torch.int64, device=h.device)
+        self.lm_head.readout(h, logits=logits, token=tokens, status=self.status)
+        return logits, tokens
+
+    # ------------------------------------------------------------------ walks
+    def prefill(self, tokens: torch.Tensor):
+        """tokens [S, n] -> (logits [S, vocab] of each last position, greedy next tokens [S])."""
+        S, n = tokens.shape
+        if S > self.max_seqs or n > self.max_len:
+            raise ValueError("prompt exceeds the prepared capacity")
+        x = self.embed[tokens.reshape(-1)]
+        for i in range(self.cfg.layers):
+            x = self._layer(i, x, S, n, 0)
+        self.length, self.seqs = n, S
+        return self._readout(x.view(S, n, -1)[:, -1])
+
+    def decode(self, tokens: torch.Tensor):
+        """tokens [S] at the next position of every sequence -> (logits [S, vocab], next tokens [S])."""
+        S = tokens.shape[0]
+        if self.length >= self.max_len:
+            raise ValueError("sequence capacity exhausted")
+        x = self.embed[tokens.reshape(-1)]
+        for i in range(self.cfg.layers):
+            x = self._layer(i, x, S, 1, self.length)
+        self.length += 1
+        return self._readout(x)
+
+    def close(self) -> None:
+        for L in self.layers:
+            L["qkv"].close()
+            L["o"].close()
+            L["moe"].close()
+        self.lm_head.close()
