@@ -16,9 +16,10 @@
 // Kernel: persistent, one CTA per SM over 128 x 128 tiles, 10 warps: warp 0 TMA
 // producer (int8 boxes of 128 bytes = 4 blocks of K, 128B swizzle, 4-stage ring),
 // warp 1 one thread issuing one MMA per block into a ring of four 128-column
-// TMEM slots, warps 2-9 epilogue (two per TMEM lane quarter, 64 columns each):
-// tcgen05.ld the block's sums, release the slot, fold in fp32. Every wait is
-// bounded (status bit value 2).
+// TMEM slots, warps 2-17 epilogue (four per TMEM lane quarter, 32 columns each):
+// tcgen05.ld the block's sums, release the slot, fold in fp32 with the packed
+// f32x2 pipe (each lane an IEEE RN operation). Every wait is bounded (status bit
+// value 2).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -33,7 +34,7 @@ constexpr int EX_STAGES = 4;
 constexpr int EX_A_BYTES = EX_BM * EX_BKB, EX_B_BYTES = EX_BN * EX_BKB;
 constexpr int EX_STAGE_BYTES = EX_A_BYTES + EX_B_BYTES;
 constexpr int EX_SLOTS = 4;                 // TMEM accumulators of 128 columns
-constexpr int EX_EPI_WARPS = 8;
+constexpr int EX_EPI_WARPS = 16;
 constexpr int EX_THREADS = 64 + 32 * EX_EPI_WARPS;
 constexpr int EX_GROUP_M = 8;
 // instruction descriptor: D s32 (bits 4-5 = 2), A and B signed 8-bit (bits 7-9, 10-12 = 1),
@@ -58,9 +59,13 @@ __device__ __forceinline__ void umma_i8(uint32_t tmem, uint64_t da, uint64_t db)
                  : "memory");
 }
 
-// exact int -> float for |i| < 2^22 (a block dot is at most 32 * 127 * 127 < 2^19)
-__device__ __forceinline__ float i2f_exact(uint32_t bits) {
-    return __fsub_rn(__int_as_float(int(bits) + 0x4B400000), 12582912.0f);
+// packed fp32 pair subtraction, each lane an IEEE RN operation
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+    float2 r;
+    asm("{.reg .b64 ra, rb, rc; mov.b64 ra, {%2,%3}; mov.b64 rb, {%4,%5}; sub.rn.f32x2 rc, ra, rb; "
+        "mov.b64 {%0,%1}, rc;}"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
 }
 
 __global__ void __launch_bounds__(EX_THREADS, 1)
@@ -158,16 +163,17 @@ __global__ void __launch_bounds__(EX_THREADS, 1)
         }
     } else {
         const int q = warp & 3;
-        const int c0 = ((warp - 2) / 4) * 64;   // first of this warp's 64 columns
+        const int c0 = ((warp - 2) / 4) * 32;   // first of this warp's 32 columns
+        const float2 magic = make_float2(12582912.0f, 12582912.0f);
         int64_t blk = 0;
         for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
             int64_t m0, n0;
             tile_coords(tile, m0, n0);
             const int64_t row = m0 + 32 * q + lane;
             const bool live = row < a.M;
-            float acc[64];
+            float2 acc[16];
 #pragma unroll
-            for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
+            for (int j = 0; j < 16; ++j) acc[j] = make_float2(0.0f, 0.0f);
             bool ok = true;
             for (int64_t b = 0; b < nb; ++b, ++blk) {
                 const int slot = int(blk % EX_SLOTS);
@@ -177,39 +183,34 @@ __global__ void __launch_bounds__(EX_THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                uint32_t r0[32], r1[32];
-                const uint32_t taddr = tmem + (uint32_t(32 * q) << 16) + uint32_t(slot * EX_BN + c0);
-                tmem_ld32(taddr, r0);
-                tmem_ld32(taddr + 32, r1);
+                uint32_t r[32];
+                tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(slot * EX_BN + c0), r);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(blk_empty + slot);   // the slot is free for the next block
                 const float dx = live ? __ldg(a.x_scale + row * nb + b) : 0.0f;
+                const float2 dx2 = make_float2(dx, dx);
                 const float4 *ws = reinterpret_cast<const float4 *>(a.w_scale + b * a.n_pad + n0 + c0);
 #pragma unroll
                 for (int j = 0; j < 32; j += 4) {
                     const float4 w4 = __ldg(ws + j / 4);
-                    acc[j] = __fadd_rn(acc[j], __fmul_rn(i2f_exact(r0[j]), __fmul_rn(w4.x, dx)));
-                    acc[j + 1] = __fadd_rn(acc[j + 1], __fmul_rn(i2f_exact(r0[j + 1]), __fmul_rn(w4.y, dx)));
-                    acc[j + 2] = __fadd_rn(acc[j + 2], __fmul_rn(i2f_exact(r0[j + 2]), __fmul_rn(w4.z, dx)));
-                    acc[j + 3] = __fadd_rn(acc[j + 3], __fmul_rn(i2f_exact(r0[j + 3]), __fmul_rn(w4.w, dx)));
-                }
-#pragma unroll
-                for (int j = 0; j < 32; j += 4) {
-                    const float4 w4 = __ldg(ws + 8 + j / 4);
-                    acc[32 + j] = __fadd_rn(acc[32 + j], __fmul_rn(i2f_exact(r1[j]), __fmul_rn(w4.x, dx)));
-                    acc[33 + j] = __fadd_rn(acc[33 + j], __fmul_rn(i2f_exact(r1[j + 1]), __fmul_rn(w4.y, dx)));
-                    acc[34 + j] = __fadd_rn(acc[34 + j], __fmul_rn(i2f_exact(r1[j + 2]), __fmul_rn(w4.z, dx)));
-                    acc[35 + j] = __fadd_rn(acc[35 + j], __fmul_rn(i2f_exact(r1[j + 3]), __fmul_rn(w4.w, dx)));
+                    // float(sumi): the int added to 1.5 * 2^23's bit pattern, then 1.5 * 2^23 taken off (exact)
+                    const float2 s0 = sub2(make_float2(__int_as_float(int(r[j]) + 0x4B400000),
+                                                       __int_as_float(int(r[j + 1]) + 0x4B400000)), magic);
+                    const float2 s1 = sub2(make_float2(__int_as_float(int(r[j + 2]) + 0x4B400000),
+                                                       __int_as_float(int(r[j + 3]) + 0x4B400000)), magic);
+                    acc[j / 2] = add2(acc[j / 2], mul2(s0, mul2(make_float2(w4.x, w4.y), dx2)));
+                    acc[j / 2 + 1] = add2(acc[j / 2 + 1], mul2(s1, mul2(make_float2(w4.z, w4.w), dx2)));
                 }
             }
             if (!ok) break;
             if (live) {
                 float *o = a.out + row * a.ldo + n0 + c0;
 #pragma unroll
-                for (int j = 0; j < 64; ++j) {
-                    const int64_t n = n0 + c0 + j;
-                    if (n < a.N) o[j] = a.bias ? __fadd_rn(acc[j], a.bias[n]) : acc[j];
+                for (int j = 0; j < 16; ++j) {
+                    const int64_t n = n0 + c0 + 2 * j;
+                    if (n < a.N) o[2 * j] = a.bias ? __fadd_rn(acc[j].x, a.bias[n]) : acc[j].x;
+                    if (n + 1 < a.N) o[2 * j + 1] = a.bias ? __fadd_rn(acc[j].y, a.bias[n + 1]) : acc[j].y;
                 }
             }
         }
