@@ -34,7 +34,11 @@ def _worker(rank, world, port, results, multicast):
         from mstar_accelerators_b200.encoder_tp import WhisperEncoderTP
         w = synthetic_weights(TINY, seed=1)
         mel = synthetic_mel(TINY, 2, seed=2).cuda()
-        tp = WhisperEncoderTP(w, TINY, max_batch=2, multicast=multicast)
+        try:
+            tp = WhisperEncoderTP(w, TINY, max_batch=2, multicast=multicast)
+        except ValueError:   # no multicast object on this platform
+            results[rank] = None
+            return
         got = tp(mel)
         assert int(tp.status.item()) == 0
         ref = WhisperEncoderB200({k: v.cuda() for k, v in w.items()}, TINY, max_batch=2)(mel)
@@ -57,18 +61,19 @@ def _port():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("multicast", [False, None])
+@pytest.mark.parametrize("multicast", [False, True])
 def test_tensor_parallel_encoder_matches_single_gpu(multicast):
-    """multicast False: peer loads and stores; None: the NVSwitch multicast path where the
-    platform offers it (the result records which path ran)."""
+    """multicast False: peer loads and stores; True: the NVSwitch multicast path (skipped where
+    the platform has no multicast object for the symmetric buffers)."""
     world = 2
     ctx = mp.get_context("spawn")
     with ctx.Manager() as manager:
         results = manager.dict()
         mp.start_processes(_worker, args=(world, _port(), results, multicast), nprocs=world, join=True,
                            start_method="spawn")
+        if any(results[r] is None for r in range(world)):
+            pytest.skip("no NVSwitch multicast on this platform")
         for rank in range(world):
             same, mx, mean, used = results[rank]
             assert same and mx <= 3e-2 and mean <= 2e-3, (rank, mx, mean, used)
-            if multicast is False:
-                assert not used
+            assert used == multicast
