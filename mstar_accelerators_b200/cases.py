@@ -102,23 +102,28 @@ def gemm_fc1_exact_and_f16():
 
 def thinker_stack_48():
     """The Qwen3-Omni thinker 48-layer stack (Q8_0 linears and experts) on one GPU: 32 sequences of
-    1024 synthetic prompt tokens, then 128 greedy decode steps; prints the device times."""
+    1024 synthetic prompt tokens (a warm-up prefill, then the timed one), then 128 greedy decode
+    steps, each one CUDA-graph replay of the 48 layers and the readout; prints the device times."""
     import json
     from .thinker_stack import ThinkerStackB200, ThinkerStackConfig
     cfg = ThinkerStackConfig()
-    stack = ThinkerStackB200(cfg, max_seqs=32, max_len=1024 + 128)
+    stack = ThinkerStackB200(cfg, max_seqs=32, max_len=1024 + 128 + 4)
     g = torch.Generator().manual_seed(3)
     prompt = torch.randint(0, cfg.vocab, (32, 1024), generator=g).cuda()
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    stack.prefill(prompt)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     torch.cuda.synchronize()
     ev[0].record()
     _, tok = stack.prefill(prompt)
     ev[1].record()
-    for _ in range(128):
-        _, tok = stack.decode(tok)
+    for _ in range(2):       # capture and a first replay
+        _, tok = stack.decode(tok, graph=True)
     ev[2].record()
+    for _ in range(128):
+        _, tok = stack.decode(tok, graph=True)
+    ev[3].record()
     torch.cuda.synchronize()
-    pre, dec = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    pre, dec = ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3])
     print(json.dumps({"prefill_ms": round(pre, 2), "prefill_tokens_per_s": round(32 * 1024 / (pre / 1e3), 1),
                       "decode_ms_per_step": round(dec / 128, 3), "decode_tokens_per_s": round(32 * 128 / (dec / 1e3), 1),
                       "status": int(stack.status.item())}))

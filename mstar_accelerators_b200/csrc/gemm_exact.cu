@@ -17,9 +17,8 @@
 // producer (int8 boxes of 128 bytes = 4 blocks of K, 128B swizzle, 4-stage ring),
 // warp 1 one thread issuing one MMA per block into a ring of four 128-column
 // TMEM slots, warps 2-17 epilogue (four per TMEM lane quarter, 32 columns each):
-// tcgen05.ld the block's sums, release the slot, fold in fp32 with the packed
-// f32x2 pipe (each lane an IEEE RN operation). Every wait is bounded (status bit
-// value 2).
+// tcgen05.ld the block's sums, release the slot, fold in fp32. Every wait is
+// bounded (status bit value 2).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -59,13 +58,9 @@ __device__ __forceinline__ void umma_i8(uint32_t tmem, uint64_t da, uint64_t db)
                  : "memory");
 }
 
-// packed fp32 pair subtraction, each lane an IEEE RN operation
-__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
-    float2 r;
-    asm("{.reg .b64 ra, rb, rc; mov.b64 ra, {%2,%3}; mov.b64 rb, {%4,%5}; sub.rn.f32x2 rc, ra, rb; "
-        "mov.b64 {%0,%1}, rc;}"
-        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-    return r;
+// exact int -> float for |i| < 2^22 (a block dot is at most 32 * 127 * 127 < 2^19)
+__device__ __forceinline__ float i2f_exact(uint32_t bits) {
+    return __fsub_rn(__int_as_float(int(bits) + 0x4B400000), 12582912.0f);
 }
 
 __global__ void __launch_bounds__(EX_THREADS, 1)
@@ -164,16 +159,15 @@ __global__ void __launch_bounds__(EX_THREADS, 1)
     } else {
         const int q = warp & 3;
         const int c0 = ((warp - 2) / 4) * 32;   // first of this warp's 32 columns
-        const float2 magic = make_float2(12582912.0f, 12582912.0f);
         int64_t blk = 0;
         for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
             int64_t m0, n0;
             tile_coords(tile, m0, n0);
             const int64_t row = m0 + 32 * q + lane;
             const bool live = row < a.M;
-            float2 acc[16];
+            float acc[32];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) acc[j] = make_float2(0.0f, 0.0f);
+            for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
             bool ok = true;
             for (int64_t b = 0; b < nb; ++b, ++blk) {
                 const int slot = int(blk % EX_SLOTS);
@@ -189,28 +183,23 @@ __global__ void __launch_bounds__(EX_THREADS, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(blk_empty + slot);   // the slot is free for the next block
                 const float dx = live ? __ldg(a.x_scale + row * nb + b) : 0.0f;
-                const float2 dx2 = make_float2(dx, dx);
                 const float4 *ws = reinterpret_cast<const float4 *>(a.w_scale + b * a.n_pad + n0 + c0);
 #pragma unroll
                 for (int j = 0; j < 32; j += 4) {
                     const float4 w4 = __ldg(ws + j / 4);
-                    // float(sumi): the int added to 1.5 * 2^23's bit pattern, then 1.5 * 2^23 taken off (exact)
-                    const float2 s0 = sub2(make_float2(__int_as_float(int(r[j]) + 0x4B400000),
-                                                       __int_as_float(int(r[j + 1]) + 0x4B400000)), magic);
-                    const float2 s1 = sub2(make_float2(__int_as_float(int(r[j + 2]) + 0x4B400000),
-                                                       __int_as_float(int(r[j + 3]) + 0x4B400000)), magic);
-                    acc[j / 2] = add2(acc[j / 2], mul2(s0, mul2(make_float2(w4.x, w4.y), dx2)));
-                    acc[j / 2 + 1] = add2(acc[j / 2 + 1], mul2(s1, mul2(make_float2(w4.z, w4.w), dx2)));
+                    acc[j] = __fadd_rn(acc[j], __fmul_rn(i2f_exact(r[j]), __fmul_rn(w4.x, dx)));
+                    acc[j + 1] = __fadd_rn(acc[j + 1], __fmul_rn(i2f_exact(r[j + 1]), __fmul_rn(w4.y, dx)));
+                    acc[j + 2] = __fadd_rn(acc[j + 2], __fmul_rn(i2f_exact(r[j + 2]), __fmul_rn(w4.z, dx)));
+                    acc[j + 3] = __fadd_rn(acc[j + 3], __fmul_rn(i2f_exact(r[j + 3]), __fmul_rn(w4.w, dx)));
                 }
             }
             if (!ok) break;
             if (live) {
                 float *o = a.out + row * a.ldo + n0 + c0;
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int64_t n = n0 + c0 + 2 * j;
-                    if (n < a.N) o[2 * j] = a.bias ? __fadd_rn(acc[j].x, a.bias[n]) : acc[j].x;
-                    if (n + 1 < a.N) o[2 * j + 1] = a.bias ? __fadd_rn(acc[j].y, a.bias[n + 1]) : acc[j].y;
+                for (int j = 0; j < 32; ++j) {
+                    const int64_t n = n0 + c0 + j;
+                    if (n < a.N) o[j] = a.bias ? __fadd_rn(acc[j], a.bias[n]) : acc[j];
                 }
             }
         }

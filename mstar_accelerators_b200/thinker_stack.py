@@ -123,6 +123,8 @@ class ThinkerStackB200:
         self.v_cache = [torch.zeros_like(c) for c in self.k_cache]
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.length = 0
+        self.graph = None
+        self._graph_rows = 0
 
     # ------------------------------------------------------------------ pieces
     def _linear(self, lin: BlockLinear, x: torch.Tensor) -> torch.Tensor:
@@ -141,8 +143,12 @@ class ThinkerStackB200:
             out[r0:r0 + self.gemm_rows] = L["moe"](part, w, ids)
         return out
 
-    def _layer(self, i: int, x: torch.Tensor, S: int, n: int, start: int) -> torch.Tensor:
-        """x [S * n, H] bf16: n new positions start .. start + n - 1 of each of S sequences."""
+    def _layer(self, i: int, x: torch.Tensor, S: int, n: int, start, pos: torch.Tensor) -> torch.Tensor:
+        """x [S * n, H] bf16: n new positions of each of S sequences; pos [S * n] int64 their
+        positions (device). Prefill (start == 0, n > 1): causal attention over the n positions.
+        Decode (n == 1): every query attends to the cache up to its own position through a
+        fixed-length view of the whole cache and an additive mask, so the step's shapes never
+        change (one CUDA graph replays it)."""
         cfg, L = self.cfg, self.layers[i]
         D, Hq, Hk = cfg.head_dim, cfg.q_heads, cfg.kv_heads
         T = S * n
@@ -151,23 +157,30 @@ class ThinkerStackB200:
         q = qkv[:, :Hq * D].view(T, Hq, D)
         k = qkv[:, Hq * D:(Hq + Hk) * D].view(T, Hk, D)
         v = qkv[:, (Hq + Hk) * D:].view(T, Hk, D)
-        pos = torch.arange(start, start + n, device=x.device).repeat(S)
         cos, sin = rotary(pos, cfg)
-        slots = (torch.arange(S, device=x.device).repeat_interleave(n) * self.max_len + pos).to(torch.int64)
+        slots = torch.arange(S, device=x.device).repeat_interleave(n) * self.max_len + pos
         q, _ = qknorm_rope(q, k, L["q_norm"], L["k_norm"], cos, sin, eps=cfg.eps, v=v, k_cache=self.k_cache[i],
                            v_cache=self.v_cache[i], slots=slots, status=self.status)
-        ctx = start + n
-        kk = self.k_cache[i].view(self.max_seqs, self.max_len, Hk, D)[:S, :ctx].transpose(1, 2)
-        vv = self.v_cache[i].view(self.max_seqs, self.max_len, Hk, D)[:S, :ctx].transpose(1, 2)
-        qq = q.view(S, n, Hq, D).transpose(1, 2)
         if n == 1:
-            att = F.scaled_dot_product_attention(qq, kk, vv, scale=D ** -0.5, enable_gqa=True)
-        elif start == 0:
-            att = F.scaled_dot_product_attention(qq, kk, vv, is_causal=True, scale=D ** -0.5, enable_gqa=True)
+            kk = self.k_cache[i].view(self.max_seqs, self.max_len, Hk, D)[:S].transpose(1, 2)
+            vv = self.v_cache[i].view(self.max_seqs, self.max_len, Hk, D)[:S].transpose(1, 2)
+            # the query heads of one KV head as that head's query rows: [S, Hk, Hq / Hk, D]
+            qq = q.view(S, Hk, Hq // Hk, D)
+            mask = torch.where(torch.arange(self.max_len, device=x.device)[None, :] <= pos[:, None], 0.0,
+                               float("-inf")).to(torch.bfloat16).view(S, 1, 1, self.max_len)
+            att = F.scaled_dot_product_attention(qq, kk, vv, attn_mask=mask, scale=D ** -0.5)
+            att = att.reshape(T, Hq * D)
         else:
-            mask = torch.ones((n, ctx), dtype=torch.bool, device=x.device).tril(ctx - n)
-            att = F.scaled_dot_product_attention(qq, kk, vv, attn_mask=mask, scale=D ** -0.5, enable_gqa=True)
-        att = att.transpose(1, 2).reshape(T, Hq * D)
+            ctx = start + n
+            kk = self.k_cache[i].view(self.max_seqs, self.max_len, Hk, D)[:S, :ctx].transpose(1, 2)
+            vv = self.v_cache[i].view(self.max_seqs, self.max_len, Hk, D)[:S, :ctx].transpose(1, 2)
+            qq = q.view(S, n, Hq, D).transpose(1, 2)
+            if start == 0:
+                att = F.scaled_dot_product_attention(qq, kk, vv, is_causal=True, scale=D ** -0.5, enable_gqa=True)
+            else:
+                m = torch.ones((n, ctx), dtype=torch.bool, device=x.device).tril(ctx - n)
+                att = F.scaled_dot_product_attention(qq, kk, vv, attn_mask=m, scale=D ** -0.5, enable_gqa=True)
+            att = att.transpose(1, 2).reshape(T, Hq * D)
         x = x + self._linear(L["o"], att).to(torch.bfloat16)
         h = rms_norm(x, L["ln2"], cfg.eps)
         return x + self._moe(L, h)
@@ -186,23 +199,52 @@ class ThinkerStackB200:
         if S > self.max_seqs or n > self.max_len:
             raise ValueError("prompt exceeds the prepared capacity")
         x = self.embed[tokens.reshape(-1)]
+        pos = torch.arange(n, device=self.device).repeat(S)
         for i in range(self.cfg.layers):
-            x = self._layer(i, x, S, n, 0)
+            x = self._layer(i, x, S, n, 0, pos)
         self.length, self.seqs = n, S
+        self.graph = None
         return self._readout(x.view(S, n, -1)[:, -1])
 
-    def decode(self, tokens: torch.Tensor):
-        """tokens [S] at the next position of every sequence -> (logits [S, vocab], next tokens [S])."""
+    def _decode_step(self, tokens: torch.Tensor, pos: torch.Tensor):
+        x = self.embed[tokens]
+        for i in range(self.cfg.layers):
+            x = self._layer(i, x, tokens.shape[0], 1, None, pos)
+        return self._readout(x)
+
+    def decode(self, tokens: torch.Tensor, *, graph: bool = False):
+        """tokens [S] at the next position of every sequence -> (logits [S, vocab], next tokens [S]).
+        graph=True replays the whole step (48 layers and the readout) as one captured CUDA graph,
+        captured on the first such call after a prefill."""
         S = tokens.shape[0]
         if self.length >= self.max_len:
             raise ValueError("sequence capacity exhausted")
-        x = self.embed[tokens.reshape(-1)]
-        for i in range(self.cfg.layers):
-            x = self._layer(i, x, S, 1, self.length)
+        if not graph:
+            pos = torch.full((S,), self.length, dtype=torch.int64, device=self.device)
+            out = self._decode_step(tokens.reshape(-1), pos)
+            self.length += 1
+            return out
+        if getattr(self, "graph", None) is None or self._graph_rows != S:
+            self._tok = torch.zeros(S, dtype=torch.int64, device=self.device)
+            self._pos = torch.zeros(S, dtype=torch.int64, device=self.device)
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):   # warm-up outside capture (handles, attention plans)
+                self._pos.fill_(self.length)
+                self._decode_step(self._tok, self._pos)
+            torch.cuda.current_stream().wait_stream(side)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                self._graph_out = self._decode_step(self._tok, self._pos)
+            self._graph_rows = S
+        self._tok.copy_(tokens.reshape(-1))
+        self._pos.fill_(self.length)
+        self.graph.replay()
         self.length += 1
-        return self._readout(x)
+        return self._graph_out
 
     def close(self) -> None:
+        self.graph = None
         for L in self.layers:
             L["qkv"].close()
             L["o"].close()

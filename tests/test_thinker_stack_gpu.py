@@ -4,7 +4,9 @@ grouped MoE kernels, the Q8_0 lm_head readout) against the oracle composition
 (oracle/thinker_oracle.ThinkerStackOracle) at a reduced geometry (2 layers, hidden
 256, 4 query / 2 KV heads of 128, 16 experts top-4, vocabulary 1000): prefill of 3
 sequences x 70 tokens (the prefill linears on the tcgen05 GEMM), then 4 decode steps
-teacher-forced with the oracle's tokens (the decode linears on the bit-exact GEMV).
+teacher-forced with the oracle's tokens (the decode linears on the bit-exact GEMV), the
+whole decode step replayed as one captured CUDA graph; a second stack stepping eagerly
+gives the graph's logits bit for bit.
 The bf16 residual stream, bf16 MoE and Q8_0 activations put both sides at the
 quantization-noise level of each other after the first layer, so logits are held
 within 5e-2 of the largest |logit| (mean 1e-2) and greedy tokens to the harness's
@@ -39,8 +41,16 @@ def test_stack_matches_oracle(experts):
             assert greedy_agrees(int(gt[b]), rl[b], int(rt[b]), gl[b])
         return rt
 
+    eager = ThinkerStackB200(cfg, max_seqs=3, max_len=80, seed=3, experts=experts, gemm_rows=256,
+                             weights=lambda i: layers[i])
     nxt = check(stack.prefill(torch.from_numpy(tokens).cuda()), ref.prefill(tokens))
+    eager.prefill(torch.from_numpy(tokens).cuda())
     for _ in range(4):
-        nxt = check(stack.decode(torch.from_numpy(nxt).cuda()), ref.decode(nxt))
-    assert int(stack.status.item()) == 0
+        got = stack.decode(torch.from_numpy(nxt).cuda(), graph=True)
+        logits = got[0].clone()
+        e_logits, _ = eager.decode(torch.from_numpy(nxt).cuda())
+        assert torch.equal(logits, e_logits)
+        nxt = check(got, ref.decode(nxt))
+    assert int(stack.status.item()) == 0 and int(eager.status.item()) == 0
     stack.close()
+    eager.close()
