@@ -221,6 +221,19 @@ MSTAR_B200_API int mstar_b200_moe_run(void *handle, const void *x, int64_t token
     const float *topk_weights, const int32_t *topk_ids, void *out, int32_t *status, int32_t rounding,
     void *stream, char *error, size_t error_size);
 MSTAR_B200_API int mstar_b200_moe_close(void *handle, char *error, size_t error_size);
+/* moe_run_experts: the experts half of moe_run for a handle holding experts
+ * [expert0, expert0 + E) of experts_total (expert parallelism with every rank
+ * routing all tokens; thinker_moe.py:17-83 for the held experts): pairs whose id
+ * is another rank's expert are skipped, an id outside [0, experts_total) sets
+ * status bit value 4. The held pairs' routed down-projection rows
+ * bf16(w * down(SwiGLU(gate/up(x)))) land in y (bf16 [y_rows][hidden], 16-byte
+ * aligned) at rows row_base + their permuted position, and inv[token * top_k +
+ * slot] (int32, tokens * top_k entries) receives that row, or -1 for a pair not
+ * held here. No combine: mstar_b200_thinker_combine sums the slots. */
+MSTAR_B200_API int mstar_b200_moe_run_experts(void *handle, const void *x, int64_t tokens,
+    const float *topk_weights, const int32_t *topk_ids, int32_t expert0, int32_t experts_total, void *y,
+    int64_t y_rows, int64_t row_base, int32_t *inv, int32_t *status, int32_t rounding, void *stream,
+    char *error, size_t error_size);
 /* Slot-ordered combine of expert outputs gathered by the caller (expert
  * parallelism: rows returned by their owners, moe_sum_reduce of
  * thinker_moe.py:75-81): out[t] = bf16(sum_s fp32(y[rows[t*top_k + s]])) in slot
@@ -304,6 +317,30 @@ MSTAR_B200_API int mstar_b200_tp_reduce(const float *const *part_ptrs, int32_t w
 MSTAR_B200_API int mstar_b200_tp_reduce_multicast(const float *mc_part, int32_t world, int64_t owned, int64_t width,
     const float *bias, float *x, const float *ln_weight, const float *ln_bias, float ln_eps, void *mc_staged,
     int64_t row0, int32_t rounding, int32_t *status, void *stream, char *error, size_t error_size);
+
+/* --- thinker tensor / expert parallelism over peer memory (the thinker layer,
+ * implementations/qwen3_omni/amd/thinker_model.py:106-148, with attention
+ * column-parallel by heads and the experts spread over the ranks) ---
+ * Every rank holds the bf16 residual stream x [T][width] in a peer-visible
+ * buffer; x_ptrs / part_ptrs / y_ptrs / inv_ptrs are device arrays of `world`
+ * device pointers (peer mappings, e.g. symmetric memory; not checked on the
+ * host), rows 16-byte aligned. An owner handles rows row0 .. row0 + owned.
+ * thinker_reduce: the row-parallel o_proj reduction: s = sum over ranks p (in
+ * rank order, fp32) of part_ptrs[p][row], then x[row] = bf16(x[row] + bf16(s))
+ * (torch's bf16 residual add), the new row stored into every rank's x.
+ * thinker_combine: the expert-parallel combine (moe_sum_reduce,
+ * thinker_moe.py:75-81): for each owned token t, slot s with id = topk_ids[t *
+ * top_k + s] in [0, experts_total), rank p = id / experts_per_rank holds the
+ * routed row y_ptrs[p][inv_ptrs[p][t * top_k + s]]; the slots are summed in slot
+ * order in fp32, rounded to bf16 and added to x[t] as above, the new row stored
+ * into every rank's x. A row index at or above y_rows adds nothing and sets
+ * status bit value 64. */
+MSTAR_B200_API int mstar_b200_thinker_reduce(const float *const *part_ptrs, void *const *x_ptrs, int32_t rank,
+    int32_t world, int64_t owned, int64_t width, int64_t row0, void *stream, char *error, size_t error_size);
+MSTAR_B200_API int mstar_b200_thinker_combine(const void *const *y_ptrs, const int32_t *const *inv_ptrs,
+    int64_t y_rows, const int32_t *topk_ids, int32_t experts_per_rank, int32_t experts_total, int32_t top_k,
+    void *const *x_ptrs, int32_t rank, int32_t world, int64_t owned, int64_t hidden, int64_t row0,
+    int32_t *status, void *stream, char *error, size_t error_size);
 
 /* --- exact Q8_0 GEMM (ggml_vec_dot_q8_0_q8_0 generic order, ggml-cpu/quants.c:451-480, at
  * prefill row counts; the tcgen05 int8 tensor pipe computes each block's integer dot) ---

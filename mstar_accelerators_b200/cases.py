@@ -130,6 +130,54 @@ def thinker_stack_48():
     stack.close()
 
 
+def thinker_stack_48_tp():
+    """The 48-layer thinker stack with attention tensor-parallel and the experts expert-parallel over
+    the ranks of a torchrun launch (one process per GPU, RANK / WORLD_SIZE / MASTER_* from the
+    environment): the same workload as thinker-stack-48; device times are the maximum over ranks."""
+    import json
+    import os
+    from datetime import timedelta
+    import torch.distributed as dist
+    from .thinker_stack import ThinkerStackConfig
+    from .thinker_stack_tp import ThinkerStackTP
+    rank = int(os.environ["RANK"])
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                            device_id=torch.device("cuda", torch.cuda.current_device()))
+    try:
+        cfg = ThinkerStackConfig()
+        stack = ThinkerStackTP(cfg, max_seqs=32, max_len=1024 + 128 + 4, max_tokens=32 * 1024)
+        g = torch.Generator().manual_seed(3)
+        prompt = torch.randint(0, cfg.vocab, (32, 1024), generator=g).cuda()
+        stack.prefill(prompt)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        torch.cuda.synchronize()
+        dist.barrier()
+        ev[0].record()
+        _, tok = stack.prefill(prompt)
+        ev[1].record()
+        for _ in range(2):       # capture and a first replay
+            _, tok = stack.decode(tok, graph=True)
+        ev[2].record()
+        for _ in range(128):
+            _, tok = stack.decode(tok, graph=True)
+        ev[3].record()
+        torch.cuda.synchronize()
+        t = torch.tensor([ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3])], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        st = torch.tensor([int(stack.status.item()) | stack.expert_status()], device="cuda")
+        dist.all_reduce(st, op=dist.ReduceOp.BOR)
+        pre, dec = t.tolist()
+        if rank == 0:
+            print(json.dumps({"ranks": dist.get_world_size(), "prefill_ms": round(pre, 2),
+                              "prefill_tokens_per_s": round(32 * 1024 / (pre / 1e3), 1),
+                              "decode_ms_per_step": round(dec / 128, 3),
+                              "decode_tokens_per_s": round(32 * 128 / (dec / 1e3), 1), "status": int(st.item())}))
+        stack.close()
+    finally:
+        dist.destroy_process_group()
+
+
 def _encoder(cfg, batch, calls):
     from .encoder import WhisperEncoderB200, synthetic_mel, synthetic_weights
     w = {k: v.cuda() for k, v in synthetic_weights(cfg, seed=1).items()}
@@ -182,6 +230,7 @@ def moe_prefill_4096_q8():
 CASES = {"readout-q4-b32": readout_q4_b32, "decode-step-b32": decode_step_b32,
          "gemm-q8-8192x5120x1280": gemm_q8_8192x5120x1280, "gemm-encoder-large-layer": gemm_encoder_large_layer,
          "gemm-fc1-exact-and-f16": gemm_fc1_exact_and_f16, "thinker-stack-48": thinker_stack_48,
+         "thinker-stack-48-tp": thinker_stack_48_tp,
          "encoder-tiny-b1": encoder_tiny_b1,
          "encoder-large-b16": encoder_large_b16, "moe-prefill-4096": moe_prefill_4096,
          "moe-prefill-4096-q8": moe_prefill_4096_q8}

@@ -179,16 +179,20 @@ struct MoePlan {
     int *valid;       // [1] pairs with a valid expert id (the permuted rows in use)
 };
 
-__global__ void k_moe_count(const int32_t *__restrict__ ids, int P, int E, int *__restrict__ counts,
-                            int *__restrict__ status) {
+// The handle holds experts [e0, e0 + E) of e_total (all of them without expert
+// parallelism): an id outside [0, e_total) sets status bit value 4, an id of
+// another rank's expert is skipped silently; both contribute nothing here.
+__global__ void k_moe_count(const int32_t *__restrict__ ids, int P, int E, int e0, int e_total,
+                            int *__restrict__ counts, int *__restrict__ status) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= P) return;
-    const int e = ids[i];
-    if (e < 0 || e >= E) {
+    const int id = ids[i];
+    if (id < 0 || id >= e_total) {
         atomicOr(status, 4);
         return;
     }
-    atomicAdd(counts + e, 1);
+    const int e = id - e0;
+    if (e >= 0 && e < E) atomicAdd(counts + e, 1);
 }
 
 // single CTA: exclusive scans of the counts and of the 128-row tile counts
@@ -225,11 +229,11 @@ __global__ void k_moe_plan(MoePlan p, int E, int max_tiles) {
     }
 }
 
-__global__ void k_moe_scatter(const int32_t *__restrict__ ids, int P, int E, MoePlan p) {
+__global__ void k_moe_scatter(const int32_t *__restrict__ ids, int P, int E, int e0, int e_total, MoePlan p) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= P) return;
-    const int e = ids[i];
-    if (e < 0 || e >= E) {  // contributes nothing (status bit value 4 is already set)
+    const int id = ids[i], e = id - e0;
+    if (id < 0 || id >= e_total || e < 0 || e >= E) {  // invalid (status bit 4 already set) or not held here
         p.inv[i] = -1;
         return;
     }
@@ -945,6 +949,65 @@ void *mstar_b200_moe_create(int32_t format, const void *w1, uint64_t w1_bytes, c
     }
 }
 
+}  // extern "C"
+
+namespace mb {
+
+// Routing plan, permuted activations and both grouped GEMMs of one call: expert
+// rows land in y at their permuted positions (y rows [0, pairs with a held
+// expert)); plan.inv maps each (token, slot) pair to its row, or -1.
+static void moe_experts(Moe &m, const void *x, int64_t tokens, const float *topk_weights, const int32_t *topk_ids,
+                        int e0, int e_total, __nv_bfloat16 *y, int32_t *status, int32_t rounding, bool vec,
+                        cudaStream_t s) {
+    const int P = int(tokens) * m.topk;
+    cuda_check(cudaMemsetAsync(status, 0, 4, s), "status reset");
+    cuda_check(cudaMemsetAsync(m.plan.counts, 0, size_t(m.E) * 4, s), "count reset");
+    k_moe_count<<<unsigned(ceil_div(P, 256)), 256, 0, s>>>(topk_ids, P, m.E, e0, e_total, m.plan.counts, status);
+    k_moe_plan<<<1, 256, 0, s>>>(m.plan, m.E, m.max_tiles);
+    k_moe_scatter<<<unsigned(ceil_div(P, 256)), 256, 0, s>>>(topk_ids, P, m.E, e0, e_total, m.plan);
+    if (vec)
+        k_moe_gather_vec<<<unsigned(P), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), m.plan.perm,
+                                                     m.plan.valid, P, m.H, m.topk, m.q8, rounding, m.xp);
+    else
+        k_moe_gather<<<unsigned(P), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), m.plan.perm, m.plan.valid,
+                                                 P, m.H, m.topk, m.q8, rounding, m.xp);
+    MoeGemmArgs g{};
+    g.tiles = m.plan.tiles;
+    g.num_tiles = m.plan.num_tiles;
+    g.status = status;
+    g.q8 = m.q8;
+    g.rounding = rounding;
+    g.perm = m.plan.perm;
+    g.topk_w = topk_weights;
+    // gate/up: N = 2I rows per expert, output I columns of mid
+    g.n_tiles = 2 * m.I / MOE_BN;
+    g.w_rows = 2 * m.I;
+    g.K = m.H;
+    g.mid = m.mid;
+    g.I = m.I;
+    if (m.q8) launch_moe_gemm<MOE_SWIGLU, false>(m.map_x, m.map_w1, g, m.max_tiles, s);
+    else launch_moe_gemm<MOE_SWIGLU, true>(m.map_x, m.map_w1, g, m.max_tiles, s);
+    // down: N = H rows per expert, K = I
+    g.n_tiles = m.H / MOE_BN;
+    g.w_rows = m.H;
+    g.K = m.I;
+    g.y = y;
+    if (m.q8) launch_moe_gemm<MOE_DOWN, false>(m.map_mid, m.map_w2, g, m.max_tiles, s);
+    else launch_moe_gemm<MOE_DOWN, true>(m.map_mid, m.map_w2, g, m.max_tiles, s);
+}
+
+// out_inv[i] = inv[i] + row_base for a held pair, -1 otherwise
+__global__ void k_moe_inv_out(const int *__restrict__ inv, int P, int64_t row_base, int32_t *__restrict__ out_inv) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= P) return;
+    const int r = inv[i];
+    out_inv[i] = r < 0 ? -1 : int32_t(row_base + r);
+}
+
+}  // namespace mb
+
+extern "C" {
+
 int mstar_b200_moe_run(void *handle, const void *x, int64_t tokens, const float *topk_weights,
                        const int32_t *topk_ids, void *out, int32_t *status, int32_t rounding, void *stream,
                        char *error, size_t error_size) {
@@ -965,48 +1028,53 @@ int mstar_b200_moe_run(void *handle, const void *x, int64_t tokens, const float 
                               (const void *)status})
             check_device(p, "MoE operand");
         cudaStream_t s = as_stream(stream);
-        const int P = int(tokens) * m.topk;
-        cuda_check(cudaMemsetAsync(status, 0, 4, s), "status reset");
-        cuda_check(cudaMemsetAsync(m.plan.counts, 0, size_t(m.E) * 4, s), "count reset");
-        k_moe_count<<<unsigned(ceil_div(P, 256)), 256, 0, s>>>(topk_ids, P, m.E, m.plan.counts, status);
-        k_moe_plan<<<1, 256, 0, s>>>(m.plan, m.E, m.max_tiles);
-        k_moe_scatter<<<unsigned(ceil_div(P, 256)), 256, 0, s>>>(topk_ids, P, m.E, m.plan);
         const bool vec = uintptr_t(x) % 16 == 0 && uintptr_t(out) % 16 == 0 && m.H % 128 == 0;
-        if (vec)
-            k_moe_gather_vec<<<unsigned(P), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), m.plan.perm,
-                                                         m.plan.valid, P, m.H, m.topk, m.q8, rounding, m.xp);
-        else
-            k_moe_gather<<<unsigned(P), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), m.plan.perm,
-                                                     m.plan.valid, P, m.H, m.topk, m.q8, rounding, m.xp);
-        MoeGemmArgs g{};
-        g.tiles = m.plan.tiles;
-        g.num_tiles = m.plan.num_tiles;
-        g.status = status;
-        g.q8 = m.q8;
-        g.rounding = rounding;
-        g.perm = m.plan.perm;
-        g.topk_w = topk_weights;
-        // gate/up: N = 2I rows per expert, output I columns of mid
-        g.n_tiles = 2 * m.I / MOE_BN;
-        g.w_rows = 2 * m.I;
-        g.K = m.H;
-        g.mid = m.mid;
-        g.I = m.I;
-        if (m.q8) launch_moe_gemm<MOE_SWIGLU, false>(m.map_x, m.map_w1, g, m.max_tiles, s);
-        else launch_moe_gemm<MOE_SWIGLU, true>(m.map_x, m.map_w1, g, m.max_tiles, s);
-        // down: N = H rows per expert, K = I
-        g.n_tiles = m.H / MOE_BN;
-        g.w_rows = m.H;
-        g.K = m.I;
-        g.y = m.y;
-        if (m.q8) launch_moe_gemm<MOE_DOWN, false>(m.map_mid, m.map_w2, g, m.max_tiles, s);
-        else launch_moe_gemm<MOE_DOWN, true>(m.map_mid, m.map_w2, g, m.max_tiles, s);
+        moe_experts(m, x, tokens, topk_weights, topk_ids, 0, m.E, m.y, status, rounding, vec, s);
         if (vec)
             k_moe_combine_vec<<<unsigned(tokens), 256, 0, s>>>(m.y, m.plan.inv, int(tokens), m.H, m.topk,
                                                                static_cast<__nv_bfloat16 *>(out));
         else
             k_moe_combine<<<unsigned(tokens), 256, 0, s>>>(m.y, m.plan.inv, int(tokens), m.H, m.topk,
                                                            static_cast<__nv_bfloat16 *>(out));
+        cuda_check(cudaGetLastError(), "MoE launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+int mstar_b200_moe_run_experts(void *handle, const void *x, int64_t tokens, const float *topk_weights,
+                               const int32_t *topk_ids, int32_t expert0, int32_t experts_total, void *y,
+                               int64_t y_rows, int64_t row_base, int32_t *inv, int32_t *status, int32_t rounding,
+                               void *stream, char *error, size_t error_size) {
+    try {
+        require(handle, "missing MoE handle");
+        auto &m = *static_cast<Moe *>(handle);
+        require(!m.busy.test_and_set(std::memory_order_acquire), "MoE handle is busy");
+        struct Release {
+            std::atomic_flag &f;
+            ~Release() { f.clear(std::memory_order_release); }
+        } release{m.busy};
+        require(tokens >= 1 && tokens <= m.max_tokens, "token count outside the prepared capacity");
+        require(rounding >= 0 && rounding <= 2, "unknown Q8_0 activation rounding");
+        require(expert0 >= 0 && experts_total >= m.E && int64_t(expert0) + m.E <= experts_total,
+                "the held experts must lie inside [0, experts_total)");
+        require(x && topk_weights && topk_ids && y && inv && status, "missing MoE operand");
+        const int64_t P = tokens * m.topk;
+        require(row_base >= 0 && y_rows >= row_base + P && y_rows <= (int64_t(1) << 31) - 1,
+                "expert output rows outside the given buffer");
+        require(uintptr_t(y) % 16 == 0 && uintptr_t(x) % 16 == 0, "x and y must be 16-byte aligned");
+        const uint64_t xb = uint64_t(tokens) * m.H * 2;
+        require(disjoint({x, xb}, {y, uint64_t(y_rows) * m.H * 2}), "expert outputs overlap the input");
+        for (const void *p : {x, (const void *)topk_weights, (const void *)topk_ids, (const void *)y,
+                              (const void *)inv, (const void *)status})
+            check_device(p, "MoE operand");
+        cudaStream_t s = as_stream(stream);
+        const bool vec = m.H % 128 == 0;
+        moe_experts(m, x, tokens, topk_weights, topk_ids, expert0, experts_total,
+                    static_cast<__nv_bfloat16 *>(y) + row_base * m.H, status, rounding, vec, s);
+        k_moe_inv_out<<<unsigned(ceil_div(P, 256)), 256, 0, s>>>(m.plan.inv, int(P), row_base, inv);
         cuda_check(cudaGetLastError(), "MoE launch");
         return 0;
     } catch (const std::exception &e) {

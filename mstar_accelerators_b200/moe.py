@@ -85,6 +85,26 @@ class ThinkerMoEB200:
                                           _stream(x.device), e, len(e)), e, "B200 MoE")
         return out.view(hidden_states.shape)
 
+    def run_experts(self, hidden_states: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor, *,
+                    expert0: int, experts_total: int, y: torch.Tensor, row_base: int, inv: torch.Tensor) -> None:
+        """The held experts [expert0, expert0 + E) of experts_total, without the combine: each held
+        (token, slot) pair's routed row goes to y (bf16 [rows, H]) at row_base + its permuted
+        position and inv[token * top_k + slot] (int32) names that row, or -1 (another rank's expert)."""
+        x = hidden_states.reshape(-1, self.H)
+        if x.dtype != torch.bfloat16 or y.dtype != torch.bfloat16 or inv.dtype != torch.int32:
+            raise ValueError("bf16 activations and outputs, int32 row indices expected")
+        x = x.contiguous()
+        w = topk_weights.to(torch.float32).contiguous()
+        ids = topk_ids.to(torch.int32).contiguous()
+        if inv.numel() < x.shape[0] * self.top_k or not inv.is_contiguous() or not y.is_contiguous():
+            raise ValueError("inv needs tokens * top_k contiguous entries")
+        e = error_buffer()
+        check(self.lib.mstar_b200_moe_run_experts(self.handle, x.data_ptr(), x.shape[0], w.data_ptr(), ids.data_ptr(),
+                                                  int(expert0), int(experts_total), y.data_ptr(), y.numel() // self.H,
+                                                  int(row_base), inv.data_ptr(), self.status.data_ptr(),
+                                                  native.ROUNDING[self.rounding], _stream(x.device), e, len(e)),
+              e, "B200 MoE experts")
+
     def close(self):
         if getattr(self, "handle", None):
             e = error_buffer()

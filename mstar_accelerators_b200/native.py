@@ -94,6 +94,11 @@ SIGNATURES = {
     "mstar_b200_moe_run": (_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, C.c_int32, _vp, *_err]),
     "mstar_b200_moe_close": (_int, [_vp, *_err]),
     "mstar_b200_moe_combine": (_int, [_vp, _i64, _vp, _i64, C.c_int32, _i64, _vp, _vp, *_err]),
+    "mstar_b200_moe_run_experts": (_int, [_vp, _vp, _i64, _vp, _vp, C.c_int32, C.c_int32, _vp, _i64, _i64, _vp,
+                                          _vp, C.c_int32, _vp, *_err]),
+    "mstar_b200_thinker_reduce": (_int, [_vp, _vp, C.c_int32, C.c_int32, _i64, _i64, _i64, _vp, *_err]),
+    "mstar_b200_thinker_combine": (_int, [_vp, _vp, _i64, _vp, C.c_int32, C.c_int32, C.c_int32, _vp,
+                                          C.c_int32, C.c_int32, _i64, _i64, _i64, _vp, _vp, *_err]),
     "mstar_b200_moe_dispatch": (_int, [_vp, _i64, _i64, _vp, _vp, C.c_int32, C.c_int32, C.c_int32, _vp, _vp, _vp,
                                        _vp, _vp, *_err]),
     "mstar_b200_decode_step_create": (_vp, [_vp, *_err]),

@@ -93,32 +93,21 @@ class ThinkerStackB200:
         self.cfg, self.max_seqs, self.max_len = cfg, max_seqs, max_len
         self.device = torch.device(device)
         self.gemm_rows = gemm_rows
-        H, D = cfg.hidden, cfg.head_dim
+        self.experts_fmt = experts
+        D = cfg.head_dim
+        # heads and experts held by this process: [q0, q0 + q_heads), [k0, k0 + kv_heads), [e0, e0 + local_experts)
+        self.q0, self.q_heads, self.k0, self.kv_heads, self.e0, self.local_experts = self._shard_plan()
         self.layers = []
         for i in range(cfg.layers):
             w = weights(i) if weights is not None else layer_weights(cfg, i, seed, self.device)
-            qkv = BlockLinear(torch.cat([w["q"], w["k"], w["v"]]).float().contiguous(), fmt="q8_0")
-            o = BlockLinear(w["o"].float().contiguous(), fmt="q8_0")
-            qkv.prepare_gemm(gemm_rows)
-            o.prepare_gemm(gemm_rows)
-            if experts == "q8_0":
-                I = cfg.moe_intermediate
-                b1 = pack(w["w1"].float().reshape(-1, H), "q8_0", preround=False).reshape(cfg.experts, 2 * I, -1)
-                b2 = pack(w["w2"].float().reshape(-1, I), "q8_0", preround=False).reshape(cfg.experts, H, -1)
-                moe = ThinkerMoEB200(b1, b2, fmt="q8_0", top_k=cfg.top_k, max_tokens=gemm_rows, intermediate=I,
-                                     hidden=H)
-                del b1, b2
-            else:
-                moe = ThinkerMoEB200(w["w1"], w["w2"], fmt="bf16", top_k=cfg.top_k, max_tokens=gemm_rows)
-            self.layers.append({"ln1": w["ln1"], "ln2": w["ln2"], "q_norm": w["q_norm"], "k_norm": w["k_norm"],
-                                "router": w["router"].contiguous(), "qkv": qkv, "o": o, "moe": moe})
+            self.layers.append(self._build_layer(w))
             del w
         hw = head_weights(cfg, seed, self.device)
         self.embed, self.final_norm = hw["embed"], hw["norm"]
         self.lm_head = BlockLinear(hw["lm_head"].float().contiguous(), fmt="q8_0")
         self.lm_head.prepare_readout()
         slots = max_seqs * max_len
-        self.k_cache = [torch.zeros((slots, cfg.kv_heads, D), dtype=torch.bfloat16, device=self.device)
+        self.k_cache = [torch.zeros((slots, self.kv_heads, D), dtype=torch.bfloat16, device=self.device)
                         for _ in range(cfg.layers)]
         self.v_cache = [torch.zeros_like(c) for c in self.k_cache]
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
@@ -126,10 +115,40 @@ class ThinkerStackB200:
         self.graph = None
         self._graph_rows = 0
 
+    def _shard_plan(self):
+        """(q0, q_heads, k0, kv_heads, e0, experts) held here: everything on one GPU."""
+        c = self.cfg
+        return 0, c.q_heads, 0, c.kv_heads, 0, c.experts
+
+    def _build_layer(self, w: dict) -> dict:
+        """One layer's device state from its full bf16 weights: the held heads' rows of the fused QKV,
+        the held heads' columns of o_proj, the held experts."""
+        cfg, D, H, I = self.cfg, self.cfg.head_dim, self.cfg.hidden, self.cfg.moe_intermediate
+        q = w["q"][self.q0 * D:(self.q0 + self.q_heads) * D]
+        k = w["k"][self.k0 * D:(self.k0 + self.kv_heads) * D]
+        v = w["v"][self.k0 * D:(self.k0 + self.kv_heads) * D]
+        qkv = BlockLinear(torch.cat([q, k, v]).float().contiguous(), fmt="q8_0")
+        o = BlockLinear(w["o"][:, self.q0 * D:(self.q0 + self.q_heads) * D].float().contiguous(), fmt="q8_0")
+        qkv.prepare_gemm(self.gemm_rows)
+        o.prepare_gemm(self.gemm_rows)
+        e0, en = self.e0, self.local_experts
+        if self.experts_fmt == "q8_0":
+            b1 = pack(w["w1"][e0:e0 + en].float().reshape(-1, H), "q8_0", preround=False).reshape(en, 2 * I, -1)
+            b2 = pack(w["w2"][e0:e0 + en].float().reshape(-1, I), "q8_0", preround=False).reshape(en, H, -1)
+            moe = ThinkerMoEB200(b1, b2, fmt="q8_0", top_k=cfg.top_k, max_tokens=self.gemm_rows, intermediate=I,
+                                 hidden=H)
+            del b1, b2
+        else:
+            moe = ThinkerMoEB200(w["w1"][e0:e0 + en].contiguous(), w["w2"][e0:e0 + en].contiguous(), fmt="bf16",
+                                 top_k=cfg.top_k, max_tokens=self.gemm_rows)
+        return {"ln1": w["ln1"], "ln2": w["ln2"], "q_norm": w["q_norm"], "k_norm": w["k_norm"],
+                "router": w["router"].contiguous(), "qkv": qkv, "o": o, "moe": moe}
+
     # ------------------------------------------------------------------ pieces
-    def _linear(self, lin: BlockLinear, x: torch.Tensor) -> torch.Tensor:
+    def _linear(self, lin: BlockLinear, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         x = x.float().contiguous()
-        out = torch.empty((x.shape[0], lin.rows), dtype=torch.float32, device=x.device)
+        if out is None:
+            out = torch.empty((x.shape[0], lin.rows), dtype=torch.float32, device=x.device)
         step = self.gemm_rows if x.shape[0] >= 64 else max(x.shape[0], 1)
         for r0 in range(0, x.shape[0], step):
             lin(x[r0:r0 + step], out=out[r0:r0 + step])
@@ -143,6 +162,17 @@ class ThinkerStackB200:
             out[r0:r0 + self.gemm_rows] = L["moe"](part, w, ids)
         return out
 
+    def _embed(self, tokens: torch.Tensor) -> torch.Tensor:
+        return self.embed[tokens.reshape(-1)]
+
+    def _attention_out(self, L, att: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+        """x + o_proj(att) in bf16."""
+        return x + self._linear(L["o"], att).to(torch.bfloat16)
+
+    def _moe_residual(self, L, h: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+        """x + MoE(h) in bf16."""
+        return x + self._moe(L, h)
+
     def _layer(self, i: int, x: torch.Tensor, S: int, n: int, start, pos: torch.Tensor) -> torch.Tensor:
         """x [S * n, H] bf16: n new positions of each of S sequences; pos [S * n] int64 their
         positions (device). Prefill (start == 0, n > 1): causal attention over the n positions.
@@ -150,7 +180,7 @@ class ThinkerStackB200:
         fixed-length view of the whole cache and an additive mask, so the step's shapes never
         change (one CUDA graph replays it)."""
         cfg, L = self.cfg, self.layers[i]
-        D, Hq, Hk = cfg.head_dim, cfg.q_heads, cfg.kv_heads
+        D, Hq, Hk = cfg.head_dim, self.q_heads, self.kv_heads
         T = S * n
         h = rms_norm(x, L["ln1"], cfg.eps)
         qkv = self._linear(L["qkv"], h).to(torch.bfloat16)
@@ -181,9 +211,9 @@ class ThinkerStackB200:
                 m = torch.ones((n, ctx), dtype=torch.bool, device=x.device).tril(ctx - n)
                 att = F.scaled_dot_product_attention(qq, kk, vv, attn_mask=m, scale=D ** -0.5, enable_gqa=True)
             att = att.transpose(1, 2).reshape(T, Hq * D)
-        x = x + self._linear(L["o"], att).to(torch.bfloat16)
+        x = self._attention_out(L, att, x)
         h = rms_norm(x, L["ln2"], cfg.eps)
-        return x + self._moe(L, h)
+        return self._moe_residual(L, h, x)
 
     def _readout(self, last: torch.Tensor):
         h = rms_norm(last, self.final_norm, self.cfg.eps).float().contiguous()
@@ -198,7 +228,7 @@ class ThinkerStackB200:
         S, n = tokens.shape
         if S > self.max_seqs or n > self.max_len:
             raise ValueError("prompt exceeds the prepared capacity")
-        x = self.embed[tokens.reshape(-1)]
+        x = self._embed(tokens)
         pos = torch.arange(n, device=self.device).repeat(S)
         for i in range(self.cfg.layers):
             x = self._layer(i, x, S, n, 0, pos)
@@ -207,7 +237,7 @@ class ThinkerStackB200:
         return self._readout(x.view(S, n, -1)[:, -1])
 
     def _decode_step(self, tokens: torch.Tensor, pos: torch.Tensor):
-        x = self.embed[tokens]
+        x = self._embed(tokens)
         for i in range(self.cfg.layers):
             x = self._layer(i, x, tokens.shape[0], 1, None, pos)
         return self._readout(x)
