@@ -451,8 +451,8 @@ def run_b200(args):
                 "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s",
                         "h2d_bytes_per_step": mel_host.numel() * 4, "d2h_bytes_per_step": states_host.numel() * 4},
                 "gpu_launches": launches,
-                "roofline": {"bound": "tensor", "kernel": "k_gemm_f16 (tcgen05 GEMM of the encoder linears; "
-                                                          "average over one layer's four shapes)",
+                "roofline": {"bound": "tensor", "kernel": "k_gemm_pair (tcgen05 CTA-pair GEMM of the encoder "
+                                                          "linears; average over one layer's four shapes)",
                              "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                              "frac": round(achieved / peaks["bf16_tflops"], 4),
                              "peak_kind": peak_kind + " (burst bf16: the GEMMs are timed alone)",

@@ -317,6 +317,35 @@ MSTAR_B200_API int mstar_b200_tp_reduce(const float *const *part_ptrs, int32_t w
 MSTAR_B200_API int mstar_b200_tp_reduce_multicast(const float *mc_part, int32_t world, int64_t owned, int64_t width,
     const float *bias, float *x, const float *ln_weight, const float *ln_bias, float ln_eps, void *mc_staged,
     int64_t row0, int32_t rounding, int32_t *status, void *stream, char *error, size_t error_size);
+/* linear_gemm_push + tp_reduce_recv: the row-parallel reduction fused into the GEMM
+ * epilogue (the same sum as tp_reduce, decoder_all_reduce.py:64-90, with no barrier
+ * between the GEMM and the reduction).
+ * linear_gemm_push: the prepared linear's product of `rows` (> 128) staged rows, fp32
+ * and without bias, delivered by the epilogue straight into the owning rank's receive
+ * buffer: row r belongs to owner o = r / owner_rows (owner_rows a multiple of 32,
+ * owner_rows * world >= rows) and lands in recv_ptrs[o] at slot `rank`, local row
+ * r - o * owner_rows ([world][owner_rows][rows of the linear] fp32, 16-byte aligned).
+ * After its stores (system-scope fence) each epilogue warp adds 1 (release) to
+ * flag_ptrs[o][(r - o * owner_rows) / 32] for its 32 rows: every 32-row group receives
+ * 4 * ceil(N / 256) arrivals from every rank per call. recv_ptrs / flag_ptrs: device
+ * arrays of `world` device pointers (peer mappings), not checked on the host.
+ * tp_reduce_recv: the owner's side, for its `owned` rows (global rows row0 ..): waits
+ * (bounded, status bit value 16) until each 32-row group's counter holds all
+ * world * 4 * ceil(width / 256) arrivals, then x = x + (sum over slots p = 0 .. world-1
+ * in rank order of recv[p][r] + bias), x updated in place, and with ln_weight the
+ * LayerNorm + Q8_0 staging of tp_reduce into every rank's staged operand (staged_ptrs,
+ * or the multicast address mc_staged when not null); then clears the counters.
+ * counters: this rank's int32[owner_rows / 32 + 1], zero before the first push (the
+ * last word is the reduction's own count of finished CTAs). Every rank must pass a
+ * barrier (tp_barrier) after this call before any rank pushes into the same receive
+ * buffer again. */
+MSTAR_B200_API int mstar_b200_linear_gemm_push(void *handle, const void *staged, uint64_t staged_bytes, int64_t rows,
+    float *const *recv_ptrs, int32_t *const *flag_ptrs, int32_t world, int32_t rank, int64_t owner_rows,
+    int32_t *status, void *stream, char *error, size_t error_size);
+MSTAR_B200_API int mstar_b200_tp_reduce_recv(const float *recv, int32_t *counters, int32_t world, int64_t owned,
+    int64_t owner_rows, int64_t width, const float *bias, float *x, const float *ln_weight, const float *ln_bias,
+    float ln_eps, void *const *staged_ptrs, void *mc_staged, int64_t row0, int32_t rounding, int32_t *status,
+    void *stream, char *error, size_t error_size);
 
 /* --- thinker tensor / expert parallelism over peer memory (the thinker layer,
  * implementations/qwen3_omni/amd/thinker_model.py:106-148, with attention

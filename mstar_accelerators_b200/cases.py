@@ -165,8 +165,12 @@ def thinker_stack_48_tp():
         torch.cuda.synchronize()
         t = torch.tensor([ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3])], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        st = torch.tensor([int(stack.status.item()) | stack.expert_status()], device="cuda")
-        dist.all_reduce(st, op=dist.ReduceOp.BOR)
+        mine = torch.tensor([int(stack.status.item()) | stack.expert_status()], device="cuda")
+        every = [torch.zeros_like(mine) for _ in range(dist.get_world_size())]
+        dist.all_gather(every, mine)   # status bits of every rank (NCCL has no bitwise-or reduction)
+        st = torch.tensor([0])
+        for e in every:
+            st |= e.cpu()
         pre, dec = t.tolist()
         if rank == 0:
             print(json.dumps({"ranks": dist.get_world_size(), "prefill_ms": round(pre, 2),

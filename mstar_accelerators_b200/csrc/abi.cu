@@ -647,6 +647,46 @@ int mstar_b200_linear_gemm(void *handle, const void *staged, uint64_t staged_byt
     }
 }
 
+int mstar_b200_linear_gemm_push(void *handle, const void *staged, uint64_t staged_bytes, int64_t rows,
+                                float *const *recv_ptrs, int32_t *const *flag_ptrs, int32_t world, int32_t rank,
+                                int64_t owner_rows, int32_t *status, void *stream, char *error, size_t error_size) {
+    try {
+        require(handle, "missing linear handle");
+        auto &h = *static_cast<Linear *>(handle);
+        Busy busy(h.busy);
+        require(h.w16, "linear_gemm_push needs prepare_gemm first");
+        require(world >= 1 && world <= 8 && rank >= 0 && rank < world, "invalid rank / world");
+        require(rows > GEMM_TILE_M && rows <= (int64_t(1) << 31), "pushed partial products need more than 128 rows");
+        require(h.rows % QK == 0, "pushed partial products need a multiple of 32 output columns");
+        require(owner_rows > 0 && owner_rows % 32 == 0, "owner rows must be a positive multiple of 32");
+        require(owner_rows * world >= rows, "the owners' row ranges must cover every row");
+        require(recv_ptrs && flag_ptrs && status, "missing push operand");
+        const uint64_t sb = uint64_t(rows) * h.width * 2;
+        check_range({staged, staged_bytes}, sb, 16, "staged operand");
+        check_device(staged, "staged operand");
+        check_device(status, "status word");
+        CUtensorMap xmap;
+        make_fp16_map(&xmap, staged, rows, h.width, GEMM_TILE_M);
+        GemmArgs g{};
+        g.M = rows;
+        g.N = h.rows;
+        g.K = h.width;
+        g.ldo = h.rows;
+        g.out_mode = GEMM_OUT_PUSH;
+        g.status = status;
+        g.push_out = recv_ptrs;
+        g.push_flags = flag_ptrs;
+        g.push_rows = owner_rows;
+        g.push_rank = rank;
+        launch_gemm(xmap, h.wmap, h.wmap_pair, g, as_stream(stream));
+        cuda_check(cudaGetLastError(), "GEMM launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
 int mstar_b200_linear_set_split(void *handle, int warps, char *error, size_t error_size) {
     try {
         require(handle, "missing linear handle");

@@ -343,12 +343,113 @@ constexpr int PAIR_BM = 2 * GEMM_BM;                          // output rows per
 constexpr int PAIR_GROUP_M = 4;                               // pair row tiles per group (1024 rows)
 // instruction descriptor: D f32, A/B f16, K-major, N = 256, M = 256 (the pair)
 constexpr uint32_t PAIR_IDESC = (1u << 4) | (uint32_t(GEMM_BN >> 3) << 17) | (uint32_t(PAIR_BM >> 4) << 24);
-template <int STAGES, bool GELU_TABLE>
+// Epilogue forms of the pair kernel: EPI_ROWS, one thread = one row x one 32-column block
+// stored from registers (every output mode); EPI_PUSH, the partial product delivered to
+// its owner (GEMM_OUT_PUSH); EPI_F32T, fp32 output with bias / residual where every
+// global access of the epilogue is coalesced. The last two re-lay each warp's 32 x 32 fp32
+// block through shared memory (row stride 36 floats: conflict-free 16-byte writes by row
+// and reads by column), so one load or store instruction covers four whole 128-byte row
+// segments instead of 32 rows of 16 bytes each (which makes the fp32 residual stream of
+// the out_proj / fc2 shapes bound by load/store wavefronts, not by DRAM).
+// The 32 x 32 block is unpadded (4 KB per warp, so the ring keeps five stages); its 16-byte
+// chunks are XOR-swizzled by row, which keeps both access patterns conflict-free.
+constexpr int EPI_ROWS = 0, EPI_PUSH = 1, EPI_F32T = 2;
+constexpr size_t PUSH_STAGE_BYTES = size_t(GEMM_EPI_WARPS) * 32 * 32 * 4;
+// float offset of 16-byte chunk c4 (0..7) of row r in a warp's swizzled 32 x 32 block
+__device__ __forceinline__ int blk_at(int r, int c4) { return r * 32 + ((c4 ^ (r & 7)) << 2); }
+template <int STAGES, bool GELU_TABLE, int EPI = EPI_ROWS>
 constexpr size_t pair_smem_bytes() {
-    return size_t(STAGES) * PAIR_STAGE_BYTES + 1024 + 256 + (GELU_TABLE ? GELU_TABLE_BYTES : 0);
+    return size_t(STAGES) * PAIR_STAGE_BYTES + 1024 + 256 + (GELU_TABLE ? GELU_TABLE_BYTES : 0) +
+           (EPI != EPI_ROWS ? PUSH_STAGE_BYTES : 0);
 }
 
-template <int STAGES, bool GELU_TABLE>
+// One warp's 32 rows x 32 columns of a pushed partial product: registers (one row per
+// lane) -> shared memory -> owner's receive slot, four rows of 128 bytes per store.
+__device__ __forceinline__ void push_block(const GemmArgs &a, const uint32_t (&r)[32], float *st, int lane,
+                                           int64_t row_base, int64_t nc) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4 *>(st + blk_at(lane, j >> 2)) = make_float4(
+            __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+    __syncwarp();
+    // N is a multiple of 32: a block is wholly inside or outside; rows at or past M (the
+    // last tile's padding) have no owner (owner_rows * world >= M is checked on the host)
+    if (nc < a.N && row_base < a.M) {
+        const int owner = int(row_base / a.push_rows);   // a 32-row group never straddles two owners
+        float *slot = a.push_out[owner] + (int64_t(a.push_rank) * a.push_rows + (row_base - owner * a.push_rows)) * a.N;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int rr = i * 4 + (lane >> 3), col = (lane & 7) * 4;
+            if (row_base + rr < a.M)
+                *reinterpret_cast<float4 *>(slot + int64_t(rr) * a.N + nc + col) =
+                    *reinterpret_cast<const float4 *>(st + blk_at(rr, lane & 7));
+        }
+    }
+    __syncwarp();
+}
+
+// EPI_F32T, first half: the residual rows of one warp's 32 x 32 block copied into its
+// swizzled shared block, four 128-byte row segments per instruction (cp.async, issued
+// before the block's TMEM load so the copy overlaps it; no registers held).
+__device__ __forceinline__ void f32t_residual(const GemmArgs &a, float *st, int lane, int64_t row_base, int64_t nc) {
+    if (!(a.flags & 4) || nc >= a.N) return;   // warp-uniform
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int rr = i * 4 + (lane >> 3);
+        const int64_t row = row_base + rr;
+        const int64_t rrow = a.res_period ? row % a.res_period : row;
+        // rows past M copy nothing (zero source bytes) from a clamped, valid address
+        const float *src = a.residual + (row < a.M ? rrow : 0) * a.ldr + nc + (lane & 7) * 4;
+        cp_async16(st + blk_at(rr, lane & 7), src, row < a.M ? 16 : 0);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// EPI_F32T, second half: bias, the residual from the shared block, then the fp32 rows
+// stored four 128-byte row segments at a time.
+__device__ __forceinline__ void f32t_block(const GemmArgs &a, const uint32_t (&r)[32], float *st, int lane,
+                                           int64_t row_base, int64_t nc) {
+    if (nc >= a.N) return;   // warp-uniform: N is a multiple of 32
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    if (a.flags & 1) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+            const float4 bb = *reinterpret_cast<const float4 *>(a.bias + nc + j);
+            v[j] = __fadd_rn(v[j], bb.x); v[j + 1] = __fadd_rn(v[j + 1], bb.y);
+            v[j + 2] = __fadd_rn(v[j + 2], bb.z); v[j + 3] = __fadd_rn(v[j + 3], bb.w);
+        }
+    }
+    if (a.flags & 4) {
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+            const float4 rr = *reinterpret_cast<const float4 *>(st + blk_at(lane, j >> 2));
+            v[j] = __fadd_rn(rr.x, v[j]); v[j + 1] = __fadd_rn(rr.y, v[j + 1]);
+            v[j + 2] = __fadd_rn(rr.z, v[j + 2]); v[j + 3] = __fadd_rn(rr.w, v[j + 3]);
+        }
+        __syncwarp();
+    }
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4 *>(st + blk_at(lane, j >> 2)) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int rr = i * 4 + (lane >> 3), col = (lane & 7) * 4;
+        const int64_t row = row_base + rr;
+        if (row < a.M) {
+            const int64_t orow = a.seg_rows ? (row / a.seg_rows) * a.out_seg_rows + row % a.seg_rows : row;
+            *reinterpret_cast<float4 *>(static_cast<float *>(a.out) + orow * a.ldo + nc + col) =
+                *reinterpret_cast<const float4 *>(st + blk_at(rr, lane & 7));
+        }
+    }
+    __syncwarp();
+}
+
+template <int STAGES, bool GELU_TABLE, int EPI = EPI_ROWS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_pair(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const GemmArgs a) {
     extern __shared__ __align__(1024) unsigned char gemm_smem[];
@@ -375,7 +476,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         const int64_t first_m = (tile / per_group) * PAIR_GROUP_M;
         const int64_t gsz = tiles_m - first_m < PAIR_GROUP_M ? tiles_m - first_m : PAIR_GROUP_M;
         const int64_t r = tile % per_group;
-        m0 = (first_m + r % gsz) * PAIR_BM;
+        int64_t mi = first_m + r % gsz;
+        if (EPI == EPI_PUSH) {
+            // owner-interleaved row tiles: the k-th W-tuple of row tiles takes the k-th tile of
+            // each owner's share (the tail past W * P in order), so every wave stores to all
+            // owners at once and the NVLink stores overlap the MMAs instead of the local and
+            // the remote halves of the kernel running one after the other
+            const int64_t owners = (a.M + a.push_rows - 1) / a.push_rows;
+            const int64_t share = tiles_m / owners;
+            if (mi < owners * share) mi = (mi % owners) * share + mi / owners;
+        }
+        m0 = mi * PAIR_BM;
         n0 = (r / gsz) * GEMM_BN;
     };
 
@@ -456,17 +567,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         const int c0 = ((warp - 2) / 4) * (GEMM_BN / 32 / (GEMM_EPI_WARPS / 4));
         const uint32_t leader_acc_empty[2] = {cluster_smem(acc_empty, 0), cluster_smem(acc_empty + 1, 0)};
         int64_t local = 0;
+        bool stored_all = true;
         for (int64_t tile = cluster; tile < tiles; tile += clusters, ++local) {
             const int buf = int(local & 1);
             int64_t m0, n0;
             tile_coords(tile, m0, n0);
             const int64_t row = m0 + int64_t(rank) * GEMM_BM + 32 * q + lane;
-            prefetch_residual(a, row, n0, c0, GEMM_BN / 32 / (GEMM_EPI_WARPS / 4));
+            if (EPI != EPI_PUSH) prefetch_residual(a, row, n0, c0, GEMM_BN / 32 / (GEMM_EPI_WARPS / 4));
             if (!mbar_wait_bounded(acc_full + buf, uint32_t((local >> 1) & 1))) {
                 atomicOr(&failed, 1);
+                stored_all = false;
                 break;
             }
             tc_fence_after();
+            if (EPI == EPI_F32T) {
+                const int64_t row_base = row - lane;
+                float *st = reinterpret_cast<float *>(gelu_smem) + (warp - 2) * (32 * 32);
+                for (int c = c0; c < c0 + GEMM_BN / 32 / (GEMM_EPI_WARPS / 4); ++c) {
+                    f32t_residual(a, st, lane, row_base, n0 + c * 32);
+                    uint32_t r[32];
+                    tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(buf * GEMM_BN + c * 32), r);
+                    f32t_block(a, r, st, lane, row_base, n0 + c * 32);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(leader_acc_empty[buf]);
+                continue;
+            }
+            if (EPI == EPI_PUSH) {
+                const int64_t row_base = row - lane;
+                float *st = reinterpret_cast<float *>(gelu_smem) + (warp - 2) * (32 * 32);
+                for (int c = c0; c < c0 + GEMM_BN / 32 / (GEMM_EPI_WARPS / 4); ++c) {
+                    uint32_t r[32];
+                    tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(buf * GEMM_BN + c * 32), r);
+                    push_block(a, r, st, lane, row_base, n0 + c * 32);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(leader_acc_empty[buf]);
+                continue;
+            }
             const int64_t orow_i = a.seg_rows ? (row / a.seg_rows) * a.out_seg_rows + row % a.seg_rows : row;
             const int64_t rrow_i = a.res_period ? row % a.res_period : row;
             for (int c = c0; c < c0 + GEMM_BN / 32 / (GEMM_EPI_WARPS / 4); ++c) {
@@ -477,6 +617,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(leader_acc_empty[buf]);
+        }
+        if (EPI == EPI_PUSH) {
+            // every lane's stores of every tile reach their owners before the arrivals that
+            // publish them: one system-scope fence per warp (a fence per tile stalls the
+            // epilogue on a remote round trip while the MMAs wait for the accumulator)
+            // (after a timed-out wait nothing is published: the owners' bounded waits run out)
+            __threadfence_system();
+            __syncwarp();
+            if (lane == 0 && stored_all) {
+                for (int64_t tile = cluster; tile < tiles; tile += clusters) {
+                    int64_t m0, n0;
+                    tile_coords(tile, m0, n0);
+                    const int64_t row_base = m0 + int64_t(rank) * GEMM_BM + 32 * q;
+                    if (row_base >= a.M) continue;
+                    const int owner = int(row_base / a.push_rows);
+                    int *flag = a.push_flags[owner] + (row_base - owner * a.push_rows) / 32;
+                    // relaxed: the fence above already orders every store before these
+                    // (a release per arrival would fence the system again each time)
+                    asm volatile("red.relaxed.sys.global.add.s32 [%0], %1;" ::"l"(flag), "r"(1) : "memory");
+                }
+            }
         }
     }
     tc_fence_before();
@@ -569,13 +730,18 @@ void launch_dequant_act(int mode, const float *x, int64_t ldx, int64_t m, int64_
     else k_dequant_act<1><<<grid, 256, 0, s>>>(x, ldx, m, k, out, status);
 }
 
-// Pair kernel shapes: 6 stages (192 KB) without GELU, 4 stages + the 75 KB GELU table with it.
-constexpr int PAIR_STAGES = 6, PAIR_STAGES_GELU = 4;
+// Pair kernel shapes: 6 stages (192 KB) without GELU, 4 stages + the 75 KB GELU table with it,
+// 5 stages + the 64 KB block staging of the push and coalesced fp32 epilogues.
+constexpr int PAIR_STAGES = 6, PAIR_STAGES_GELU = 4, PAIR_STAGES_PUSH = 5, PAIR_STAGES_F32T = 5;
+static_assert(pair_smem_bytes<PAIR_STAGES_F32T, false, EPI_F32T>() + 64 <= 232448 &&
+                  pair_smem_bytes<PAIR_STAGES, false>() + 64 <= 232448 &&
+                  pair_smem_bytes<PAIR_STAGES_GELU, true>() + 64 <= 232448,
+              "pair GEMM shared memory exceeds 227 KB per CTA");
 
 void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tb_pair, const GemmArgs &a,
                  cudaStream_t s) {
     static bool configured = false;
-    static int pair_clusters = 0, pair_clusters_gelu = 0;
+    static int pair_clusters = 0, pair_clusters_gelu = 0, pair_clusters_push = 0, pair_clusters_f32t = 0;
     if (!configured) {
         cuda_check(cudaFuncSetAttribute(k_gemm_f16<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         int(gemm_smem_bytes<4, false>())),
@@ -589,6 +755,14 @@ void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap
         cuda_check(cudaFuncSetAttribute(k_gemm_pair<PAIR_STAGES_GELU, true>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         int(pair_smem_bytes<PAIR_STAGES_GELU, true>())),
+                   "pair GEMM shared-memory attribute");
+        cuda_check(cudaFuncSetAttribute(k_gemm_pair<PAIR_STAGES_PUSH, false, EPI_PUSH>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(pair_smem_bytes<PAIR_STAGES_PUSH, false, EPI_PUSH>())),
+                   "pair GEMM shared-memory attribute");
+        cuda_check(cudaFuncSetAttribute(k_gemm_pair<PAIR_STAGES_F32T, false, EPI_F32T>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(pair_smem_bytes<PAIR_STAGES_F32T, false, EPI_F32T>())),
                    "pair GEMM shared-memory attribute");
         // persistent grid: as many CTA pairs as can be resident at once
         auto clusters = [](const void *fn, size_t smem) {
@@ -605,7 +779,12 @@ void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap
                                  pair_smem_bytes<PAIR_STAGES, false>());
         pair_clusters_gelu = clusters(reinterpret_cast<const void *>(k_gemm_pair<PAIR_STAGES_GELU, true>),
                                       pair_smem_bytes<PAIR_STAGES_GELU, true>());
-        require(pair_clusters > 0 && pair_clusters_gelu > 0, "pair GEMM cannot be resident");
+        pair_clusters_push = clusters(reinterpret_cast<const void *>(k_gemm_pair<PAIR_STAGES_PUSH, false, EPI_PUSH>),
+                                      pair_smem_bytes<PAIR_STAGES_PUSH, false, EPI_PUSH>());
+        pair_clusters_f32t = clusters(reinterpret_cast<const void *>(k_gemm_pair<PAIR_STAGES_F32T, false, EPI_F32T>),
+                                      pair_smem_bytes<PAIR_STAGES_F32T, false, EPI_F32T>());
+        require(pair_clusters > 0 && pair_clusters_gelu > 0 && pair_clusters_push > 0 && pair_clusters_f32t > 0,
+                "pair GEMM cannot be resident");
         configured = true;
     }
     static int sms = 0;
@@ -615,12 +794,32 @@ void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (sms <= 0) sms = 148;
     }
+    if (a.out_mode == GEMM_OUT_PUSH) {
+        // partial products to their owners: CTA pairs only (callers pass more than 128 rows)
+        require(a.M > GEMM_BM && a.flags == 0, "pushed partial products need > 128 rows and no epilogue flags");
+        const int64_t tiles = ceil_div(a.N, GEMM_BN) * ceil_div(a.M, PAIR_BM);
+        const unsigned grid = unsigned(2 * (tiles < pair_clusters_push ? tiles : pair_clusters_push));
+        k_gemm_pair<PAIR_STAGES_PUSH, false, EPI_PUSH>
+            <<<grid, GEMM_THREADS, pair_smem_bytes<PAIR_STAGES_PUSH, false, EPI_PUSH>(), s>>>(ta, tb_pair, a);
+        return;
+    }
     if (a.M > GEMM_BM) {
         const int64_t tiles = ceil_div(a.N, GEMM_BN) * ceil_div(a.M, PAIR_BM);
         const bool gelu = (a.flags & 2) != 0;
-        const int64_t resident = gelu ? pair_clusters_gelu : pair_clusters;
+        // fp32 rows without the GELU table and with a short K (the epilogue-bound shapes, e.g.
+        // out_proj: 1280): the coalesced epilogue, where every row segment it touches is 16-byte
+        // aligned. With a long K the MMAs dominate and the re-lay's shared-memory traffic costs
+        // them more than the coalescing saves (fc2, K = 5120: 276 us against 262 us).
+        const bool aligned = uintptr_t(a.out) % 16 == 0 && a.ldo % 4 == 0 &&
+                             (!(a.flags & 4) || (uintptr_t(a.residual) % 16 == 0 && a.ldr % 4 == 0)) &&
+                             (!(a.flags & 1) || uintptr_t(a.bias) % 16 == 0);
+        const bool f32t = !gelu && a.out_mode == GEMM_OUT_F32 && a.N % 32 == 0 && a.K <= 2048 && aligned;
+        const int64_t resident = gelu ? pair_clusters_gelu : f32t ? pair_clusters_f32t : pair_clusters;
         const unsigned grid = unsigned(2 * (tiles < resident ? tiles : resident));
-        if (gelu)
+        if (f32t)
+            k_gemm_pair<PAIR_STAGES_F32T, false, EPI_F32T>
+                <<<grid, GEMM_THREADS, pair_smem_bytes<PAIR_STAGES_F32T, false, EPI_F32T>(), s>>>(ta, tb_pair, a);
+        else if (gelu)
             k_gemm_pair<PAIR_STAGES_GELU, true><<<grid, GEMM_THREADS, pair_smem_bytes<PAIR_STAGES_GELU, true>(), s>>>(
                 ta, tb_pair, a);
         else

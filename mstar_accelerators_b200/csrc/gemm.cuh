@@ -20,12 +20,22 @@ struct GemmArgs {
     int out_mode;           // GEMM_OUT_F32 / GEMM_OUT_F16 / GEMM_OUT_Q8
     int rounding;           // Q8_0 rounding of GEMM_OUT_Q8
     int *status;            // bit value 2: a bounded pipeline wait timed out; 1: nonfinite Q8_0 input
+    // GEMM_OUT_PUSH (row-parallel partial products delivered to their owners):
+    float *const *push_out; // [world] device pointers: each rank's receive buffer [world][push_rows][N] fp32
+    int *const *push_flags; // [world] device pointers: each rank's arrival counters, one per 32 owned rows
+    int64_t push_rows;      // rows per owner (a multiple of 32); row r belongs to owner r / push_rows
+    int push_rank;          // this rank: the slot its partials land in at every owner
 };
 
 // Output modes: fp32 rows; fp16 rows; or each 32-column block Q8_0-quantized
 // (ggml quantize_row_q8_0, selected rounding) and stored as fp16(q * d), the
-// staged A operand of the next GEMM.
-constexpr int GEMM_OUT_F32 = 0, GEMM_OUT_F16 = 1, GEMM_OUT_Q8 = 2;
+// staged A operand of the next GEMM; or (PUSH) the fp32 partial product stored
+// straight into the owning rank's receive slot over NVLink, followed by an
+// arrival on the owner's counter of those rows.
+constexpr int GEMM_OUT_F32 = 0, GEMM_OUT_F16 = 1, GEMM_OUT_Q8 = 2, GEMM_OUT_PUSH = 3;
+// Arrivals a 32-row group of an owner receives from one rank per pushed GEMM: one per
+// epilogue warp column group (4) and 256-column tile.
+__host__ __device__ constexpr int push_arrivals_per_rank(int64_t n) { return int(4 * ((n + 255) / 256)); }
 
 void make_fp16_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t k, int box_rows);
 void launch_dequant_weights(const uint8_t *blocks, __half *out, int64_t rows, int64_t nb, int q4, cudaStream_t s);

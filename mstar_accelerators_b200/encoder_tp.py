@@ -8,24 +8,28 @@ encoder block):
   * the convolution stems run replicated (1-2 % of the work);
   * QKV is column-parallel by heads (an uneven split when the heads do not
     divide, e.g. 20 heads over 8 ranks), attention runs on the local heads;
-  * out_proj is row-parallel (its K = the local heads' columns): every rank
-    writes its fp32 partial product into its own peer-visible buffer; rows are
-    split evenly into W owner ranges;
-  * after a peer barrier each owner pulls its rows' W partials over NVLink
-    (coalesced peer loads), sums them in rank order, adds the bias once, then
-    the residual (x = x + (sum + b)), LayerNorms and Q8_0-stages the new rows
-    straight into every rank's staged operand with peer stores (the all-gather
-    of the next column-parallel GEMM), and a second barrier publishes them;
+  * out_proj is row-parallel (its K = the local heads' columns); rows are split
+    into W owner ranges (whole 32-row groups);
+  * the row-parallel GEMM's epilogue stores each partial tile straight into
+    the owner's receive slot over NVLink and raises the owner's arrival counter
+    of those 32 rows (the reduction fused into the GEMM: the transfer runs under
+    the GEMM's MMAs, and no barrier separates the GEMM from the reduction);
+    each owner waits per 32-row group for every rank's arrivals, sums the slots
+    in rank order, adds the bias once, then the residual (x = x + (sum + b)),
+    LayerNorms and Q8_0-stages the new rows straight into every rank's staged
+    operand (the all-gather of the next column-parallel GEMM), and a barrier
+    publishes them;
   * fc1 is column-parallel (bias + GELU + Q8_0-staged output local), fc2
     row-parallel with the same fused reduction, whose staging applies the next
     layer's first LayerNorm;
   * the final LayerNorm runs on each owner's rows; ``forward`` all-gathers the
     rows (NCCL) so every rank returns the full encoder states.
-Where NVSwitch multicast (NVLS) is available, the reduction instead reads each
-owned row's sum over all ranks with multimem loads that add in the switch, and
-writes the staged rows once through the multicast address to every rank
-(mstar_b200_tp_reduce_multicast): an owner then moves its own rows over NVLink,
-not the W - 1 other ranks' partials of them.
+Two earlier forms stay selectable (``reduction``): "pull" (each rank's GEMM writes
+its partial locally, a barrier, then each owner pulls the W partials of its rows
+with peer loads) and "multicast" (after the barrier the owner reads each row's
+sum over all ranks with NVSwitch multimem loads that add in the switch). Where the
+platform binds the staged operand to a multicast object and there are at least
+four ranks, the staged rows are written once through the multicast address.
 Q8_0 blocks lie along K and every shard boundary is a multiple of 32, so each
 rank's weights are exactly sub-blocks of the single-GPU weights.
 """
@@ -88,14 +92,14 @@ class WhisperEncoderTP:
     """This rank's part of a tensor-parallel encoder for up to ``max_batch`` utterances."""
 
     def __init__(self, weights: dict, cfg: EncoderConfig, *, max_batch: int = 1, group=None, rounding: str = "arm",
-                 multicast: bool | None = None):
-        """multicast: reduce through the NVSwitch multicast object of the symmetric buffers
-        (multimem loads that sum in the switch, multimem stores to every rank); False keeps the
-        peer loads and stores; None picks multicast from 4 ranks up where the platform offers it.
-        Measured on 2 B200s (large-v3 shape, batch 16): peer loads 32.3 ms per forward, multicast
-        39.8 ms -- at two ranks an owner pulls the same bytes either way (one peer's partial rows)
-        and the multimem loads are slower; from four ranks the peer loads pull (W - 1) / W of the
-        partials against 1 / W reduced in the switch."""
+                 reduction: str = "push"):
+        """reduction: "push" (the default: partial tiles stored into the owners' receive slots
+        by the GEMM epilogue, per-32-row arrival counters, no barrier before the reduction);
+        "pull" (local partials, a peer barrier, owners pull with peer loads); "multicast"
+        (local partials, a barrier, owners read the sums with NVSwitch multimem loads; raises
+        ValueError where the platform has no multicast object). Measured on 2 B200s
+        (large-v3 shape, batch 16, before the push form): pull 32.3 ms per forward, multicast
+        39.8 ms."""
         import torch.distributed._symmetric_memory as symm
         self.lib = native.require_capability()
         self.group = group
@@ -144,11 +148,16 @@ class WhisperEncoderTP:
         # buffers
         T, P = cfg.positions, cfg.padded_keys
         M = max_batch * T
+        if reduction not in ("push", "pull", "multicast"):
+            raise ValueError("reduction must be 'push', 'pull' or 'multicast'")
+        self.reduction = reduction
         self.owner_rows_max = owner_split(M, self.world)
+        # pushed partials: owner ranges of whole 32-row groups (a group never spans two owners)
+        self.push_rows_max = -(-self.owner_rows_max // 32) * 32
         self.staged = torch.empty(max(2 * M * self.k1, M * self.k2), dtype=torch.float16, device=dev)
         self.conv_out = torch.empty((2 * M, d), dtype=torch.float32, device=dev)
         self.x_full = torch.empty((M, d), dtype=torch.float32, device=dev)
-        self.x_own = torch.empty((self.owner_rows_max, d), dtype=torch.float32, device=dev)
+        self.x_own = torch.empty((self.push_rows_max, d), dtype=torch.float32, device=dev)
         self.qkv16 = torch.zeros((max_batch, P, 3 * self.d_local), dtype=torch.float16, device=dev)
         self.att_staged = torch.empty((M, self.d_local), dtype=torch.float16, device=dev)
         self.hidden16 = torch.empty((M, self.f_local), dtype=torch.float16, device=dev)
@@ -158,25 +167,30 @@ class WhisperEncoderTP:
         pg = group if group is not None else dist.group.WORLD
         if hasattr(symm, "is_symm_mem_enabled_for_group") and not symm.is_symm_mem_enabled_for_group(pg.group_name):
             symm.enable_symm_mem_for_group(pg.group_name)
-        self.part = symm.empty(M * d, dtype=torch.float32, device=dev)
+        # partials: [M][d] local (pull / multicast) or the receive slots [world][push_rows][d] (push)
+        part_rows = self.world * self.push_rows_max if reduction == "push" else M
+        self.part = symm.empty(part_rows * d, dtype=torch.float32, device=dev)
         self.ln_staged = symm.empty(M * d, dtype=torch.float16, device=dev)
         self.flags = symm.empty(self.world, dtype=torch.int32, device=dev)
+        self.arrivals = symm.empty(self.push_rows_max // 32 + 1, dtype=torch.int32, device=dev)
         self.flags.zero_()
+        self.arrivals.zero_()
         torch.cuda.synchronize()
         pg = group if group is not None else dist.group.WORLD
-        self._h = [symm.rendezvous(t, pg) for t in (self.part, self.ln_staged, self.flags)]
+        self._h = [symm.rendezvous(t, pg) for t in (self.part, self.ln_staged, self.flags, self.arrivals)]
         def ptrs(h):
             return torch.tensor(h.buffer_ptrs, dtype=torch.int64, device=dev)
-        self.part_ptrs, self.staged_ptrs, self.flag_ptrs = (ptrs(h) for h in self._h)
+        self.part_ptrs, self.staged_ptrs, self.flag_ptrs, self.arrival_ptrs = (ptrs(h) for h in self._h)
         mc = [int(getattr(h, "multicast_ptr", 0) or 0) for h in self._h[:2]]
-        available = self.world > 1 and all(mc)
-        if multicast and not available:
+        # every rank must take the same path: an all-reduce of what each rank can do
+        avail = torch.tensor([1 if self.world > 1 and mc[0] else 0, 1 if self.world > 1 and mc[1] else 0],
+                             dtype=torch.int32, device=dev)
+        dist.all_reduce(avail, op=dist.ReduceOp.MIN, group=group)
+        if reduction == "multicast" and not bool(avail[0].item() and avail[1].item()):
             raise ValueError("the symmetric buffers have no multicast object on this platform")
-        # every rank must take the same path: use multicast only if all ranks have it
-        want = multicast if multicast is not None else self.world >= MULTICAST_FROM_RANKS
-        flag = torch.tensor([1 if available and want else 0], dtype=torch.int32, device=dev)
-        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
-        self.multicast = bool(flag.item())
+        self.multicast = reduction == "multicast"
+        # the staged rows of the pushed form go through the multicast address from four ranks up
+        self.mc_staged_rows = reduction == "push" and bool(avail[1].item()) and self.world >= MULTICAST_FROM_RANKS
         self.mc_part, self.mc_staged = mc
         dist.barrier(group=group)
 
@@ -187,14 +201,30 @@ class WhisperEncoderTP:
                                              self.counter.data_ptr(), self.status.data_ptr(), _stream(self.device),
                                              e, len(e)), e, "B200 TP barrier")
 
-    def _partial(self, lin: BlockLinear, staged: torch.Tensor):
-        """Row-parallel partial product [M][width] fp32 into this rank's peer-visible buffer."""
+    def _partial(self, lin: BlockLinear, staged: torch.Tensor, owner_rows: int):
+        """Row-parallel partial product: pushed into the owners' receive slots, or [M][width]
+        fp32 into this rank's peer-visible buffer followed by the barrier the pull needs."""
+        if self.reduction == "push":
+            lin.gemm_push(staged, recv_ptrs=self.part_ptrs, flag_ptrs=self.arrival_ptrs, world=self.world,
+                          rank=self.rank, owner_rows=owner_rows, status=self.status)
+            return
         lin.gemm(staged, out=self.part[:staged.shape[0] * lin.rows].view(-1, lin.rows), bias=False,
                  rounding=self.rounding, status=self.status)
+        self._barrier()
 
     def _reduce(self, owner_rows: int, owned: int, bias: torch.Tensor, norm):
         lw, lb, eps = (norm[0].data_ptr(), norm[1].data_ptr(), float(norm[2])) if norm else (None, None, 0.0)
         e = error_buffer()
+        if self.reduction == "push":
+            staged = (None, self.mc_staged) if self.mc_staged_rows else (self.staged_ptrs.data_ptr(), None)
+            check(self.lib.mstar_b200_tp_reduce_recv(self.part.data_ptr(), self.arrivals.data_ptr(), self.world,
+                                                     owned, owner_rows, self.cfg.width, bias.data_ptr(),
+                                                     self.x_own.data_ptr(), lw, lb, eps,
+                                                     staged[0] if norm else None, staged[1] if norm else None,
+                                                     self.rank * owner_rows, native.ROUNDING[self.rounding],
+                                                     self.status.data_ptr(), _stream(self.device), e, len(e)),
+                  e, "B200 TP reduce")
+            return
         if self.multicast:
             check(self.lib.mstar_b200_tp_reduce_multicast(self.mc_part, self.world, owned, self.cfg.width,
                                                           bias.data_ptr(), self.x_own.data_ptr(), lw, lb, eps,
@@ -209,12 +239,15 @@ class WhisperEncoderTP:
                                             _stream(self.device), e, len(e)), e, "B200 TP reduce")
 
     # ------------------------------------------------------------------ forward
-    # Buffer hazards between ranks are covered by the barrier after each partial
-    # GEMM (every partial is complete, and every rank has finished the GEMMs
-    # that read ln_staged, before any owner reads partials or writes staged
-    # rows) and the barrier after each reduction (the staged rows are complete
-    # before the next column-parallel GEMM reads them, and every owner has read
-    # the partials before any rank overwrites its partial buffer).
+    # Buffer hazards between ranks. Pull / multicast: the barrier after each partial
+    # GEMM (every partial is complete, and every rank has finished the GEMMs that read
+    # ln_staged, before any owner reads partials or writes staged rows). Push: an owner
+    # finishes a 32-row group only after every rank's arrivals for it, and a rank's
+    # pushing GEMM starts after its own GEMMs that read ln_staged, so no staged row is
+    # overwritten while a rank still reads it. Both: the barrier after each reduction
+    # (the staged rows are complete before the next column-parallel GEMM reads them, and
+    # every owner has consumed the partials and cleared its counters before any rank
+    # writes partials again).
     def forward(self, mel: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """mel fp32 [batch, mels, 2 * positions] (the same on every rank) ->
         encoder_states fp32 [batch, positions, width] on every rank (into ``out`` when given)."""
@@ -225,6 +258,8 @@ class WhisperEncoderTP:
         d, T, P, H = cfg.width, cfg.positions, cfg.padded_keys, self.heads_local
         M = B * T
         own_rows = owner_split(M, self.world)
+        if self.reduction == "push":
+            own_rows = -(-own_rows // 32) * 32
         row0 = self.rank * own_rows
         owned = max(0, min(M, row0 + own_rows) - row0)
         st = self.status
@@ -249,14 +284,12 @@ class WhisperEncoderTP:
             v = qkv[:, :, 2 * dl:].unflatten(-1, (H, hd)).transpose(1, 2)
             att = F.scaled_dot_product_attention(q, k, v, scale=hd ** -0.5).transpose(1, 2).reshape(M, dl)
             sa = stage_rows(att, rounding=r, out=self.att_staged[:M], status=st)
-            self._partial(L["out"], sa)
-            self._barrier()
+            self._partial(L["out"], sa, own_rows)
             self._reduce(own_rows, owned, L["out_b"], L["ln2"])
             self._barrier()
             h = L["fc1"].gemm(ln_staged, out=self.hidden16[:M], out_format="staged", gelu="tanh", rounding=r,
                               status=st)
-            self._partial(L["fc2"], h)
-            self._barrier()
+            self._partial(L["fc2"], h, own_rows)
             nxt = self.layers[i + 1]["ln1"] if i + 1 < len(self.layers) else None
             self._reduce(own_rows, owned, L["fc2_b"], nxt)
             self._barrier()
@@ -276,10 +309,10 @@ class WhisperEncoderTP:
     def launches_per_forward(self) -> int:
         """This library's kernel launches in one forward: the replicated stems (two stagings,
         two GEMMs), the first LayerNorm staging, per layer two column-parallel GEMMs, the
-        attention staging, two row-parallel partial GEMMs, two reductions and four peer
-        barriers, then the final LayerNorm. The attention, the row copy and the closing
-        all-gather are torch / NCCL."""
-        return 4 + 1 + 11 * len(self.layers) + 1
+        attention staging, two row-parallel partial GEMMs, two reductions and two peer
+        barriers (four with the pulled forms), then the final LayerNorm. The attention, the
+        row copy and the closing all-gather are torch / NCCL."""
+        return 4 + 1 + (9 if self.reduction == "push" else 11) * len(self.layers) + 1
 
     def close(self):
         for lin in [self.conv1, self.conv2] + [L[k] for L in self.layers for k in ("qkv", "out", "fc1", "fc2")]:

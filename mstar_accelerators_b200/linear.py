@@ -347,6 +347,25 @@ class BlockLinear:
               e, "B200 GEMM")
         return out
 
+    def gemm_push(self, staged: torch.Tensor, *, recv_ptrs: torch.Tensor, flag_ptrs: torch.Tensor, world: int,
+                  rank: int, owner_rows: int, status: torch.Tensor) -> None:
+        """Row-parallel partial product (fp32, no bias) of more than 128 staged rows, stored by
+        the GEMM epilogue into the owning ranks' receive slots (row r -> owner r // owner_rows,
+        slot ``rank``) with one arrival per 32 rows on the owner's counters.
+
+        recv_ptrs / flag_ptrs: int64 device tensors of ``world`` device pointers (symmetric memory)."""
+        if not self.gemm_rows:
+            raise ValueError("prepare_gemm must run before gemm_push")
+        _require_cuda(staged, "staged operand", torch.float16)
+        if staged.ndim != 2 or staged.shape[1] != self.width or not staged.is_contiguous():
+            raise ValueError("staged operand must be a contiguous [rows, width] fp16 matrix")
+        rows = staged.shape[0]
+        e = error_buffer()
+        check(self.lib.mstar_b200_linear_gemm_push(self.handle, staged.data_ptr(), rows * self.width * 2, rows,
+                                                   recv_ptrs.data_ptr(), flag_ptrs.data_ptr(), world, rank,
+                                                   owner_rows, status.data_ptr(), _stream(staged.device), e, len(e)),
+              e, "B200 pushed GEMM")
+
     def prepare_exact(self) -> None:
         """Lay the Q8_0 weights out for the exact int8-tensor-pipe GEMM (int8 quants + fp32 scales)."""
         if self.fmt != "q8_0":

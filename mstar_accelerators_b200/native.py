@@ -57,6 +57,10 @@ SIGNATURES = {
     "mstar_b200_linear_gemm": (_int, [_vp, _vp, _u64, _i64, _vp, _u64, _i64, C.c_int32, _vp, _u64, _i64, _i64, _i64,
                                       _i64, C.c_int32, C.c_int32, _vp, _vp, *_err]),
     "mstar_b200_tp_barrier": (_int, [_vp, _vp, C.c_int32, C.c_int32, _vp, _vp, _vp, *_err]),
+    "mstar_b200_linear_gemm_push": (_int, [_vp, _vp, _u64, _i64, _vp, _vp, C.c_int32, C.c_int32, _i64, _vp, _vp,
+                                           *_err]),
+    "mstar_b200_tp_reduce_recv": (_int, [_vp, _vp, C.c_int32, _i64, _i64, _i64, _vp, _vp, _vp, _vp, C.c_float, _vp,
+                                         _vp, _i64, C.c_int32, _vp, _vp, *_err]),
     "mstar_b200_tp_reduce_multicast": (_int, [_vp, C.c_int32, _i64, _i64, _vp, _vp, _vp, _vp, C.c_float, _vp, _i64,
                                               C.c_int32, _vp, _vp, *_err]),
     "mstar_b200_set_wait_limits": (_int, [_i64, _i64, *_err]),
