@@ -591,7 +591,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(leader_acc_empty[buf]);
+                if (lane == 0) mbar_arrive_cluster_relaxed(leader_acc_empty[buf]);
                 continue;
             }
             if (EPI == EPI_PUSH) {
@@ -604,7 +604,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(leader_acc_empty[buf]);
+                if (lane == 0) mbar_arrive_cluster_relaxed(leader_acc_empty[buf]);
                 continue;
             }
             const int64_t orow_i = a.seg_rows ? (row / a.seg_rows) * a.out_seg_rows + row % a.seg_rows : row;
@@ -616,7 +616,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(leader_acc_empty[buf]);
+            if (lane == 0) mbar_arrive_cluster_relaxed(leader_acc_empty[buf]);
         }
         if (EPI == EPI_PUSH) {
             // every lane's stores of every tile reach their owners before the arrivals that

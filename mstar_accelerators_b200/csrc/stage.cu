@@ -5,9 +5,11 @@
 //                 activation side of ggml_mul_mat(Q8_0 W, x) after
 //                 encoder_norm_affine (encoder.cpp:117-142) or on the fp32
 //                 attention output;
-//   k_stage_conv  (a warp per Q8_0 block) the im2col columns of convolution_q8 (encoder.cpp:45-52: kernel
-//                 3, padding 1, column = channel * 3 + tap, K zero-padded to a
-//                 multiple of 32, encoder.cpp:551) quantized the same way;
+//   k_stage_conv_tm / _cm  (a warp per output row, the source tile in shared memory;
+//                 k_stage_conv, a warp per Q8_0 block, for sources too wide for it) the
+//                 im2col columns of convolution_q8 (encoder.cpp:45-52: kernel 3, padding 1,
+//                 column = channel * 3 + tap, K zero-padded to a multiple of 32,
+//                 encoder.cpp:551) quantized the same way;
 //   k_layer_norm  the final encoder_norm_affine to fp32 (encoder.cpp:725).
 // Q8_0 quantization follows ggml quantize_row_q8_0 with the selected rounding
 // (ref / ARM / x86); a nonfinite input sets status bit value 1.
@@ -192,6 +194,89 @@ __global__ void __launch_bounds__(STAGE_WARPS * 32)
     out[row * k_padded + col] = __float2half_rn(q8_staged<MODE>(v, status));
 }
 
+// The same columns, a warp per output row and four columns per lane (eight lanes per
+// Q8_0 block, as k_stage_rows), read from the source in shared memory so that every
+// global load is a whole 16-byte vector of a contiguous run:
+//   k_stage_conv_tm: time-major source [batch][time_in][channels]; the warp copies the
+//     three source rows its output row needs (zeros outside the input) into its own
+//     shared rows [3][channels], then column c * 3 + tap is shared row tap, entry c;
+//   k_stage_conv_cm: channel-major source [batch][channels][time_in]; the CTA copies the
+//     time span CONV_TILE output rows need of every channel ([channels][span] floats,
+//     contiguous runs per channel) and each warp stages CONV_TILE / CONV_WARPS rows.
+// Bytes are those of k_stage_conv (the same block quantization of the same values).
+constexpr int CONV_WARPS = 4, CONV_TILE = 32;
+constexpr int64_t CONV_TM_MAX_CHANNELS = 2048;   // 24 KB of shared rows per warp
+constexpr int64_t CONV_CM_MAX_SMEM = 96 * 1024;  // channel-major tile
+
+template <int MODE>
+__device__ __forceinline__ void conv_row_out(const float *sm, int64_t cstride, int64_t tstride, int64_t channels,
+                                             int64_t k_padded, __half *out_row, int lane, int *status) {
+    // column c * 3 + tap of this row is sm[c * cstride + tap * tstride]
+    for (int64_t i = 0; i * 128 < k_padded; ++i) {   // warp-uniform: every lane takes part in the block shuffles
+        const int64_t col0 = (i * 32 + lane) * 4;
+        float e[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t col = col0 + u;
+            e[u] = col < 3 * channels ? sm[(col / 3) * cstride + (col % 3) * tstride] : 0.0f;
+        }
+        const float4 q = q8_block8<MODE>(make_float4(e[0], e[1], e[2], e[3]), status);
+        if (col0 < k_padded) store4(out_row, col0, q);
+    }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(CONV_WARPS * 32)
+    k_stage_conv_tm(const float *__restrict__ src, int64_t batch, int64_t channels, int64_t time_in,
+                    int64_t time_out, int stride, int64_t k_padded, __half *__restrict__ out,
+                    int *__restrict__ status) {
+    extern __shared__ __align__(16) float conv_smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t row = int64_t(blockIdx.x) * CONV_WARPS + warp;
+    if (row >= batch * time_out) return;   // warp-uniform; no CTA-wide barrier follows
+    float *sm = conv_smem + int64_t(warp) * 3 * channels;   // [tap][channels]
+    const int64_t b = row / time_out, t = row % time_out;
+#pragma unroll
+    for (int tap = 0; tap < 3; ++tap) {
+        const int64_t ti = t * stride + tap - 1;
+        const bool in = ti >= 0 && ti < time_in;
+        const float *s = src + (b * time_in + (in ? ti : 0)) * channels;
+        if (channels % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {   // whole 16-byte vectors
+            for (int64_t c4 = lane; c4 < channels / 4; c4 += 32)
+                *reinterpret_cast<float4 *>(sm + tap * channels + 4 * c4) =
+                    in ? *reinterpret_cast<const float4 *>(s + 4 * c4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        } else {
+            for (int64_t c = lane; c < channels; c += 32) sm[tap * channels + c] = in ? s[c] : 0.0f;
+        }
+    }
+    __syncwarp();
+    conv_row_out<MODE>(sm, 1, channels, channels, k_padded, out + row * k_padded, lane, status);
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(CONV_WARPS * 32)
+    k_stage_conv_cm(const float *__restrict__ src, int64_t batch, int64_t channels, int64_t time_in,
+                    int64_t time_out, int stride, int64_t k_padded, __half *__restrict__ out,
+                    int *__restrict__ status) {
+    extern __shared__ __align__(16) float conv_smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t tiles = (time_out + CONV_TILE - 1) / CONV_TILE;
+    const int64_t b = blockIdx.x / tiles, t0 = (blockIdx.x % tiles) * CONV_TILE;
+    const int64_t span = (CONV_TILE - 1) * stride + 3;   // source times t0 * stride - 1 .. of every channel
+    const int64_t first = t0 * stride - 1;
+    for (int64_t i = threadIdx.x; i < channels * span; i += blockDim.x) {
+        const int64_t c = i / span, j = i % span, ti = first + j;
+        conv_smem[i] = ti >= 0 && ti < time_in ? src[(b * channels + c) * time_in + ti] : 0.0f;
+    }
+    __syncthreads();
+    for (int r = warp; r < CONV_TILE; r += CONV_WARPS) {
+        const int64_t t = t0 + r;
+        if (t >= time_out) break;   // warp-uniform
+        conv_row_out<MODE>(conv_smem + int64_t(r) * stride, span, 1, channels, k_padded,
+                           out + (b * time_out + t) * k_padded, lane, status);
+    }
+}
+
 __global__ void __launch_bounds__(STAGE_WARPS * 32)
     k_layer_norm(const float *__restrict__ x, int64_t ldx, int64_t rows, int64_t k, const float *__restrict__ w,
                  const float *__restrict__ bias, float eps, float *__restrict__ out, int64_t ldo) {
@@ -236,8 +321,39 @@ void launch_stage_rows(int mode, const void *x, int x_f16, int64_t ldx, int64_t 
     else stage_rows_mode<1>(x, x_f16, ldx, rows, k, ln_w, ln_b, ln_eps, out, ldo, status, s);
 }
 
+template <int MODE>
+static bool launch_stage_conv_rows(const float *src, int time_major, int64_t batch, int64_t channels,
+                                   int64_t time_in, int64_t time_out, int stride, int64_t k_padded, __half *out,
+                                   int *status, cudaStream_t s) {
+    const int threads = CONV_WARPS * 32;
+    if (time_major) {
+        if (channels > CONV_TM_MAX_CHANNELS) return false;
+        const size_t smem = size_t(CONV_WARPS) * 3 * channels * 4;
+        cuda_check(cudaFuncSetAttribute(k_stage_conv_tm<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+                   "convolution staging shared memory");
+        k_stage_conv_tm<MODE><<<unsigned(ceil_div(batch * time_out, CONV_WARPS)), threads, smem, s>>>(
+            src, batch, channels, time_in, time_out, stride, k_padded, out, status);
+        return true;
+    }
+    const size_t smem = size_t(channels) * ((CONV_TILE - 1) * stride + 3) * 4;
+    if (smem > size_t(CONV_CM_MAX_SMEM)) return false;
+    cuda_check(cudaFuncSetAttribute(k_stage_conv_cm<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+               "convolution staging shared memory");
+    k_stage_conv_cm<MODE><<<unsigned(batch * ceil_div(time_out, CONV_TILE)), threads, smem, s>>>(
+        src, batch, channels, time_in, time_out, stride, k_padded, out, status);
+    return true;
+}
+
 void launch_stage_conv(int mode, const float *src, int time_major, int64_t batch, int64_t channels, int64_t time_in,
                        int64_t time_out, int stride, int64_t k_padded, __half *out, int *status, cudaStream_t s) {
+    // row kernels where the source tile fits in shared memory; a warp per block otherwise
+    const bool rows = mode == 0   ? launch_stage_conv_rows<0>(src, time_major, batch, channels, time_in, time_out,
+                                                                stride, k_padded, out, status, s)
+                      : mode == 2 ? launch_stage_conv_rows<2>(src, time_major, batch, channels, time_in, time_out,
+                                                                stride, k_padded, out, status, s)
+                                  : launch_stage_conv_rows<1>(src, time_major, batch, channels, time_in, time_out,
+                                                                stride, k_padded, out, status, s);
+    if (rows) return;
     const unsigned grid = unsigned(ceil_div(batch * time_out * (k_padded / QK), STAGE_WARPS));
     const int threads = STAGE_WARPS * 32;
     if (mode == 0)

@@ -54,6 +54,13 @@ __device__ __forceinline__ uint32_t cluster_smem(const void *p, uint32_t rank) {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
+// Arrival on a pair barrier that orders nothing but the arriving warp's completed TMEM
+// loads (tcgen05.wait::ld, then tcgen05.fence::before_thread_sync): the accumulator-free
+// signal. A release arrival would first wait for every global store the warp issued
+// (the epilogue's output rows) to reach L2, holding the accumulator from the MMAs.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
 // 2-D tile into this CTA's shared memory whose byte count completes on the pair
 // leader's barrier (`leader_bar`, a shared::cluster address); no multicast.
 __device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, int x, int y, uint32_t leader_bar) {
