@@ -42,7 +42,12 @@
 
 namespace mb {
 
-constexpr int MOE_BM = 128, MOE_BN = 256, MOE_BK = 64, MOE_STAGES = 4, MOE_THREADS = 192;
+// 2 + 16 warps: the TMA producer, the MMA issuer and four epilogue warps per TMEM lane
+// quarter, each taking a quarter of a tile's columns (the SwiGLU epilogue's exp and
+// bf16 roundings and the down epilogue's 16-byte row stores have four warps per
+// scheduler to hide their latencies)
+constexpr int MOE_EPI_WARPS = 16;
+constexpr int MOE_BM = 128, MOE_BN = 256, MOE_BK = 64, MOE_STAGES = 4, MOE_THREADS = 64 + 32 * MOE_EPI_WARPS;
 constexpr int MOE_A_BYTES = MOE_BM * MOE_BK * 2, MOE_B_BYTES = MOE_BN * MOE_BK * 2;
 constexpr int MOE_STAGE_BYTES = MOE_A_BYTES + MOE_B_BYTES;
 constexpr size_t MOE_SMEM = size_t(MOE_STAGES) * MOE_STAGE_BYTES + 1024 + 256;
@@ -568,7 +573,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(acc_full + b, 1);
-            mbar_init(acc_empty + b, 4);
+            mbar_init(acc_empty + b, MOE_EPI_WARPS);
         }
         fence_mbar_init();
     }
@@ -640,7 +645,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1)
             }
         }
     } else {
-        const int q = warp & 3;
+        const int q = warp & 3;            // TMEM lane quarter this warp may read
+        const int cg = (warp - 2) / 4;     // its quarter of the tile's columns
         int64_t local = 0;
         for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
             const int buf = int(local & 1);
@@ -654,8 +660,9 @@ __global__ void __launch_bounds__(MOE_THREADS, 1)
             const int row = r0 + 32 * q + lane;
             const uint32_t tb0 = tmem + (uint32_t(32 * q) << 16) + uint32_t(buf * MOE_BN);
             if (MODE == MOE_SWIGLU) {
-                // columns [0,128) gate, [128,256) up of output columns nt*128 + [0,128)
-                for (int c = 0; c < 4; ++c) {
+                // columns [0,128) gate, [128,256) up of output columns nt*128 + [0,128):
+                // this warp's block c = cg of each
+                for (int c = cg; c < cg + 1; ++c) {
                     uint32_t g[32], u[32];
                     tmem_ld32(tb0 + uint32_t(c * 32), g);
                     tmem_ld32(tb0 + uint32_t(128 + c * 32), u);
@@ -709,7 +716,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1)
                 }
             } else {
                 const float w = row < r1 ? a.topk_w[a.perm[row]] : 0.0f;
-                for (int c = 0; c < MOE_BN / 32; ++c) {
+                for (int c = 2 * cg; c < 2 * cg + 2; ++c) {   // this warp's two 32-column blocks
                     uint32_t r[32];
                     tmem_ld32(tb0 + uint32_t(c * 32), r);
                     if (row < r1) {  // 16-byte stores: 4 per row chunk

@@ -173,22 +173,32 @@ class ThinkerStackB200:
         """x + MoE(h) in bf16."""
         return x + self._moe(L, h)
 
-    def _layer(self, i: int, x: torch.Tensor, S: int, n: int, start, pos: torch.Tensor) -> torch.Tensor:
-        """x [S * n, H] bf16: n new positions of each of S sequences; pos [S * n] int64 their
-        positions (device). Prefill (start == 0, n > 1): causal attention over the n positions.
+    def _positions(self, S: int, n: int, pos: torch.Tensor):
+        """What every layer of a step shares, computed once per step: the rotary tables of the
+        positions, each new row's KV-cache slot and (decode) the additive mask over the cache."""
+        cos, sin = rotary(pos, self.cfg)
+        slots = torch.arange(S, device=pos.device).repeat_interleave(n) * self.max_len + pos
+        mask = None
+        if n == 1:
+            mask = torch.where(torch.arange(self.max_len, device=pos.device)[None, :] <= pos[:, None], 0.0,
+                               float("-inf")).to(torch.bfloat16).view(S, 1, 1, self.max_len)
+        return cos, sin, slots, mask
+
+    def _layer(self, i: int, x: torch.Tensor, S: int, n: int, start, shared) -> torch.Tensor:
+        """x [S * n, H] bf16: n new positions of each of S sequences; shared: _positions() of
+        their positions. Prefill (start == 0, n > 1): causal attention over the n positions.
         Decode (n == 1): every query attends to the cache up to its own position through a
         fixed-length view of the whole cache and an additive mask, so the step's shapes never
         change (one CUDA graph replays it)."""
         cfg, L = self.cfg, self.layers[i]
         D, Hq, Hk = cfg.head_dim, self.q_heads, self.kv_heads
         T = S * n
+        cos, sin, slots, mask = shared
         h = rms_norm(x, L["ln1"], cfg.eps)
         qkv = self._linear(L["qkv"], h).to(torch.bfloat16)
         q = qkv[:, :Hq * D].view(T, Hq, D)
         k = qkv[:, Hq * D:(Hq + Hk) * D].view(T, Hk, D)
         v = qkv[:, (Hq + Hk) * D:].view(T, Hk, D)
-        cos, sin = rotary(pos, cfg)
-        slots = torch.arange(S, device=x.device).repeat_interleave(n) * self.max_len + pos
         q, _ = qknorm_rope(q, k, L["q_norm"], L["k_norm"], cos, sin, eps=cfg.eps, v=v, k_cache=self.k_cache[i],
                            v_cache=self.v_cache[i], slots=slots, status=self.status)
         if n == 1:
@@ -196,8 +206,6 @@ class ThinkerStackB200:
             vv = self.v_cache[i].view(self.max_seqs, self.max_len, Hk, D)[:S].transpose(1, 2)
             # the query heads of one KV head as that head's query rows: [S, Hk, Hq / Hk, D]
             qq = q.view(S, Hk, Hq // Hk, D)
-            mask = torch.where(torch.arange(self.max_len, device=x.device)[None, :] <= pos[:, None], 0.0,
-                               float("-inf")).to(torch.bfloat16).view(S, 1, 1, self.max_len)
             att = F.scaled_dot_product_attention(qq, kk, vv, attn_mask=mask, scale=D ** -0.5)
             att = att.reshape(T, Hq * D)
         else:
@@ -230,16 +238,18 @@ class ThinkerStackB200:
             raise ValueError("prompt exceeds the prepared capacity")
         x = self._embed(tokens)
         pos = torch.arange(n, device=self.device).repeat(S)
+        shared = self._positions(S, n, pos)
         for i in range(self.cfg.layers):
-            x = self._layer(i, x, S, n, 0, pos)
+            x = self._layer(i, x, S, n, 0, shared)
         self.length, self.seqs = n, S
         self.graph = None
         return self._readout(x.view(S, n, -1)[:, -1])
 
     def _decode_step(self, tokens: torch.Tensor, pos: torch.Tensor):
         x = self._embed(tokens)
+        shared = self._positions(tokens.shape[0], 1, pos)
         for i in range(self.cfg.layers):
-            x = self._layer(i, x, tokens.shape[0], 1, None, pos)
+            x = self._layer(i, x, tokens.shape[0], 1, None, shared)
         return self._readout(x)
 
     def decode(self, tokens: torch.Tensor, *, graph: bool = False):
