@@ -392,6 +392,25 @@ MSTAR_B200_API int mstar_b200_gemm_q8_exact(const void *x_i8, const float *x_sca
     const float *w_scales, int64_t out_features, int64_t width, const float *bias, float *out, int64_t out_stride,
     int32_t *status, void *stream, char *error, size_t error_size);
 
+/* --- thinker layer norms (transformers' Qwen3OmniMoeThinkerTextRMSNorm, the input and
+ * post-attention norms of the reference's thinker layer, implementations/qwen3_omni/amd/
+ * thinker_model.py:106-148) ---
+ * rms_norm: for every row of `width` bf16 values (8..4096, a multiple of 8): h = fp32(x),
+ * r = rsqrtf(sum(h^2) / width + eps), out = bf16(fp32(weight) * fp32(bf16(h * r))) (bf16
+ * [rows][out_stride]); when out_f32 is given the same values are also written as fp32.
+ * The sum of squares is a per-lane fp32 sum and a warp butterfly (torch reduces in
+ * another order: the mean can differ in the last bit). Operands 16-byte aligned,
+ * strides in elements. */
+MSTAR_B200_API int mstar_b200_rms_norm(const void *x, int64_t x_stride, int64_t rows, int64_t width,
+    const void *weight, float eps, void *out, int64_t out_stride, float *out_f32, int64_t out_f32_stride,
+    void *stream, char *error, size_t error_size);
+/* residual_add_bf16: out = bf16(fp32(x) + fp32(bf16(v))) for n elements (a multiple of 8):
+ * the layer's bf16 residual add of a projection computed in fp32 and rounded to bf16
+ * (x + o_proj(att), thinker_model.py:106-148). x, out bf16, v fp32, 16-byte aligned; out
+ * may be x. */
+MSTAR_B200_API int mstar_b200_residual_add_bf16(const void *x, const float *v, int64_t n, void *out, void *stream,
+    char *error, size_t error_size);
+
 /* --- thinker attention prologue (implementations/qwen3_omni/amd/qknorm_rope.py:9-53, the
  * fused QK RMSNorm + prepared MRoPE op; KV write as cp_kernels.py:16-58) ---
  * qknorm_rope: for every token t and head of 128 bf16 values: x = q or k head row,

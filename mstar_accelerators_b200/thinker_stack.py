@@ -28,8 +28,10 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
-from .linear import BlockLinear, pack
+from . import native
+from .linear import BlockLinear, _stream, pack
 from .moe import ThinkerMoEB200, route
+from .native import check, error_buffer
 from .thinker import qknorm_rope
 
 
@@ -69,11 +71,32 @@ def head_weights(cfg: ThinkerStackConfig, seed: int = 1, device="cuda") -> dict:
             "lm_head": (torch.randn((cfg.vocab, cfg.hidden), generator=g, device=device) * 0.02).to(torch.bfloat16)}
 
 
-def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    """transformers' Qwen3OmniMoeThinkerTextRMSNorm: fp32 normalisation, bf16 before the weight."""
-    h = x.float()
-    h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + eps)
-    return w * h.to(x.dtype)
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, *, f32: bool = False) -> torch.Tensor:
+    """transformers' Qwen3OmniMoeThinkerTextRMSNorm (fp32 normalisation, bf16 before the weight)
+    in one launch (mstar_b200_rms_norm): bf16 x [rows, width] -> bf16 rows, or with f32 the
+    same values as fp32 (the Q8_0 linears' input)."""
+    lib = native.require_capability()
+    x = x.contiguous()
+    rows, width = x.shape
+    out = torch.empty_like(x)
+    out32 = torch.empty((rows, width), dtype=torch.float32, device=x.device) if f32 else None
+    e = error_buffer()
+    check(lib.mstar_b200_rms_norm(x.data_ptr(), width, rows, width, w.contiguous().data_ptr(), float(eps),
+                                  out.data_ptr(), width, out32.data_ptr() if f32 else None, width,
+                                  _stream(x.device), e, len(e)), e, "B200 RMSNorm")
+    return out32 if f32 else out
+
+
+def residual_add(x: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """x + v.to(bf16) in bf16 (torch's residual add of a projection computed in fp32) in one
+    launch (mstar_b200_residual_add_bf16): bf16 x, fp32 v of the same shape -> new bf16 tensor."""
+    lib = native.require_capability()
+    x, v = x.contiguous(), v.contiguous()
+    out = torch.empty_like(x)
+    e = error_buffer()
+    check(lib.mstar_b200_residual_add_bf16(x.data_ptr(), v.data_ptr(), x.numel(), out.data_ptr(), _stream(x.device),
+                                           e, len(e)), e, "B200 residual add")
+    return out
 
 
 def rotary(positions: torch.Tensor, cfg: ThinkerStackConfig):
@@ -155,6 +178,9 @@ class ThinkerStackB200:
         return out
 
     def _moe(self, L, h: torch.Tensor) -> torch.Tensor:
+        if h.shape[0] <= self.gemm_rows:   # one chunk: the layer's output as it comes
+            w, ids = route(h, L["router"], top_k=self.cfg.top_k)
+            return L["moe"](h, w, ids)
         out = torch.empty_like(h)
         for r0 in range(0, h.shape[0], self.gemm_rows):
             part = h[r0:r0 + self.gemm_rows]
@@ -167,7 +193,7 @@ class ThinkerStackB200:
 
     def _attention_out(self, L, att: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
         """x + o_proj(att) in bf16."""
-        return x + self._linear(L["o"], att).to(torch.bfloat16)
+        return residual_add(x, self._linear(L["o"], att))
 
     def _moe_residual(self, L, h: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
         """x + MoE(h) in bf16."""
@@ -194,7 +220,7 @@ class ThinkerStackB200:
         D, Hq, Hk = cfg.head_dim, self.q_heads, self.kv_heads
         T = S * n
         cos, sin, slots, mask = shared
-        h = rms_norm(x, L["ln1"], cfg.eps)
+        h = rms_norm(x, L["ln1"], cfg.eps, f32=True)
         qkv = self._linear(L["qkv"], h).to(torch.bfloat16)
         q = qkv[:, :Hq * D].view(T, Hq, D)
         k = qkv[:, Hq * D:(Hq + Hk) * D].view(T, Hk, D)
@@ -224,7 +250,7 @@ class ThinkerStackB200:
         return self._moe_residual(L, h, x)
 
     def _readout(self, last: torch.Tensor):
-        h = rms_norm(last, self.final_norm, self.cfg.eps).float().contiguous()
+        h = rms_norm(last, self.final_norm, self.cfg.eps, f32=True)
         logits = torch.empty((h.shape[0], self.cfg.vocab), dtype=torch.float32, device=h.device)
         tokens = torch.empty(h.shape[0], dtype=torch.int64, device=h.device)
         self.lm_head.readout(h, logits=logits, token=tokens, status=self.status)
