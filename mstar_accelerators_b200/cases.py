@@ -130,6 +130,43 @@ def thinker_stack_48():
     stack.close()
 
 
+def thinker_stack_4_decode():
+    """Four thinker layers (the 48-layer stack's geometry) decoding 32 sequences after a
+    1024-token prompt: three warm-up steps, then one step inside the NVTX range "step"
+    (not graph-captured, so a profiler sees each launch)."""
+    from dataclasses import replace
+    from .thinker_stack import ThinkerStackB200, ThinkerStackConfig
+    cfg = replace(ThinkerStackConfig(), layers=4)
+    stack = ThinkerStackB200(cfg, max_seqs=32, max_len=1024 + 8)
+    g = torch.Generator().manual_seed(3)
+    _, tok = stack.prefill(torch.randint(0, cfg.vocab, (32, 1024), generator=g).cuda())
+    for _ in range(3):
+        _, tok = stack.decode(tok)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("step")
+    _, tok = stack.decode(tok)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    stack.close()
+
+
+def thinker_stack_4_prefill():
+    """Four thinker layers (the 48-layer stack's geometry) prefilling 32 sequences of 1024
+    tokens: a warm-up prefill, then one inside the NVTX range "prefill"."""
+    from dataclasses import replace
+    from .thinker_stack import ThinkerStackB200, ThinkerStackConfig
+    cfg = replace(ThinkerStackConfig(), layers=4)
+    stack = ThinkerStackB200(cfg, max_seqs=32, max_len=1024 + 8)
+    prompt = torch.randint(0, cfg.vocab, (32, 1024), generator=torch.Generator().manual_seed(3)).cuda()
+    stack.prefill(prompt)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("prefill")
+    stack.prefill(prompt)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    stack.close()
+
+
 def thinker_stack_48_tp():
     """The 48-layer thinker stack with attention tensor-parallel and the experts expert-parallel over
     the ranks of a torchrun launch (one process per GPU, RANK / WORLD_SIZE / MASTER_* from the
@@ -234,7 +271,8 @@ def moe_prefill_4096_q8():
 CASES = {"readout-q4-b32": readout_q4_b32, "decode-step-b32": decode_step_b32,
          "gemm-q8-8192x5120x1280": gemm_q8_8192x5120x1280, "gemm-encoder-large-layer": gemm_encoder_large_layer,
          "gemm-fc1-exact-and-f16": gemm_fc1_exact_and_f16, "thinker-stack-48": thinker_stack_48,
-         "thinker-stack-48-tp": thinker_stack_48_tp,
+         "thinker-stack-48-tp": thinker_stack_48_tp, "thinker-stack-4-decode": thinker_stack_4_decode,
+         "thinker-stack-4-prefill": thinker_stack_4_prefill,
          "encoder-tiny-b1": encoder_tiny_b1,
          "encoder-large-b16": encoder_large_b16, "moe-prefill-4096": moe_prefill_4096,
          "moe-prefill-4096-q8": moe_prefill_4096_q8}

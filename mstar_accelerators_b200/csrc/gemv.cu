@@ -72,7 +72,12 @@ __device__ __forceinline__ float finish(const GemvArgs &a, int m, int64_t n, flo
     return v;
 }
 
-template <int MT, bool Q4, bool READOUT, bool SUMS, bool SPLIT>
+// GX: the activation fragments, scales and quant sums are read where the quantize kernel
+// left them (L2) instead of being staged in shared memory, which then holds only the
+// split path's per-block terms: the split-K form for wide rows (K >= 2048 at 32 queries,
+// where staging 80-160 KB per CTA allowed one CTA per SM or did not fit next to the
+// terms at all).
+template <int MT, bool Q4, bool READOUT, bool SUMS, bool SPLIT, bool GX = false>
 __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(const GemvArgs a) {
     constexpr int BPC = Q4 ? 4 : 2;  // blocks per 16-byte chunk
     constexpr int MPAD = MT * 16;
@@ -106,10 +111,17 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(const GemvArgs a) {
     const int total = ngroups * c_len;
 
     GemvSmem s;
-    s.xf = reinterpret_cast<uint4 *>(smem_raw);
-    s.xs = reinterpret_cast<float *>(s.xf + nb_pad * MT * 32);
-    s.xsum = reinterpret_cast<int *>(s.xs + nb_pad * MPAD);
-    s.stats = reinterpret_cast<float *>(s.xsum + nb_pad * MPAD);
+    if (GX) {
+        s.xf = const_cast<uint4 *>(a.xf);
+        s.xs = const_cast<float *>(a.xs);
+        s.xsum = const_cast<int *>(a.xsum);
+        s.stats = reinterpret_cast<float *>(smem_raw);
+    } else {
+        s.xf = reinterpret_cast<uint4 *>(smem_raw);
+        s.xs = reinterpret_cast<float *>(s.xf + nb_pad * MT * 32);
+        s.xsum = reinterpret_cast<int *>(s.xs + nb_pad * MPAD);
+        s.stats = reinterpret_cast<float *>(s.xsum + nb_pad * MPAD);
+    }
     s.best = reinterpret_cast<unsigned long long *>(s.stats + 2 * MPAD);
     s.terms = reinterpret_cast<float *>(s.best + MPAD);
     if (READOUT && threadIdx.x < MPAD) s.best[threadIdx.x] = 0ull;
@@ -135,7 +147,8 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(const GemvArgs a) {
     for (int u = 0; u < RING; ++u) load_next(u);  // immutable weights: before waiting on x's producer
     pdl_wait();
     pdl_trigger();  // the next kernel may launch now; it waits for this grid before reading
-    stage_activations<MT>(a, s);
+    if (GX) __syncthreads();   // the readout's shared maxima are initialised before use
+    else stage_activations<MT>(a, s);
 
     bool hi_live[MT];
 #pragma unroll
@@ -443,14 +456,16 @@ static int sm_count() {
     return n;
 }
 
-size_t gemv_smem_bytes(int64_t nb_pad, int mt, int wpg) {
-    size_t bytes = size_t(nb_pad) * mt * 512 + 2 * size_t(nb_pad) * mt * 16 * 4 + 2 * mt * 16 * 4 + mt * 16 * 8;
+size_t gemv_smem_bytes(int64_t nb_pad, int mt, int wpg, bool gx = false) {
+    size_t bytes = 2 * mt * 16 * 4 + mt * 16 * 8;
+    if (!gx) bytes += size_t(nb_pad) * mt * 512 + 2 * size_t(nb_pad) * mt * 16 * 4;   // staged activations
     if (wpg > 1) bytes += size_t(nb_pad) * mt * 512;  // one group per CTA when K is split
     return bytes;
 }
 
 constexpr size_t SMEM_LIMIT = 200 * 1024;
-size_t gemv_smem_bytes(int64_t nb_pad, int mt, int wpg);
+size_t gemv_smem_bytes(int64_t nb_pad, int mt, int wpg, bool gx);
+constexpr int64_t GX_MIN_BLOCKS = 64;   // K >= 2048: the split form reads the activations from L2
 
 int choose_wpg(const GemvArgs &a, int q4, int mt) {
     const int64_t chunks = a.nb_pad / (q4 ? 4 : 2);
@@ -463,10 +478,10 @@ int choose_wpg(const GemvArgs &a, int q4, int mt) {
     return wpg;
 }
 
-template <int MT, bool Q4, bool READOUT, bool SUMS, bool SPLIT>
+template <int MT, bool Q4, bool READOUT, bool SUMS, bool SPLIT, bool GX = false>
 static void launch_one(GemvArgs a, cudaStream_t s) {
-    const size_t smem = gemv_smem_bytes(a.nb_pad, MT, a.wpg);
-    auto kernel = k_gemv<MT, Q4, READOUT, SUMS, SPLIT>;
+    const size_t smem = gemv_smem_bytes(a.nb_pad, MT, a.wpg, GX);
+    auto kernel = k_gemv<MT, Q4, READOUT, SUMS, SPLIT, GX>;
     static size_t configured = 0;
     if (smem > 48 * 1024 && smem > configured) {
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_LIMIT + 8192));
@@ -519,8 +534,19 @@ static void launch_stream(const GemvArgs &a, cudaStream_t s) {
 
 template <int MT, bool Q4>
 static void launch_variant(GemvArgs a, cudaStream_t s) {
-    a.wpg = a.sums ? 1 : choose_wpg(a, Q4, MT);
     if (a.ctas_per_sm <= 0) a.ctas_per_sm = 4;
+    if (!a.sums && a.wpg_override == 0 && a.nb_pad >= GX_MIN_BLOCKS &&
+        gemv_smem_bytes(a.nb_pad, MT, 2, true) <= SMEM_LIMIT) {
+        // wide rows: split K over the warps of one row group per CTA, activations from L2
+        const int64_t chunks = a.nb_pad / (Q4 ? 4 : 2);
+        const int64_t target = int64_t(sm_count()) * 24;
+        a.wpg = 2;
+        while (a.wpg < GEMV_WARPS && a.groups * a.wpg < target && chunks >= 2 * a.wpg) a.wpg *= 2;
+        if (a.keys) launch_one<MT, Q4, true, false, true, true>(a, s);
+        else launch_one<MT, Q4, false, false, true, true>(a, s);
+        return;
+    }
+    a.wpg = a.sums ? 1 : choose_wpg(a, Q4, MT);
     if (!a.sums && a.wpg == 1 && stream_smem_bytes(a.nb_pad, MT, Q4) <= SMEM_LIMIT) {
         launch_stream<MT, Q4>(a, s);
         return;
@@ -535,7 +561,7 @@ static void launch_variant(GemvArgs a, cudaStream_t s) {
     }
 }
 
-bool gemv_supported(int64_t nb_pad) { return gemv_smem_bytes(nb_pad, 2, 1) <= SMEM_LIMIT; }
+bool gemv_supported(int64_t nb_pad) { return gemv_smem_bytes(nb_pad, 2, 1, false) <= SMEM_LIMIT; }
 
 // Split-K GEMV over Q8_0 weights whose CTA owns FRAG_GROUPS = 4 row groups: 32
 // consecutive outputs, one Q8_0 block of the next linear's input. After the

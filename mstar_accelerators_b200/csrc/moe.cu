@@ -53,16 +53,18 @@ constexpr int MOE_STAGE_BYTES = MOE_A_BYTES + MOE_B_BYTES;
 constexpr size_t MOE_SMEM = size_t(MOE_STAGES) * MOE_STAGE_BYTES + 1024 + 256;
 constexpr int MOE_MAX_TOPK = 8;
 constexpr int ROUTER_TOKENS = 16;
-constexpr int ROUTER_CHUNK = 256;
 
 __device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
 // ------------------------------------------------------------------ router
-// Logits: CTA (32 warps) per (16 tokens, 32 experts). The 16 token rows sit in
-// shared memory as bf16; warp w owns expert e and its lanes stream the expert's
-// row with 16-byte loads, accumulating 16 fp32 dots that are then reduced
-// across the warp. Output logits[t][e] = bf16(dot) (F.linear's output dtype).
-__global__ void __launch_bounds__(1024) k_router_logits(const __nv_bfloat16 *__restrict__ x,
+// Logits: CTA per (16 tokens, one expert per warp: 32 warps, or 8 for few tokens so
+// that a decode step's 32 tokens still spread over 32 CTAs). The 16 token rows sit
+// in shared memory as bf16; warp w owns expert e and its lanes stream the expert's
+// row with 16-byte loads, accumulating 16 fp32 dots that are then reduced across
+// the warp (the same order whatever the CTA shape). Output logits[t][e] = bf16(dot)
+// (F.linear's output dtype).
+template <int WARPS>
+__global__ void __launch_bounds__(WARPS * 32) k_router_logits(const __nv_bfloat16 *__restrict__ x,
                                                         const __nv_bfloat16 *__restrict__ wr, int T, int H, int E,
                                                         float *__restrict__ logits) {
     extern __shared__ __align__(16) __nv_bfloat16 xs[];  // [ROUTER_TOKENS][H]
@@ -76,12 +78,14 @@ __global__ void __launch_bounds__(1024) k_router_logits(const __nv_bfloat16 *__r
             tt < nt ? reinterpret_cast<const uint4 *>(x + int64_t(t0 + tt) * H)[c] : make_uint4(0, 0, 0, 0);
     }
     __syncthreads();
-    const int e = blockIdx.y * 32 + warp;
+    const int e = blockIdx.y * (blockDim.x >> 5) + warp;
     if (e >= E) return;
     float acc[ROUTER_TOKENS];
 #pragma unroll
     for (int i = 0; i < ROUTER_TOKENS; ++i) acc[i] = 0.0f;
     const uint4 *wrow = reinterpret_cast<const uint4 *>(wr + int64_t(e) * H);
+    constexpr int UNROLL = WARPS <= 8 ? 4 : 1;   // registers allow it below 1024 threads
+#pragma unroll UNROLL   // the row's weight loads in flight together (the per-lane order of the sums is unchanged)
     for (int c = lane; c < vec; c += 32) {
         const uint4 wv = __ldg(wrow + c);
         const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&wv);
@@ -873,16 +877,20 @@ int mstar_b200_moe_route(const void *x, int64_t tokens, int64_t hidden, const vo
         require(smem <= 200 * 1024, "router token tile exceeds shared memory");
         static bool configured = false;
         if (!configured) {
-            cuda_check(cudaFuncSetAttribute(k_router_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
+            cuda_check(cudaFuncSetAttribute(k_router_logits<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
+                       "router shared memory");
+            cuda_check(cudaFuncSetAttribute(k_router_logits<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
                        "router shared memory");
             configured = true;
         }
         check_device(logits, "router logits");
         cudaStream_t s = as_stream(stream);
-        const dim3 grid(unsigned(ceil_div(tokens, ROUTER_TOKENS)), unsigned(ceil_div(experts, 32)));
-        k_router_logits<<<grid, 1024, smem, s>>>(static_cast<const __nv_bfloat16 *>(x),
-                                                 static_cast<const __nv_bfloat16 *>(router_weight), int(tokens),
-                                                 int(hidden), experts, logits);
+        const int warps = tokens < 512 ? 8 : 32;   // experts per CTA
+        const dim3 grid(unsigned(ceil_div(tokens, ROUTER_TOKENS)), unsigned(ceil_div(experts, warps)));
+        auto logits_kernel = warps == 8 ? k_router_logits<8> : k_router_logits<32>;
+        logits_kernel<<<grid, 32 * warps, smem, s>>>(static_cast<const __nv_bfloat16 *>(x),
+                                                     static_cast<const __nv_bfloat16 *>(router_weight), int(tokens),
+                                                     int(hidden), experts, logits);
         k_router_topk<<<unsigned(ceil_div(tokens, 8)), 256, 0, s>>>(logits, int(tokens), experts, top_k, renormalize,
                                                                    topk_weights, topk_ids);
         cuda_check(cudaGetLastError(), "router launch");

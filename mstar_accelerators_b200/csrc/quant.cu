@@ -216,7 +216,9 @@ __global__ void __launch_bounds__(256) k_quantize_frag(const float *__restrict__
     const int64_t mt = token / 16;
     const int r = int(token % 16), g = r & 7, hi = r >> 3;
     const int t = (lane & 15) >> 2, half = lane >> 4;
-    for (int64_t b = warp; b < nb_pad; b += nwarps) {
+    // blocks of this token: all of them (gridDim.y == 1, as the LayerNorm statistics need
+    // the whole row), or without a LayerNorm this CTA's share (blocks are independent)
+    for (int64_t b = int64_t(blockIdx.y) * nwarps + warp; b < nb_pad; b += int64_t(gridDim.y) * nwarps) {
         const bool live = live_token && b < nb;
         float v = 0.0f;
         if (live) {
@@ -487,6 +489,12 @@ void launch_quantize_frag(int mode, const float *x, int64_t ldx, int64_t m, int6
         launch_quantize_warp(mode, int(nch), cfg, x, ldx, m, k, mpad, nb_pad, ln_w, ln_b, ln_eps, xf, xs, xsum,
                              status);
         return;
+    }
+    // without a LayerNorm, 8 blocks per CTA over a second grid dimension: a wide row (o_proj's
+    // 4096 at 32 queries) no longer leaves most SMs idle while 32 CTAs walk 128 blocks each
+    if (!ln_w) {
+        cfg.blockDim = dim3(256);
+        cfg.gridDim = dim3(unsigned(mpad), unsigned(ceil_div(nb_pad, 8)));
     }
     auto kernel = mode == 0 ? k_quantize_frag<0> : mode == 2 ? k_quantize_frag<2> : k_quantize_frag<1>;
     cudaLaunchKernelEx(&cfg, kernel, x, ldx, m, k, mpad, nb_pad, ln_w, ln_b, ln_eps, xf, xs, xsum, status);
