@@ -247,7 +247,12 @@ int mstar_b200_linear_run(void *handle, const float *x, int64_t x_stride, int64_
         } else require(!residual, "residual given without its epilogue flag");
         cudaStream_t s = as_stream(stream);
         if (h.w16 && !ln_weight && queries >= GEMM_MIN_QUERIES && queries <= h.gemm_rows) {
-            launch_dequant_act(rounding, x, x_stride, queries, h.width, h.x16, h.status, s);
+            // the activation side of the GEMM: Q8_0 blocks staged as fp16(q * d); a warp per row
+            // with 16-byte loads where the rows allow it (the same bytes as a warp per block)
+            if (uintptr_t(x) % 16 == 0 && x_stride % 4 == 0)
+                launch_stage_rows(rounding, x, 0, x_stride, queries, h.width, nullptr, nullptr, 0.0f, h.x16, h.width,
+                                  h.status, s);
+            else launch_dequant_act(rounding, x, x_stride, queries, h.width, h.x16, h.status, s);
             CUtensorMap xmap;
             make_fp16_map(&xmap, h.x16, queries, h.width, GEMM_TILE_M);
             GemmArgs g{};

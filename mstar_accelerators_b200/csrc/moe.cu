@@ -57,13 +57,16 @@ constexpr int ROUTER_TOKENS = 16;
 __device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
 // ------------------------------------------------------------------ router
-// Logits: CTA per (16 tokens, one expert per warp: 32 warps, or 8 for few tokens so
-// that a decode step's 32 tokens still spread over 32 CTAs). The 16 token rows sit
-// in shared memory as bf16; warp w owns expert e and its lanes stream the expert's
-// row with 16-byte loads, accumulating 16 fp32 dots that are then reduced across
-// the warp (the same order whatever the CTA shape). Output logits[t][e] = bf16(dot)
+// Logits: CTA of WARPS warps per (16 tokens, WARPS * EPW experts). The 16 token rows sit
+// in shared memory as bf16; warp w owns experts e0 .. e0 + EPW - 1 and its lanes stream
+// their rows with 16-byte loads, accumulating 16 fp32 dots per expert that are then
+// reduced across the warp. Per (token, expert) the order of the sums is the same for
+// every CTA shape: lane l's fused multiply-adds over chunks l, l + 32, ... and within a
+// chunk its eight elements, then the butterfly. EPW > 1 (prefill) reads each token
+// chunk from shared memory once for EPW experts; decode uses one expert per warp and 8
+// warps, so 32 tokens still spread over 32 CTAs. Output logits[t][e] = bf16(dot)
 // (F.linear's output dtype).
-template <int WARPS>
+template <int WARPS, int EPW>
 __global__ void __launch_bounds__(WARPS * 32) k_router_logits(const __nv_bfloat16 *__restrict__ x,
                                                         const __nv_bfloat16 *__restrict__ wr, int T, int H, int E,
                                                         float *__restrict__ logits) {
@@ -78,23 +81,28 @@ __global__ void __launch_bounds__(WARPS * 32) k_router_logits(const __nv_bfloat1
             tt < nt ? reinterpret_cast<const uint4 *>(x + int64_t(t0 + tt) * H)[c] : make_uint4(0, 0, 0, 0);
     }
     __syncthreads();
-    const int e = blockIdx.y * (blockDim.x >> 5) + warp;
-    if (e >= E) return;
-    float acc[ROUTER_TOKENS];
+    const int e0 = (blockIdx.y * WARPS + warp) * EPW;
+    if (e0 >= E) return;
+    float acc[EPW][ROUTER_TOKENS];
 #pragma unroll
-    for (int i = 0; i < ROUTER_TOKENS; ++i) acc[i] = 0.0f;
-    const uint4 *wrow = reinterpret_cast<const uint4 *>(wr + int64_t(e) * H);
-    constexpr int UNROLL = WARPS <= 8 ? 4 : 1;   // registers allow it below 1024 threads
-#pragma unroll UNROLL   // the row's weight loads in flight together (the per-lane order of the sums is unchanged)
+    for (int q = 0; q < EPW; ++q)
+#pragma unroll
+        for (int i = 0; i < ROUTER_TOKENS; ++i) acc[q][i] = 0.0f;
+    constexpr int UNROLL = EPW == 1 ? 4 : 1;   // one expert: its row's weight loads in flight together
+#pragma unroll UNROLL
     for (int c = lane; c < vec; c += 32) {
-        const uint4 wv = __ldg(wrow + c);
-        const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&wv);
-        float wf[8];
+        float wf[EPW][8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float2 f = __bfloat1622float2(w2[j]);
-            wf[2 * j] = f.x;
-            wf[2 * j + 1] = f.y;
+        for (int q = 0; q < EPW; ++q) {
+            const uint4 wv = e0 + q < E ? __ldg(reinterpret_cast<const uint4 *>(wr + int64_t(e0 + q) * H) + c)
+                                        : make_uint4(0, 0, 0, 0);
+            const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&wv);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 f = __bfloat1622float2(w2[j]);
+                wf[q][2 * j] = f.x;
+                wf[q][2 * j + 1] = f.y;
+            }
         }
 #pragma unroll
         for (int tt = 0; tt < ROUTER_TOKENS; ++tt) {
@@ -103,21 +111,26 @@ __global__ void __launch_bounds__(WARPS * 32) k_router_logits(const __nv_bfloat1
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const float2 f = __bfloat1622float2(x2[j]);
-                acc[tt] = fmaf(f.y, wf[2 * j + 1], fmaf(f.x, wf[2 * j], acc[tt]));
+#pragma unroll
+                for (int q = 0; q < EPW; ++q)
+                    acc[q][tt] = fmaf(f.y, wf[q][2 * j + 1], fmaf(f.x, wf[q][2 * j], acc[q][tt]));
             }
         }
     }
 #pragma unroll
-    for (int tt = 0; tt < ROUTER_TOKENS; ++tt) {
+    for (int q = 0; q < EPW; ++q) {
 #pragma unroll
-        for (int o = 16; o; o >>= 1) acc[tt] += __shfl_xor_sync(0xffffffffu, acc[tt], o);
-    }
-    if (lane < nt) {
-        float v = acc[0];
+        for (int tt = 0; tt < ROUTER_TOKENS; ++tt) {
 #pragma unroll
-        for (int tt = 1; tt < ROUTER_TOKENS; ++tt)
-            if (lane == tt) v = acc[tt];
-        logits[int64_t(t0 + lane) * E + e] = bf16r(v);
+            for (int o = 16; o; o >>= 1) acc[q][tt] += __shfl_xor_sync(0xffffffffu, acc[q][tt], o);
+        }
+        if (lane < nt && e0 + q < E) {
+            float v = acc[q][0];
+#pragma unroll
+            for (int tt = 1; tt < ROUTER_TOKENS; ++tt)
+                if (lane == tt) v = acc[q][tt];
+            logits[int64_t(t0 + lane) * E + e0 + q] = bf16r(v);
+        }
     }
 }
 
@@ -877,18 +890,20 @@ int mstar_b200_moe_route(const void *x, int64_t tokens, int64_t hidden, const vo
         require(smem <= 200 * 1024, "router token tile exceeds shared memory");
         static bool configured = false;
         if (!configured) {
-            cuda_check(cudaFuncSetAttribute(k_router_logits<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
+            cuda_check(cudaFuncSetAttribute(k_router_logits<8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            200 * 1024),
                        "router shared memory");
-            cuda_check(cudaFuncSetAttribute(k_router_logits<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
+            cuda_check(cudaFuncSetAttribute(k_router_logits<8, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            200 * 1024),
                        "router shared memory");
             configured = true;
         }
         check_device(logits, "router logits");
         cudaStream_t s = as_stream(stream);
-        const int warps = tokens < 512 ? 8 : 32;   // experts per CTA
-        const dim3 grid(unsigned(ceil_div(tokens, ROUTER_TOKENS)), unsigned(ceil_div(experts, warps)));
-        auto logits_kernel = warps == 8 ? k_router_logits<8> : k_router_logits<32>;
-        logits_kernel<<<grid, 32 * warps, smem, s>>>(static_cast<const __nv_bfloat16 *>(x),
+        const int epw = tokens < 512 ? 1 : 4;   // experts per warp (8 warps per CTA)
+        const dim3 grid(unsigned(ceil_div(tokens, ROUTER_TOKENS)), unsigned(ceil_div(experts, 8 * epw)));
+        auto logits_kernel = epw == 1 ? k_router_logits<8, 1> : k_router_logits<8, 4>;
+        logits_kernel<<<grid, 256, smem, s>>>(static_cast<const __nv_bfloat16 *>(x),
                                                      static_cast<const __nv_bfloat16 *>(router_weight), int(tokens),
                                                      int(hidden), experts, logits);
         k_router_topk<<<unsigned(ceil_div(tokens, 8)), 256, 0, s>>>(logits, int(tokens), experts, top_k, renormalize,
