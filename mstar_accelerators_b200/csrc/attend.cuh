@@ -12,8 +12,16 @@ constexpr int TILE_KEYS = 64;        // keys per shared-memory tile
 constexpr int ATT_THREADS = 128;      // CTA size for up to 4 row tiles
 constexpr int ATT_MAX_THREADS = 256;  // one warp per 16-row tile up to 128 rows
 constexpr int ATT_MAX_ROWS = 128;    // query rows one CTA attends (all B*NQ rows when the planes are shared)
-constexpr int SHARED_SPLITS = 8;     // key splits per head over shared planes (one thread-block cluster per head)
+constexpr int SHARED_SPLITS = 16;    // key splits per head over shared planes at most (one thread-block cluster per head)
 constexpr int ATT_PRE = 4;           // key tiles a CTA loads into shared memory at once
+
+// Key splits of one head over shared planes: at most SHARED_SPLITS, each with the same
+// number of 64-key tiles (a 1500-position source: 24 tiles as 12 splits of 2), so that no
+// CTA of the head's cluster is left without keys.
+__host__ __device__ inline int shared_splits(int tiles) {
+    const int per = (tiles + SHARED_SPLITS - 1) / SHARED_SPLITS;
+    return (tiles + per - 1) / per;
+}
 
 struct AttArgs {
     const float *q;

@@ -108,7 +108,7 @@ static SplitPlan split_plan(int heads, int batch, int queries, int64_t capacity,
     p.groups = shared ? 1 : batch;
     p.rows = shared ? batch * queries : queries;
     const int tiles = int(ceil_div(capacity, TILE_KEYS));
-    p.splits = shared ? (tiles < SHARED_SPLITS ? tiles : SHARED_SPLITS) : 1;
+    p.splits = shared ? shared_splits(tiles) : 1;
     p.tiles_per_split = int(ceil_div(tiles, p.splits));
     p.partial_bytes = p.splits > 1 ? uint64_t(p.groups) * heads * p.splits * p.rows * (HEAD_DIM + 2) * 4 : 0;
     return p;
@@ -187,6 +187,9 @@ int mstar_b200_attend_q8(const float *q, int64_t q_stride, const float *k_new, c
             cuda_check(cudaFuncSetAttribute(k_attend_cluster, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             int(tiles_smem_bytes(ATT_MAX_ROWS) + ATT_MAX_ROWS * (HEAD_DIM + 2) * 4)),
                        "attention shared-memory attribute");
+            // clusters of more than 8 CTAs (up to SHARED_SPLITS key splits of a head)
+            cuda_check(cudaFuncSetAttribute(k_attend_cluster, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                       "attention cluster size attribute");
             cuda_check(cudaFuncSetAttribute(k_attend_tiles<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             int(tiles_smem_bytes(ATT_MAX_ROWS))),
                        "attention shared-memory attribute");

@@ -508,7 +508,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_decode_step(const StepArgs 
             at.batch = a.B;
             at.shared = a.shared;
             const int tiles = int(ceil_div(a.source, TILE_KEYS));
-            at.splits = a.shared ? (tiles < SHARED_SPLITS ? tiles : SHARED_SPLITS) : 1;
+            at.splits = a.shared ? shared_splits(tiles) : 1;
             at.rows = a.shared ? a.B : 1;
             at.tiles_per_split = int(ceil_div(tiles, at.splits));
             at.kv_len = a.cross_len;
@@ -750,7 +750,7 @@ void *mstar_b200_decode_step_create(const mstar_b200_decode_step_config *c, char
         a.xs = st->alloc<float>(size_t(nbp_max * mpad), "decode-step scales");
         a.xsum = st->alloc<int>(size_t(nbp_max * mpad), "decode-step quant sums");
         const int tiles = int(ceil_div(c->source, TILE_KEYS));
-        const int splits = tiles < SHARED_SPLITS ? tiles : SHARED_SPLITS;
+        const int splits = shared_splits(tiles);
         a.part = st->alloc<float>(size_t(c->heads) * splits * B * (HEAD_DIM + 2), "decode-step partials");
         a.keys = st->alloc<unsigned long long>(32, "decode-step argmax keys");
         a.bar = st->alloc<unsigned int>(2, "decode-step barrier");
