@@ -277,6 +277,17 @@ MSTAR_B200_API int mstar_b200_stage_rows(const void *x, int32_t x_format, int64_
 MSTAR_B200_API int mstar_b200_stage_conv(const float *source, int32_t time_major, int64_t batch,
     int64_t channels, int64_t time_in, int32_t stride, int64_t k_padded, void *staged, uint64_t staged_bytes,
     int32_t rounding, int32_t *status, void *stream, char *error, size_t error_size);
+/* stage_heads: the thinker's prefill attention output (bf16 [seqs][heads][positions]
+ * [head_dim] with element strides seq_stride, head_stride, position_stride, head_dim
+ * contiguous; the layout scaled_dot_product_attention returns before the transpose in
+ * thinker_model.py:106-148) as the output projection's staged operand: row
+ * s * positions + t = the heads of position t of sequence s side by side, each 32-value
+ * block Q8_0-quantized (rounding) and stored as fp16(q * d), [seqs * positions][heads *
+ * head_dim]; the same bytes as mstar_b200_stage_rows on the transposed fp32 rows.
+ * head_dim a multiple of 32; the attention output 8-byte aligned, strides multiples of 4. */
+MSTAR_B200_API int mstar_b200_stage_heads(const void *attention, int64_t seqs, int64_t heads, int64_t positions,
+    int64_t head_dim, int64_t seq_stride, int64_t head_stride, int64_t position_stride, void *staged,
+    uint64_t staged_bytes, int32_t rounding, int32_t *status, void *stream, char *error, size_t error_size);
 /* layer_norm: fp32 rows -> ggml_norm(eps), mul, add (the final encoder_norm_affine,
  * encoder.cpp:725) -> fp32 out; width <= 1536. */
 MSTAR_B200_API int mstar_b200_layer_norm(const float *x, int64_t x_stride, int64_t rows, int64_t width,

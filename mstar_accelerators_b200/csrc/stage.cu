@@ -15,6 +15,8 @@
 // (ref / ARM / x86); a nonfinite input sets status bit value 1.
 #include <cmath>
 
+#include <cuda_bf16.h>
+
 #include "../../include/mstar_b200.h"
 #include "gemm.cuh"
 
@@ -277,6 +279,39 @@ __global__ void __launch_bounds__(CONV_WARPS * 32)
     }
 }
 
+// Attention output rows staged for the output projection straight from the attention's
+// [seqs][heads][positions][head_dim] bf16 output (any strides over the first three, head_dim
+// contiguous): row s * positions + t is head 0 .. heads-1 of position t of sequence s side by
+// side (the transpose and fp32 conversion a torch reshape would first write out), then Q8_0
+// blocks as k_stage_rows: a warp per row, four values per lane (an 8-byte load from one
+// head's contiguous run), eight lanes per block.
+template <int MODE>
+__global__ void __launch_bounds__(STAGE_WARPS * 32)
+    k_stage_heads(const __nv_bfloat16 *__restrict__ att, int64_t seqs, int64_t heads, int64_t positions,
+                  int64_t head_dim, int64_t seq_stride, int64_t head_stride, int64_t position_stride,
+                  __half *__restrict__ out, int *__restrict__ status) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = int64_t(blockIdx.x) * STAGE_WARPS + (threadIdx.x >> 5);
+    if (row >= seqs * positions) return;   // warp-uniform
+    const int64_t s = row / positions, t = row % positions, k = heads * head_dim, chunks = k / 4;
+    const __nv_bfloat16 *base = att + s * seq_stride + t * position_stride;
+    for (int64_t i = 0; i * 32 < chunks; ++i) {   // warp-uniform: every lane takes part in the block shuffles
+        const int64_t c = i * 32 + lane;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (c < chunks) {
+            const int64_t e = 4 * c, h = e / head_dim, d = e - h * head_dim;
+            const uint2 u = *reinterpret_cast<const uint2 *>(base + h * head_stride + d);
+            __nv_bfloat162 lo, hi;
+            memcpy(&lo, &u.x, 4);
+            memcpy(&hi, &u.y, 4);
+            const float2 a = __bfloat1622float2(lo), b = __bfloat1622float2(hi);
+            v = make_float4(a.x, a.y, b.x, b.y);
+        }
+        v = q8_block8<MODE>(v, status);
+        if (c < chunks) store4(out, row * k + 4 * c, v);
+    }
+}
+
 __global__ void __launch_bounds__(STAGE_WARPS * 32)
     k_layer_norm(const float *__restrict__ x, int64_t ldx, int64_t rows, int64_t k, const float *__restrict__ w,
                  const float *__restrict__ bias, float eps, float *__restrict__ out, int64_t ldo) {
@@ -406,6 +441,41 @@ int mstar_b200_stage_rows(const void *x, int32_t x_format, int64_t x_stride, int
         launch_stage_rows(rounding, x, x_format == MSTAR_B200_ACT_F16, x_stride, rows, width, ln_weight, ln_bias, ln_eps,
                           static_cast<__half *>(staged), width, status, as_stream(stream));
         cuda_check(cudaGetLastError(), "staging launch");
+        return 0;
+    } catch (const std::exception &e) {
+        message(error, error_size, e.what());
+        return -1;
+    }
+}
+
+int mstar_b200_stage_heads(const void *attention, int64_t seqs, int64_t heads, int64_t positions,
+                           int64_t head_dim, int64_t seq_stride, int64_t head_stride, int64_t position_stride,
+                           void *staged, uint64_t staged_bytes, int32_t rounding, int32_t *status, void *stream,
+                           char *error, size_t error_size) {
+    try {
+        require(rounding >= 0 && rounding <= 2, "unknown Q8_0 activation rounding");
+        require(seqs >= 1 && heads >= 1 && positions >= 1 && head_dim >= QK && head_dim % QK == 0 &&
+                    seqs * positions <= (int64_t(1) << 31) && heads * head_dim <= 65536,
+                "invalid attention layout (head_dim a multiple of 32)");
+        require(seq_stride >= 0 && head_stride >= 0 && position_stride >= 0 && seq_stride % 4 == 0 &&
+                    head_stride % 4 == 0 && position_stride % 4 == 0,
+                "attention strides must be non-negative multiples of 4 elements");
+        require(attention && staged && status, "missing staging operand");
+        require(uintptr_t(attention) % 8 == 0, "attention output must be 8-byte aligned");
+        const uint64_t ab = uint64_t((seqs - 1) * seq_stride + (heads - 1) * head_stride +
+                                     (positions - 1) * position_stride + head_dim) * 2;
+        const uint64_t ob = uint64_t(seqs * positions * heads * head_dim) * 2;
+        check_range({staged, staged_bytes}, ob, 16, "staged operand");
+        require(disjoint({attention, ab}, {staged, ob}), "staged operand overlaps the attention output");
+        check_device(attention, "attention output");
+        check_device(staged, "staged operand");
+        check_device(status, "status word");
+        const unsigned grid = unsigned(ceil_div(seqs * positions, int64_t(STAGE_WARPS)));
+        auto kernel = rounding == 0 ? k_stage_heads<0> : rounding == 2 ? k_stage_heads<2> : k_stage_heads<1>;
+        kernel<<<grid, STAGE_WARPS * 32, 0, as_stream(stream)>>>(
+            static_cast<const __nv_bfloat16 *>(attention), seqs, heads, positions, head_dim, seq_stride, head_stride,
+            position_stride, static_cast<__half *>(staged), status);
+        cuda_check(cudaGetLastError(), "attention staging launch");
         return 0;
     } catch (const std::exception &e) {
         message(error, error_size, e.what());

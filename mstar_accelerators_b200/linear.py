@@ -94,6 +94,27 @@ def stage_rows(x: torch.Tensor, *, norm: tuple | None = None, rounding: str = "a
     return out
 
 
+def stage_heads(attention: torch.Tensor, *, rounding: str = "arm", out: torch.Tensor | None = None,
+                status: torch.Tensor | None = None) -> torch.Tensor:
+    """Attention output bf16 [S, heads, n, D] (any strides over S, heads, n) -> the output
+    projection's staged operand fp16(q * d) [S * n, heads * D] (row s * n + t: the heads of
+    position t side by side), in one pass."""
+    lib = native.require_capability()
+    _require_cuda(attention, "attention output", torch.bfloat16)
+    a = attention if attention.stride(-1) == 1 else attention.contiguous()
+    S, H, n, D = a.shape
+    if out is None:
+        out = torch.empty((S * n, H * D), dtype=torch.float16, device=a.device)
+    if status is None:
+        status = torch.zeros(1, dtype=torch.int32, device=a.device)
+    e = error_buffer()
+    check(lib.mstar_b200_stage_heads(a.data_ptr(), S, H, n, D, a.stride(0), a.stride(1), a.stride(2),
+                                     out.data_ptr(), out.numel() * 2, native.ROUNDING[rounding], status.data_ptr(),
+                                     _stream(a.device), e, len(e)),
+          e, "B200 attention staging")
+    return out
+
+
 def stage_conv(source: torch.Tensor, *, time_major: bool, stride: int, k_padded: int, rounding: str = "arm",
                out: torch.Tensor | None = None, status: torch.Tensor | None = None) -> torch.Tensor:
     """Convolution columns (kernel 3, padding 1) of fp32 [B, C, T] (or [B, T, C] when time_major),

@@ -57,6 +57,8 @@ SIGNATURES = {
     "mstar_b200_linear_gemm": (_int, [_vp, _vp, _u64, _i64, _vp, _u64, _i64, C.c_int32, _vp, _u64, _i64, _i64, _i64,
                                       _i64, C.c_int32, C.c_int32, _vp, _vp, *_err]),
     "mstar_b200_residual_add_bf16": (_int, [_vp, _vp, _i64, _vp, _vp, *_err]),
+    "mstar_b200_stage_heads": (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _u64, C.c_int32, _vp,
+                                      _vp, *_err]),
     "mstar_b200_rms_norm": (_int, [_vp, _i64, _i64, _i64, _vp, C.c_float, _vp, _i64, _vp, _i64, _vp, *_err]),
     "mstar_b200_tp_barrier": (_int, [_vp, _vp, C.c_int32, C.c_int32, _vp, _vp, _vp, *_err]),
     "mstar_b200_linear_gemm_push": (_int, [_vp, _vp, _u64, _i64, _vp, _vp, C.c_int32, C.c_int32, _i64, _vp, _vp,

@@ -29,7 +29,7 @@ import torch
 import torch.nn.functional as F
 
 from . import native
-from .linear import BlockLinear, _stream, pack
+from .linear import BlockLinear, _stream, pack, stage_heads
 from .moe import ThinkerMoEB200, route
 from .native import check, error_buffer
 from .thinker import qknorm_rope
@@ -191,9 +191,29 @@ class ThinkerStackB200:
     def _embed(self, tokens: torch.Tensor) -> torch.Tensor:
         return self.embed[tokens.reshape(-1)]
 
+    def _o_proj(self, L, att: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """o_proj (fp32) of the attention output: decode rows [T, heads * D] go through the linear
+        as they are; the prefill's [S, heads, n, D] is staged for the GEMM in one pass (the same
+        bytes the linear stages from the transposed fp32 rows, without writing those out)."""
+        lin = L["o"]
+        if att.ndim == 2:
+            return self._linear(lin, att, out=out)
+        S, Hq, n, D = att.shape
+        T = S * n
+        if out is None:
+            out = torch.empty((T, lin.rows), dtype=torch.float32, device=att.device)
+        if T < 64 or (T % self.gemm_rows and T % self.gemm_rows < 64):
+            # a short (last) chunk takes the linear's GEMV path on the fp32 rows, as _linear does
+            return self._linear(lin, att.transpose(1, 2).reshape(T, Hq * D), out=out)
+        staged = stage_heads(att, status=self.status)
+        for r0 in range(0, T, self.gemm_rows):
+            r1 = min(T, r0 + self.gemm_rows)
+            lin.gemm(staged[r0:r1], out=out[r0:r1], bias=False, status=self.status)
+        return out
+
     def _attention_out(self, L, att: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
         """x + o_proj(att) in bf16."""
-        return residual_add(x, self._linear(L["o"], att))
+        return residual_add(x, self._o_proj(L, att))
 
     def _moe_residual(self, L, h: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
         """x + MoE(h) in bf16."""
@@ -212,7 +232,8 @@ class ThinkerStackB200:
 
     def _layer(self, i: int, x: torch.Tensor, S: int, n: int, start, shared) -> torch.Tensor:
         """x [S * n, H] bf16: n new positions of each of S sequences; shared: _positions() of
-        their positions. Prefill (start == 0, n > 1): causal attention over the n positions.
+        their positions. The attention output reaches _attention_out as [S * n, heads * D] rows
+        (decode) or as [S, heads, n, D] (prefill). Prefill (start == 0, n > 1): causal attention over the n positions.
         Decode (n == 1): every query attends to the cache up to its own position through a
         fixed-length view of the whole cache and an additive mask, so the step's shapes never
         change (one CUDA graph replays it)."""
@@ -244,7 +265,6 @@ class ThinkerStackB200:
             else:
                 m = torch.ones((n, ctx), dtype=torch.bool, device=x.device).tril(ctx - n)
                 att = F.scaled_dot_product_attention(qq, kk, vv, attn_mask=m, scale=D ** -0.5, enable_gqa=True)
-            att = att.transpose(1, 2).reshape(T, Hq * D)
         x = self._attention_out(L, att, x)
         h = rms_norm(x, L["ln2"], cfg.eps)
         return self._moe_residual(L, h, x)

@@ -128,8 +128,8 @@ class ThinkerStackTP(ThinkerStackB200):
     # barrier after each reduction (combine) publishes the new x before anyone reads
     # it, and comes before any rank overwrites its partial (expert) buffer again.
     def _attention_out(self, L, att: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
-        T, H = att.shape[0], self.cfg.hidden
-        self._linear(L["o"], att, out=self.part[:T * H].view(T, H))
+        T, H = x.shape[0], self.cfg.hidden
+        self._o_proj(L, att, out=self.part[:T * H].view(T, H))
         self._barrier()
         row0, owned = owner_rows(T, self.world, self.rank)
         e = error_buffer()
