@@ -284,7 +284,7 @@ MSTAR_B200_API int mstar_b200_stage_conv(const float *source, int32_t time_major
  * s * positions + t = the heads of position t of sequence s side by side, each 32-value
  * block Q8_0-quantized (rounding) and stored as fp16(q * d), [seqs * positions][heads *
  * head_dim]; the same bytes as mstar_b200_stage_rows on the transposed fp32 rows.
- * head_dim a multiple of 32; the attention output 8-byte aligned, strides multiples of 4. */
+ * head_dim a multiple of 32; the attention output 16-byte aligned, strides multiples of 8. */
 MSTAR_B200_API int mstar_b200_stage_heads(const void *attention, int64_t seqs, int64_t heads, int64_t positions,
     int64_t head_dim, int64_t seq_stride, int64_t head_stride, int64_t position_stride, void *staged,
     uint64_t staged_bytes, int32_t rounding, int32_t *status, void *stream, char *error, size_t error_size);

@@ -12,8 +12,8 @@
 // interleaved by the caller, as for the reference op). q heads go to out_q; k
 // heads go to k_cache at the token's slot, and (when v is given) the token's v
 // heads are copied to v_cache at the same slot (the KV write of the code
-// predictor's prologue, cp_kernels.py:16-58). One warp per (token, head), four
-// elements per lane; the rotation partner is lane ^ 16. The sum of squares is a
+// predictor's prologue, cp_kernels.py:16-58). One warp per four heads of a token,
+// four elements of a head per lane; the rotation partner is lane ^ 16. The sum of squares is a
 // fixed butterfly in fp32, so a result can sit one bf16 step from another
 // summation order's where it lands on a rounding boundary.
 #include <cmath>
@@ -27,6 +27,7 @@ namespace mb {
 
 constexpr int QK_HEAD_DIM = 128;
 constexpr int QK_WARPS = 8;
+constexpr int QK_HEADS_PER_WARP = 4;
 
 struct QkArgs {
     const __nv_bfloat16 *q, *k, *v;      // [T, heads, 128] rows with strides (elements)
@@ -48,63 +49,94 @@ struct QkArgs {
 
 __device__ __forceinline__ float bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+__device__ __forceinline__ void bf16x4(const __nv_bfloat16 *p, float (&f)[4]) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(p);   // 8-byte aligned (checked by the entry point)
+    __nv_bfloat162 lo, hi;
+    memcpy(&lo, &u.x, 4);
+    memcpy(&hi, &u.y, 4);
+    const float2 a = __bfloat1622float2(lo), b = __bfloat1622float2(hi);
+    f[0] = a.x, f[1] = a.y, f[2] = b.x, f[3] = b.y;
+}
+
+// A warp takes QK_HEADS_PER_WARP heads of one token: their rows are loaded together
+// (one 8-byte load per lane and head) and the token's cos / sin rows once for all of them.
 __global__ void __launch_bounds__(QK_WARPS * 32) k_qknorm_rope(const QkArgs a) {
     const int lane = threadIdx.x & 31;
-    const int64_t item = int64_t(blockIdx.x) * QK_WARPS + (threadIdx.x >> 5);
     const int heads = a.qh + a.kh;
-    if (item >= a.tokens * heads) return;
-    const int64_t t = item / heads;
-    const int h = int(item % heads);
-    const bool is_q = h < a.qh;
-    const __nv_bfloat16 *src = is_q ? a.q + t * a.q_s0 + int64_t(h) * a.q_s1 : a.k + t * a.k_s0 + int64_t(h - a.qh) * a.k_s1;
-    const __nv_bfloat16 *w = is_q ? a.qw : a.kw;
+    const int groups = (heads + QK_HEADS_PER_WARP - 1) / QK_HEADS_PER_WARP;
+    const int64_t item = int64_t(blockIdx.x) * QK_WARPS + (threadIdx.x >> 5);
+    if (item >= a.tokens * groups) return;   // warp-uniform
+    const int64_t t = item / groups;
+    const int h0 = int(item % groups) * QK_HEADS_PER_WARP;
     const int d0 = 4 * lane;
-    float x[4], ww[4], c[4], s[4];
+    uint2 xr[QK_HEADS_PER_WARP], vr[QK_HEADS_PER_WARP];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        x[i] = __bfloat162float(src[d0 + i]);
-        ww[i] = __bfloat162float(w[d0 + i]);
-        c[i] = __bfloat162float(a.cos[t * a.cs0 + d0 + i]);
-        s[i] = __bfloat162float(a.sin[t * a.ss0 + d0 + i]);
-    }
-    float ss = __fadd_rn(__fadd_rn(__fmul_rn(x[0], x[0]), __fmul_rn(x[1], x[1])),
-                         __fadd_rn(__fmul_rn(x[2], x[2]), __fmul_rn(x[3], x[3])));
-#pragma unroll
-    for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(QK_HEAD_DIM)), a.eps)));
-    float n[4], p[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) n[i] = bf(__fmul_rn(__fmul_rn(x[i], r), ww[i]));
-#pragma unroll
-    for (int i = 0; i < 4; ++i) p[i] = __shfl_xor_sync(0xffffffffu, n[i], 16);  // element d +- 64
-    const float sign = lane < 16 ? -1.0f : 1.0f;
-    __align__(8) __nv_bfloat16 y[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        float av = __fmul_rn(n[i], c[i]), bv = __fmul_rn(sign * p[i], s[i]);
-        if (a.round_products) {
-            av = bf(av);
-            bv = bf(bv);
+    for (int j = 0; j < QK_HEADS_PER_WARP; ++j) {
+        const int h = h0 + j;
+        xr[j] = make_uint2(0u, 0u);
+        vr[j] = make_uint2(0u, 0u);
+        if (h < a.qh) {
+            xr[j] = *reinterpret_cast<const uint2 *>(a.q + t * a.q_s0 + int64_t(h) * a.q_s1 + d0);
+        } else if (h < heads) {
+            xr[j] = *reinterpret_cast<const uint2 *>(a.k + t * a.k_s0 + int64_t(h - a.qh) * a.k_s1 + d0);
+            if (a.v) vr[j] = *reinterpret_cast<const uint2 *>(a.v + t * a.v_s0 + int64_t(h - a.qh) * a.v_s1 + d0);
         }
-        y[i] = __float2bfloat16_rn(__fadd_rn(av, bv));
     }
-    if (is_q) {
-        *reinterpret_cast<uint2 *>(a.out_q + (t * a.qh + h) * QK_HEAD_DIM + d0) = *reinterpret_cast<const uint2 *>(y);
-        return;
+    float c[4], s[4], wq[4], wk[4];
+    bf16x4(a.cos + t * a.cs0 + d0, c);
+    bf16x4(a.sin + t * a.ss0 + d0, s);
+    bf16x4(a.qw + d0, wq);
+    bf16x4(a.kw + d0, wk);
+    int64_t slot = 0;
+    bool slot_ok = true;
+    if (h0 + QK_HEADS_PER_WARP > a.qh) {   // the group holds k heads
+        slot = a.slots ? a.slots[t] : t;
+        slot_ok = slot >= 0 && slot < a.num_slots;
+        if (!slot_ok && lane == 0 && a.status) atomicOr(a.status, 1);
     }
-    const int hk = h - a.qh;
-    const int64_t slot = a.slots ? a.slots[t] : t;
-    if (slot < 0 || slot >= a.num_slots) {
-        if (lane == 0 && a.status) atomicOr(a.status, 1);
-        return;
-    }
-    __nv_bfloat16 *kd = a.k_cache + slot * a.cache_s0 + int64_t(hk) * QK_HEAD_DIM + d0;
-    *reinterpret_cast<uint2 *>(kd) = *reinterpret_cast<const uint2 *>(y);
-    if (a.v) {
-        const __nv_bfloat16 *vs = a.v + t * a.v_s0 + int64_t(hk) * a.v_s1 + d0;
-        __nv_bfloat16 *vd = a.v_cache + slot * a.cache_s0 + int64_t(hk) * QK_HEAD_DIM + d0;
+    const float sign = lane < 16 ? -1.0f : 1.0f;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) vd[i] = vs[i];
+    for (int j = 0; j < QK_HEADS_PER_WARP; ++j) {
+        const int h = h0 + j;
+        if (h >= heads) break;   // warp-uniform
+        const bool is_q = h < a.qh;
+        float x[4];
+        {
+            __nv_bfloat162 lo, hi;
+            memcpy(&lo, &xr[j].x, 4);
+            memcpy(&hi, &xr[j].y, 4);
+            const float2 p = __bfloat1622float2(lo), q = __bfloat1622float2(hi);
+            x[0] = p.x, x[1] = p.y, x[2] = q.x, x[3] = q.y;
+        }
+        float ss = __fadd_rn(__fadd_rn(__fmul_rn(x[0], x[0]), __fmul_rn(x[1], x[1])),
+                             __fadd_rn(__fmul_rn(x[2], x[2]), __fmul_rn(x[3], x[3])));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+        const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(QK_HEAD_DIM)), a.eps)));
+        float n[4], p[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) n[i] = bf(__fmul_rn(__fmul_rn(x[i], r), is_q ? wq[i] : wk[i]));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) p[i] = __shfl_xor_sync(0xffffffffu, n[i], 16);  // element d +- 64
+        __align__(8) __nv_bfloat16 y[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float av = __fmul_rn(n[i], c[i]), bv = __fmul_rn(sign * p[i], s[i]);
+            if (a.round_products) {
+                av = bf(av);
+                bv = bf(bv);
+            }
+            y[i] = __float2bfloat16_rn(__fadd_rn(av, bv));
+        }
+        if (is_q) {
+            *reinterpret_cast<uint2 *>(a.out_q + (t * a.qh + h) * QK_HEAD_DIM + d0) =
+                *reinterpret_cast<const uint2 *>(y);
+            continue;
+        }
+        if (!slot_ok) continue;
+        const int64_t at = slot * a.cache_s0 + int64_t(h - a.qh) * QK_HEAD_DIM + d0;
+        *reinterpret_cast<uint2 *>(a.k_cache + at) = *reinterpret_cast<const uint2 *>(y);
+        if (a.v) *reinterpret_cast<uint2 *>(a.v_cache + at) = vr[j];
     }
 }
 
@@ -134,8 +166,12 @@ int mstar_b200_qknorm_rope(const void *q, int64_t q_s0, int64_t q_s1, const void
         require(slots || num_slots >= tokens, "without a slot table the cache needs a slot per token");
         const int64_t strides[] = {q_s0, q_s1, k_s0, k_s1, cos_s0, sin_s0, cache_slot_stride};
         for (int64_t st : strides) require(st % 4 == 0, "strides must keep 8-byte alignment");
-        if (v) require(v_s1 >= QK_HEAD_DIM && v_s0 >= v_s1 * kv_heads, "v row strides smaller than the rows");
-        const void *ptrs[] = {q, k, out_q, k_cache, cos, sin};
+        if (v) {
+            require(v_s1 >= QK_HEAD_DIM && v_s0 >= v_s1 * kv_heads, "v row strides smaller than the rows");
+            require(v_s0 % 4 == 0 && v_s1 % 4 == 0, "strides must keep 8-byte alignment");
+            require(uintptr_t(v) % 8 == 0 && uintptr_t(v_cache) % 8 == 0, "prologue tensors must be 8-byte aligned");
+        }
+        const void *ptrs[] = {q, k, out_q, k_cache, cos, sin, q_weight, k_weight};
         for (const void *p : ptrs) require(uintptr_t(p) % 8 == 0, "prologue tensors must be 8-byte aligned");
         check_device(q, "q");
         check_device(out_q, "out_q");
@@ -161,7 +197,7 @@ int mstar_b200_qknorm_rope(const void *q, int64_t q_s0, int64_t q_s1, const void
         a.slots = slots;
         a.num_slots = num_slots;
         a.status = status;
-        const int64_t items = tokens * (q_heads + kv_heads);
+        const int64_t items = tokens * ceil_div(q_heads + kv_heads, QK_HEADS_PER_WARP);
         k_qknorm_rope<<<unsigned(ceil_div(items, QK_WARPS)), QK_WARPS * 32, 0, as_stream(stream)>>>(a);
         cuda_check(cudaGetLastError(), "QK norm / RoPE launch");
         return 0;

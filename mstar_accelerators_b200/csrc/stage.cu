@@ -83,8 +83,33 @@ __device__ __forceinline__ float4 q8_block8(float4 v, int *status) {
     return make_float4(q(v.x), q(v.y), q(v.z), q(v.w));
 }
 
+// The same quantization of a block held by 4 consecutive lanes, 8 values each (v in place).
+template <int MODE>
+__device__ __forceinline__ void q8_block4(float (&v)[8], int *status) {
+    bool finite = true;
+    float amax = fabsf(v[0]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        finite = finite && isfinite(v[i]);
+        amax = fmaxf(amax, fabsf(v[i]));
+    }
+    if (!finite && status) atomicOr(status, 1);
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 127.0f);
+    float id;
+    if (MODE == 2) id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+    else id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float dh = __half2float(__float2half_rn(d));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float sv = __fmul_rn(v[i], id);
+        v[i] = __fmul_rn(float(MODE == 0 ? int(roundf(sv)) : __float2int_rn(sv)), dh);
+    }
+}
+
 constexpr int STAGE_MAX_CHUNKS = STAGE_MAX_PER_LANE / 4;  // float4 chunks a lane keeps for a LayerNorm row
-constexpr int STAGE_BATCH = 4;                            // chunk rows in flight per lane without LayerNorm
+constexpr int STAGE_BATCH = 8;                            // chunk rows in flight per lane without LayerNorm
 
 // ggml_compute_forward_norm_f32 (ggml-cpu/ops.cpp:4094-4137): mean, centred
 // variance, y = (x - mean) * (1 / sqrt(var + eps)); then ggml mul and add.
@@ -170,6 +195,68 @@ __global__ void __launch_bounds__(STAGE_WARPS * 32)
                     const int64_t c = (i0 + u) * 32 + lane;
                     const float4 q = q8_block8<MODE>(v[u], status);
                     if (c < chunks) store4(out, row * ldo + 4 * c, q);
+                }
+            }
+        }
+    }
+}
+
+// Rows without a LayerNorm, eight values per lane (four lanes per Q8_0 block): every
+// 32-value block costs one amax butterfly and one pair of divisions for 8 values a lane
+// instead of 4, with 4 KB per warp in flight (STAGE_BATCH8 16-byte fp16 chunks or half
+// as many 32-byte fp32 ones). fp16 rows need 16-byte aligned rows.
+template <int MODE, bool F16>
+__global__ void __launch_bounds__(STAGE_WARPS * 32)
+    k_stage_rows8(const void *__restrict__ x, int64_t ldx, int64_t rows, int64_t k, __half *__restrict__ out,
+                  int64_t ldo, int *__restrict__ status) {
+    constexpr int BATCH = F16 ? 8 : 4;
+    const int lane = threadIdx.x & 31;
+    const int64_t row = int64_t(blockIdx.x) * STAGE_WARPS + (threadIdx.x >> 5);
+    if (row >= rows) return;   // warp-uniform
+    const int chunks = int(k / 8);   // k <= 65536
+    const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const char *>(x) + row * ldx * (F16 ? 2 : 4));
+    uint4 *dst = reinterpret_cast<uint4 *>(out + row * ldo);
+    for (int i0 = 0; i0 * 32 < chunks; i0 += BATCH) {
+        uint4 raw[F16 ? BATCH : 2 * BATCH];   // the loads in flight, converted when quantized
+#pragma unroll
+        for (int j = 0; j < BATCH; ++j) {
+            const int c = (i0 + j) * 32 + lane;
+            if constexpr (F16) {
+                raw[j] = c < chunks ? src[c] : make_uint4(0u, 0u, 0u, 0u);
+            } else {
+                raw[2 * j] = c < chunks ? src[2 * c] : make_uint4(0u, 0u, 0u, 0u);
+                raw[2 * j + 1] = c < chunks ? src[2 * c + 1] : make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < BATCH; ++j) {
+            if ((i0 + j) * 32 < chunks) {   // warp-uniform: every lane takes part in the block shuffles
+                const int c = (i0 + j) * 32 + lane;
+                float v[8];
+                if constexpr (F16) {
+                    const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        __half2 h2;
+                        memcpy(&h2, &w[e], 4);
+                        const float2 f = __half22float2(h2);
+                        v[2 * e] = f.x;
+                        v[2 * e + 1] = f.y;
+                    }
+                } else {
+                    const uint32_t w[8] = {raw[2 * j].x,     raw[2 * j].y,     raw[2 * j].z,     raw[2 * j].w,
+                                           raw[2 * j + 1].x, raw[2 * j + 1].y, raw[2 * j + 1].z, raw[2 * j + 1].w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(w[e]);
+                }
+                q8_block4<MODE>(v, status);
+                if (c < chunks) {
+                    uint4 o;
+                    o.x = half2_bits(__floats2half2_rn(v[0], v[1]));
+                    o.y = half2_bits(__floats2half2_rn(v[2], v[3]));
+                    o.z = half2_bits(__floats2half2_rn(v[4], v[5]));
+                    o.w = half2_bits(__floats2half2_rn(v[6], v[7]));
+                    dst[c] = o;
                 }
             }
         }
@@ -283,8 +370,10 @@ __global__ void __launch_bounds__(CONV_WARPS * 32)
 // [seqs][heads][positions][head_dim] bf16 output (any strides over the first three, head_dim
 // contiguous): row s * positions + t is head 0 .. heads-1 of position t of sequence s side by
 // side (the transpose and fp32 conversion a torch reshape would first write out), then Q8_0
-// blocks as k_stage_rows: a warp per row, four values per lane (an 8-byte load from one
-// head's contiguous run), eight lanes per block.
+// blocks as k_stage_rows: a warp per row, eight values per lane (a 16-byte load from one
+// head's contiguous run, STAGE_HEADS_BATCH of them in flight), four lanes per block.
+constexpr int STAGE_HEADS_BATCH = 8;
+
 template <int MODE>
 __global__ void __launch_bounds__(STAGE_WARPS * 32)
     k_stage_heads(const __nv_bfloat16 *__restrict__ att, int64_t seqs, int64_t heads, int64_t positions,
@@ -293,22 +382,46 @@ __global__ void __launch_bounds__(STAGE_WARPS * 32)
     const int lane = threadIdx.x & 31;
     const int64_t row = int64_t(blockIdx.x) * STAGE_WARPS + (threadIdx.x >> 5);
     if (row >= seqs * positions) return;   // warp-uniform
-    const int64_t s = row / positions, t = row % positions, k = heads * head_dim, chunks = k / 4;
+    const int64_t s = row / positions, t = row % positions;
+    const int k = int(heads * head_dim), chunks = k / 8, hd = int(head_dim);   // k <= 65536
     const __nv_bfloat16 *base = att + s * seq_stride + t * position_stride;
-    for (int64_t i = 0; i * 32 < chunks; ++i) {   // warp-uniform: every lane takes part in the block shuffles
-        const int64_t c = i * 32 + lane;
-        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (c < chunks) {
-            const int64_t e = 4 * c, h = e / head_dim, d = e - h * head_dim;
-            const uint2 u = *reinterpret_cast<const uint2 *>(base + h * head_stride + d);
-            __nv_bfloat162 lo, hi;
-            memcpy(&lo, &u.x, 4);
-            memcpy(&hi, &u.y, 4);
-            const float2 a = __bfloat1622float2(lo), b = __bfloat1622float2(hi);
-            v = make_float4(a.x, a.y, b.x, b.y);
+    __half *dst = out + row * k;
+    for (int i0 = 0; i0 * 32 < chunks; i0 += STAGE_HEADS_BATCH) {
+        uint4 u[STAGE_HEADS_BATCH];
+#pragma unroll
+        for (int j = 0; j < STAGE_HEADS_BATCH; ++j) {
+            const int c = (i0 + j) * 32 + lane;
+            u[j] = make_uint4(0u, 0u, 0u, 0u);
+            if (c < chunks) {
+                const int h = 8 * c / hd, d = 8 * c - h * hd;
+                u[j] = *reinterpret_cast<const uint4 *>(base + h * head_stride + d);
+            }
         }
-        v = q8_block8<MODE>(v, status);
-        if (c < chunks) store4(out, row * k + 4 * c, v);
+#pragma unroll
+        for (int j = 0; j < STAGE_HEADS_BATCH; ++j) {
+            if ((i0 + j) * 32 < chunks) {   // warp-uniform: every lane takes part in the block shuffles
+                const int c = (i0 + j) * 32 + lane;
+                const uint32_t w[4] = {u[j].x, u[j].y, u[j].z, u[j].w};
+                float v[8];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    __nv_bfloat162 b2;
+                    memcpy(&b2, &w[e], 4);
+                    const float2 f = __bfloat1622float2(b2);
+                    v[2 * e] = f.x;
+                    v[2 * e + 1] = f.y;
+                }
+                q8_block4<MODE>(v, status);
+                if (c < chunks) {
+                    uint4 o;
+                    o.x = half2_bits(__floats2half2_rn(v[0], v[1]));
+                    o.y = half2_bits(__floats2half2_rn(v[2], v[3]));
+                    o.z = half2_bits(__floats2half2_rn(v[4], v[5]));
+                    o.w = half2_bits(__floats2half2_rn(v[6], v[7]));
+                    *reinterpret_cast<uint4 *>(dst + 8 * c) = o;
+                }
+            }
+        }
     }
 }
 
@@ -340,11 +453,16 @@ static void stage_rows_mode(const void *x, int x_f16, int64_t ldx, int64_t rows,
                             const float *ln_b, float eps, __half *out, int64_t ldo, int *status, cudaStream_t s) {
     const unsigned grid = unsigned(ceil_div(rows, STAGE_WARPS));
     const int threads = STAGE_WARPS * 32;
+    // eight values per lane where the rows allow 16-byte loads and stores (the same bytes)
+    const bool wide = ldo % 8 == 0 && uintptr_t(out) % 16 == 0 &&
+                      (!x_f16 || (uintptr_t(x) % 16 == 0 && ldx % 8 == 0));
     if (x_f16) {
         if (ln_w) k_stage_rows<MODE, true, true><<<grid, threads, 0, s>>>(x, ldx, rows, k, ln_w, ln_b, eps, out, ldo, status);
+        else if (wide) k_stage_rows8<MODE, true><<<grid, threads, 0, s>>>(x, ldx, rows, k, out, ldo, status);
         else k_stage_rows<MODE, true, false><<<grid, threads, 0, s>>>(x, ldx, rows, k, ln_w, ln_b, eps, out, ldo, status);
     } else {
         if (ln_w) k_stage_rows<MODE, false, true><<<grid, threads, 0, s>>>(x, ldx, rows, k, ln_w, ln_b, eps, out, ldo, status);
+        else if (wide) k_stage_rows8<MODE, false><<<grid, threads, 0, s>>>(x, ldx, rows, k, out, ldo, status);
         else k_stage_rows<MODE, false, false><<<grid, threads, 0, s>>>(x, ldx, rows, k, ln_w, ln_b, eps, out, ldo, status);
     }
 }
@@ -457,11 +575,11 @@ int mstar_b200_stage_heads(const void *attention, int64_t seqs, int64_t heads, i
         require(seqs >= 1 && heads >= 1 && positions >= 1 && head_dim >= QK && head_dim % QK == 0 &&
                     seqs * positions <= (int64_t(1) << 31) && heads * head_dim <= 65536,
                 "invalid attention layout (head_dim a multiple of 32)");
-        require(seq_stride >= 0 && head_stride >= 0 && position_stride >= 0 && seq_stride % 4 == 0 &&
-                    head_stride % 4 == 0 && position_stride % 4 == 0,
-                "attention strides must be non-negative multiples of 4 elements");
+        require(seq_stride >= 0 && head_stride >= 0 && position_stride >= 0 && seq_stride % 8 == 0 &&
+                    head_stride % 8 == 0 && position_stride % 8 == 0,
+                "attention strides must be non-negative multiples of 8 elements");
         require(attention && staged && status, "missing staging operand");
-        require(uintptr_t(attention) % 8 == 0, "attention output must be 8-byte aligned");
+        require(uintptr_t(attention) % 16 == 0, "attention output must be 16-byte aligned");
         const uint64_t ab = uint64_t((seqs - 1) * seq_stride + (heads - 1) * head_stride +
                                      (positions - 1) * position_stride + head_dim) * 2;
         const uint64_t ob = uint64_t(seqs * positions * heads * head_dim) * 2;

@@ -53,6 +53,21 @@ def test_stage_rows_exact(mode, f16):
     np.testing.assert_array_equal(got.view(np.uint16), staged_ref(x, mode).view(np.uint16))
 
 
+@pytest.mark.parametrize("f16", [False, True])
+def test_stage_rows_strided(f16):
+    """Rows 1284 elements apart: fp32 rows keep the eight-values-per-lane kernel, fp16 rows
+    (not 16-byte aligned) take the four-values-per-lane one; both give the oracle's bytes."""
+    from mstar_accelerators_b200 import linear
+    rng = np.random.default_rng(17)
+    x = (rng.standard_normal((77, 1284)) * 3).astype(np.float32)
+    x[3, 96:128] = 0.0
+    if f16:
+        x = x.astype(np.float16).astype(np.float32)
+    t = dev(x).half() if f16 else dev(x)
+    got = linear.stage_rows(t[:, :1280]).cpu().numpy()
+    np.testing.assert_array_equal(got.view(np.uint16), staged_ref(x[:, :1280], "arm").view(np.uint16))
+
+
 def test_stage_rows_layer_norm():
     from mstar_accelerators_b200 import linear
     rng = np.random.default_rng(8)
