@@ -439,6 +439,16 @@ MSTAR_B200_API int mstar_b200_qknorm_rope(const void *q, int64_t q_s0, int64_t q
     int32_t kv_heads, int32_t head_dim, float eps, int32_t round_products, void *out_q, void *k_cache,
     void *v_cache, int64_t cache_slot_stride, const int64_t *slots, int64_t num_slots, int32_t *status, void *stream,
     char *error, size_t error_size);
+/* qknorm_rope_f32: the same op on fp32 q / k / v rows (the QKV projection's fp32 output,
+ * 16-byte aligned), each value rounded to bf16 to nearest even as it is read: the result
+ * of qknorm_rope on the .to(bfloat16) of those rows (thinker_model.py:106-148), without
+ * writing that bf16 copy. Strides in fp32 elements; everything else as qknorm_rope. */
+MSTAR_B200_API int mstar_b200_qknorm_rope_f32(const void *q, int64_t q_s0, int64_t q_s1, const void *k, int64_t k_s0,
+    int64_t k_s1, const void *v, int64_t v_s0, int64_t v_s1, const void *q_weight, const void *k_weight,
+    const void *cos, int64_t cos_s0, const void *sin, int64_t sin_s0, int64_t tokens, int32_t q_heads,
+    int32_t kv_heads, int32_t head_dim, float eps, int32_t round_products, void *out_q, void *k_cache,
+    void *v_cache, int64_t cache_slot_stride, const int64_t *slots, int64_t num_slots, int32_t *status, void *stream,
+    char *error, size_t error_size);
 
 /* --- categorical sampling of readout logits (backends/pi/docs/categorical.md, the
  * Graph.categorical operation; scalar oracle backends/pi/torch/tests/categorical_reference.py) ---

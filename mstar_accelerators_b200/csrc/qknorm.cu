@@ -30,7 +30,7 @@ constexpr int QK_WARPS = 8;
 constexpr int QK_HEADS_PER_WARP = 4;
 
 struct QkArgs {
-    const __nv_bfloat16 *q, *k, *v;      // [T, heads, 128] rows with strides (elements)
+    const void *q, *k, *v;               // [T, heads, 128] bf16 (or fp32) rows with strides (elements)
     int64_t q_s0, q_s1, k_s0, k_s1, v_s0, v_s1;
     const __nv_bfloat16 *qw, *kw;        // [128]
     const __nv_bfloat16 *cos, *sin;      // [T, 128] rows
@@ -58,8 +58,26 @@ __device__ __forceinline__ void bf16x4(const __nv_bfloat16 *p, float (&f)[4]) {
     f[0] = a.x, f[1] = a.y, f[2] = b.x, f[3] = b.y;
 }
 
+// Four consecutive elements of a q / k / v row as bf16: loaded as they are, or, for fp32
+// rows (the projection's fp32 output), rounded to bf16 to nearest even on the way in,
+// which is the .to(bfloat16) the op would otherwise run first.
+template <bool F32>
+__device__ __forceinline__ uint2 load_head4(const void *base, int64_t e) {
+    if constexpr (F32) {
+        const float4 f = *reinterpret_cast<const float4 *>(static_cast<const float *>(base) + e);
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(f.x, f.y), hi = __floats2bfloat162_rn(f.z, f.w);
+        uint2 u;
+        memcpy(&u.x, &lo, 4);
+        memcpy(&u.y, &hi, 4);
+        return u;
+    } else {
+        return *reinterpret_cast<const uint2 *>(static_cast<const __nv_bfloat16 *>(base) + e);
+    }
+}
+
 // A warp takes QK_HEADS_PER_WARP heads of one token: their rows are loaded together
-// (one 8-byte load per lane and head) and the token's cos / sin rows once for all of them.
+// (one load per lane and head) and the token's cos / sin rows once for all of them.
+template <bool F32>
 __global__ void __launch_bounds__(QK_WARPS * 32) k_qknorm_rope(const QkArgs a) {
     const int lane = threadIdx.x & 31;
     const int heads = a.qh + a.kh;
@@ -76,10 +94,10 @@ __global__ void __launch_bounds__(QK_WARPS * 32) k_qknorm_rope(const QkArgs a) {
         xr[j] = make_uint2(0u, 0u);
         vr[j] = make_uint2(0u, 0u);
         if (h < a.qh) {
-            xr[j] = *reinterpret_cast<const uint2 *>(a.q + t * a.q_s0 + int64_t(h) * a.q_s1 + d0);
+            xr[j] = load_head4<F32>(a.q, t * a.q_s0 + int64_t(h) * a.q_s1 + d0);
         } else if (h < heads) {
-            xr[j] = *reinterpret_cast<const uint2 *>(a.k + t * a.k_s0 + int64_t(h - a.qh) * a.k_s1 + d0);
-            if (a.v) vr[j] = *reinterpret_cast<const uint2 *>(a.v + t * a.v_s0 + int64_t(h - a.qh) * a.v_s1 + d0);
+            xr[j] = load_head4<F32>(a.k, t * a.k_s0 + int64_t(h - a.qh) * a.k_s1 + d0);
+            if (a.v) vr[j] = load_head4<F32>(a.v, t * a.v_s0 + int64_t(h - a.qh) * a.v_s1 + d0);
         }
     }
     float c[4], s[4], wq[4], wk[4];
@@ -146,7 +164,7 @@ using namespace mb;
 
 extern "C" {
 
-int mstar_b200_qknorm_rope(const void *q, int64_t q_s0, int64_t q_s1, const void *k, int64_t k_s0, int64_t k_s1,
+static int qknorm_rope_impl(bool f32, const void *q, int64_t q_s0, int64_t q_s1, const void *k, int64_t k_s0, int64_t k_s1,
                            const void *v, int64_t v_s0, int64_t v_s1, const void *q_weight, const void *k_weight,
                            const void *cos, int64_t cos_s0, const void *sin, int64_t sin_s0, int64_t tokens,
                            int32_t q_heads, int32_t kv_heads, int32_t head_dim, float eps, int32_t round_products,
@@ -173,14 +191,16 @@ int mstar_b200_qknorm_rope(const void *q, int64_t q_s0, int64_t q_s1, const void
         }
         const void *ptrs[] = {q, k, out_q, k_cache, cos, sin, q_weight, k_weight};
         for (const void *p : ptrs) require(uintptr_t(p) % 8 == 0, "prologue tensors must be 8-byte aligned");
+        if (f32) require(uintptr_t(q) % 16 == 0 && uintptr_t(k) % 16 == 0 && uintptr_t(v) % 16 == 0,
+                         "fp32 q / k / v rows must be 16-byte aligned");
         check_device(q, "q");
         check_device(out_q, "out_q");
         check_device(k_cache, "k_cache");
         if (tokens == 0) return 0;
         QkArgs a{};
-        a.q = static_cast<const __nv_bfloat16 *>(q);
-        a.k = static_cast<const __nv_bfloat16 *>(k);
-        a.v = static_cast<const __nv_bfloat16 *>(v);
+        a.q = q;
+        a.k = k;
+        a.v = v;
         a.q_s0 = q_s0; a.q_s1 = q_s1; a.k_s0 = k_s0; a.k_s1 = k_s1; a.v_s0 = v_s0; a.v_s1 = v_s1;
         a.qw = static_cast<const __nv_bfloat16 *>(q_weight);
         a.kw = static_cast<const __nv_bfloat16 *>(k_weight);
@@ -198,13 +218,38 @@ int mstar_b200_qknorm_rope(const void *q, int64_t q_s0, int64_t q_s1, const void
         a.num_slots = num_slots;
         a.status = status;
         const int64_t items = tokens * ceil_div(q_heads + kv_heads, QK_HEADS_PER_WARP);
-        k_qknorm_rope<<<unsigned(ceil_div(items, QK_WARPS)), QK_WARPS * 32, 0, as_stream(stream)>>>(a);
+        auto kernel = f32 ? k_qknorm_rope<true> : k_qknorm_rope<false>;
+        kernel<<<unsigned(ceil_div(items, QK_WARPS)), QK_WARPS * 32, 0, as_stream(stream)>>>(a);
         cuda_check(cudaGetLastError(), "QK norm / RoPE launch");
         return 0;
     } catch (const std::exception &e) {
         message(error, error_size, e.what());
         return -1;
     }
+}
+
+int mstar_b200_qknorm_rope(const void *q, int64_t q_s0, int64_t q_s1, const void *k, int64_t k_s0, int64_t k_s1,
+                           const void *v, int64_t v_s0, int64_t v_s1, const void *q_weight, const void *k_weight,
+                           const void *cos, int64_t cos_s0, const void *sin, int64_t sin_s0, int64_t tokens,
+                           int32_t q_heads, int32_t kv_heads, int32_t head_dim, float eps, int32_t round_products,
+                           void *out_q, void *k_cache, void *v_cache, int64_t cache_slot_stride,
+                           const int64_t *slots, int64_t num_slots, int32_t *status, void *stream, char *error,
+                           size_t error_size) {
+    return qknorm_rope_impl(false, q, q_s0, q_s1, k, k_s0, k_s1, v, v_s0, v_s1, q_weight, k_weight, cos, cos_s0, sin,
+                            sin_s0, tokens, q_heads, kv_heads, head_dim, eps, round_products, out_q, k_cache, v_cache,
+                            cache_slot_stride, slots, num_slots, status, stream, error, error_size);
+}
+
+int mstar_b200_qknorm_rope_f32(const void *q, int64_t q_s0, int64_t q_s1, const void *k, int64_t k_s0, int64_t k_s1,
+                               const void *v, int64_t v_s0, int64_t v_s1, const void *q_weight, const void *k_weight,
+                               const void *cos, int64_t cos_s0, const void *sin, int64_t sin_s0, int64_t tokens,
+                               int32_t q_heads, int32_t kv_heads, int32_t head_dim, float eps, int32_t round_products,
+                               void *out_q, void *k_cache, void *v_cache, int64_t cache_slot_stride,
+                               const int64_t *slots, int64_t num_slots, int32_t *status, void *stream, char *error,
+                               size_t error_size) {
+    return qknorm_rope_impl(true, q, q_s0, q_s1, k, k_s0, k_s1, v, v_s0, v_s1, q_weight, k_weight, cos, cos_s0, sin,
+                            sin_s0, tokens, q_heads, kv_heads, head_dim, eps, round_products, out_q, k_cache, v_cache,
+                            cache_slot_stride, slots, num_slots, status, stream, error, error_size);
 }
 
 }  // extern "C"

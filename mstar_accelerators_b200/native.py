@@ -76,6 +76,9 @@ SIGNATURES = {
     "mstar_b200_qknorm_rope": (_int, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _i64,
                                       _i64, C.c_int32, C.c_int32, C.c_int32, C.c_float, C.c_int32, _vp, _vp, _vp, _i64,
                                       _vp, _i64, _vp, _vp, *_err]),
+    "mstar_b200_qknorm_rope_f32": (_int, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp,
+                                          _i64, _i64, C.c_int32, C.c_int32, C.c_int32, C.c_float, C.c_int32, _vp, _vp,
+                                          _vp, _i64, _vp, _i64, _vp, _vp, *_err]),
     "mstar_b200_categorical": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _u64, _vp, *_err]),
     "mstar_b200_wait_selftest": (_int, [C.c_int32, _i64, _vp, _vp, _vp, *_err]),
     "mstar_b200_tp_reduce": (_int, [_vp, C.c_int32, _i64, _i64, _vp, _vp, _vp, _vp, C.c_float, _vp, _i64,

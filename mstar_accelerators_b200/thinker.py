@@ -76,17 +76,22 @@ def qknorm_rope(q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_weig
                 status: torch.Tensor | None = None):
     """The thinker's QK RMSNorm + prepared MRoPE (+ KV write) in one launch (the reference's
     fused op, qknorm_rope.py:9-53). q [T, Hq, 128], k / v [T, Hkv, 128], weights [128], cos / sin
-    [T, 128], all bf16. Returns (q_out [T, Hq, 128], k_cache); without a cache the normed, roped
-    k comes back as a fresh [T, Hkv, 128] tensor. slots [T] int64 picks each token's cache row."""
+    [T, 128], all bf16; or q / k / v fp32 (the projection's output, rounded to bf16 as they are
+    read). Returns (q_out [T, Hq, 128], k_cache); without a cache the normed, roped k comes back
+    as a fresh [T, Hkv, 128] tensor. slots [T] int64 picks each token's cache row."""
     from . import native
     from .linear import _stream
     from .native import check, error_buffer
     lib = native.require_capability()
     T, Hq, D = q.shape
     Hkv = k.shape[1]
-    for t in (q, k, q_weight, k_weight, cos, sin) + ((v,) if v is not None else ()):
-        if t.dtype != torch.bfloat16 or not t.is_cuda or t.stride(-1) != 1:
-            raise ValueError("bf16 CUDA tensors with unit last stride expected")
+    f32 = q.dtype == torch.float32
+    rows = (q, k) + ((v,) if v is not None else ())
+    for t in rows + (q_weight, k_weight, cos, sin):
+        want = torch.float32 if f32 and any(t is r for r in rows) else torch.bfloat16
+        if t.dtype != want or not t.is_cuda or t.stride(-1) != 1:
+            raise ValueError("CUDA tensors with unit last stride expected: q / k / v all bf16 or all fp32, "
+                             "weights and cos / sin bf16")
     out_q = torch.empty((T, Hq, D), dtype=torch.bfloat16, device=q.device)
     if k_cache is None:
         k_cache = torch.empty((T, Hkv, D), dtype=torch.bfloat16, device=q.device)
@@ -97,7 +102,8 @@ def qknorm_rope(q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_weig
         raise ValueError("slots must be int64 [T]")
     st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=q.device)
     e = error_buffer()
-    check(lib.mstar_b200_qknorm_rope(
+    op = lib.mstar_b200_qknorm_rope_f32 if f32 else lib.mstar_b200_qknorm_rope
+    check(op(
         q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), k.stride(1),
         v.data_ptr() if v is not None else None, v.stride(0) if v is not None else 0,
         v.stride(1) if v is not None else 0, q_weight.data_ptr(), k_weight.data_ptr(), cos.data_ptr(), cos.stride(0),

@@ -242,7 +242,7 @@ class ThinkerStackB200:
         T = S * n
         cos, sin, slots, mask = shared
         h = rms_norm(x, L["ln1"], cfg.eps, f32=True)
-        qkv = self._linear(L["qkv"], h).to(torch.bfloat16)
+        qkv = self._linear(L["qkv"], h)   # fp32; the prologue rounds q / k / v to bf16 as it reads them
         q = qkv[:, :Hq * D].view(T, Hq, D)
         k = qkv[:, Hq * D:(Hq + Hk) * D].view(T, Hk, D)
         v = qkv[:, (Hq + Hk) * D:].view(T, Hk, D)

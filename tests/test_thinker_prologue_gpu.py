@@ -65,3 +65,42 @@ def test_out_of_range_slot_sets_status():
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     thinker.qknorm_rope(q, k, w, w, cs, cs, k_cache=kc, slots=torch.tensor([1, 9], device="cuda"), status=status)
     assert int(status.item()) & 1 and kc[1].any() and not kc[[0, 2, 3]].any()
+
+
+@pytest.mark.parametrize("T", [1, 37, 300])
+def test_fp32_rows_equal_their_bf16_rounding(T):
+    """mstar_b200_qknorm_rope_f32 on the fp32 projection output gives, bit for bit, what
+    mstar_b200_qknorm_rope gives on its .to(bfloat16): q, the k cache rows and the v copies."""
+    from mstar_accelerators_b200 import thinker
+    g = torch.Generator(device="cuda").manual_seed(T)
+    Hq, Hk = 32, 4
+    x32 = torch.randn((T, (Hq + 2 * Hk) * 128), device="cuda", generator=g) * 2
+    w = (1 + 0.1 * torch.randn((2, 128), device="cuda", generator=g)).to(torch.bfloat16)
+    ang = torch.rand((T, 64), device="cuda", generator=g) * 200
+    cos = torch.cos(torch.cat([ang, ang], -1)).to(torch.bfloat16)
+    sin = torch.sin(torch.cat([ang, ang], -1)).to(torch.bfloat16)
+    slots = torch.randperm(512, device="cuda", generator=g)[:T]
+    outs = []
+    for x in (x32, x32.to(torch.bfloat16)):
+        q = x[:, :Hq * 128].view(T, Hq, 128)
+        k = x[:, Hq * 128:(Hq + Hk) * 128].view(T, Hk, 128)
+        v = x[:, (Hq + Hk) * 128:].view(T, Hk, 128)
+        kc = torch.zeros((512, Hk, 128), dtype=torch.bfloat16, device="cuda")
+        vc = torch.zeros_like(kc)
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        oq, kc = thinker.qknorm_rope(q, k, w[0], w[1], cos, sin, eps=1e-6, v=v, k_cache=kc, v_cache=vc, slots=slots,
+                                     status=status)
+        assert int(status.item()) == 0
+        outs.append((oq, kc, vc))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+
+
+def test_mixed_input_dtypes_are_rejected():
+    from mstar_accelerators_b200 import thinker
+    q = torch.zeros((2, 4, 128), device="cuda")
+    k = torch.zeros((2, 1, 128), device="cuda", dtype=torch.bfloat16)
+    w = torch.ones(128, device="cuda", dtype=torch.bfloat16)
+    cs = torch.ones(2, 128, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        thinker.qknorm_rope(q, k, w, w, cs, cs)
