@@ -44,6 +44,10 @@ void launch_dequant_act(int mode, const float *x, int64_t ldx, int64_t m, int64_
 // rows of fp32 or fp16 [-> LayerNorm] -> Q8_0 (selected rounding) -> fp16(q * d) [rows][k]
 void launch_stage_rows(int mode, const void *x, int x_f16, int64_t ldx, int64_t rows, int64_t k, const float *ln_w,
                        const float *ln_b, float ln_eps, __half *out, int64_t ldo, int *status, cudaStream_t s);
+// contiguous bf16 rows [rows][k] (16-byte aligned, k a multiple of 32) -> Q8_0 (selected
+// rounding) -> fp16(q * d) [rows][k]; status (may be null) gets bit value 1 for a nonfinite value
+void launch_stage_rows_bf16(int mode, const void *x, int64_t rows, int64_t k, __half *out, int *status,
+                            cudaStream_t s);
 // 1-D convolution columns (kernel 3, padding 1, dilation 1) -> Q8_0 -> fp16(q * d),
 // K = 3 * channels zero-padded to k_padded; row = b * time_out + t, column = c * 3 + tap
 void launch_stage_conv(int mode, const float *src, int time_major, int64_t batch, int64_t channels,

@@ -829,6 +829,7 @@ struct Moe {
     int q8 = 0, E = 0, I = 0, H = 0, topk = 0, max_tokens = 0, max_tiles = 0;
     void *w1 = nullptr, *w2 = nullptr;   // prepared 16-bit weights
     void *xp = nullptr, *mid = nullptr;  // permuted activations / intermediate
+    __half *xs = nullptr;                // Q8_0 experts: the tokens' staged rows, before the permutation
     __nv_bfloat16 *y = nullptr;          // per-pair down outputs
     int *ibuf = nullptr;                 // counts, offsets, cursor, tiles, num_tiles, perm, inv
     int *status = nullptr;
@@ -836,7 +837,7 @@ struct Moe {
     CUtensorMap map_w1{}, map_w2{}, map_x{}, map_mid{};
     std::atomic_flag busy = ATOMIC_FLAG_INIT;
     ~Moe() {
-        for (void *p : {w1, w2, xp, mid, (void *)y, (void *)ibuf, (void *)status})
+        for (void *p : {w1, w2, xp, mid, (void *)xs, (void *)y, (void *)ibuf, (void *)status})
             if (p) cudaFree(p);
     }
 };
@@ -945,6 +946,9 @@ void *mstar_b200_moe_create(int32_t format, const void *w1, uint64_t w1_bytes, c
         cuda_check(cudaMalloc(&m->w2, size_t(E * H * I * 2)), "w2 allocation");
         cuda_check(cudaMalloc(&m->xp, size_t((P + MOE_BM) * H * 2)), "permuted activations");
         cuda_check(cudaMalloc(&m->mid, size_t((P + MOE_BM) * I * 2)), "intermediate");
+        if (m->q8)
+            cuda_check(cudaMalloc(reinterpret_cast<void **>(&m->xs), size_t(int64_t(max_tokens) * H * 2)),
+                       "staged token rows");
         cuda_check(cudaMalloc(reinterpret_cast<void **>(&m->y), size_t(P * H * 2)), "expert outputs");
         const int64_t ints = 3 * E + 3 * int64_t(m->max_tiles) + 1 + 2 * P + 1;
         cuda_check(cudaMalloc(reinterpret_cast<void **>(&m->ibuf), size_t(ints * 4)), "plan buffers");
@@ -995,7 +999,12 @@ static void moe_experts(Moe &m, const void *x, int64_t tokens, const float *topk
     k_moe_count<<<unsigned(ceil_div(P, 256)), 256, 0, s>>>(topk_ids, P, m.E, e0, e_total, m.plan.counts, status);
     k_moe_plan<<<1, 256, 0, s>>>(m.plan, m.E, m.max_tiles);
     k_moe_scatter<<<unsigned(ceil_div(P, 256)), 256, 0, s>>>(topk_ids, P, m.E, e0, e_total, m.plan);
-    if (vec)
+    if (vec && m.q8) {
+        // each token's Q8_0 staging once (not once per routed pair), then a 16-byte row copy
+        launch_stage_rows_bf16(rounding, x, tokens, m.H, m.xs, nullptr, s);
+        k_moe_gather_vec<<<unsigned(P), 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16 *>(m.xs), m.plan.perm,
+                                                     m.plan.valid, P, m.H, m.topk, 0, rounding, m.xp);
+    } else if (vec)
         k_moe_gather_vec<<<unsigned(P), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), m.plan.perm,
                                                      m.plan.valid, P, m.H, m.topk, m.q8, rounding, m.xp);
     else

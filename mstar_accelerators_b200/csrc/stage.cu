@@ -203,12 +203,15 @@ __global__ void __launch_bounds__(STAGE_WARPS * 32)
 
 // Rows without a LayerNorm, eight values per lane (four lanes per Q8_0 block): every
 // 32-value block costs one amax butterfly and one pair of divisions for 8 values a lane
-// instead of 4, with 4 KB per warp in flight (STAGE_BATCH8 16-byte fp16 chunks or half
-// as many 32-byte fp32 ones). fp16 rows need 16-byte aligned rows.
-template <int MODE, bool F16>
+// instead of 4, with 4 KB per warp in flight (8 16-byte chunks of fp16 / bf16 rows or
+// half as many 32-byte fp32 ones). 16-bit rows need 16-byte aligned rows.
+constexpr int ROWS_F32 = 0, ROWS_F16 = 1, ROWS_BF16 = 2;
+
+template <int MODE, int IN>
 __global__ void __launch_bounds__(STAGE_WARPS * 32)
     k_stage_rows8(const void *__restrict__ x, int64_t ldx, int64_t rows, int64_t k, __half *__restrict__ out,
                   int64_t ldo, int *__restrict__ status) {
+    constexpr bool F16 = IN != ROWS_F32;   // 16-bit rows: one 16-byte load per chunk
     constexpr int BATCH = F16 ? 8 : 4;
     const int lane = threadIdx.x & 31;
     const int64_t row = int64_t(blockIdx.x) * STAGE_WARPS + (threadIdx.x >> 5);
@@ -237,9 +240,16 @@ __global__ void __launch_bounds__(STAGE_WARPS * 32)
                     const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        __half2 h2;
-                        memcpy(&h2, &w[e], 4);
-                        const float2 f = __half22float2(h2);
+                        float2 f;
+                        if constexpr (IN == ROWS_BF16) {
+                            __nv_bfloat162 b2;
+                            memcpy(&b2, &w[e], 4);
+                            f = __bfloat1622float2(b2);
+                        } else {
+                            __half2 h2;
+                            memcpy(&h2, &w[e], 4);
+                            f = __half22float2(h2);
+                        }
                         v[2 * e] = f.x;
                         v[2 * e + 1] = f.y;
                     }
@@ -458,11 +468,11 @@ static void stage_rows_mode(const void *x, int x_f16, int64_t ldx, int64_t rows,
                       (!x_f16 || (uintptr_t(x) % 16 == 0 && ldx % 8 == 0));
     if (x_f16) {
         if (ln_w) k_stage_rows<MODE, true, true><<<grid, threads, 0, s>>>(x, ldx, rows, k, ln_w, ln_b, eps, out, ldo, status);
-        else if (wide) k_stage_rows8<MODE, true><<<grid, threads, 0, s>>>(x, ldx, rows, k, out, ldo, status);
+        else if (wide) k_stage_rows8<MODE, ROWS_F16><<<grid, threads, 0, s>>>(x, ldx, rows, k, out, ldo, status);
         else k_stage_rows<MODE, true, false><<<grid, threads, 0, s>>>(x, ldx, rows, k, ln_w, ln_b, eps, out, ldo, status);
     } else {
         if (ln_w) k_stage_rows<MODE, false, true><<<grid, threads, 0, s>>>(x, ldx, rows, k, ln_w, ln_b, eps, out, ldo, status);
-        else if (wide) k_stage_rows8<MODE, false><<<grid, threads, 0, s>>>(x, ldx, rows, k, out, ldo, status);
+        else if (wide) k_stage_rows8<MODE, ROWS_F32><<<grid, threads, 0, s>>>(x, ldx, rows, k, out, ldo, status);
         else k_stage_rows<MODE, false, false><<<grid, threads, 0, s>>>(x, ldx, rows, k, ln_w, ln_b, eps, out, ldo, status);
     }
 }
@@ -472,6 +482,15 @@ void launch_stage_rows(int mode, const void *x, int x_f16, int64_t ldx, int64_t 
     if (mode == 0) stage_rows_mode<0>(x, x_f16, ldx, rows, k, ln_w, ln_b, ln_eps, out, ldo, status, s);
     else if (mode == 2) stage_rows_mode<2>(x, x_f16, ldx, rows, k, ln_w, ln_b, ln_eps, out, ldo, status, s);
     else stage_rows_mode<1>(x, x_f16, ldx, rows, k, ln_w, ln_b, ln_eps, out, ldo, status, s);
+}
+
+void launch_stage_rows_bf16(int mode, const void *x, int64_t rows, int64_t k, __half *out, int *status,
+                            cudaStream_t s) {
+    const unsigned grid = unsigned(ceil_div(rows, STAGE_WARPS));
+    const int threads = STAGE_WARPS * 32;
+    if (mode == 0) k_stage_rows8<0, ROWS_BF16><<<grid, threads, 0, s>>>(x, k, rows, k, out, k, status);
+    else if (mode == 2) k_stage_rows8<2, ROWS_BF16><<<grid, threads, 0, s>>>(x, k, rows, k, out, k, status);
+    else k_stage_rows8<1, ROWS_BF16><<<grid, threads, 0, s>>>(x, k, rows, k, out, k, status);
 }
 
 template <int MODE>
