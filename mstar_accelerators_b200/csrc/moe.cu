@@ -295,51 +295,18 @@ __global__ void k_moe_gather(const __nv_bfloat16 *__restrict__ x, const int *__r
     }
 }
 
-// k_moe_gather with 16-byte rows pieces (x 16-byte aligned, H a multiple of
-// 128): bf16 rows as one uint4 per thread and pass; Q8_0 rows four blocks per
-// warp and pass (8 lanes per block, 4 elements per lane), the same quantization.
-__global__ void __launch_bounds__(256) k_moe_gather_vec(const __nv_bfloat16 *__restrict__ x,
-                                                        const int *__restrict__ perm, const int *__restrict__ valid,
-                                                        int P, int H, int topk, int q8, int rounding,
+// k_moe_gather with 16-byte row pieces (rows 16-byte aligned, H a multiple of 128), one
+// uint4 per thread and pass: bf16 token rows, or (Q8_0 experts) the tokens' rows already
+// staged as fp16(q * d), the same 2-byte elements.
+__global__ void __launch_bounds__(256) k_moe_gather_vec(const void *__restrict__ x, const int *__restrict__ perm,
+                                                        const int *__restrict__ valid, int P, int H, int topk,
                                                         void *__restrict__ xp) {
     const int pos = blockIdx.x;
     if (pos >= P || pos >= *valid) return;
     const int64_t t = perm[pos] / topk;
-    const __nv_bfloat16 *src = x + t * H;
-    if (!q8) {
-        const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
-        uint4 *d4 = reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(xp) + int64_t(pos) * H);
-        for (int i = threadIdx.x; i < H / 8; i += blockDim.x) d4[i] = s4[i];
-        return;
-    }
-    __half *dst = static_cast<__half *>(xp) + int64_t(pos) * H;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    for (int c = warp; c < H / 128; c += nwarps) {  // 128 elements = 4 blocks per warp and pass
-        const int e0 = c * 128 + 4 * lane;
-        const uint2 raw = *reinterpret_cast<const uint2 *>(src + e0);
-        __nv_bfloat162 p0, p1;
-        memcpy(&p0, &raw.x, 4);
-        memcpy(&p1, &raw.y, 4);
-        const float2 f0 = __bfloat1622float2(p0), f1 = __bfloat1622float2(p1);
-        float amax = fmaxf(fmaxf(fabsf(f0.x), fabsf(f0.y)), fmaxf(fabsf(f1.x), fabsf(f1.y)));
-#pragma unroll
-        for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        const float d = __fdiv_rn(amax, 127.0f);
-        float id;
-        if (rounding == 2) id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-        else id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        const float dh = __half2float(__float2half_rn(d));
-        auto qd = [&](float v) {
-            const float sv = __fmul_rn(v, id);
-            const int q = rounding == 0 ? int(roundf(sv)) : __float2int_rn(sv);
-            return __float2half_rn(__fmul_rn(float(q), dh));
-        };
-        __half2 h0 = __halves2half2(qd(f0.x), qd(f0.y)), h1 = __halves2half2(qd(f1.x), qd(f1.y));
-        uint2 o;
-        memcpy(&o.x, &h0, 4);
-        memcpy(&o.y, &h1, 4);
-        *reinterpret_cast<uint2 *>(dst + e0) = o;
-    }
+    const uint4 *s4 = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) + t * H);
+    uint4 *d4 = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(xp) + int64_t(pos) * H);
+    for (int i = threadIdx.x; i < H / 8; i += blockDim.x) d4[i] = s4[i];
 }
 
 // k_moe_combine with 8 outputs per thread (y and out 16-byte aligned, H a multiple of 8)
@@ -1002,11 +969,9 @@ static void moe_experts(Moe &m, const void *x, int64_t tokens, const float *topk
     if (vec && m.q8) {
         // each token's Q8_0 staging once (not once per routed pair), then a 16-byte row copy
         launch_stage_rows_bf16(rounding, x, tokens, m.H, m.xs, nullptr, s);
-        k_moe_gather_vec<<<unsigned(P), 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16 *>(m.xs), m.plan.perm,
-                                                     m.plan.valid, P, m.H, m.topk, 0, rounding, m.xp);
+        k_moe_gather_vec<<<unsigned(P), 256, 0, s>>>(m.xs, m.plan.perm, m.plan.valid, P, m.H, m.topk, m.xp);
     } else if (vec)
-        k_moe_gather_vec<<<unsigned(P), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), m.plan.perm,
-                                                     m.plan.valid, P, m.H, m.topk, m.q8, rounding, m.xp);
+        k_moe_gather_vec<<<unsigned(P), 256, 0, s>>>(x, m.plan.perm, m.plan.valid, P, m.H, m.topk, m.xp);
     else
         k_moe_gather<<<unsigned(P), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), m.plan.perm, m.plan.valid,
                                                  P, m.H, m.topk, m.q8, rounding, m.xp);
