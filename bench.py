@@ -181,7 +181,8 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- peaks / traffic
 def measured_peaks():
-    """(peaks dict, "measured" | "fallback") from the pool's measured peak file."""
+    """(peaks dict, "measured" | "fallback"): the measured copy bandwidth and bf16 GEMM rates in
+    MEASURED_PEAKS.json beside this script when it exists, else fixed fallback figures."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())

@@ -11,8 +11,8 @@
  * written here from scratch, and (2) a row-parallel mul_mat loop standing in
  * for ggml_compute_forward_mul_mat (ggml-cpu.c:1255): quantize each fp32
  * activation row with the vec_dot_type quantizer, then one vec_dot per
- * (row, column). It is the CPU baseline "reference" leg and a second checker
- * for oracle/q8_oracle.c.
+ * (row, column). It is the CPU baseline "reference" leg and a second reference
+ * for the restatement in oracle/q8_oracle.c.
  */
 #include <stdint.h>
 #include <stddef.h>

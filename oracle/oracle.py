@@ -3,7 +3,7 @@
 numpy/ctypes front end of the CPU restatement in ``q8_oracle.c`` and of the
 reference's own vendored ggml quantizers compiled into ``_ref/`` (see the
 Makefile). Only tests, ``__graft_entry__.smoke`` and bench.py's CPU-baseline
-leg import this module, and only as the checker. The product package never
+leg import this module, and only to compare against. The product package never
 imports it.
 
 Byte formats follow ggml-common.h:194-199 (Q4_0, 18-byte blocks) and

@@ -3,7 +3,7 @@
  *
  * A plain-C restatement of the reference's block-quantized arithmetic for the
  * Q8_0 / Q4_0 linear contractions, used by the tests, the smoke check and the
- * CPU-baseline leg of bench.py as the checker. Nothing in the product path
+ * CPU-baseline leg of bench.py to compare against. Nothing in the product path
  * (mstar_accelerators_b200) links or calls this file.
  *
  * Every function names the reference file:line it restates (paths are inside

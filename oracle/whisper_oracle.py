@@ -9,7 +9,7 @@ weights (generic block order) plus bias; LayerNorm is ggml_norm + mul + add
 stock fp16-table form (decoder.cpp:580); the readout is Q4_0 (or Q8_0) mul_mat
 of the final-LayerNorm output, suppression, and the first-index / NaN-first
 argmax (decoder.cpp:583-588, 686-696). Parity of the pieces is pinned in
-tests/test_oracle.py; this composition is the checker for the GPU decoder.
+tests/test_oracle.py; the GPU decoder is compared against this composition.
 """
 from __future__ import annotations
 
