@@ -78,3 +78,31 @@ def test_rms_norm_and_residual_refusals(lib):
     assert rms(eps=-1.0)[1] == "invalid epsilon"
     rc, msg = _call(lib.mstar_b200_residual_add_bf16, FAKE, FAKE, 12, FAKE, None)
     assert (rc, msg) == (-1, "element count must be a multiple of 8")
+
+
+def test_pack_refusals(lib):
+    def pack(fmt=8, rows=4, width=64, inp=FAKE, out=FAKE + 4096, out_bytes=4 * 2 * 34):
+        return _call(lib.mstar_b200_pack, fmt, inp, rows * width * 4, out, out_bytes, rows, width, 1, 1, None)
+    assert pack(fmt=3) == (-1, "unsupported block format")
+    assert pack(width=48)[0] == -1 and pack(width=48)[1] != "unsupported block format"
+    # borrowed extents must be exactly the bytes the shape implies
+    assert pack(out_bytes=4 * 2 * 34 + 2)[1] == "invalid borrowed storage extent/alignment: packing output"
+    assert pack(out=FAKE + 512)[1] == "packing input/output overlap"
+
+
+def test_categorical_refusals(lib):
+    def cat(rows=2, vocab=100, ld=100, workspace_bytes=1 << 16, seeds=FAKE):
+        return _call(lib.mstar_b200_categorical, FAKE, rows, vocab, ld, seeds, FAKE + 256, FAKE + 512, FAKE + 768,
+                     FAKE + 1024, workspace_bytes, None)
+    assert cat(rows=0) == (-1, "rows must be 1..65535")
+    assert cat(ld=50)[1] == "invalid vocabulary extent"
+    assert cat(seeds=None)[1] == "missing sampling operand"
+    assert cat(workspace_bytes=1)[1] == "sampling workspace too small"
+
+
+def test_router_refusals(lib):
+    def route(experts=128, top_k=8, x=FAKE):
+        return _call(lib.mstar_b200_moe_route, x, 4, 2048, FAKE, experts, top_k, 1, FAKE, FAKE, FAKE, None)
+    assert route(x=None) == (-1, "missing router operand")
+    assert route(experts=300)[1] == "router geometry: 1..256 experts"
+    assert route(top_k=9)[1] == "top_k outside 1..8"
